@@ -1,0 +1,49 @@
+"""Shared test set-up: the ``gpu`` marker, the package import and the golden fixtures."""
+
+from __future__ import annotations
+
+import importlib
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def load_package():
+    """The product package lives in the directory ``spikingbrain-cpu_b200``."""
+    return importlib.import_module("spikingbrain-cpu_b200")
+
+
+def golden_cases(kind: str | None = None) -> list[str]:
+    meta = json.loads((GOLDEN / "golden_meta.json").read_text())["cases"]
+    return sorted(n for n, m in meta.items() if kind is None or m["kind"] == kind)
+
+
+_NPZ = None
+
+
+def golden(name: str) -> dict:
+    global _NPZ
+    if _NPZ is None:
+        _NPZ = dict(np.load(GOLDEN / "golden.npz"))
+    meta = json.loads((GOLDEN / "golden_meta.json").read_text())["cases"][name]
+    out = {k.split("/", 1)[1]: v for k, v in _NPZ.items() if k.startswith(name + "/")}
+    out["meta"] = meta
+    return out
+
+
+@pytest.fixture(scope="session")
+def sbq():
+    return load_package()
