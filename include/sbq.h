@@ -1,0 +1,154 @@
+/*
+ * sbq.h - C ABI of the B200 (sm_100a) int8 / int8-dyn quantised-linear library (libsbq.so).
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA stream handle
+ * (cudaStream_t passed as void*; NULL = the legacy default stream), launches asynchronously on
+ * that stream and returns an int status (SBQ_OK = 0).  Nothing here synchronises the device or
+ * allocates memory.  Argument errors are detected on the host before any launch.  The last error
+ * message of the calling host thread is available from sbq_last_error().
+ *
+ * Matrices are row-major.  "ld*" arguments are row strides in elements.  Weights are [n, k]
+ * (output channels x input features), activations [m, k], outputs [m, n] - the shapes of the
+ * reference's nn.Linear replacements.
+ *
+ * Packed weights: an int8 [n, k] matrix stored as 16 x 64 tiles of 1 KiB, tile (nt, kt) at byte
+ * (nt * ceil(k/64) + kt) * 1024, rows row-major inside the tile, padding zero-filled.  Its size is
+ * sbq_packed_bytes(n, k); it must be 256-byte aligned.
+ *
+ * Reference interfaces replaced (paths inside the reference project, spikingbrain_cpu/):
+ *   quant.py:25-29   quantize_per_channel             -> sbq_quantize_pack
+ *   quant.py:35-37   Int8Linear qweight/scale buffers  -> sbq_pack_int8 / sbq_unpack_int8
+ *   quant.py:41-53   Int8Linear.forward               -> sbq_linear_w8 (sbq_gemv_w8 / sbq_gemm_w8a16)
+ *   model.py:239-240 GatedMLP.forward (gate, up, SiLU) -> sbq_mlp_gateup_w8
+ *   quant.py:57-61   DynamicInt8Linear packing         -> sbq_quantize_pack (+ row sums)
+ *   quant.py:63-66   DynamicInt8Linear.forward        -> sbq_linear_dyn
+ *                    (= sbq_quant_act_per_tensor + sbq_gemm_w8a8)
+ */
+#ifndef SBQ_H_
+#define SBQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SBQ_API __attribute__((visibility("default")))
+#else
+#define SBQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------------- */
+#define SBQ_OK 0
+#define SBQ_ERR_INVALID_ARGUMENT 1 /* null pointer, negative or inconsistent size, bad stride */
+#define SBQ_ERR_ALIGNMENT 2        /* pointer or stride not aligned as the kernel requires    */
+#define SBQ_ERR_UNSUPPORTED 3      /* dtype / shape combination this build does not handle    */
+#define SBQ_ERR_CUDA 4             /* a CUDA runtime call or kernel launch failed             */
+#define SBQ_ERR_TIMEOUT 5          /* a bounded device-side wait expired (error flag set)     */
+#define SBQ_ERR_DEVICE 6           /* no device, or not an sm_100 device                      */
+#define SBQ_ERR_WORKSPACE 7        /* the workspace passed in is too small                    */
+
+/* ---- element types --------------------------------------------------------------------- */
+#define SBQ_F32 0
+#define SBQ_F16 1
+#define SBQ_BF16 2
+#define SBQ_I8 3
+#define SBQ_U8 4
+#define SBQ_I32 5
+
+/* ---- activation quantisation modes for the int8-dyn path ------------------------------- */
+#define SBQ_ACT_PER_TENSOR 0 /* the reference's mode: one uint8 scale + zero point per call */
+#define SBQ_ACT_PER_TOKEN 1  /* symmetric int8, one scale per row (no reference counterpart) */
+
+/* ---- library ---------------------------------------------------------------------------- */
+SBQ_API int sbq_version(void);                     /* MAJOR * 10000 + MINOR * 100 + PATCH */
+SBQ_API const char* sbq_last_error(void);          /* last message of this host thread ("" if none) */
+SBQ_API const char* sbq_status_string(int status); /* static name of a status code */
+
+/* Bytes of the packed layout of an [n, k] int8 weight. */
+SBQ_API size_t sbq_packed_bytes(int64_t n, int64_t k);
+
+/* ---- weight preparation (once per weight, at load) -------------------------------------- */
+
+/* quant.py:25-29 on the device: scale[r] = max(max_c |w[r,c]|, 1e-8) / 127 (fp32),
+ * q = clamp(rint(w / scale), -127, 127), written in the packed layout.  Bit-identical to the
+ * reference.  w is [n, k] with row stride ldw, dtype SBQ_F32, SBQ_BF16 or SBQ_F16.  rowsum (may be
+ * NULL) receives sum_c q[r, c] as int32 (used by the int8-dyn zero-point correction). */
+SBQ_API int sbq_quantize_pack(const void* w, int w_dtype, int64_t n, int64_t k, int64_t ldw, void* packed,
+                      float* scale, int32_t* rowsum, void* stream);
+
+/* Already-quantised int8 [n, k] (row stride ldq) -> packed layout (+ optional row sums).
+ * The state-dict load path of the qweight buffer (quant.py:36). */
+SBQ_API int sbq_pack_int8(const int8_t* q, int64_t n, int64_t k, int64_t ldq, void* packed, int32_t* rowsum,
+                  void* stream);
+
+/* Packed layout -> row-major int8 [n, k] (row stride ldq).  The state-dict save path. */
+SBQ_API int sbq_unpack_int8(const void* packed, int64_t n, int64_t k, int8_t* q, int64_t ldq, void* stream);
+
+/* ---- int8 weight-only linear (format "int8") --------------------------------------------- */
+
+/* Int8Linear.forward (quant.py:41-53): y[m, n] = (x[m, :] . q[n, :]) * scale[n] (+ bias[n]).
+ * x dtype SBQ_F16, SBQ_BF16 or SBQ_F32 (fp32 is split into two bf16 terms, ~16 mantissa bits);
+ * y dtype SBQ_F32 (the reference's output type) or SBQ_F16.  bias may be NULL.  Chooses the
+ * decode GEMV for small m and the tensor-memory GEMM otherwise. */
+SBQ_API int sbq_linear_w8(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
+                  const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
+                  void* stream);
+
+/* The decode GEMV alone (any m >= 1; streams the weight once per 16 rows of x). */
+SBQ_API int sbq_gemv_w8(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
+                const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
+                void* stream);
+
+/* The prefill GEMM alone: TMA-fed, int8 tiles dequantised to fp16 in shared memory, tcgen05 MMA
+ * with fp32 accumulators in tensor memory, scale epilogue.  x must be SBQ_F16. */
+SBQ_API int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
+                   const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
+                   void* stream);
+
+/* GatedMLP.forward's first half (model.py:239-240): h = silu(x q_gate^T * s_gate) * (x q_up^T * s_up),
+ * computed in one pass over both weights ([n, k] each) with h written as h_dtype (SBQ_F16 or
+ * SBQ_F32).  The down projection is a separate sbq_linear_w8 call on h. */
+SBQ_API int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const void* packed_gate,
+                      const float* scale_gate, const void* packed_up, const float* scale_up, int64_t m,
+                      int64_t n, int64_t k, void* h, int h_dtype, int64_t ldh, void* stream);
+
+/* ---- int8-dyn: dynamic activation quantisation + int8 x int8 -> int32 GEMM ------------- */
+
+/* Bytes of workspace sbq_linear_dyn / sbq_quant_act_* need for an [m, k] activation. */
+SBQ_API size_t sbq_dyn_workspace_bytes(int64_t m, int64_t k, int mode);
+
+/* Quantise x [m, k] (SBQ_F32 / SBQ_F16 / SBQ_BF16) the way fbgemm's dynamic linear does:
+ * per-tensor min/max (widened to 0), torch's ChooseQuantizationParams (uint8, zero point),
+ * xq = clamp(rint(fma(x, 1/s, zp)), 0, 255).  Writes xq (uint8 [m, k], row stride k), s_x (1 fp32)
+ * and zp (1 int32).  Bit-identical to the reference. */
+SBQ_API int sbq_quant_act_per_tensor(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, uint8_t* xq,
+                             float* s_x, int32_t* zp, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/* Per-token symmetric mode: s_t = max(max|x_t|, 1e-8) / 127, xq = clamp(rint(x / s_t), +-127) int8. */
+SBQ_API int sbq_quant_act_per_token(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int8_t* xq,
+                            float* s_tok, void* stream);
+
+/* acc[m, n] = sum_k (xq - zp) * q (per-tensor; xq uint8) or sum_k xq * q (per-token; xq int8),
+ * y = float(acc) * (s * scale[n]) (or fma with bias[n]).  rowsum is required for the per-tensor
+ * mode (zero-point correction).  acc_out (may be NULL) receives the int32 accumulators. */
+SBQ_API int sbq_gemm_w8a8(const void* xq, int mode, const void* packed, const int32_t* rowsum, const float* s_x,
+                  const int32_t* zp, const float* scale, const float* bias, int64_t m, int64_t n, int64_t k,
+                  float* y, int64_t ldy, int32_t* acc_out, void* stream);
+
+/* DynamicInt8Linear.forward (quant.py:63-66): quantise + GEMM + epilogue.  xq_out / s_out / zp_out
+ * may be NULL; when given they receive the quantised activation and its parameters.  workspace
+ * must hold sbq_dyn_workspace_bytes(m, k, mode) bytes. */
+SBQ_API int sbq_linear_dyn(const void* x, int x_dtype, int64_t ldx, int mode, const void* packed,
+                   const int32_t* rowsum, const float* scale, const float* bias, int64_t m, int64_t n,
+                   int64_t k, float* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SBQ_H_ */

@@ -1,0 +1,14 @@
+"""B200 (sm_100a) int8 / int8-dyn quantised-linear path of spikingbrain-cpu.
+
+A drop-in for ``spikingbrain_cpu.quant`` (same names and contracts) backed by libsbq.so, the
+hand-written CUDA kernels behind the C ABI in ``include/sbq.h``.  Import it by its directory
+name: ``importlib.import_module("spikingbrain-cpu_b200")``.
+"""
+
+from . import _lib, workloads
+from .mlp import FusedGatedMLP, fuse_gated_mlp
+from .quant import (FORMATS, BF16Linear, DynamicInt8Linear, FloatLinear, FP16Linear, Int8Linear, make_linear,
+                    pack_int8, pack_weight, quantize_per_channel, unpack_int8)
+
+__all__ = ["FORMATS", "BF16Linear", "DynamicInt8Linear", "FloatLinear", "FP16Linear", "Int8Linear", "make_linear",
+           "pack_int8", "pack_weight", "quantize_per_channel", "unpack_int8", "_lib", "workloads", "FusedGatedMLP", "fuse_gated_mlp"]

@@ -1,0 +1,74 @@
+"""Fused SwiGLU MLP over int8 projections (GatedMLP.forward, spikingbrain_cpu/model.py:239-240).
+
+The reference runs ``down(silu(gate(x)) * up(x))`` as three Int8Linear calls plus two
+elementwise ops.  For decode-sized inputs ``FusedGatedMLP`` streams the gate and up weights in one
+kernel (sbq_mlp_gateup_w8), applies SiLU(gate) * up in its epilogue, writes the hidden activation
+once (fp16 by default) and runs the down projection on it.  ``fuse_gated_mlp`` swaps the module
+in place inside a loaded model.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from . import _lib as L
+from .quant import _DTYPE_CODE, Int8Linear, _prepare_x, _ptr, _stream
+
+# Above this many rows the gate/up products go through the GEMM path instead of the fused GEMV.
+FUSED_MAX_ROWS = 64
+
+
+class FusedGatedMLP(nn.Module):
+    def __init__(self, gate: Int8Linear, up: Int8Linear, down: Int8Linear, h_dtype: torch.dtype = torch.float16):
+        super().__init__()
+        if not all(isinstance(mod, Int8Linear) for mod in (gate, up, down)):
+            raise ValueError("FusedGatedMLP needs int8 gate, up and down projections")
+        if gate.bias is not None or up.bias is not None:
+            raise ValueError("the fused gate/up epilogue has no bias term")
+        if gate.out_features != up.out_features or gate.in_features != up.in_features:
+            raise ValueError("gate and up projections must have the same shape")
+        if down.in_features != gate.out_features:
+            raise ValueError("down projection input must match the gate/up output")
+        if h_dtype not in (torch.float16, torch.float32):
+            raise ValueError("hidden activation dtype must be float16 or float32")
+        self.gate_proj, self.up_proj, self.down_proj = gate, up, down
+        self.h_dtype = h_dtype
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        dev = self.gate_proj.scale.device
+        x2, k16, on_host = _prepare_x(x, self.gate_proj.in_features, dev)
+        m, n = x2.shape[0], self.gate_proj.out_features
+        if m > FUSED_MAX_ROWS:
+            g = self.gate_proj(x2[:, :self.gate_proj.in_features])
+            h = torch.nn.functional.silu(g) * self.up_proj(x2[:, :self.gate_proj.in_features])
+        else:
+            h = torch.empty(m, n, dtype=self.h_dtype, device=dev)
+            if m > 0:
+                L.call("sbq_mlp_gateup_w8", _ptr(x2), _DTYPE_CODE[x2.dtype], x2.stride(0), _ptr(self.gate_proj.packed),
+                       _ptr(self.gate_proj.scale), _ptr(self.up_proj.packed), _ptr(self.up_proj.scale), m, n, k16,
+                       _ptr(h), L.F16 if self.h_dtype == torch.float16 else L.F32, n, _stream(dev))
+        y = self.down_proj(h).reshape(*shape[:-1], self.down_proj.out_features)
+        return y.to("cpu") if on_host else y
+
+
+def fuse_gated_mlp(model: nn.Module, h_dtype: torch.dtype = torch.float16) -> int:
+    """Replace every submodule holding int8 ``gate_proj``/``up_proj``/``down_proj`` by FusedGatedMLP.
+
+    Returns how many were replaced.
+    """
+    count = 0
+    for name, mod in list(model.named_modules()):
+        if isinstance(mod, FusedGatedMLP):
+            continue
+        parts = [getattr(mod, a, None) for a in ("gate_proj", "up_proj", "down_proj")]
+        if all(isinstance(p, Int8Linear) for p in parts) and parts[0].bias is None and parts[1].bias is None:
+            parent_name, _, child = name.rpartition(".")
+            parent = model.get_submodule(parent_name) if parent_name else None
+            fused = FusedGatedMLP(*parts, h_dtype=h_dtype)
+            if parent is None:
+                raise ValueError("cannot replace the root module in place")
+            setattr(parent, child, fused)
+            count += 1
+    return count

@@ -1,0 +1,62 @@
+"""The C-ABI library loads and exports every entry point include/sbq.h declares (no GPU needed)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from conftest import ROOT
+
+
+def declared_functions():
+    text = (ROOT / "include" / "sbq.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*SBQ_API\s+(?:const\s+)?\w+\**\s+\**(sbq_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "sbq_gemv_w8" in names and "sbq_linear_dyn" in names and len(names) >= 16
+
+
+def test_library_exports_every_declared_symbol(sbq):
+    lib = sbq._lib.load()
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_header(sbq):
+    assert set(declared_functions()) == set(sbq._lib.SIGNATURES)
+
+
+def test_host_side_calls_without_gpu(sbq):
+    lib = sbq._lib.load()
+    assert lib.sbq_version() >= 10000
+    assert lib.sbq_packed_bytes(16, 64) == 1024
+    assert lib.sbq_packed_bytes(17, 65) == 4096
+    assert lib.sbq_packed_bytes(0, 64) == 0
+    assert lib.sbq_status_string(0) == b"SBQ_OK"
+
+
+def test_argument_errors_raise_before_launch(sbq):
+    L = sbq._lib
+    # a null weight pointer is rejected on the host with ValueError (no device touched)
+    with pytest.raises(ValueError, match="SBQ_ERR_INVALID_ARGUMENT"):
+        L.call("sbq_gemv_w8", ctypes.c_void_p(16), L.F16, 64, None, None, None, 1, 16, 64, ctypes.c_void_p(16),
+               L.F32, 16, None)
+    with pytest.raises(ValueError, match="SBQ_ERR_UNSUPPORTED"):
+        L.call("sbq_gemv_w8", ctypes.c_void_p(256), 7, 64, ctypes.c_void_p(256), ctypes.c_void_p(256), None, 1, 16,
+               64, ctypes.c_void_p(256), L.F32, 16, None)
+    with pytest.raises(ValueError, match="SBQ_ERR_ALIGNMENT"):
+        L.call("sbq_gemv_w8", ctypes.c_void_p(8), L.F16, 64, ctypes.c_void_p(256), ctypes.c_void_p(256), None, 1, 16,
+               64, ctypes.c_void_p(256), L.F32, 16, None)
+    with pytest.raises(ValueError, match="multiple of 16"):
+        L.call("sbq_gemv_w8", ctypes.c_void_p(256), L.F16, 72, ctypes.c_void_p(256), ctypes.c_void_p(256), None, 1,
+               16, 72, ctypes.c_void_p(256), L.F32, 16, None)
+
+
+def test_make_linear_unknown_format(sbq):
+    import torch
+    with pytest.raises(ValueError, match="unknown weight format"):
+        sbq.make_linear("int4", torch.zeros(4, 4))
