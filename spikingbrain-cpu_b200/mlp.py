@@ -41,16 +41,28 @@ class FusedGatedMLP(nn.Module):
         x2, k16, on_host = _prepare_x(x, self.gate_proj.in_features, dev)
         m, n = x2.shape[0], self.gate_proj.out_features
         if m > FUSED_MAX_ROWS:
-            g = self.gate_proj(x2[:, :self.gate_proj.in_features])
-            h = torch.nn.functional.silu(g) * self.up_proj(x2[:, :self.gate_proj.in_features])
+            h = self.gateup_into(x2, torch.empty(m, n, dtype=torch.float32, device=dev))
         else:
-            h = torch.empty(m, n, dtype=self.h_dtype, device=dev)
-            if m > 0:
-                L.call("sbq_mlp_gateup_w8", _ptr(x2), _DTYPE_CODE[x2.dtype], x2.stride(0), _ptr(self.gate_proj.packed),
-                       _ptr(self.gate_proj.scale), _ptr(self.up_proj.packed), _ptr(self.up_proj.scale), m, n, k16,
-                       _ptr(h), L.F16 if self.h_dtype == torch.float16 else L.F32, n, _stream(dev))
+            h = self.gateup_into(x2, torch.empty(m, n, dtype=self.h_dtype, device=dev))
         y = self.down_proj(h).reshape(*shape[:-1], self.down_proj.out_features)
         return y.to("cpu") if on_host else y
+
+    def gateup_into(self, x2: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+        """Low-level device call: silu(gate(x2)) * up(x2) into ``h`` [m, n] (fp16/fp32, unit column stride).
+
+        x2 is [m, k'] with 16-byte aligned rows (k' = in_features rounded up to 16).  Rows beyond
+        FUSED_MAX_ROWS go through the unfused GEMM composition.
+        """
+        m, n = x2.shape[0], self.gate_proj.out_features
+        if m > FUSED_MAX_ROWS:
+            xk = x2[:, :self.gate_proj.in_features]
+            h.copy_(torch.nn.functional.silu(self.gate_proj(xk)) * self.up_proj(xk))
+        elif m > 0:
+            L.call("sbq_mlp_gateup_w8", _ptr(x2), _DTYPE_CODE[x2.dtype], x2.stride(0), _ptr(self.gate_proj.packed),
+                   _ptr(self.gate_proj.scale), _ptr(self.up_proj.packed), _ptr(self.up_proj.scale), m, n,
+                   x2.shape[1], _ptr(h), L.F16 if h.dtype == torch.float16 else L.F32, h.stride(0),
+                   _stream(h.device))
+        return h
 
 
 def fuse_gated_mlp(model: nn.Module, h_dtype: torch.dtype = torch.float16) -> int:

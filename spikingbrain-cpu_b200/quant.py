@@ -177,17 +177,25 @@ class Int8Linear(_PackedLinear):
         self.block = block
         self.out_dtype = torch.float32
 
+    def forward_into(self, x2: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Low-level device call: x2 [m, k'] (k' = in_features rounded up to 16, 16-byte aligned rows)
+        into ``out`` [m, out_features] (fp32 or fp16, unit column stride, any row stride)."""
+        m, n = x2.shape[0], self.out_features
+        if out.shape != (m, n) or out.stride(1) != 1 or out.dtype not in (torch.float32, torch.float16):
+            raise ValueError("output must be an fp32/fp16 [%d, %d] view with unit column stride" % (m, n))
+        if m > 0:
+            L.call("sbq_linear_w8", _ptr(x2), _DTYPE_CODE[x2.dtype], x2.stride(0), _ptr(self.packed),
+                   _ptr(self.scale), _ptr(self.bias), m, n, x2.shape[1], _ptr(out),
+                   L.F32 if out.dtype == torch.float32 else L.F16, out.stride(0), _stream(out.device))
+        return out
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape
         dev = self.scale.device
-        x2, k16, on_host = _prepare_x(x, self.in_features, dev)
-        m, n = x2.shape[0], self.out_features
-        out = torch.empty(m, n, dtype=self.out_dtype, device=dev)
-        if m > 0:
-            L.call("sbq_linear_w8", _ptr(x2), _DTYPE_CODE[x2.dtype], x2.stride(0), _ptr(self.packed),
-                   _ptr(self.scale), _ptr(self.bias), m, n, k16, _ptr(out),
-                   L.F32 if self.out_dtype == torch.float32 else L.F16, n, _stream(dev))
-        out = out.reshape(*shape[:-1], n)
+        x2, _, on_host = _prepare_x(x, self.in_features, dev)
+        out = torch.empty(x2.shape[0], self.out_features, dtype=self.out_dtype, device=dev)
+        self.forward_into(x2, out)
+        out = out.reshape(*shape[:-1], self.out_features)
         return out.to("cpu") if on_host else out
 
 

@@ -1,0 +1,184 @@
+"""Synthetic 36-layer projection stack (benchmark configuration 4), optionally output-channel sharded.
+
+Each layer holds the projections the hybrid model runs through its int8 linears
+(spikingbrain_cpu/model.py:232-301): q/k/v/o and the delta-net in/out projections
+([hidden x hidden] each) and the gate/up/down MLP ([inter x hidden], [hidden x inter]).  The data
+flow between them is real, so every projection depends on the one before it:
+
+    qkvd = [q | k | v | delta_in](x)          one GEMV/GEMM over the concatenated weight (fp16 out)
+    od   = [o(v) | delta_out(delta_in)]       two launches writing one fp16 buffer
+    h    = silu(gate(x)) * up(x)              fused gate/up kernel (fp16 h)
+    x'   = down(h)                            fp16, the next layer's input
+
+so a decode step streams every weight of every layer exactly once.  Constant factors are folded
+into the per-row scales of the projections whose outputs are consumed (v, delta_in, down) so
+the activations stay near unit variance over 36 layers; the int8 weights themselves follow the
+reference quantiser on ``N(0, 0.02)`` weights.
+
+Sharding (``world > 1``): rank r owns rows [r n / world, (r+1) n / world) of every projection and
+produces that slice of each output; ``torch.distributed.all_gather_into_tensor`` (NCCL over
+NVLink) assembles the full activation before its consumer.  x is replicated.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+
+from . import workloads as W
+from .mlp import FusedGatedMLP
+from .quant import Int8Linear
+
+
+def _fold(k: int, second_moment: float = 1.0) -> float:
+    """Factor that maps sum_k w x (w ~ N(0, 0.02)) of inputs with E[x^2] = second_moment to unit variance."""
+    return 1.0 / math.sqrt(k * 0.02 * 0.02 * second_moment)
+
+
+# E[(silu(g) * u)^2] for independent g, u ~ N(0, 0.02^2 * hidden) at hidden = 4096, estimated once.
+_H_MOMENT = 1.08
+
+
+class StackLayer(nn.Module):
+    def __init__(self, layer: int, hidden: int, inter: int, seed: int, device, rank: int = 0, world: int = 1):
+        super().__init__()
+        self.hidden, self.inter, self.rank, self.world = hidden, inter, rank, world
+        dev = torch.device(device)
+        base = seed * 1000 + layer * 16
+
+        def rows(w: torch.Tensor) -> torch.Tensor:
+            n = w.shape[0]
+            return w[rank * n // world:(rank + 1) * n // world]
+
+        def shard(n: int, k: int, idx: int) -> torch.Tensor:
+            return rows(W.float_weight(n, k, seed=base + idx, device=dev))
+
+        f_h = _fold(hidden)
+        # the concatenation is sharded as one matrix so the gathered output keeps the q|k|v|d order
+        qkvd_w = rows(torch.cat([W.float_weight(hidden, hidden, seed=base + i, device=dev) for i in range(4)], 0))
+        self.qkvd = Int8Linear(qkvd_w, None, device=dev)
+        self.qkvd.scale.mul_(f_h)
+        self.qkvd.out_dtype = torch.float16
+        self.o = Int8Linear(shard(hidden, hidden, 4), None, device=dev)
+        self.o.scale.mul_(f_h)
+        self.o.out_dtype = torch.float16
+        self.dout = Int8Linear(shard(hidden, hidden, 5), None, device=dev)
+        self.dout.scale.mul_(f_h)
+        self.dout.out_dtype = torch.float16
+        gate = Int8Linear(shard(inter, hidden, 6), None, device=dev)
+        up = Int8Linear(shard(inter, hidden, 7), None, device=dev)
+        down = Int8Linear(shard(hidden, inter, 8), None, device=dev)
+        down.scale.mul_(_fold(inter, _H_MOMENT))
+        down.out_dtype = torch.float16
+        self.mlp = FusedGatedMLP(gate, up, down)
+        del qkvd_w
+
+    def weight_bytes(self) -> int:
+        mods = (self.qkvd, self.o, self.dout, self.mlp.gate_proj, self.mlp.up_proj, self.mlp.down_proj)
+        return sum(m.out_features * m.in_features for m in mods)
+
+
+class ProjectionStack(nn.Module):
+    """The stack; ``forward(x)`` maps fp16 [m, hidden] to fp16 [m, hidden] on the device."""
+
+    def __init__(self, layers: int = W.LAYERS, hidden: int = W.HIDDEN, inter: int = W.INTER, seed: int = 4,
+                 device=None, group=None):
+        super().__init__()
+        import torch.distributed as dist
+
+        self.group = group
+        self.world = dist.get_world_size(group) if group is not None else 1
+        self.rank = dist.get_rank(group) if group is not None else 0
+        for n in (hidden, inter):
+            if n % (16 * self.world):
+                raise ValueError("%d rows do not split into %d 16-row shards" % (n, self.world))
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.device, self.hidden, self.inter = dev, hidden, inter
+        self.layers = nn.ModuleList(StackLayer(i, hidden, inter, seed, dev, self.rank, self.world)
+                                    for i in range(layers))
+
+    def weight_bytes(self) -> int:
+        """int8 weight bytes this rank streams per decode step."""
+        return sum(layer.weight_bytes() for layer in self.layers)
+
+    def _gather(self, part: torch.Tensor) -> torch.Tensor:
+        """[m, n/world] slice on every rank -> [m, n] everywhere (NCCL all-gather + reorder)."""
+        if self.world == 1:
+            return part
+        import torch.distributed as dist
+
+        m, ns = part.shape
+        buf = torch.empty(self.world * m, ns, dtype=part.dtype, device=part.device)
+        dist.all_gather_into_tensor(buf, part.contiguous(), group=self.group)
+        if m == 1:
+            return buf.view(1, self.world * ns)
+        return buf.view(self.world, m, ns).permute(1, 0, 2).reshape(m, self.world * ns)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """fp16 [m, hidden] on the device -> fp16 [m, hidden] (the last layer's down projection)."""
+        hd, w = self.hidden, self.world
+        m = x.shape[0]
+        for layer in self.layers:
+            qkvd = self._gather(layer.qkvd.forward_into(x, x.new_empty(m, 4 * hd // w)))
+            od = x.new_empty(m, 2 * hd // w)
+            layer.o.forward_into(qkvd[:, 2 * hd:3 * hd], od[:, :hd // w])
+            layer.dout.forward_into(qkvd[:, 3 * hd:], od[:, hd // w:])
+            self._gather(od)
+            h = self._gather(layer.mlp.gateup_into(x, x.new_empty(m, self.inter // w)))
+            x = self._gather(layer.mlp.down_proj.forward_into(h, x.new_empty(m, hd // w)))
+        return x
+
+    def launches_per_step(self, m: int) -> int:
+        """Kernels of this library one forward launches (GEMV path, m <= 16 rows per pass)."""
+        passes = -(-m // 16)
+        return len(self.layers) * 5 * passes
+
+
+class CapturedStack:
+    """ProjectionStack.forward captured once in a CUDA graph at a fixed batch size.
+
+    ``run()`` replays it on the device-resident input buffer ``x``; calling the object with a host
+    tensor copies it in (from pinned memory), replays the graph, copies the result back into a
+    pinned host buffer and waits for it, which is what a host-side caller of a decode step sees.
+    Launch overhead of the per-projection kernels disappears inside the graph.
+    """
+
+    def __init__(self, stack: ProjectionStack, m: int = 1, stream: torch.cuda.Stream | None = None):
+        self.stack = stack
+        self.stream = stream or torch.cuda.Stream(stack.device)
+        self.x = torch.zeros(m, stack.hidden, dtype=torch.float16, device=stack.device)
+        with torch.cuda.stream(self.stream):
+            stack(self.x)  # warm-up outside the capture (allocator, communicators)
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.y = stack(self.x)
+        self.x_host = torch.empty(m, stack.hidden, dtype=torch.float16).pin_memory()
+        self.y_host = torch.empty(m, stack.hidden, dtype=torch.float16).pin_memory()
+
+    def run(self) -> torch.Tensor:
+        with torch.cuda.stream(self.stream):
+            self.graph.replay()
+        return self.y
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if x.device.type == "cuda":
+            with torch.cuda.stream(self.stream):
+                self.x.copy_(x)
+                self.graph.replay()
+            return self.y
+        if x.data_ptr() != self.x_host.data_ptr():
+            self.x_host.copy_(x)
+        with torch.cuda.stream(self.stream):
+            self.x.copy_(self.x_host, non_blocking=True)
+            self.graph.replay()
+            self.y_host.copy_(self.y, non_blocking=True)
+        self.stream.synchronize()
+        return self.y_host
+
+    def release(self) -> None:
+        """Drop the graph (required before destroying a process group whose NCCL calls it holds)."""
+        self.graph.reset()
+        self.graph = None
