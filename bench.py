@@ -198,6 +198,7 @@ def main() -> None:
     runner = sbq.stack.CapturedStack(stack, m=1, stream=stream)
     x_static = runner.x
     x_static.copy_(sbq.workloads.activation(1, hidden, seed=5, device=dev))
+    torch.cuda.synchronize()
     graph = runner.graph
     for _ in range(args.warmup):
         runner.run()

@@ -37,8 +37,14 @@ def _fold(k: int, second_moment: float = 1.0) -> float:
     return 1.0 / math.sqrt(k * 0.02 * 0.02 * second_moment)
 
 
-# E[(silu(g) * u)^2] for independent g, u ~ N(0, 0.02^2 * hidden) at hidden = 4096, estimated once.
-_H_MOMENT = 1.08
+def _h_moment(hidden: int) -> float:
+    """E[(silu(g) * u)^2] for independent g, u ~ N(0, 0.02^2 * hidden) (unit-variance x), by quadrature."""
+    var = hidden * 0.02 * 0.02
+    sd = math.sqrt(var)
+    t = torch.linspace(-10.0, 10.0, 4001, dtype=torch.float64) * sd
+    pdf = torch.exp(-0.5 * (t / sd) ** 2) / (sd * math.sqrt(2.0 * math.pi))
+    silu2 = (t * torch.sigmoid(t)) ** 2
+    return float((silu2 * pdf).sum() * (t[1] - t[0])) * var
 
 
 class StackLayer(nn.Module):
@@ -70,7 +76,7 @@ class StackLayer(nn.Module):
         gate = Int8Linear(shard(inter, hidden, 6), None, device=dev)
         up = Int8Linear(shard(inter, hidden, 7), None, device=dev)
         down = Int8Linear(shard(hidden, inter, 8), None, device=dev)
-        down.scale.mul_(_fold(inter, _H_MOMENT))
+        down.scale.mul_(_fold(inter, _h_moment(hidden)))
         down.out_dtype = torch.float16
         self.mlp = FusedGatedMLP(gate, up, down)
         del qkvd_w
@@ -159,15 +165,24 @@ class CapturedStack:
         self.y_host = torch.empty(m, stack.hidden, dtype=torch.float16).pin_memory()
 
     def run(self) -> torch.Tensor:
+        """Replay on the device-resident ``x``; the caller's current stream is ordered after it."""
+        caller = torch.cuda.current_stream(self.stack.device)
+        self.stream.wait_stream(caller)
         with torch.cuda.stream(self.stream):
             self.graph.replay()
+        caller.wait_stream(self.stream)
         return self.y
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         if x.device.type == "cuda":
+            # the graph runs on its own (non-blocking) stream: order it after the producer of x and
+            # the caller's later work after it
+            caller = torch.cuda.current_stream(self.stack.device)
+            self.stream.wait_stream(caller)
             with torch.cuda.stream(self.stream):
                 self.x.copy_(x)
                 self.graph.replay()
+            caller.wait_stream(self.stream)
             return self.y
         if x.data_ptr() != self.x_host.data_ptr():
             self.x_host.copy_(x)

@@ -60,3 +60,12 @@ def test_make_linear_unknown_format(sbq):
     import torch
     with pytest.raises(ValueError, match="unknown weight format"):
         sbq.make_linear("int4", torch.zeros(4, 4))
+
+
+def test_package_surface(sbq):
+    # the drop-in names of spikingbrain_cpu/quant.py plus the stack and MLP modules
+    for name in ("FORMATS", "quantize_per_channel", "Int8Linear", "DynamicInt8Linear", "FP16Linear", "BF16Linear",
+                 "FloatLinear", "make_linear", "FusedGatedMLP", "fuse_gated_mlp", "stack", "workloads"):
+        assert hasattr(sbq, name), name
+    assert sbq.FORMATS == ("float32", "bfloat16", "float16", "int8", "int8-dyn")
+    assert hasattr(sbq.stack, "ProjectionStack") and hasattr(sbq.stack, "CapturedStack")

@@ -52,6 +52,8 @@ def test_captured_stack_matches_eager(sbq):
     assert torch.equal(host, eager)
     dev = runner(x.cuda()).cpu()
     assert torch.equal(dev, eager)
+    again = runner.run().cpu()
+    assert torch.equal(again, eager)
     runner.release()
 
 
