@@ -67,6 +67,11 @@ SBQ_API int sbq_version(void);                     /* MAJOR * 10000 + MINOR * 10
 SBQ_API const char* sbq_last_error(void);          /* last message of this host thread ("" if none) */
 SBQ_API const char* sbq_status_string(int status); /* static name of a status code */
 
+/* Synchronises the current device, then returns (and clears) the error a kernel recorded on the
+ * device: SBQ_ERR_TIMEOUT if one of its bounded waits expired, else SBQ_OK.  Diagnostic call; the
+ * launch entry points never synchronise. */
+SBQ_API int sbq_check_device_error(void);
+
 /* Bytes of the packed layout of an [n, k] int8 weight. */
 SBQ_API size_t sbq_packed_bytes(int64_t n, int64_t k);
 

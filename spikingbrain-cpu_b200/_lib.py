@@ -25,6 +25,7 @@ SIGNATURES = {
     "sbq_version": (_c_int, []),
     "sbq_last_error": (ctypes.c_char_p, []),
     "sbq_status_string": (ctypes.c_char_p, [_c_int]),
+    "sbq_check_device_error": (_c_int, []),
     "sbq_packed_bytes": (_sz, [_c_i64, _c_i64]),
     "sbq_quantize_pack": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _vp]),
     "sbq_pack_int8": (_c_int, [_vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp]),

@@ -1,0 +1,610 @@
+// Format "int8-dyn": dynamic activation quantisation and the int8 x int8 -> int32 tensor-memory GEMM.
+//
+// Reference: DynamicInt8Linear.forward (spikingbrain_cpu/quant.py:63-66), i.e. torch's
+// quantized::linear_dynamic on the fbgemm/x86 engine.  Restated bit for bit:
+//   1. min / max over the whole activation, widened to include 0;
+//   2. torch's ChooseQuantizationParams (uint8, qmin 0, qmax 255, no range reduction): double scale,
+//      zero point from whichever end rounds better, nudged with round-half-even; fp32 scale;
+//   3. xq = clamp(rint(fma(x, 1/s, zp)), 0, 255), 1/s an fp32 reciprocal, one rounding;
+//   4. acc = sum_k (xq - zp) * q  (int32);  5. y = float(acc) * (s * scale[n]) (fma with a bias).
+// The GEMM multiplies uint8 xq by the int8 weight on the tensor cores (tcgen05 kind::i8, int32
+// accumulators in tensor memory) and applies the zero-point correction acc - zp * rowsum[n] in the
+// epilogue, which is exact integer arithmetic.  The per-token mode (symmetric int8, one scale per
+// row, no reference counterpart) shares the GEMM with a signed A operand.
+#include "tc.cuh"
+
+namespace sbq {
+
+// ============================================================================ quantisation ====
+
+template <typename T>
+struct Vec;
+template <>
+struct Vec<float> {
+    static constexpr int kN = 4;
+    __device__ static void load(const float* p, float (&v)[4]) {
+        float4 t = __ldg(reinterpret_cast<const float4*>(p));
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    }
+};
+template <>
+struct Vec<__half> {
+    static constexpr int kN = 8;
+    __device__ static void load(const __half* p, float (&v)[8]) {
+        uint4 t = __ldg(reinterpret_cast<const uint4*>(p));
+        const __half2* h = reinterpret_cast<const __half2*>(&t);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float2 f = __half22float2(h[i]);
+            v[2 * i] = f.x; v[2 * i + 1] = f.y;
+        }
+    }
+};
+template <>
+struct Vec<__nv_bfloat16> {
+    static constexpr int kN = 8;
+    __device__ static void load(const __nv_bfloat16* p, float (&v)[8]) {
+        uint4 t = __ldg(reinterpret_cast<const uint4*>(p));
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&t);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float2 f = __bfloat1622float2(h[i]);
+            v[2 * i] = f.x; v[2 * i + 1] = f.y;
+        }
+    }
+};
+
+constexpr int kQuantThreads = 256;
+constexpr int kMaxPartials = 1024;
+
+// Step 1: per-CTA (min, max) of x [m, k] (row stride ldx; k a multiple of the vector width).
+template <typename T>
+__global__ void __launch_bounds__(kQuantThreads) minmax_partial_kernel(const T* __restrict__ x, int64_t ldx, int m,
+                                                                      int k, float2* __restrict__ partials) {
+    constexpr int V = Vec<T>::kN;
+    const int64_t per_row = k / V, total = (int64_t)m * per_row;
+    float mn = INFINITY, mx = -INFINITY;
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = v / per_row, col = (v - row * per_row) * V;
+        float e[V];
+        Vec<T>::load(x + row * ldx + col, e);
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            mn = fminf(mn, e[i]);
+            mx = fmaxf(mx, e[i]);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    __shared__ float2 red[kQuantThreads / 32];
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(mn, mx);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kQuantThreads / 32; ++w) {
+            mn = fminf(mn, red[w].x);
+            mx = fmaxf(mx, red[w].y);
+        }
+        partials[blockIdx.x] = make_float2(mn, mx);
+    }
+}
+
+// Step 2: torch ChooseQuantizationParams (quint8, reduce_range = false, preserve_sparsity = false).
+__device__ void choose_qparams(float mn, float mx, float* scale_out, int* zp_out) {
+    const int qmin = 0, qmax = 255;
+    const float small_scale = 6.1e-5f;
+    if (mn > 0.0f) mn = 0.0f;
+    if (mx < 0.0f) mx = 0.0f;
+    double scale = ((double)mx - (double)mn) / (double)(qmax - qmin);
+    if ((float)scale == 0.0f || isinf(__fdiv_rn(1.0f, (float)scale))) scale = 0.1;
+    if (scale < (double)small_scale) {
+        const float org_scale = (float)scale;
+        scale = small_scale;
+        if (mn == 0.0f) {
+            mx = __fmul_rn(small_scale, (float)(qmax - qmin));
+        } else if (mx == 0.0f) {
+            mn = -__fmul_rn(small_scale, (float)(qmax - qmin));
+        } else {
+            const float amplifier = __fdiv_rn(small_scale, org_scale);
+            mn = __fmul_rn(mn, amplifier);
+            mx = __fmul_rn(mx, amplifier);
+        }
+    }
+    const double zp_from_min = qmin - (double)mn / scale;
+    const double zp_from_max = qmax - (double)mx / scale;
+    const double err_min = fabs((double)qmin) - fabs((double)mn / scale);
+    const double err_max = fabs((double)qmax) - fabs((double)mx / scale);
+    const double zp0 = err_min < err_max ? zp_from_min : zp_from_max;
+    int zp;
+    if (zp0 < qmin) zp = qmin;
+    else if (zp0 > qmax) zp = qmax;
+    else zp = (int)rint(zp0);
+    *scale_out = (float)scale;
+    *zp_out = zp;
+}
+
+// Step 3.  Every CTA folds the partials and derives the parameters itself (identical result, no
+// grid-wide synchronisation or counters); CTA 0 publishes them.
+template <typename T>
+__global__ void __launch_bounds__(kQuantThreads) quantize_per_tensor_kernel(const T* __restrict__ x, int64_t ldx, int m,
+                                                                           int k, const float2* __restrict__ partials,
+                                                                           int nparts, uint8_t* __restrict__ xq,
+                                                                           float* __restrict__ s_out,
+                                                                           int32_t* __restrict__ zp_out) {
+    __shared__ float2 red[kQuantThreads / 32];
+    __shared__ float s_inv, s_zp;
+    float mn = INFINITY, mx = -INFINITY;
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+        const float2 p = partials[i];
+        mn = fminf(mn, p.x);
+        mx = fmaxf(mx, p.y);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(mn, mx);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kQuantThreads / 32; ++w) {
+            mn = fminf(mn, red[w].x);
+            mx = fmaxf(mx, red[w].y);
+        }
+        float s;
+        int zp;
+        choose_qparams(mn, mx, &s, &zp);
+        s_inv = __fdiv_rn(1.0f, s);
+        s_zp = (float)zp;
+        if (blockIdx.x == 0) {
+            *s_out = s;
+            *zp_out = zp;
+        }
+    }
+    __syncthreads();
+    const float inv = s_inv, fzp = s_zp;
+    constexpr int V = Vec<T>::kN;
+    const int64_t per_row = k / V, total = (int64_t)m * per_row;
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = v / per_row, col = (v - row * per_row) * V;
+        float e[V];
+        Vec<T>::load(x + row * ldx + col, e);
+        uint32_t packed[V / 4];
+#pragma unroll
+        for (int w = 0; w < V / 4; ++w) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float t = rintf(__fmaf_rn(e[4 * w + i], inv, fzp));
+                t = fminf(fmaxf(t, 0.0f), 255.0f);
+                word |= (uint32_t)t << (8 * i);
+            }
+            packed[w] = word;
+        }
+        uint8_t* dst = xq + row * (int64_t)k + col;
+        if (V == 4) {
+            *reinterpret_cast<uint32_t*>(dst) = packed[0];
+        } else {
+            *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[V / 4 - 1]);
+        }
+    }
+}
+
+// Per-token symmetric mode: one warp per row, s_t = max(max|x_t|, 1e-8) / 127, xq = clamp(rint(x / s_t)).
+template <typename T>
+__global__ void __launch_bounds__(kQuantThreads) quantize_per_token_kernel(const T* __restrict__ x, int64_t ldx, int m,
+                                                                          int k, int8_t* __restrict__ xq,
+                                                                          float* __restrict__ s_tok) {
+    constexpr int V = Vec<T>::kN;
+    const int row = blockIdx.x * (kQuantThreads / 32) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= m) return;
+    const T* xr = x + (int64_t)row * ldx;
+    float amax = 0.0f;
+    for (int c = lane * V; c < k; c += 32 * V) {
+        float e[V];
+        Vec<T>::load(xr + c, e);
+#pragma unroll
+        for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(e[i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float s = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
+    for (int c = lane * V; c < k; c += 32 * V) {
+        float e[V];
+        Vec<T>::load(xr + c, e);
+        uint32_t packed[V / 4];
+#pragma unroll
+        for (int w = 0; w < V / 4; ++w) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float t = rintf(__fdiv_rn(e[4 * w + i], s));
+                t = fminf(fmaxf(t, -127.0f), 127.0f);
+                word |= ((uint32_t)(int32_t)t & 0xFFu) << (8 * i);
+            }
+            packed[w] = word;
+        }
+        int8_t* dst = xq + (int64_t)row * k + c;
+        if (V == 4) {
+            *reinterpret_cast<uint32_t*>(dst) = packed[0];
+        } else {
+            *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[V / 4 - 1]);
+        }
+    }
+    if (lane == 0) s_tok[row] = s;
+}
+
+// ============================================================================ int8 GEMM ======
+
+struct GemmI8Params {
+    int m, n, k, num_kb;
+    const int32_t* rowsum;  // per-tensor zero-point correction (may be null in per-token mode)
+    const float* s_x;       // one scale (per-tensor) or one per row (per-token)
+    int s_stride;           // 0 or 1
+    const int32_t* zp;      // per-tensor zero point (null in per-token mode)
+    const float* scale;
+    const float* bias;
+    float* y;
+    int64_t ldy;
+    int32_t* acc_out;       // optional int32 accumulators (zero-point corrected), row stride n
+};
+
+constexpr int kI8BM = 128;         // rows of xq per CTA (MMA M)
+constexpr int kI8BK = 128;         // k per pipeline stage (bytes of an int8 row = one 128-byte swizzle row)
+constexpr int kI8Stages = 4;
+
+template <int BN>
+struct I8Smem {
+    static constexpr int kA = kI8BM * kI8BK;  // 16 KiB
+    static constexpr int kB = BN * kI8BK;     // two 64-wide halves of BN rows
+    static constexpr int kStage = kA + kB;
+    static constexpr int kBytes = kI8Stages * kStage + 1024 /* alignment */ + 256 /* barriers */ + BN * 12;
+};
+
+// One 128 x BN output tile per CTA.  Warp 0: TMA producer.  Warp 1: MMA issuer.  Warp 2: TMEM
+// allocation.  All four warps: epilogue (warp w owns accumulator lanes 32 w .. 32 w + 31).
+template <int BN, bool A_SIGNED>
+__global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                          const __grid_constant__ CUtensorMap tmap_b,
+                                                          const GemmI8Params p) {
+    using S = I8Smem<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kI8Stages * S::kStage);
+    uint64_t* empty = full + kI8Stages;
+    uint64_t* done = empty + kI8Stages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+    float* s_scale = reinterpret_cast<float*>(smem + kI8Stages * S::kStage + 256);
+    float* s_bias = s_scale + BN;
+    int32_t* s_rowsum = reinterpret_cast<int32_t*>(s_bias + BN);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * kI8BM, n0 = blockIdx.x * BN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kI8Stages; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        tc::mbar_init(done, 1);
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+        tc::prefetch_tmap(&tmap_a);
+        tc::prefetch_tmap(&tmap_b);
+    }
+    if (warp == 2) {
+        tc::tmem_alloc(tmem_slot, BN < 32 ? 32 : BN);
+        tc::tmem_relinquish();
+    }
+    for (int i = threadIdx.x; i < BN; i += blockDim.x) {
+        const int n = n0 + i;
+        s_scale[i] = n < p.n ? p.scale[n] : 0.0f;
+        s_bias[i] = (p.bias && n < p.n) ? p.bias[n] : 0.0f;
+        s_rowsum[i] = (p.rowsum && n < p.n) ? p.rowsum[n] : 0;
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+            const int s = kb % kI8Stages;
+            const uint32_t phase = (kb / kI8Stages) & 1;
+            if (!tc::mbar_wait(&empty[s], phase ^ 1)) { *abort_flag = 1; break; }
+            if (*(volatile int*)abort_flag) break;
+            uint8_t* a_s = smem + s * S::kStage;
+            uint8_t* b_s = a_s + S::kA;
+            tc::mbar_arrive_expect_tx(&full[s], S::kStage);
+            tc::tma_load_2d(a_s, &tmap_a, &full[s], kb * kI8BK, m0);
+            tc::tma_load_4d(b_s, &tmap_b, &full[s], 0, 0, 2 * kb, n0 / 16);
+            tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[s], 0, 0, 2 * kb + 1, n0 / 16);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer
+        constexpr uint32_t idesc = tc::idesc_i8(A_SIGNED, kI8BM, BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+            const int s = kb % kI8Stages;
+            const uint32_t phase = (kb / kI8Stages) & 1;
+            if (!tc::mbar_wait(&full[s], phase)) { *abort_flag = 1; break; }
+            tc::fence_after_sync();
+            const uint8_t* a_s = smem + s * S::kStage;
+            const uint8_t* b_s = a_s + S::kA;
+#pragma unroll
+            for (int j = 0; j < kI8BK / 32; ++j) {
+                const uint64_t ad = tc::smem_desc(a_s + j * 32, tc::kSwizzle128B, 1024);
+                const uint64_t bd = tc::smem_desc(b_s + (j >> 1) * (BN * 64) + (j & 1) * 32, tc::kSwizzle64B, 512);
+                tc::mma_i8(tmem, ad, bd, idesc, (kb | j) != 0);
+            }
+            tc::mma_commit(&empty[s]);
+        }
+        tc::mma_commit(done);
+    }
+    __syncwarp();
+
+    // ---- epilogue: wait for the accumulator, then TMEM -> registers -> global
+    const bool ok = tc::mbar_wait(done, 0);
+    tc::fence_after_sync();
+    if (ok && !*(volatile int*)abort_flag) {
+        const int row = m0 + warp * 32 + lane;
+        const float sx = p.s_x[p.s_stride ? (row < p.m ? row : 0) : 0];
+        const int32_t zp = p.zp ? *p.zp : 0;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
+            tc::tmem_wait_ld();
+            if (row >= p.m) continue;
+            const int nb = n0 + c * 32;
+            float* yrow = p.y + (int64_t)row * p.ldy;
+            int32_t* arow = p.acc_out ? p.acc_out + (int64_t)row * p.n : nullptr;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int n = nb + j;
+                if (n >= p.n) break;
+                const int i = c * 32 + j;
+                const int32_t a = (int32_t)r[j] - zp * s_rowsum[i];
+                const float f = __fmul_rn(sx, s_scale[i]);
+                const float af = __int2float_rn(a);
+                yrow[n] = p.bias ? __fmaf_rn(af, f, s_bias[i]) : __fmul_rn(af, f);
+                if (arow) arow[n] = a;
+            }
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 2) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, BN < 32 ? 32 : BN);
+    }
+}
+
+// ============================================================================ host side ======
+
+SBQ_DEFINE_ERROR_POLL(poll_error_dyn)
+
+static int check_x(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k) {
+    if (!x) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null activation pointer");
+    if (m <= 0 || k <= 0) return set_error(SBQ_ERR_INVALID_ARGUMENT, "m and k must be positive");
+    if (x_dtype != SBQ_F32 && x_dtype != SBQ_F16 && x_dtype != SBQ_BF16)
+        return set_error(SBQ_ERR_UNSUPPORTED, "activation dtype %d (f32, f16, bf16)", x_dtype);
+    if (k % 16) return set_error(SBQ_ERR_UNSUPPORTED, "k must be a multiple of 16 (k=%lld)", (long long)k);
+    const int es = x_dtype == SBQ_F32 ? 4 : 2;
+    if (ldx < k) return set_error(SBQ_ERR_INVALID_ARGUMENT, "row stride smaller than the row");
+    if (reinterpret_cast<uintptr_t>(x) % 16 || (ldx * es) % 16)
+        return set_error(SBQ_ERR_ALIGNMENT, "activation rows must be 16-byte aligned");
+    if (m >= (int64_t(1) << 31) || k >= (int64_t(1) << 30)) return set_error(SBQ_ERR_UNSUPPORTED, "shape too large");
+    return SBQ_OK;
+}
+
+static int minmax_blocks(int64_t m, int64_t k) {
+    const int64_t vecs = m * k / 4;
+    int64_t b = (vecs + kQuantThreads * 4 - 1) / (kQuantThreads * 4);
+    if (b > kMaxPartials) b = kMaxPartials;
+    return (int)(b < 1 ? 1 : b);
+}
+
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Workspace layout: [partials: kMaxPartials float2][xq: m*k bytes][s: m floats][zp: 1 int].
+struct DynWorkspace {
+    float2* partials;
+    uint8_t* xq;
+    float* s;
+    int32_t* zp;
+    size_t bytes;
+};
+
+static DynWorkspace dyn_workspace(void* base, int64_t m, int64_t k) {
+    DynWorkspace w{};
+    uint8_t* p = static_cast<uint8_t*>(base);
+    size_t off = 0;
+    w.partials = reinterpret_cast<float2*>(p + off);
+    off += align256(kMaxPartials * sizeof(float2));
+    w.xq = p + off;
+    off += align256((size_t)(m * k));
+    w.s = reinterpret_cast<float*>(p + off);
+    off += align256((size_t)m * sizeof(float));
+    w.zp = reinterpret_cast<int32_t*>(p + off);
+    off += 256;
+    w.bytes = off;
+    return w;
+}
+
+template <typename T>
+static void launch_quant_tensor(const void* x, int64_t ldx, int m, int k, float2* partials, uint8_t* xq, float* s,
+                                int32_t* zp, cudaStream_t st) {
+    const int nb = minmax_blocks(m, k);
+    minmax_partial_kernel<T><<<nb, kQuantThreads, 0, st>>>(static_cast<const T*>(x), ldx, m, k, partials);
+    quantize_per_tensor_kernel<T><<<nb, kQuantThreads, 0, st>>>(static_cast<const T*>(x), ldx, m, k, partials, nb, xq,
+                                                                s, zp);
+}
+
+template <typename T>
+static void launch_quant_token(const void* x, int64_t ldx, int m, int k, int8_t* xq, float* s, cudaStream_t st) {
+    const int rows_per_block = kQuantThreads / 32;
+    quantize_per_token_kernel<T><<<(m + rows_per_block - 1) / rows_per_block, kQuantThreads, 0, st>>>(
+        static_cast<const T*>(x), ldx, m, k, xq, s);
+}
+
+static int quant_tensor(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, float2* partials, uint8_t* xq,
+                        float* s, int32_t* zp, cudaStream_t st) {
+    switch (x_dtype) {
+        case SBQ_F32: launch_quant_tensor<float>(x, ldx, (int)m, (int)k, partials, xq, s, zp, st); break;
+        case SBQ_F16: launch_quant_tensor<__half>(x, ldx, (int)m, (int)k, partials, xq, s, zp, st); break;
+        default: launch_quant_tensor<__nv_bfloat16>(x, ldx, (int)m, (int)k, partials, xq, s, zp, st); break;
+    }
+    return check_launch("quantize activation (per tensor)");
+}
+
+static int quant_token(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int8_t* xq, float* s,
+                       cudaStream_t st) {
+    switch (x_dtype) {
+        case SBQ_F32: launch_quant_token<float>(x, ldx, (int)m, (int)k, xq, s, st); break;
+        case SBQ_F16: launch_quant_token<__half>(x, ldx, (int)m, (int)k, xq, s, st); break;
+        default: launch_quant_token<__nv_bfloat16>(x, ldx, (int)m, (int)k, xq, s, st); break;
+    }
+    return check_launch("quantize activation (per token)");
+}
+
+// Tensor maps: xq [m, k] bytes (SW128, 128 x 128 box) and the packed weight viewed as
+// {64 bytes, 16 rows, KT tiles, NT tile-rows} (SW64, one 64-wide tile column of BN rows per box).
+static int make_gemm_maps(CUtensorMap* ma, CUtensorMap* mb, const void* xq, int64_t m, int64_t k, const void* packed,
+                          int64_t n, int bn) {
+    const uint64_t kt = (uint64_t)ceil_div(k, kTileCols), nt = (uint64_t)ceil_div(n, kTileRows);
+    {
+        const uint64_t dims[2] = {(uint64_t)k, (uint64_t)m};
+        const uint64_t strides[1] = {(uint64_t)k};
+        const uint32_t box[2] = {kI8BK, kI8BM};
+        int st = encode_tmap(ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xq, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+    }
+    {
+        const uint64_t dims[4] = {64, 16, kt, nt};
+        const uint64_t strides[3] = {64, 1024, kt * 1024};
+        const uint32_t box[4] = {64, 16, 1, (uint32_t)(bn / 16)};
+        int st = encode_tmap(mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, packed, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_64B);
+        if (st) return st;
+    }
+    return SBQ_OK;
+}
+
+constexpr int kI8BN = 128;
+
+static int launch_gemm_i8(const void* xq, bool a_signed, const void* packed, const GemmI8Params& p, cudaStream_t st) {
+    CUtensorMap ma, mb;
+    int rc = make_gemm_maps(&ma, &mb, xq, p.m, p.k, packed, p.n, kI8BN);
+    if (rc) return rc;
+    const dim3 grid((unsigned)ceil_div(p.n, kI8BN), (unsigned)ceil_div(p.m, kI8BM));
+    const int smem = I8Smem<kI8BN>::kBytes;
+    if (a_signed) {
+        cudaFuncSetAttribute(gemm_w8a8_kernel<kI8BN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        gemm_w8a8_kernel<kI8BN, true><<<grid, 128, smem, st>>>(ma, mb, p);
+    } else {
+        cudaFuncSetAttribute(gemm_w8a8_kernel<kI8BN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        gemm_w8a8_kernel<kI8BN, false><<<grid, 128, smem, st>>>(ma, mb, p);
+    }
+    return check_launch("gemm_w8a8");
+}
+
+}  // namespace sbq
+
+using namespace sbq;
+
+extern "C" size_t sbq_dyn_workspace_bytes(int64_t m, int64_t k, int mode) {
+    (void)mode;
+    if (m <= 0 || k <= 0) return 0;
+    return dyn_workspace(nullptr, m, k).bytes;
+}
+
+extern "C" int sbq_quant_act_per_tensor(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, uint8_t* xq,
+                                        float* s_x, int32_t* zp, void* workspace, size_t workspace_bytes,
+                                        void* stream) {
+    int st = check_x(x, x_dtype, ldx, m, k);
+    if (st) return st;
+    if (!xq || !s_x || !zp || !workspace) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null output or workspace pointer");
+    if (workspace_bytes < kMaxPartials * sizeof(float2))
+        return set_error(SBQ_ERR_WORKSPACE, "workspace needs %zu bytes", (size_t)(kMaxPartials * sizeof(float2)));
+    if (reinterpret_cast<uintptr_t>(xq) % 16) return set_error(SBQ_ERR_ALIGNMENT, "xq must be 16-byte aligned");
+    return quant_tensor(x, x_dtype, ldx, m, k, static_cast<float2*>(workspace), xq, s_x, zp,
+                        static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sbq_quant_act_per_token(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, int8_t* xq,
+                                       float* s_tok, void* stream) {
+    int st = check_x(x, x_dtype, ldx, m, k);
+    if (st) return st;
+    if (!xq || !s_tok) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null output pointer");
+    if (reinterpret_cast<uintptr_t>(xq) % 16) return set_error(SBQ_ERR_ALIGNMENT, "xq must be 16-byte aligned");
+    return quant_token(x, x_dtype, ldx, m, k, xq, s_tok, static_cast<cudaStream_t>(stream));
+}
+
+static int check_gemm(const void* xq, int mode, const void* packed, const int32_t* rowsum, const float* s_x,
+                      const int32_t* zp, const float* scale, int64_t m, int64_t n, int64_t k, const float* y,
+                      int64_t ldy) {
+    if (!xq || !packed || !s_x || !scale || !y) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null pointer");
+    if (mode != SBQ_ACT_PER_TENSOR && mode != SBQ_ACT_PER_TOKEN)
+        return set_error(SBQ_ERR_INVALID_ARGUMENT, "unknown activation mode %d", mode);
+    if (mode == SBQ_ACT_PER_TENSOR && (!rowsum || !zp))
+        return set_error(SBQ_ERR_INVALID_ARGUMENT, "per-tensor mode needs rowsum and zp");
+    if (m <= 0 || n <= 0 || k <= 0) return set_error(SBQ_ERR_INVALID_ARGUMENT, "m, n, k must be positive");
+    if (k % 16) return set_error(SBQ_ERR_UNSUPPORTED, "k must be a multiple of 16");
+    if (ldy < n) return set_error(SBQ_ERR_INVALID_ARGUMENT, "ldy < n");
+    if (reinterpret_cast<uintptr_t>(xq) % 16 || reinterpret_cast<uintptr_t>(packed) % 256)
+        return set_error(SBQ_ERR_ALIGNMENT, "xq must be 16-byte and packed 256-byte aligned");
+    if (m >= (int64_t(1) << 31) || n >= (int64_t(1) << 31) || k >= (int64_t(1) << 30))
+        return set_error(SBQ_ERR_UNSUPPORTED, "shape too large");
+    return SBQ_OK;
+}
+
+extern "C" int sbq_gemm_w8a8(const void* xq, int mode, const void* packed, const int32_t* rowsum, const float* s_x,
+                             const int32_t* zp, const float* scale, const float* bias, int64_t m, int64_t n, int64_t k,
+                             float* y, int64_t ldy, int32_t* acc_out, void* stream) {
+    int st = check_gemm(xq, mode, packed, rowsum, s_x, zp, scale, m, n, k, y, ldy);
+    if (st) return st;
+    GemmI8Params p{};
+    p.m = (int)m;
+    p.n = (int)n;
+    p.k = (int)k;
+    p.num_kb = (int)ceil_div(k, kI8BK);
+    const bool per_tensor = mode == SBQ_ACT_PER_TENSOR;
+    p.rowsum = per_tensor ? rowsum : nullptr;
+    p.s_x = s_x;
+    p.s_stride = per_tensor ? 0 : 1;
+    p.zp = per_tensor ? zp : nullptr;
+    p.scale = scale;
+    p.bias = bias;
+    p.y = y;
+    p.ldy = ldy;
+    p.acc_out = acc_out;
+    return launch_gemm_i8(xq, !per_tensor, packed, p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sbq_linear_dyn(const void* x, int x_dtype, int64_t ldx, int mode, const void* packed,
+                              const int32_t* rowsum, const float* scale, const float* bias, int64_t m, int64_t n,
+                              int64_t k, float* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+    int st = check_x(x, x_dtype, ldx, m, k);
+    if (st) return st;
+    if (!workspace) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null workspace");
+    if (reinterpret_cast<uintptr_t>(workspace) % 256) return set_error(SBQ_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+    DynWorkspace w = dyn_workspace(workspace, m, k);
+    if (workspace_bytes < w.bytes) return set_error(SBQ_ERR_WORKSPACE, "workspace needs %zu bytes", w.bytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (mode == SBQ_ACT_PER_TENSOR) {
+        st = quant_tensor(x, x_dtype, ldx, m, k, w.partials, w.xq, w.s, w.zp, s);
+    } else if (mode == SBQ_ACT_PER_TOKEN) {
+        st = quant_token(x, x_dtype, ldx, m, k, reinterpret_cast<int8_t*>(w.xq), w.s, s);
+    } else {
+        return set_error(SBQ_ERR_INVALID_ARGUMENT, "unknown activation mode %d", mode);
+    }
+    if (st) return st;
+    return sbq_gemm_w8a8(w.xq, mode, packed, rowsum, w.s, w.zp, scale, bias, m, n, k, y, ldy, nullptr, stream);
+}

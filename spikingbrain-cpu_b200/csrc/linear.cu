@@ -1,5 +1,4 @@
-// Format-level entry points: Int8Linear.forward (GEMV / GEMM dispatch) and, until their kernels
-// land, the remaining int8-dyn entry points.
+// Format-level entry point of the int8 weight-only format: Int8Linear.forward (GEMV / GEMM dispatch).
 #include "common.cuh"
 
 namespace sbq {
@@ -18,26 +17,4 @@ extern "C" int sbq_linear_w8(const void* x, int x_dtype, int64_t ldx, const void
 extern "C" int sbq_gemm_w8a16(const void*, int, int64_t, const void*, const float*, const float*, int64_t, int64_t,
                               int64_t, void*, int, int64_t, void*) {
     return set_error(SBQ_ERR_UNSUPPORTED, "sbq_gemm_w8a16 not built yet");
-}
-
-extern "C" size_t sbq_dyn_workspace_bytes(int64_t, int64_t, int) { return 0; }
-
-extern "C" int sbq_quant_act_per_tensor(const void*, int, int64_t, int64_t, int64_t, uint8_t*, float*, int32_t*,
-                                        void*, size_t, void*) {
-    return set_error(SBQ_ERR_UNSUPPORTED, "not built yet");
-}
-
-extern "C" int sbq_quant_act_per_token(const void*, int, int64_t, int64_t, int64_t, int8_t*, float*, void*) {
-    return set_error(SBQ_ERR_UNSUPPORTED, "not built yet");
-}
-
-extern "C" int sbq_gemm_w8a8(const void*, int, const void*, const int32_t*, const float*, const int32_t*,
-                             const float*, const float*, int64_t, int64_t, int64_t, float*, int64_t, int32_t*,
-                             void*) {
-    return set_error(SBQ_ERR_UNSUPPORTED, "not built yet");
-}
-
-extern "C" int sbq_linear_dyn(const void*, int, int64_t, int, const void*, const int32_t*, const float*,
-                              const float*, int64_t, int64_t, int64_t, float*, int64_t, void*, size_t, void*) {
-    return set_error(SBQ_ERR_UNSUPPORTED, "not built yet");
 }

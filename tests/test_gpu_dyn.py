@@ -1,0 +1,111 @@
+"""GPU parity of the int8-dyn path (DynamicInt8Linear, spikingbrain_cpu/quant.py:56-66).
+
+The north star's bar: bit-exact int32 accumulators and quantised activations, and (since the
+epilogue is restated exactly) bit-exact fp32 outputs, against the reference's golden outputs and
+the oracle's integer stages.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden, golden_cases
+from oracle import quant_ref as R
+
+pytestmark = pytest.mark.gpu
+
+
+def _bits(a):
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def _x_tensor(g):
+    x = torch.from_numpy(g["x"])
+    if g["meta"]["x_dtype"] == "bfloat16":
+        x = x.to(torch.bfloat16)
+    return x
+
+
+@pytest.mark.parametrize("name", golden_cases("int8-dyn"))
+def test_dyn_matches_reference_golden_bit_exact(sbq, name):
+    g = golden(name)
+    bias = torch.from_numpy(g["bias"]) if "bias" in g else None
+    mod = sbq.DynamicInt8Linear(torch.from_numpy(g["w"]), bias)
+    y = mod(_x_tensor(g).cuda())
+    assert tuple(y.shape) == g["y"].shape
+    got = y.cpu().numpy()
+    assert np.array_equal(_bits(got), _bits(g["y"])), "mismatch fraction %.4f" % float((got != g["y"]).mean())
+
+
+@pytest.mark.parametrize("name", golden_cases("int8-dyn"))
+def test_dyn_integer_stages_bit_exact(sbq, name):
+    g = golden(name)
+    bias = torch.from_numpy(g["bias"]) if "bias" in g else None
+    mod = sbq.DynamicInt8Linear(torch.from_numpy(g["w"]), bias)
+    x = _x_tensor(g)
+    y, xq, s, zp, acc = mod.forward_stages(x.cuda())
+    ry, rxq, rs, rzp, racc = R.dyn_linear(x.float().numpy().reshape(-1, x.shape[-1]), g["q"], g["scale"], g.get("bias"))
+    assert float(s.item()) == float(rs) and int(zp.item()) == rzp
+    assert np.array_equal(xq.cpu().numpy(), rxq)
+    assert np.array_equal(acc.cpu().numpy(), racc)
+    assert np.array_equal(_bits(y.cpu().numpy()), _bits(ry))
+
+
+def test_config3_full_size(sbq):
+    cfg = sbq.workloads.CONFIGS[3]
+    m, k, n = cfg["m"], cfg["k"], cfg["n"]
+    w = sbq.workloads.float_weight(n, k, seed=30)
+    x = sbq.workloads.activation(m, k, seed=31)  # fp16 N(0, 1), the configuration's input
+    q, sc = R.quantize_per_channel(w.numpy())
+    mod = sbq.DynamicInt8Linear(w, None)
+    y, xq, s, zp, acc = mod.forward_stages(x.cuda())
+    rows = np.array([0, 1, 77, 128, 255, 256, 383, 510, 511])
+    ry, rxq, rs, rzp, racc = R.dyn_linear(x.float().numpy(), q, sc, rows=rows)
+    assert float(s.item()) == float(rs) and int(zp.item()) == rzp
+    # every quantised activation, and the sampled rows' accumulators and outputs
+    full_xq = R.dyn_quantize(x.float().numpy(), rs, rzp)
+    assert np.array_equal(xq.cpu().numpy(), full_xq)
+    assert np.array_equal(acc.cpu().numpy()[rows], racc)
+    assert np.array_equal(_bits(y.cpu().numpy()[rows]), _bits(ry))
+    # forward() (fused workspace path) gives the same output as the staged path
+    assert torch.equal(mod(x.cuda()), y)
+    assert sbq._lib.load().sbq_check_device_error() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 4, 64), (3, 40, 192), (127, 130, 320), (129, 300, 256), (200, 64, 2560),
+                                   (257, 4096, 128), (64, 1024, 2560)])
+@pytest.mark.parametrize("xdtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_dyn_shapes_bit_exact(sbq, m, n, k, xdtype):
+    w = sbq.workloads.float_weight(n, k, seed=m + n)
+    x = sbq.workloads.activation(m, k, seed=k, dtype=xdtype) * 2.5
+    q, sc = R.quantize_per_channel(w.numpy())
+    mod = sbq.DynamicInt8Linear(w, None)
+    y = mod(x.cuda()).cpu().numpy()
+    ry = R.dyn_linear(x.float().numpy(), q, sc)[0]
+    assert np.array_equal(_bits(y), _bits(ry)), "mismatch fraction %.4f" % float((y != ry).mean())
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 64, 128), (5, 130, 320), (128, 256, 512), (300, 200, 1024)])
+def test_per_token_mode_bit_exact(sbq, m, n, k):
+    w = sbq.workloads.float_weight(n, k, seed=n)
+    x = sbq.workloads.activation(m, k, seed=m, dtype=torch.float32)
+    x[0] = 0.0  # an all-zero token takes the 1e-8 floor
+    q, sc = R.quantize_per_channel(w.numpy())
+    mod = sbq.DynamicInt8Linear(w, None, mode="per_token")
+    y, xq, s, _, acc = mod.forward_stages(x.cuda())
+    ry, rxq, rs, racc = R.tok_linear(x.numpy(), q, sc)
+    assert np.array_equal(_bits(s.cpu().numpy()), _bits(rs))
+    assert np.array_equal(xq.cpu().numpy(), rxq)
+    assert np.array_equal(acc.cpu().numpy(), racc)
+    assert np.array_equal(_bits(y.cpu().numpy()), _bits(ry))
+    assert torch.equal(mod(x.cuda()), y)
+
+
+def test_dyn_host_input_and_batch_dims(sbq):
+    w = sbq.workloads.float_weight(48, 128, seed=40)
+    x = sbq.workloads.activation(6, 128, seed=41, dtype=torch.float32).reshape(2, 3, 128)
+    mod = sbq.DynamicInt8Linear(w, None)
+    y = mod(x)
+    assert y.device.type == "cpu" and tuple(y.shape) == (2, 3, 48)
+    q, sc = R.quantize_per_channel(w.numpy())
+    assert np.array_equal(_bits(y.numpy().reshape(6, 48)), _bits(R.dyn_linear(x.numpy().reshape(6, 128), q, sc)[0]))
