@@ -152,6 +152,23 @@ SBQ_API int sbq_linear_dyn(const void* x, int x_dtype, int64_t ldx, int mode, co
                    int64_t k, float* y, int64_t ldy, void* workspace, size_t workspace_bytes,
                    void* stream);
 
+/* sbq_linear_dyn for callers that cannot allocate device memory.  No counterpart in the reference.
+ * Some hosts of this library are not allowed to call cudaMalloc: a runtime that has already handed
+ * every byte of HBM to its own pool, a plain C / FFI caller that holds raw pointers but has no
+ * allocator, or a latency-critical decode loop where cudaMalloc / cudaFree would synchronise the
+ * device.  This entry point allocates nothing (no cudaMalloc, cudaFree or allocating library call):
+ * its scratch is a fixed 4 MiB array in the library's device memory, which every GPU that loads the
+ * library holds until the process exits.  The caller still passes x, the weight buffers and y.
+ * Limit: sbq_dyn_workspace_bytes(m, k, mode) must be <= 4 MiB (m * k up to about 4.18 million,
+ * e.g. up to 1020 rows at k = 4096); larger calls return SBQ_ERR_WORKSPACE without launching.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  Every call shares the one array and
+ * leaves its contents behind, so calls that overlap on the GPU (other streams, other threads) race;
+ * order them on one stream. */
+SBQ_API int sbq_linear_dyn_noalloc(const void* x, int x_dtype, int64_t ldx, int mode, const void* packed,
+                                   const int32_t* rowsum, const float* scale, const float* bias, int64_t m,
+                                   int64_t n, int64_t k, float* y, int64_t ldy, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,6 +42,8 @@ SIGNATURES = {
                                _vp]),
     "sbq_linear_dyn": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_i64,
                                 _vp, _sz, _vp]),
+    "sbq_linear_dyn_noalloc": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp,
+                                        _c_i64, _vp]),
 }
 
 _LIB: ctypes.CDLL | None = None

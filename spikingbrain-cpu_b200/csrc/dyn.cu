@@ -608,3 +608,58 @@ extern "C" int sbq_linear_dyn(const void* x, int x_dtype, int64_t ldx, int mode,
     if (st) return st;
     return sbq_gemm_w8a8(w.xq, mode, packed, rowsum, w.s, w.zp, scale, bias, m, n, k, y, ldy, nullptr, stream);
 }
+
+// ============================================================================ no-allocation variant
+
+// sbq_linear_dyn without a caller-provided workspace.  Its scratch (min/max partials, quantised
+// activations, per-row scales, zero point) lives in this fixed device array, which every GPU that
+// loads the library holds until the process exits.  The array is only ever written before it is
+// read within one call, so nothing in it has to start at zero; calls that overlap on the GPU share
+// it and race.
+#include <mutex>
+
+namespace sbq {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+
+// Host-side address of the array on the current device, looked up once per device.
+static int noalloc_scratch(void** out) {
+    static std::mutex mu;
+    static void* addr[kNoAllocMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return check_launch("cudaGetDevice");
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return set_error(SBQ_ERR_DEVICE, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess)
+            return set_error(SBQ_ERR_CUDA, "cudaGetSymbolAddress of the scratch array failed: %s", cudaGetErrorString(e));
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return SBQ_OK;
+}
+
+}  // namespace sbq
+
+extern "C" int sbq_linear_dyn_noalloc(const void* x, int x_dtype, int64_t ldx, int mode, const void* packed,
+                                      const int32_t* rowsum, const float* scale, const float* bias, int64_t m,
+                                      int64_t n, int64_t k, float* y, int64_t ldy, void* stream) {
+    int st = check_x(x, x_dtype, ldx, m, k);
+    if (st) return st;
+    const size_t need = dyn_workspace(nullptr, m, k).bytes;
+    if (need > kNoAllocScratchBytes)
+        return set_error(SBQ_ERR_WORKSPACE,
+                         "m=%lld x k=%lld needs %zu bytes of scratch, above the fixed %zu-byte array of "
+                         "sbq_linear_dyn_noalloc; use sbq_linear_dyn with a workspace",
+                         (long long)m, (long long)k, need, kNoAllocScratchBytes);
+    void* scratch = nullptr;
+    st = noalloc_scratch(&scratch);
+    if (st) return st;
+    return sbq_linear_dyn(x, x_dtype, ldx, mode, packed, rowsum, scale, bias, m, n, k, y, ldy, scratch,
+                          kNoAllocScratchBytes, stream);
+}
