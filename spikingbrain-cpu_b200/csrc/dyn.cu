@@ -348,9 +348,10 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
     __syncwarp();
 
     // ---- epilogue: wait for the accumulator, then TMEM -> registers -> global
-    const bool ok = tc::mbar_wait(done, 0);
+    // warp-uniform decision: tcgen05.ld below is a warp-collective instruction
+    const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(done, 0) && !*(volatile int*)abort_flag);
     tc::fence_after_sync();
-    if (ok && !*(volatile int*)abort_flag) {
+    if (ok) {
         const int row = m0 + warp * 32 + lane;
         const float sx = p.s_x[p.s_stride ? (row < p.m ? row : 0) : 0];
         const int32_t zp = p.zp ? *p.zp : 0;

@@ -41,7 +41,7 @@ class FusedGatedMLP(nn.Module):
         x2, k16, on_host = _prepare_x(x, self.gate_proj.in_features, dev)
         m, n = x2.shape[0], self.gate_proj.out_features
         if m > FUSED_MAX_ROWS:
-            h = self.gateup_into(x2, torch.empty(m, n, dtype=torch.float32, device=dev))
+            h = self.gateup_into(x2, torch.empty(m, n, dtype=self.h_dtype, device=dev))
         else:
             h = self.gateup_into(x2, torch.empty(m, n, dtype=self.h_dtype, device=dev))
         y = self.down_proj(h).reshape(*shape[:-1], self.down_proj.out_features)
