@@ -164,6 +164,132 @@ def reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def _graph_time(fn, stream, reps: int, warmup: int) -> float:
+    """ms per call of ``fn`` (captured once into a CUDA graph, replayed ``reps`` times)."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        fn()
+    stream.synchronize()
+    g, _ = capture(fn, stream)
+    for _ in range(warmup):
+        g.replay()
+    ms = timed_graph(g, reps, stream)
+    del g
+    return ms
+
+
+def kernel_cases(sbq, dev, stream, steps: int, warmup: int, which=("gemv", "mlp", "gemm", "dyn")) -> dict:
+    """Configurations 0-3 at their own shapes, each kernel timed alone (CUDA graph, CUDA events).
+
+    HBM-bound cases rotate over enough distinct weight copies that every launch reads its weight
+    from HBM (the copies together exceed twice the 126 MB L2).
+    """
+    import torch
+    from ctypes import c_void_p as vp
+
+    L = sbq._lib
+    W = sbq.workloads
+    st = vp(stream.cuda_stream)
+    pk = peaks()
+    out = {}
+
+    def int8_weights(n, k, copies):
+        mods = []
+        for c in range(copies):
+            q = torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev)
+            packed, rs = sbq.pack_int8(q, rowsum=True)
+            mods.append((packed, (torch.rand(n, device=dev) + 0.5) * (1.0 / (127.0 * k ** 0.5)), rs))
+        return mods
+
+    if "gemv" in which:  # configuration 0: m=1, k=n=4096
+        n = k = W.HIDDEN
+        copies = 16
+        ws = int8_weights(n, k, copies)
+        x = W.activation(1, k, seed=0, device=dev)
+        y = torch.empty(1, n, device=dev)
+
+        def f():
+            for p_, s_, _ in ws:
+                L.call("sbq_gemv_w8", vp(x.data_ptr()), L.F16, k, vp(p_.data_ptr()), vp(s_.data_ptr()), None, 1, n, k,
+                       vp(y.data_ptr()), L.F32, n, st)
+
+        ms = _graph_time(f, stream, max(20, steps // 10), warmup) / copies
+        b = n * k + 4 * n + 2 * k + 4 * n
+        out["cfg0_gemv"] = {"us": round(ms * 1e3, 3), "gbs": round(b / ms / 1e6, 1),
+                            "frac_hbm": round(b / ms / 1e6 / pk["hbm_gbs"], 4), "bytes": b}
+        del ws
+
+    if "mlp" in which:  # configuration 1: fused gate/up + down at m in {1, 4, 16}
+        k, n = W.HIDDEN, W.INTER
+        gs, us_, ds = int8_weights(n, k, 2), int8_weights(n, k, 2), int8_weights(k, n, 2)
+        res = {}
+        for m in (1, 4, 16):
+            x = W.activation(m, k, seed=m, device=dev)
+            h = torch.empty(m, n, dtype=torch.float16, device=dev)
+            y = torch.empty(m, k, device=dev)
+
+            def f():
+                for i in range(2):
+                    g, u, d = gs[i], us_[i], ds[i]
+                    L.call("sbq_mlp_gateup_w8", vp(x.data_ptr()), L.F16, k, vp(g[0].data_ptr()), vp(g[1].data_ptr()),
+                           vp(u[0].data_ptr()), vp(u[1].data_ptr()), m, n, k, vp(h.data_ptr()), L.F16, n, st)
+                    L.call("sbq_gemv_w8", vp(h.data_ptr()), L.F16, n, vp(d[0].data_ptr()), vp(d[1].data_ptr()), None,
+                           m, k, n, vp(y.data_ptr()), L.F32, k, st)
+
+            ms = _graph_time(f, stream, max(20, steps // 10), warmup) / 2
+            b = 3 * n * k + 12 * n + 4 * k + 2 * m * k + 4 * m * n + 4 * m * k
+            res[str(m)] = {"us": round(ms * 1e3, 3), "gbs": round(b / ms / 1e6, 1),
+                           "frac_hbm": round(b / ms / 1e6 / pk["hbm_gbs"], 4)}
+        out["cfg1_mlp"] = res
+        del gs, us_, ds
+
+    if "gemm" in which:  # configuration 2: m=2048, k=4096, n=12288, fp16 out
+        m, k, n = 2048, W.HIDDEN, W.INTER
+        (p_, s_, _), = int8_weights(n, k, 1)
+        x = W.activation(m, k, seed=2, device=dev)
+        y = torch.empty(m, n, dtype=torch.float16, device=dev)
+
+        def f():
+            L.call("sbq_gemm_w8a16", vp(x.data_ptr()), L.F16, k, vp(p_.data_ptr()), vp(s_.data_ptr()), None, m, n, k,
+                   vp(y.data_ptr()), L.F16, n, st)
+
+        ms = _graph_time(f, stream, max(20, steps // 10), warmup)
+        fl = 2 * m * n * k
+        out["cfg2_prefill_gemm"] = {"us": round(ms * 1e3, 2), "tflops": round(fl / ms / 1e9, 1),
+                                    "frac_bf16_peak": round(fl / ms / 1e9 / pk["bf16_tflops"], 4)}
+
+    if "dyn" in which:  # configuration 3: int8-dyn, m=512, k=n=4096
+        m, k, n = 512, W.HIDDEN, W.HIDDEN
+        (p_, s_, rs), = int8_weights(n, k, 1)
+        x = W.activation(m, k, seed=3, device=dev)
+        y = torch.empty(m, n, device=dev)
+        wsb = int(L.load().sbq_dyn_workspace_bytes(m, k, 0))
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+
+        def f():
+            L.call("sbq_linear_dyn", vp(x.data_ptr()), L.F16, k, 0, vp(p_.data_ptr()), vp(rs.data_ptr()),
+                   vp(s_.data_ptr()), None, m, n, k, vp(y.data_ptr()), n, vp(ws.data_ptr()), wsb, st)
+
+        ms = _graph_time(f, stream, max(20, steps // 10), warmup)
+        ops = 2 * m * n * k
+        out["cfg3_dyn"] = {"us": round(ms * 1e3, 2), "tops": round(ops / ms / 1e9, 1),
+                           "frac_int8_spec_4500": round(ops / ms / 1e9 / 4500.0, 4)}
+    return out
+
+
+def kernel_mode(args) -> None:
+    """--kernel NAME: one configuration's kernel alone (also the command the ncu captures use)."""
+    import torch
+
+    sbq = importlib.import_module("spikingbrain-cpu_b200")
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(dev)
+    res = kernel_cases(sbq, dev, stream, args.steps, args.warmup, which=(args.kernel,))
+    print(json.dumps({"kernel": args.kernel, "steps": args.steps, "warmup": args.warmup, "results": res}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -172,11 +298,16 @@ def main() -> None:
     ap.add_argument("--impl", default="sbq", choices=("sbq", "reference"))
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline measurement")
+    ap.add_argument("--no-extra", action="store_true", help="skip the per-configuration kernel timings")
+    ap.add_argument("--kernel", choices=("gemv", "mlp", "gemm", "dyn"), help="time one configuration's kernel alone")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.kernel:
+        kernel_mode(args)
         return
 
     import torch
@@ -265,6 +396,10 @@ def main() -> None:
     achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
     del g2
 
+    extra = None
+    if world == 1 and not args.no_extra:
+        extra = kernel_cases(sbq, dev, stream, args.steps, args.warmup)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import cpu_port
@@ -295,6 +430,7 @@ def main() -> None:
                     "d2h_bytes_per_step": 2 * hidden, "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": stack.launches_per_step(1) * args.steps,
             "clocks": clocks.summary(),
+            "configs_0_3": extra,
         }
         print(json.dumps(line), flush=True)
     runner.release()

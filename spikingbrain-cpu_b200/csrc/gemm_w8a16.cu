@@ -2,15 +2,17 @@
 //
 // Reference: Int8Linear.forward (spikingbrain_cpu/quant.py:41-53) at prefill shapes (512-token
 // chunks, model.py:439).  The reference dequantises 128-row weight blocks to fp32 and runs an fp32
-// sgemm, then scales.  Here:
-//   * warp 0 (one thread) streams 128 x 64 fp16 activation tiles (TMA, 128-byte swizzle) and the
-//     matching 256 x 64 int8 weight tiles (TMA over the packed layout, no swizzle) into a 4-stage ring;
-//   * warps 4-7 convert each int8 tile to fp16 (exact) into a 2-deep ring of K-major,
-//     128-byte-swizzled operand buffers, then hand them to the MMA thread;
-//   * warp 1 (one thread) issues tcgen05.mma.cta_group::1.kind::f16 (128 x 256 x 16, fp32
-//     accumulators in tensor memory) and commits each stage back to its producers;
-//   * warps 4-7 finally read the accumulators (tcgen05.ld), apply the fp32 per-row scale (and bias)
-//     and store fp16 or fp32 output.
+// sgemm, then scales.  Here one CTA computes a 128-channel x 256-token tile, transposed (channels
+// are the MMA's M):
+//   * warp 0 (one thread) streams 256 x 64 fp16 activation tiles (TMA, 128-byte swizzle) and the
+//     matching 128 x 64 int8 weight tiles (TMA over the packed layout, 64-byte swizzle) into a
+//     5-stage ring;
+//   * warps 4-7 (one weight row per thread) convert each int8 row to fp16 in registers (exact) and
+//     write it straight into tensor memory with tcgen05.st - the MMA's A operand - double-buffered;
+//   * warp 1 (one thread) issues tcgen05.mma.cta_group::1.kind::f16 with A from tensor memory and
+//     the activation tile from shared memory (128 x 256 x 16, fp32 accumulators in TMEM);
+//   * warps 4-7 finally read their channel's accumulators (tcgen05.ld), apply the fp32 per-row
+//     scale (and bias) and store fp16 or fp32 output, consecutive channels per warp store.
 // The scale stays in the fp32 epilogue, as in the reference: int8 values are exact in fp16.
 #include "tc.cuh"
 
@@ -22,23 +24,24 @@ struct GemmW16Params {
     const float* bias;
     void* y;
     int64_t ldy;
-    int out_f16;
 };
 
-constexpr int kWBM = 128;      // activation rows per CTA (MMA M)
-constexpr int kWBN = 256;      // output channels per CTA (MMA N)
+constexpr int kWCh = 128;      // output channels per CTA (MMA M, one per TMEM lane)
+constexpr int kWTok = 256;     // activation rows per CTA (MMA N)
 constexpr int kWBK = 64;       // k per stage (one 128-byte fp16 row, one packed tile column)
-constexpr int kWRaw = 4;       // raw (TMA) stages
-constexpr int kWDq = 2;        // dequantised weight buffers
+constexpr int kWStages = 5;    // TMA stages
+constexpr int kWABufs = 2;     // weight operand buffers in TMEM
 constexpr int kWThreads = 256; // 8 warps
+constexpr uint32_t kWTmemCols = 512;
+constexpr uint32_t kWAccCol = 0;    // accumulator: columns [0, 256)
+constexpr uint32_t kWACol = 256;    // weight buffers: 32 columns each from 256
 
 struct W16Smem {
-    static constexpr int kX = kWBM * kWBK * 2;   // 16 KiB fp16 activation tile
-    static constexpr int kW8 = kWBN * kWBK;      // 16 KiB int8 weight tile
-    static constexpr int kRaw = kX + kW8;
-    static constexpr int kW16 = kWBN * kWBK * 2; // 32 KiB fp16 weight operand
-    static constexpr int kBarOff = kWRaw * kRaw + kWDq * kW16;
-    static constexpr int kBytes = kBarOff + 256 + kWBN * 8 + 1024;
+    static constexpr int kX = kWTok * kWBK * 2;  // 32 KiB fp16 activation tile
+    static constexpr int kW8 = kWCh * kWBK;      // 8 KiB int8 weight tile
+    static constexpr int kStage = kX + kW8;
+    static constexpr int kBarOff = kWStages * kStage;
+    static constexpr int kBytes = kBarOff + 256 + kWCh * 8 + 1024;
 };
 
 template <bool OUT_F16>
@@ -48,28 +51,26 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
     using S = W16Smem;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* raw_base = smem;
-    uint8_t* w16_base = smem + kWRaw * S::kRaw;
-    uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
-    uint64_t* raw_empty = raw_full + kWRaw;
-    uint64_t* dq_full = raw_empty + kWRaw;
-    uint64_t* dq_empty = dq_full + kWDq;
-    uint64_t* done = dq_empty + kWDq;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
+    uint64_t* empty = full + kWStages;
+    uint64_t* a_full = empty + kWStages;
+    uint64_t* a_empty = a_full + kWABufs;
+    uint64_t* done = a_empty + kWABufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     float* s_scale = reinterpret_cast<float*>(smem + S::kBarOff + 256);
-    float* s_bias = s_scale + kWBN;
+    float* s_bias = s_scale + kWCh;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * kWBM, n0 = blockIdx.x * kWBN;
+    const int n0 = blockIdx.x * kWCh, t0 = blockIdx.y * kWTok;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kWRaw; ++s) {
-            tc::mbar_init(&raw_full[s], 1);
-            tc::mbar_init(&raw_empty[s], 4 + 1);  // 4 dequant warps (weight read) + MMA commit (x read)
+        for (int s = 0; s < kWStages; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 4 + 1);  // 4 converter warps (weight read) + MMA commit (x read)
         }
-        for (int d = 0; d < kWDq; ++d) {
-            tc::mbar_init(&dq_full[d], 4);
-            tc::mbar_init(&dq_empty[d], 1);
+        for (int d = 0; d < kWABufs; ++d) {
+            tc::mbar_init(&a_full[d], 4);
+            tc::mbar_init(&a_empty[d], 1);
         }
         tc::mbar_init(done, 1);
         tc::fence_mbar_init();
@@ -77,10 +78,10 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
         tc::prefetch_tmap(&tmap_w);
     }
     if (warp == 2) {
-        tc::tmem_alloc(tmem_slot, kWBN);
+        tc::tmem_alloc(tmem_slot, kWTmemCols);
         tc::tmem_relinquish();
     }
-    for (int i = threadIdx.x; i < kWBN; i += blockDim.x) {
+    for (int i = threadIdx.x; i < kWCh; i += blockDim.x) {
         const int n = n0 + i;
         s_scale[i] = n < p.n ? p.scale[n] : 0.0f;
         s_bias[i] = (p.bias && n < p.n) ? p.bias[n] : 0.0f;
@@ -89,126 +90,96 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    bool failed = false;
 
     if (warp == 0) {
         if (lane == 0) {
             for (int kb = 0; kb < p.num_kb; ++kb) {
-                const int s = kb % kWRaw;
-                const uint32_t ph = (kb / kWRaw) & 1;
-                if (!tc::mbar_wait(&raw_empty[s], ph ^ 1)) break;
-                uint8_t* xs = raw_base + s * S::kRaw;
-                tc::mbar_arrive_expect_tx(&raw_full[s], S::kRaw);
-                tc::tma_load_2d(xs, &tmap_x, &raw_full[s], kb * kWBK, m0);
-                tc::tma_load_4d(xs + S::kX, &tmap_w, &raw_full[s], 0, 0, kb, n0 / 16);
+                const int s = kb % kWStages;
+                const uint32_t ph = (kb / kWStages) & 1;
+                if (!tc::mbar_wait(&empty[s], ph ^ 1)) break;
+                uint8_t* xs = smem + s * S::kStage;
+                tc::mbar_arrive_expect_tx(&full[s], S::kStage);
+                tc::tma_load_2d(xs, &tmap_x, &full[s], kb * kWBK, t0);
+                tc::tma_load_4d(xs + S::kX, &tmap_w, &full[s], 0, 0, kb, n0 / 16);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_f16(kWBM, kWBN);
+            constexpr uint32_t idesc = tc::idesc_f16(kWCh, kWTok);
             for (int kb = 0; kb < p.num_kb; ++kb) {
-                const int s = kb % kWRaw, d = kb % kWDq;
-                const uint32_t ph = (kb / kWRaw) & 1, phd = (kb / kWDq) & 1;
-                if (!tc::mbar_wait(&raw_full[s], ph)) break;
-                if (!tc::mbar_wait(&dq_full[d], phd)) break;
+                const int s = kb % kWStages, d = kb % kWABufs;
+                const uint32_t ph = (kb / kWStages) & 1, phd = (kb / kWABufs) & 1;
+                if (!tc::mbar_wait(&full[s], ph)) break;
+                if (!tc::mbar_wait(&a_full[d], phd)) break;
                 tc::fence_after_sync();
-                const uint8_t* xs = raw_base + s * S::kRaw;
-                const uint8_t* ws = w16_base + d * S::kW16;
+                const uint8_t* xs = smem + s * S::kStage;
+                const uint32_t a_col = tmem + kWACol + d * (kWBK / 2);
 #pragma unroll
                 for (int j = 0; j < kWBK / 16; ++j) {
-                    const uint64_t ad = tc::smem_desc(xs + j * 32, tc::kSwizzle128B, 1024);
-                    const uint64_t bd = tc::smem_desc(ws + j * 32, tc::kSwizzle128B, 1024);
-                    tc::mma_f16(tmem, ad, bd, idesc, (kb | j) != 0);
+                    const uint64_t bd = tc::smem_desc(xs + j * 32, tc::kSwizzle128B, 1024);
+                    tc::mma_f16_ts(tmem + kWAccCol, a_col + j * 8, bd, idesc, (kb | j) != 0);
                 }
-                tc::mma_commit(&raw_empty[s]);
-                tc::mma_commit(&dq_empty[d]);
+                tc::mma_commit(&empty[s]);
+                tc::mma_commit(&a_empty[d]);
             }
             tc::mma_commit(done);
         }
     } else if (warp >= 4) {
-        // ---- dequantise: int8 tile [256 rows][64 B] -> fp16 [256 rows][128 B], K-major, 128-byte swizzle
-        const int t = threadIdx.x - 128;
-        for (int kb = 0; kb < p.num_kb && !failed; ++kb) {
-            const int s = kb % kWRaw, d = kb % kWDq;
-            const uint32_t ph = (kb / kWRaw) & 1, phd = (kb / kWDq) & 1;
-            // warp-uniform waits, so a lane never leaves the loop alone (__syncwarp below)
-            if (!__all_sync(0xffffffffu, tc::mbar_wait(&raw_full[s], ph))) { failed = true; break; }
-            if (!__all_sync(0xffffffffu, tc::mbar_wait(&dq_empty[d], phd ^ 1))) { failed = true; break; }
-            const uint8_t* w8 = raw_base + s * S::kRaw + S::kX;
-            uint8_t* w16 = w16_base + d * S::kW16;
-#pragma unroll 4
-            for (int i = 0; i < (kWBN * kWBK / 16) / 128; ++i) {
-                const int q = t + 128 * i;          // 16-byte chunk of the int8 tile
-                const int row = q >> 2, c = q & 3;  // row of the tile, 16-wide k group
-                const uint4 v = *reinterpret_cast<const uint4*>(w8 + q * 16);
-                uint32_t h[8];
-                i8x4_to_half2x2(v.x, h[0], h[1]);
-                i8x4_to_half2x2(v.y, h[2], h[3]);
-                i8x4_to_half2x2(v.z, h[4], h[5]);
-                i8x4_to_half2x2(v.w, h[6], h[7]);
-                uint8_t* rowp = w16 + (row >> 3) * 1024 + (row & 7) * 128;
-                const int sw = row & 7;
-                *reinterpret_cast<uint4*>(rowp + (((2 * c) ^ sw) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
-                *reinterpret_cast<uint4*>(rowp + (((2 * c + 1) ^ sw) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+        const int wq = warp - 4;                  // lanes 32 wq .. 32 wq + 31 of tensor memory
+        const int row = wq * 32 + lane;           // weight row (output channel) of this thread
+        const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+            const int s = kb % kWStages, d = kb % kWABufs;
+            const uint32_t ph = (kb / kWStages) & 1, phd = (kb / kWABufs) & 1;
+            // warp-uniform waits: tcgen05.st below is warp-collective
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], ph))) { ok = false; break; }
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&a_empty[d], phd ^ 1))) { ok = false; break; }
+            tc::fence_after_sync();
+            // the int8 row: 64 bytes, 16-byte chunk c at (c ^ ((row >> 1) & 3)) (64-byte swizzle)
+            const uint8_t* w8 = smem + s * S::kStage + S::kX + row * 64;
+            uint32_t h[32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint4 v = *reinterpret_cast<const uint4*>(w8 + ((c ^ ((row >> 1) & 3)) << 4));
+                i8x4_to_half2x2(v.x, h[8 * c + 0], h[8 * c + 1]);
+                i8x4_to_half2x2(v.y, h[8 * c + 2], h[8 * c + 3]);
+                i8x4_to_half2x2(v.z, h[8 * c + 4], h[8 * c + 5]);
+                i8x4_to_half2x2(v.w, h[8 * c + 6], h[8 * c + 7]);
             }
-            tc::fence_proxy_async_smem();
+            tc::tmem_st_32x32b_x32(tmem + lane_addr + kWACol + d * (kWBK / 2), h);
+            tc::tmem_wait_st();
+            tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) {
-                tc::mbar_arrive(&dq_full[d]);
-                tc::mbar_arrive(&raw_empty[s]);
+                tc::mbar_arrive(&a_full[d]);
+                tc::mbar_arrive(&empty[s]);
             }
         }
-        // ---- epilogue: accumulators (lanes 32 (warp - 4) ..) -> scale -> global
-        // warp-uniform decision: tcgen05.ld below is a warp-collective instruction
-        const bool ok = __all_sync(0xffffffffu, !failed && tc::mbar_wait(done, 0));
+        // ---- epilogue: this thread's channel, 256 tokens of accumulators
+        ok = __all_sync(0xffffffffu, ok && tc::mbar_wait(done, 0));
         tc::fence_after_sync();
         if (ok) {
-            const int wq = warp - 4;
-            const int row = m0 + wq * 32 + lane;
+            const int n = n0 + row;
+            const float sc = s_scale[row], bi = s_bias[row];
+            const bool has_bias = p.bias != nullptr;
 #pragma unroll 1
-            for (int c = 0; c < kWBN / 32; ++c) {
+            for (int c = 0; c < kWTok / 32; ++c) {
                 uint32_t r[32];
-                tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(wq * 32) << 16) + c * 32, r);
+                tc::tmem_ld_32x32b_x32(tmem + lane_addr + kWAccCol + c * 32, r);
                 tc::tmem_wait_ld();
-                if (row >= p.m) continue;
-                const int nb = n0 + c * 32;
-                float v[32];
+                if (n >= p.n) continue;
+                const int tb = t0 + c * 32;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const int i = c * 32 + j;
-                    v[j] = __fmul_rn(__uint_as_float(r[j]), s_scale[i]);
-                    if (p.bias) v[j] = __fadd_rn(v[j], s_bias[i]);
-                }
-                if (OUT_F16) {
-                    __half* yr = static_cast<__half*>(p.y) + (int64_t)row * p.ldy;
-                    if (nb + 32 <= p.n && (p.ldy % 8) == 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 8) {
-                            uint4 o;
-                            __half2 a = __floats2half2_rn(v[j], v[j + 1]), b = __floats2half2_rn(v[j + 2], v[j + 3]);
-                            __half2 cc = __floats2half2_rn(v[j + 4], v[j + 5]), dd = __floats2half2_rn(v[j + 6], v[j + 7]);
-                            o.x = *reinterpret_cast<uint32_t*>(&a);
-                            o.y = *reinterpret_cast<uint32_t*>(&b);
-                            o.z = *reinterpret_cast<uint32_t*>(&cc);
-                            o.w = *reinterpret_cast<uint32_t*>(&dd);
-                            *reinterpret_cast<uint4*>(yr + nb + j) = o;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (nb + j < p.n) yr[nb + j] = __float2half_rn(v[j]);
-                    }
-                } else {
-                    float* yr = static_cast<float*>(p.y) + (int64_t)row * p.ldy;
-                    if (nb + 32 <= p.n && (p.ldy % 4) == 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(yr + nb + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (nb + j < p.n) yr[nb + j] = v[j];
-                    }
+                    const int t = tb + j;
+                    if (t >= p.m) break;
+                    float v = __fmul_rn(__uint_as_float(r[j]), sc);
+                    if (has_bias) v = __fadd_rn(v, bi);
+                    if (OUT_F16)
+                        static_cast<__half*>(p.y)[(int64_t)t * p.ldy + n] = __float2half_rn(v);
+                    else
+                        static_cast<float*>(p.y)[(int64_t)t * p.ldy + n] = v;
                 }
             }
         }
@@ -217,7 +188,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
     __syncthreads();
     if (warp == 2) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, kWBN);
+        tc::tmem_dealloc(tmem, kWTmemCols);
     }
 }
 
@@ -240,7 +211,7 @@ extern "C" int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const voi
     {
         const uint64_t dims[2] = {(uint64_t)k, (uint64_t)m};
         const uint64_t strides[1] = {(uint64_t)ldx * 2};
-        const uint32_t box[2] = {kWBK, kWBM};
+        const uint32_t box[2] = {kWBK, kWTok};
         st = encode_tmap(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (st) return st;
     }
@@ -248,8 +219,8 @@ extern "C" int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const voi
         const uint64_t kt = (uint64_t)ceil_div(k, kTileCols), nt = (uint64_t)ceil_div(n, kTileRows);
         const uint64_t dims[4] = {64, 16, kt, nt};
         const uint64_t strides[3] = {64, 1024, kt * 1024};
-        const uint32_t box[4] = {64, 16, 1, kWBN / 16};
-        st = encode_tmap(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, packed, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        const uint32_t box[4] = {64, 16, 1, kWCh / 16};
+        st = encode_tmap(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, packed, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
         if (st) return st;
     }
     GemmW16Params p{};
@@ -261,11 +232,10 @@ extern "C" int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const voi
     p.bias = bias;
     p.y = y;
     p.ldy = ldy;
-    p.out_f16 = y_dtype == SBQ_F16;
-    const dim3 grid((unsigned)ceil_div(n, kWBN), (unsigned)ceil_div(m, kWBM));
+    const dim3 grid((unsigned)ceil_div(n, kWCh), (unsigned)ceil_div(m, kWTok));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int smem = W16Smem::kBytes;
-    if (p.out_f16) {
+    if (y_dtype == SBQ_F16) {
         cudaFuncSetAttribute(gemm_w8a16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         gemm_w8a16_kernel<true><<<grid, kWThreads, smem, s>>>(mx, mw, p);
     } else {
