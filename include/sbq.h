@@ -120,6 +120,31 @@ SBQ_API int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const voi
                       const float* scale_gate, const void* packed_up, const float* scale_up, int64_t m,
                       int64_t n, int64_t k, void* h, int h_dtype, int64_t ldh, void* stream);
 
+/* One projection of a grouped decode launch (sbq_gemv_w8_group).  A job with packed_up set is a fused
+ * gate/up job: y = silu(x q^T * scale) * (x q_up^T * scale_up), no bias. */
+typedef struct sbq_gemv_job {
+    const void* x;         /* activation [m, k], 16-byte aligned rows */
+    int64_t ldx;
+    const void* packed;    /* packed weight [n, k] (the gate weight of a fused job) */
+    const float* scale;
+    const void* packed_up; /* packed up weight [n, k], or NULL */
+    const float* scale_up;
+    const float* bias;     /* [n] or NULL (plain jobs only) */
+    int64_t n;
+    int64_t k;
+    void* y;               /* output [m, n], SBQ_F32 or SBQ_F16 */
+    int y_dtype;
+    int64_t ldy;
+} sbq_gemv_job;
+
+/* Several independent decode GEMVs in one launch (up to 8 jobs sharing the activation dtype and m,
+ * 1 <= m <= 16), e.g. the projections of one layer that read the same x (q|k|v|delta_in and gate/up)
+ * or that run between the same two dependencies (o, delta_out, down).  Fewer launches per decode
+ * step; each job gives the same result as its own sbq_gemv_w8 / sbq_mlp_gateup_w8 call.  The model's
+ * shared-input projections (model.py:317-321 and :363-365, sse_q/k/v and swa_q/k/v of one block) are
+ * such a group. */
+SBQ_API int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m, void* stream);
+
 /* ---- int8-dyn: dynamic activation quantisation + int8 x int8 -> int32 GEMM ------------- */
 
 /* Bytes of workspace sbq_linear_dyn / sbq_quant_act_* need for an [m, k] activation. */

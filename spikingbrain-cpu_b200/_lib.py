@@ -20,6 +20,15 @@ ACT_PER_TENSOR, ACT_PER_TOKEN = 0, 1
 
 _c_i64, _c_int, _vp, _sz = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
 
+class GemvJob(ctypes.Structure):
+    """struct sbq_gemv_job of include/sbq.h."""
+
+    _fields_ = [("x", ctypes.c_void_p), ("ldx", ctypes.c_int64), ("packed", ctypes.c_void_p),
+                ("scale", ctypes.c_void_p), ("packed_up", ctypes.c_void_p), ("scale_up", ctypes.c_void_p),
+                ("bias", ctypes.c_void_p), ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("y", ctypes.c_void_p),
+                ("y_dtype", ctypes.c_int), ("ldy", ctypes.c_int64)]
+
+
 # name -> (restype, argtypes); kept in the order of include/sbq.h
 SIGNATURES = {
     "sbq_version": (_c_int, []),
@@ -35,6 +44,7 @@ SIGNATURES = {
     "sbq_gemm_w8a16": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_int, _c_i64, _vp]),
     "sbq_mlp_gateup_w8": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_int,
                                    _c_i64, _vp]),
+    "sbq_gemv_w8_group": (_c_int, [ctypes.POINTER(GemvJob), _c_int, _c_int, _c_i64, _vp]),
     "sbq_dyn_workspace_bytes": (_sz, [_c_i64, _c_i64, _c_int]),
     "sbq_quant_act_per_tensor": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "sbq_quant_act_per_token": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp]),

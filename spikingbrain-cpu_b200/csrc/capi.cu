@@ -52,6 +52,7 @@ namespace sbq {
 
 int poll_error_dyn();
 int poll_error_w8a16();
+int poll_error_gemv();
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -94,6 +95,7 @@ extern "C" int sbq_check_device_error(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) return sbq::check_launch("device synchronise");
     int h = sbq::poll_error_dyn();
     if (h == 0) h = sbq::poll_error_w8a16();
+    if (h == 0) h = sbq::poll_error_gemv();
     if (h != 0)
         return sbq::set_error(h, "a kernel reported %s (bounded device-side wait expired)", sbq_status_string(h));
     return SBQ_OK;

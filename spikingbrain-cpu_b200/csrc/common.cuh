@@ -6,7 +6,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#include "../../include/sbq.h"
+#include "sbq.h"
 
 namespace sbq {
 

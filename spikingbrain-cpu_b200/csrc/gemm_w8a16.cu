@@ -8,7 +8,7 @@
 //     matching 128 x 64 int8 weight tiles (TMA over the packed layout, 64-byte swizzle) into a
 //     5-stage ring;
 //   * warps 4-7 (one weight row per thread) convert each int8 row to fp16 in registers (exact) and
-//     write it straight into tensor memory with tcgen05.st - the MMA's A operand - double-buffered;
+//     write it straight into tensor memory with tcgen05.st - the MMA's A operand - in a 4-deep ring;
 //   * warp 1 (one thread) issues tcgen05.mma.cta_group::1.kind::f16 with A from tensor memory and
 //     the activation tile from shared memory (128 x 256 x 16, fp32 accumulators in TMEM);
 //   * warps 4-7 finally read their channel's accumulators (tcgen05.ld), apply the fp32 per-row
@@ -30,7 +30,7 @@ constexpr int kWCh = 128;      // output channels per CTA (MMA M, one per TMEM l
 constexpr int kWTok = 256;     // activation rows per CTA (MMA N)
 constexpr int kWBK = 64;       // k per stage (one 128-byte fp16 row, one packed tile column)
 constexpr int kWStages = 5;    // TMA stages
-constexpr int kWABufs = 2;     // weight operand buffers in TMEM
+constexpr int kWABufs = 4;     // weight operand buffers in TMEM (32 columns each)
 constexpr int kWThreads = 256; // 8 warps
 constexpr uint32_t kWTmemCols = 512;
 constexpr uint32_t kWAccCol = 0;    // accumulator: columns [0, 256)

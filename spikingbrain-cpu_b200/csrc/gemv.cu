@@ -5,59 +5,75 @@
 // each 128-row block of the weight to fp32 and runs an fp32 sgemm, then multiplies by the
 // per-row scale.  Here the weight is streamed from HBM exactly once per launch:
 //
-//   * one CTA per 16-row tile of the weight, 8 warps splitting K; each warp streams its 1 KiB
-//     tiles with two contiguous 512-byte, 128-bit loads per tile (no L1 allocation);
-//   * int8 -> fp16 (or bf16) conversion in registers (exact), m16n8k16 tensor-core MMAs with
-//     fp32 accumulation; the activation rows form the n dimension (8 or 16 tokens per pass), so
-//     the k-permutation of the packed layout is applied to x on load;
-//   * partial sums of the 8 warps are reduced in shared memory, then the fp32 per-row scale (and
-//     bias, or the SiLU(gate) * up product) is applied before the single store.
+//   * one CTA per 16-row tile of a weight; a producer warp streams the tile's contiguous K strip
+//     (ceil(k/64) KiB per matrix) with cp.async.bulk copies into a 64 KiB shared-memory ring
+//     (8 KiB chunks, mbarrier transaction counts); several CTAs share an SM;
+//   * eight consumer warps take one 1 KiB tile of each chunk: two conflict-free 16-byte shared
+//     loads per lane, int8 -> fp16 (or bf16) in registers (exact), m16n8k16 tensor-core MMAs with
+//     fp32 accumulation and the activation rows as the n dimension (8 or 16 tokens per pass);
+//   * the warps' partial sums are reduced through the drained ring, then the fp32 per-row scale
+//     (and bias, or the SiLU(gate) * up product) is applied before one store;
+//   * one launch can carry several independent projections ("jobs": e.g. q|k|v|delta_in and
+//     gate/up of one layer, which read the same x); each CTA finds its job from its block index;
+//   * programmatic dependent launch: the weights never depend on the previous kernel, so the
+//     producer starts streaming at once; only the consumers wait (griddepcontrol.wait) before
+//     reading x, and each CTA releases the next launch as soon as it starts.
 //
 // fp32 activations are split into a bf16 high and low part (two MMAs, ~16 mantissa bits kept);
 // the dot product of int8 weights and fp16/bf16 activations is exact up to fp32 accumulation.
-#include "common.cuh"
+#include "tc.cuh"
 
 namespace sbq {
 
 enum XKind { kXF16 = 0, kXBF16 = 1, kXF32 = 2 };
 
-struct GemvParams {
-    const void* x;
+// One projection of a launch.
+struct GemvJob {
+    const void* x;     // activation [m, k], 16-byte aligned rows
     int64_t ldx;
-    const int8_t* w0;  // packed weight (gate for the MLP variant)
+    const int8_t* w0;  // packed weight (gate for a fused gate/up job)
     const float* s0;
-    const int8_t* w1;  // packed up weight (MLP variant only)
+    const int8_t* w1;  // packed up weight (fused job only, else null)
     const float* s1;
     const float* bias;
     void* y;
     int64_t ldy;
-    int m;  // rows of x handled by this launch (<= 8 * MT)
+    int m;             // rows of x handled by this launch (<= 8 * MT)
     int n;
     int k;
-    int kt_total;
-    int kt_per_warp;
+    int kt_total;      // ceil(k / 64)
+    int chunk_tiles;   // tiles per streamed chunk: the largest of 8, 4, 2, 1 dividing kt_total
+    int out_f16;       // 1: fp16 output, 0: fp32
+    int tile_begin;    // first block index of this job in the grid
 };
 
-constexpr int kGemvWarps = 8;
-constexpr int kGemvUnroll = 4;
+constexpr int kMaxJobs = 8;
 
-// Loads the 16 activation values lane (g, c) needs for span kt, row `row`, as MMA B fragments:
-// b[s][0..1] for the four k16 steps s.  Rows beyond m (or spans beyond k) read as zero.
+struct GemvGroup {
+    GemvJob job[kMaxJobs];
+    int njobs;
+};
+
+constexpr int kGemvWarps = 8;  // consumer warps
+
 template <int XK>
 struct XFrag {
     uint32_t b[4][2];      // fp16 / bf16 main part
     uint32_t blo[4][2];    // bf16 low part (fp32 input only)
 };
 
+// Loads the 16 activation values lane (g, c) needs for k0 .. k0 + 15 of row `row` as MMA B fragments
+// b[s][0..1] (s = the four k16 steps).  Rows beyond m (or spans beyond k) read as zero.
 template <int XK>
-__device__ __forceinline__ void load_x(XFrag<XK>& f, const void* x, int64_t ldx, int row, int m, int64_t k0, int k) {
+__device__ __forceinline__ void load_x(XFrag<XK>& f, const void* xv, int64_t ldx, int row, int m, int64_t k0, int k) {
+    const uint8_t* x = static_cast<const uint8_t*>(xv);
     const bool ok = row < m && k0 < k;
     if (XK == kXF16 || XK == kXBF16) {
         uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
         if (ok) {
-            const uint16_t* p = static_cast<const uint16_t*>(x) + (int64_t)row * ldx + k0;
-            v0 = ld_act(p);
-            v1 = ld_act(p + 8);
+            const uint4* q = reinterpret_cast<const uint4*>(x + ((int64_t)row * ldx + k0) * 2);
+            v0 = q[0];
+            v1 = q[1];
         }
         f.b[0][0] = v0.x; f.b[0][1] = v0.y; f.b[1][0] = v0.z; f.b[1][1] = v0.w;
         f.b[2][0] = v1.x; f.b[2][1] = v1.y; f.b[3][0] = v1.z; f.b[3][1] = v1.w;
@@ -66,10 +82,10 @@ __device__ __forceinline__ void load_x(XFrag<XK>& f, const void* x, int64_t ldx,
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = 0.0f;
         if (ok) {
-            const float* p = static_cast<const float*>(x) + (int64_t)row * ldx + k0;
+            const uint4* q = reinterpret_cast<const uint4*>(x + ((int64_t)row * ldx + k0) * 4);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                uint4 t = ld_act(p + 4 * i);
+                const uint4 t = q[i];
                 v[4 * i + 0] = __uint_as_float(t.x);
                 v[4 * i + 1] = __uint_as_float(t.y);
                 v[4 * i + 2] = __uint_as_float(t.z);
@@ -128,108 +144,197 @@ __device__ __forceinline__ void store_out<__half>(void* y, int64_t idx, float v)
     static_cast<__half*>(y)[idx] = __float2half_rn(v);
 }
 
-// NMAT = 1: y = x . W^T * scale (+ bias).   NMAT = 2: y = silu(x . Wg^T * sg) * (x . Wu^T * su).
-template <int XK, int MT, int NMAT, typename OutT>
-__global__ void __launch_bounds__(kGemvWarps * 32) gemv_w8_kernel(const GemvParams p) {
-    __shared__ float red[kGemvWarps][NMAT][MT][16][9];  // +1 column against bank conflicts
+constexpr int kGemvThreads = (kGemvWarps + 1) * 32;  // 8 consumer warps + 1 producer warp
+constexpr int kChunkTiles = 8;                         // tiles (KiB) per chunk and matrix, at most
+constexpr int kRingBytes = 64 * 1024;                  // 8 stages of 8 KiB, or 4 of 16 KiB (gate + up)
+constexpr int kMaxStages = 8;
+constexpr int kGemvSmem = kRingBytes + 2 * kMaxStages * 8;
 
+// Named barrier 1 over the consumer warps.
+__device__ __forceinline__ void consumers_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kGemvWarps * 32) : "memory");
+}
+
+// Named barrier 1 over the consumer warps with an AND of `v` across them.
+__device__ __forceinline__ int consumers_sync_and(int v) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.s32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, %2, p;\n\t"
+        "selp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(v), "n"(kGemvWarps * 32)
+        : "memory");
+    return r;
+}
+
+// The body of one CTA: one 16-row tile `nt` of job `jb`, NMAT matrices (1, or 2 for gate/up).
+template <int XK, int MT, int NMAT>
+__device__ __forceinline__ void gemv_tile(const GemvJob& jb, int nt, uint8_t* ring, uint64_t* full, uint64_t* empty) {
+    constexpr int S = kMaxStages / NMAT;
+    constexpr int kStageBytes = NMAT * kChunkTiles * kTileBytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, c = lane & 3;
-    const int nt = blockIdx.x;
-    const int kt_begin = warp * p.kt_per_warp;
-    const int kt_end = min(kt_begin + p.kt_per_warp, p.kt_total);
+    const int C = jb.chunk_tiles;
+    const int nchunks = jb.kt_total / C;
 
+    if (warp == kGemvWarps) {
+        // ---- producer: this tile-row's K strip, chunk by chunk
+        if (lane == 0) {
+            const uint32_t bytes = (uint32_t)C * kTileBytes;
+            const int8_t* src0 = jb.w0 + (int64_t)nt * jb.kt_total * kTileBytes;
+            const int8_t* src1 = NMAT == 2 ? jb.w1 + (int64_t)nt * jb.kt_total * kTileBytes : nullptr;
+            for (int i = 0; i < nchunks; ++i) {
+                const int s = i % S;
+                if (!tc::mbar_wait(&empty[s], ((i / S) & 1) ^ 1)) break;
+                uint8_t* dst = ring + s * kStageBytes;
+                tc::mbar_arrive_expect_tx(&full[s], bytes * NMAT);
+                tc::bulk_load(dst, src0 + (int64_t)i * bytes, bytes, &full[s]);
+                if (NMAT == 2) tc::bulk_load(dst + kChunkTiles * kTileBytes, src1 + (int64_t)i * bytes, bytes, &full[s]);
+            }
+        }
+        return;
+    }
+
+    // ---- consumers
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
+    const int g = lane >> 2, c = lane & 3;
     float acc[NMAT][MT][4];
 #pragma unroll
-    for (int i = 0; i < NMAT; ++i)
+    for (int a = 0; a < NMAT; ++a)
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][mt][j] = 0.0f;
+            for (int e = 0; e < 4; ++e) acc[a][mt][e] = 0.0f;
 
-    const int64_t tile0 = (int64_t)nt * p.kt_total;
-    const int8_t* wp0 = p.w0 + tile0 * kTileBytes + lane * 16;
-    const int8_t* wp1 = NMAT == 2 ? p.w1 + tile0 * kTileBytes + lane * 16 : nullptr;
-
-    for (int kt = kt_begin; kt < kt_end; kt += kGemvUnroll) {
-        uint4 wa[NMAT][kGemvUnroll], wb[NMAT][kGemvUnroll];
+    bool ok = true;
+    const bool mine = warp < C;
+    for (int i = 0; i < nchunks; ++i) {
+        const int s = i % S;
+        XFrag<XK> xf[MT];
+        if (mine) {
+            const int64_t k0 = (int64_t)(i * C + warp) * kTileCols + 16 * c;
 #pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u) {
-            const bool live = kt + u < kt_end;
+            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], jb.x, jb.ldx, 8 * mt + g, jb.m, k0, jb.k);
+        }
+        // warp-uniform wait (the __syncwarp below must see every lane)
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (i / S) & 1))) {
+            ok = false;
+            break;
+        }
+        if (mine) {
+            const uint8_t* st = ring + s * kStageBytes + warp * kTileBytes + lane * 16;
 #pragma unroll
-            for (int i = 0; i < NMAT; ++i) {
-                const int8_t* wp = (i == 0 ? wp0 : wp1) + (int64_t)(kt + u) * kTileBytes;
-                wa[i][u] = live ? ld_stream(wp) : make_uint4(0, 0, 0, 0);
-                wb[i][u] = live ? ld_stream(wp + 512) : make_uint4(0, 0, 0, 0);
+            for (int a = 0; a < NMAT; ++a) {
+                const uint8_t* t = st + a * (kChunkTiles * kTileBytes);
+                const uint4 wa = *reinterpret_cast<const uint4*>(t);
+                const uint4 wb = *reinterpret_cast<const uint4*>(t + 512);
+                tile_mma<XK, MT>(acc[a], wa, wb, xf);
             }
         }
-#pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u) {
-            if (kt + u >= kt_end) break;
-            XFrag<XK> xf[MT];
-            const int64_t k0 = (int64_t)(kt + u) * kTileCols + 16 * c;
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], p.x, p.ldx, 8 * mt + g, p.m, k0, p.k);
-#pragma unroll
-            for (int i = 0; i < NMAT; ++i) tile_mma<XK, MT>(acc[i], wa[i][u], wb[i][u], xf);
-        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&empty[s]);
     }
 
-    // Fragment (row g / g+8, token 2c / 2c+1) -> shared memory.
+    // ---- reduce the 8 warps' partial sums through the drained ring, then the epilogue
+    consumers_sync();
+    float* red = reinterpret_cast<float*>(ring);  // [warp][mat][mt][16 rows][9]
+#define SBQ_RED(w, a, mt, r, col) red[((((w) * NMAT + (a)) * MT + (mt)) * 16 + (r)) * 9 + (col)]
 #pragma unroll
-    for (int i = 0; i < NMAT; ++i)
+    for (int a = 0; a < NMAT; ++a)
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
-            red[warp][i][mt][g][2 * c] = acc[i][mt][0];
-            red[warp][i][mt][g][2 * c + 1] = acc[i][mt][1];
-            red[warp][i][mt][g + 8][2 * c] = acc[i][mt][2];
-            red[warp][i][mt][g + 8][2 * c + 1] = acc[i][mt][3];
+            SBQ_RED(warp, a, mt, g, 2 * c) = acc[a][mt][0];
+            SBQ_RED(warp, a, mt, g, 2 * c + 1) = acc[a][mt][1];
+            SBQ_RED(warp, a, mt, g + 8, 2 * c) = acc[a][mt][2];
+            SBQ_RED(warp, a, mt, g + 8, 2 * c + 1) = acc[a][mt][3];
         }
-    __syncthreads();
-
-    for (int t = threadIdx.x; t < MT * 8 * 16; t += blockDim.x) {
+    if (!consumers_sync_and(ok)) {
+        if (threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
+        return;
+    }
+    for (int t = threadIdx.x; t < MT * 8 * 16; t += kGemvWarps * 32) {
         const int r = t & 15, tok = t >> 4, mt = tok >> 3, col = tok & 7;
         const int n = nt * 16 + r;
-        if (n >= p.n || tok >= p.m) continue;
+        if (n >= jb.n || tok >= jb.m) continue;
         float v[NMAT];
 #pragma unroll
-        for (int i = 0; i < NMAT; ++i) {
-            float s = 0.0f;
+        for (int a = 0; a < NMAT; ++a) {
+            float sum = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kGemvWarps; ++w) s += red[w][i][mt][r][col];
-            v[i] = s;
+            for (int w = 0; w < kGemvWarps; ++w) sum += SBQ_RED(w, a, mt, r, col);
+            v[a] = sum;
         }
         float out;
         if (NMAT == 1) {
-            out = v[0] * p.s0[n];
-            if (p.bias) out += p.bias[n];
+            out = v[0] * jb.s0[n];
+            if (jb.bias) out += jb.bias[n];
         } else {
-            const float gv = v[0] * p.s0[n];
-            const float uv = v[1] * p.s1[n];
+            const float gv = v[0] * jb.s0[n];
+            const float uv = v[1] * jb.s1[n];
             out = gv / (1.0f + expf(-gv)) * uv;
         }
-        store_out<OutT>(p.y, (int64_t)tok * p.ldy + n, out);
+        const int64_t idx = (int64_t)tok * jb.ldy + n;
+        if (jb.out_f16)
+            static_cast<__half*>(jb.y)[idx] = __float2half_rn(out);
+        else
+            static_cast<float*>(jb.y)[idx] = out;
     }
+#undef SBQ_RED
 }
 
-template <int XK, int MT, int NMAT>
-static void launch_gemv(const GemvParams& p, int out_dtype, cudaStream_t s) {
-    const dim3 grid((unsigned)ceil_div(p.n, 16)), block(kGemvWarps * 32);
-    if (out_dtype == SBQ_F16)
-        gemv_w8_kernel<XK, MT, NMAT, __half><<<grid, block, 0, s>>>(p);
+template <int XK, int MT>
+__global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2) gemv_w8_kernel(const __grid_constant__ GemvGroup grp) {
+    extern __shared__ __align__(128) uint8_t ring[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRingBytes);
+    uint64_t* empty = full + kMaxStages;
+    int j = 0;
+    while (j + 1 < grp.njobs && (int)blockIdx.x >= grp.job[j + 1].tile_begin) ++j;
+    const GemvJob& jb = grp.job[j];
+    const int nmat = jb.w1 ? 2 : 1;
+    if (threadIdx.x == 0) {
+        const int stages = kMaxStages / nmat;
+        for (int i = 0; i < stages; ++i) {
+            tc::mbar_init(&full[i], 1);
+            tc::mbar_init(&empty[i], kGemvWarps);
+        }
+        tc::fence_mbar_init();
+    }
+    __syncthreads();
+    // the next launch may start its own weight stream now (it waits for this grid before reading x)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int nt = (int)blockIdx.x - jb.tile_begin;
+    if (nmat == 2)
+        gemv_tile<XK, MT, 2>(jb, nt, ring, full, empty);
     else
-        gemv_w8_kernel<XK, MT, NMAT, float><<<grid, block, 0, s>>>(p);
+        gemv_tile<XK, MT, 1>(jb, nt, ring, full, empty);
 }
 
-template <int NMAT>
-static void dispatch_gemv(const GemvParams& p, int xk, int out_dtype, cudaStream_t s) {
-    const bool two = p.m > 8;
+template <int XK, int MT>
+static void launch_group(const GemvGroup& grp, int total_tiles, cudaStream_t s) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)total_tiles);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = kGemvSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaFuncSetAttribute(gemv_w8_kernel<XK, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+    cudaLaunchKernelEx(&cfg, gemv_w8_kernel<XK, MT>, grp);
+}
+
+static void dispatch_group(const GemvGroup& grp, int total_tiles, int xk, int mt, cudaStream_t s) {
     switch (xk) {
-        case kXF16: two ? launch_gemv<kXF16, 2, NMAT>(p, out_dtype, s) : launch_gemv<kXF16, 1, NMAT>(p, out_dtype, s); break;
-        case kXBF16: two ? launch_gemv<kXBF16, 2, NMAT>(p, out_dtype, s) : launch_gemv<kXBF16, 1, NMAT>(p, out_dtype, s); break;
-        default: two ? launch_gemv<kXF32, 2, NMAT>(p, out_dtype, s) : launch_gemv<kXF32, 1, NMAT>(p, out_dtype, s); break;
+        case kXF16: mt == 2 ? launch_group<kXF16, 2>(grp, total_tiles, s) : launch_group<kXF16, 1>(grp, total_tiles, s); break;
+        case kXBF16: mt == 2 ? launch_group<kXBF16, 2>(grp, total_tiles, s) : launch_group<kXBF16, 1>(grp, total_tiles, s); break;
+        default: mt == 2 ? launch_group<kXF32, 2>(grp, total_tiles, s) : launch_group<kXF32, 1>(grp, total_tiles, s); break;
     }
 }
+
+SBQ_DEFINE_ERROR_POLL(poll_error_gemv)
 
 static int x_kind(int dtype) {
     switch (dtype) {
@@ -262,35 +367,38 @@ int check_linear_args(const void* x, int x_dtype, int64_t ldx, const void* packe
     return SBQ_OK;
 }
 
-static GemvParams make_params(const void* x, int64_t ldx, const void* w0, const float* s0, const void* w1,
-                              const float* s1, const float* bias, int64_t n, int64_t k, void* y, int64_t ldy) {
-    GemvParams p{};
-    p.x = x;
-    p.ldx = ldx;
-    p.w0 = static_cast<const int8_t*>(w0);
-    p.s0 = s0;
-    p.w1 = static_cast<const int8_t*>(w1);
-    p.s1 = s1;
-    p.bias = bias;
-    p.y = y;
-    p.ldy = ldy;
-    p.n = (int)n;
-    p.k = (int)k;
-    p.kt_total = (int)ceil_div(k, kTileCols);
-    p.kt_per_warp = (int)ceil_div(p.kt_total, kGemvWarps);
-    return p;
+static void fill_job(GemvJob& jb, const void* x, int64_t ldx, const void* w0, const float* s0, const void* w1,
+                     const float* s1, const float* bias, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy) {
+    jb = GemvJob{};
+    jb.x = x;
+    jb.ldx = ldx;
+    jb.w0 = static_cast<const int8_t*>(w0);
+    jb.s0 = s0;
+    jb.w1 = static_cast<const int8_t*>(w1);
+    jb.s1 = s1;
+    jb.bias = bias;
+    jb.y = y;
+    jb.ldy = ldy;
+    jb.n = (int)n;
+    jb.k = (int)k;
+    jb.kt_total = (int)ceil_div(k, kTileCols);
+    jb.chunk_tiles = jb.kt_total % 8 == 0 ? 8 : jb.kt_total % 4 == 0 ? 4 : jb.kt_total % 2 == 0 ? 2 : 1;
+    jb.out_f16 = y_dtype == SBQ_F16;
 }
 
-// Runs the GEMV over x in chunks of 16 rows (each chunk streams the weight once).
-template <int NMAT>
-static int run_gemv(GemvParams p, int64_t m, int x_dtype, int y_dtype, cudaStream_t s, const char* what) {
+// One job over all rows of x, in passes of 16 rows (each pass streams the weight once).
+static int run_single(GemvJob jb, int64_t m, int x_dtype, int y_dtype, cudaStream_t s, const char* what) {
     const int xs = elem_size(x_dtype), ys = y_dtype == SBQ_F32 ? 4 : 2;
+    GemvGroup grp{};
+    grp.njobs = 1;
     for (int64_t m0 = 0; m0 < m; m0 += 16) {
-        GemvParams q = p;
+        GemvJob q = jb;
         q.m = (int)(m - m0 < 16 ? m - m0 : 16);
-        q.x = static_cast<const char*>(p.x) + m0 * p.ldx * xs;
-        q.y = static_cast<char*>(p.y) + m0 * p.ldy * ys;
-        dispatch_gemv<NMAT>(q, x_kind(x_dtype), y_dtype, s);
+        q.x = static_cast<const char*>(jb.x) + m0 * jb.ldx * xs;
+        q.y = static_cast<char*>(jb.y) + m0 * jb.ldy * ys;
+        q.tile_begin = 0;
+        grp.job[0] = q;
+        dispatch_group(grp, (int)ceil_div(q.n, 16), x_kind(x_dtype), q.m > 8 ? 2 : 1, s);
     }
     return check_launch(what);
 }
@@ -304,8 +412,9 @@ extern "C" int sbq_gemv_w8(const void* x, int x_dtype, int64_t ldx, const void* 
                            void* stream) {
     int st = check_linear_args(x, x_dtype, ldx, packed, scale, m, n, k, y, y_dtype, ldy);
     if (st) return st;
-    GemvParams p = make_params(x, ldx, packed, scale, nullptr, nullptr, bias, n, k, y, ldy);
-    return run_gemv<1>(p, m, x_dtype, y_dtype, static_cast<cudaStream_t>(stream), "gemv_w8");
+    GemvJob jb;
+    fill_job(jb, x, ldx, packed, scale, nullptr, nullptr, bias, n, k, y, y_dtype, ldy);
+    return run_single(jb, m, x_dtype, y_dtype, static_cast<cudaStream_t>(stream), "gemv_w8");
 }
 
 extern "C" int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const void* packed_gate,
@@ -315,6 +424,35 @@ extern "C" int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const 
     if (st) return st;
     if (!packed_up || !scale_up) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null up-projection pointer");
     if (reinterpret_cast<uintptr_t>(packed_up) % 256) return set_error(SBQ_ERR_ALIGNMENT, "packed weight must be 256-byte aligned");
-    GemvParams p = make_params(x, ldx, packed_gate, scale_gate, packed_up, scale_up, nullptr, n, k, h, ldh);
-    return run_gemv<2>(p, m, x_dtype, h_dtype, static_cast<cudaStream_t>(stream), "mlp_gateup_w8");
+    GemvJob jb;
+    fill_job(jb, x, ldx, packed_gate, scale_gate, packed_up, scale_up, nullptr, n, k, h, h_dtype, ldh);
+    return run_single(jb, m, x_dtype, h_dtype, static_cast<cudaStream_t>(stream), "mlp_gateup_w8");
+}
+
+extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m, void* stream) {
+    if (!jobs || njobs < 1 || njobs > kMaxJobs)
+        return set_error(SBQ_ERR_INVALID_ARGUMENT, "njobs must be 1..%d", kMaxJobs);
+    if (m < 1 || m > 16) return set_error(SBQ_ERR_UNSUPPORTED, "a grouped launch takes 1..16 rows of x (m=%lld)", (long long)m);
+    GemvGroup grp{};
+    grp.njobs = njobs;
+    int tiles = 0;
+    for (int i = 0; i < njobs; ++i) {
+        const sbq_gemv_job& j = jobs[i];
+        int st = check_linear_args(j.x, x_dtype, j.ldx, j.packed, j.scale, m, j.n, j.k, j.y, j.y_dtype, j.ldy);
+        if (st) return set_error(st, "job %d: %s", i, sbq_last_error());
+        if (j.packed_up) {
+            if (!j.scale_up) return set_error(SBQ_ERR_INVALID_ARGUMENT, "job %d: null up-projection scale", i);
+            if (reinterpret_cast<uintptr_t>(j.packed_up) % 256)
+                return set_error(SBQ_ERR_ALIGNMENT, "job %d: packed weight must be 256-byte aligned", i);
+            if (j.bias) return set_error(SBQ_ERR_UNSUPPORTED, "job %d: a fused gate/up job takes no bias", i);
+        }
+        fill_job(grp.job[i], j.x, j.ldx, j.packed, j.scale, j.packed_up, j.scale_up, j.bias, j.n, j.k, j.y, j.y_dtype,
+                 j.ldy);
+        grp.job[i].m = (int)m;
+        grp.job[i].tile_begin = tiles;
+        tiles += (int)ceil_div(j.n, 16);
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    dispatch_group(grp, tiles, x_kind(x_dtype), m > 8 ? 2 : 1, s);
+    return check_launch("gemv_w8_group");
 }

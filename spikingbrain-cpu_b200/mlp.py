@@ -47,6 +47,13 @@ class FusedGatedMLP(nn.Module):
         y = self.down_proj(h).reshape(*shape[:-1], self.down_proj.out_features)
         return y.to("cpu") if on_host else y
 
+    def gateup_job(self, x2: torch.Tensor, h: torch.Tensor) -> L.GemvJob:
+        """silu(gate(x2)) * up(x2) into ``h`` as one job of a grouped decode launch."""
+        g, u = self.gate_proj, self.up_proj
+        return L.GemvJob(x2.data_ptr(), x2.stride(0), g.packed.data_ptr(), g.scale.data_ptr(), u.packed.data_ptr(),
+                         u.scale.data_ptr(), None, g.out_features, x2.shape[1], h.data_ptr(),
+                         L.F32 if h.dtype == torch.float32 else L.F16, h.stride(0))
+
     def gateup_into(self, x2: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
         """Low-level device call: silu(gate(x2)) * up(x2) into ``h`` [m, n] (fp16/fp32, unit column stride).
 

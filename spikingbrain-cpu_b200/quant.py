@@ -189,6 +189,12 @@ class Int8Linear(_PackedLinear):
                    L.F32 if out.dtype == torch.float32 else L.F16, out.stride(0), _stream(out.device))
         return out
 
+    def gemv_job(self, x2: torch.Tensor, out: torch.Tensor) -> L.GemvJob:
+        """This projection as one job of a grouped decode launch (see ``gemv_group``)."""
+        return L.GemvJob(x2.data_ptr(), x2.stride(0), self.packed.data_ptr(), self.scale.data_ptr(), None, None,
+                         None if self.bias is None else self.bias.data_ptr(), self.out_features, x2.shape[1],
+                         out.data_ptr(), L.F32 if out.dtype == torch.float32 else L.F16, out.stride(0))
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape
         dev = self.scale.device
@@ -197,6 +203,13 @@ class Int8Linear(_PackedLinear):
         self.forward_into(x2, out)
         out = out.reshape(*shape[:-1], self.out_features)
         return out.to("cpu") if on_host else out
+
+
+def gemv_group(jobs, x_dtype: torch.dtype, m: int, device: torch.device) -> None:
+    """Run several decode projections (``Int8Linear.gemv_job`` / ``FusedGatedMLP.gateup_job``) in one
+    launch: up to 8 jobs, all with ``m`` <= 16 rows of x of dtype ``x_dtype``."""
+    arr = (L.GemvJob * len(jobs))(*jobs)
+    L.call("sbq_gemv_w8_group", arr, len(jobs), _DTYPE_CODE[x_dtype], m, _stream(device))
 
 
 class DynamicInt8Linear(_PackedLinear):

@@ -123,7 +123,13 @@ class ProjectionStack(nn.Module):
         return buf.view(self.world, m, ns).permute(1, 0, 2).reshape(m, self.world * ns)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """fp16 [m, hidden] on the device -> fp16 [m, hidden] (the last layer's down projection)."""
+        """fp16 [m, hidden] on the device -> fp16 [m, hidden] (the last layer's down projection).
+
+        Decode sizes (m <= 16) run each layer as two grouped launches: [gate/up, q|k|v|delta_in]
+        (both read x) and [down, o, delta_out] (after their inputs are gathered).
+        """
+        if x.shape[0] <= 16:
+            return self._forward_grouped(x)
         hd, w = self.hidden, self.world
         m = x.shape[0]
         for layer in self.layers:
@@ -136,10 +142,29 @@ class ProjectionStack(nn.Module):
             x = self._gather(layer.mlp.down_proj.forward_into(h, x.new_empty(m, hd // w)))
         return x
 
+    def _forward_grouped(self, x: torch.Tensor) -> torch.Tensor:
+        from .quant import gemv_group
+
+        hd, w = self.hidden, self.world
+        m = x.shape[0]
+        for layer in self.layers:
+            qkvd = x.new_empty(m, 4 * hd // w)
+            h = x.new_empty(m, self.inter // w)
+            gemv_group([layer.mlp.gateup_job(x, h), layer.qkvd.gemv_job(x, qkvd)], x.dtype, m, x.device)
+            qkvd, h = self._gather(qkvd), self._gather(h)
+            od = x.new_empty(m, 2 * hd // w)
+            xn = x.new_empty(m, hd // w)
+            gemv_group([layer.mlp.down_proj.gemv_job(h, xn), layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], od[:, :hd // w]),
+                        layer.dout.gemv_job(qkvd[:, 3 * hd:], od[:, hd // w:])], x.dtype, m, x.device)
+            self._gather(od)
+            x = self._gather(xn)
+        return x
+
     def launches_per_step(self, m: int) -> int:
-        """Kernels of this library one forward launches (GEMV path, m <= 16 rows per pass)."""
-        passes = -(-m // 16)
-        return len(self.layers) * 5 * passes
+        """Kernels of this library one forward launches (grouped decode path for m <= 16)."""
+        if m <= 16:
+            return len(self.layers) * 2
+        return len(self.layers) * 5
 
 
 class CapturedStack:

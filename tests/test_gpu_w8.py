@@ -159,3 +159,21 @@ def test_fused_gateup_mlp_vs_oracle(sbq, m):
     # the unfused reference composition gives the same answer
     ref = down(torch.nn.functional.silu(gate(x.cuda())) * up(x.cuda()))
     assert R.rel_l2(_np(y), _np(ref)) < REL_L2
+
+
+@pytest.mark.parametrize("m", [1, 5, 16])
+def test_grouped_launch_matches_single_calls(sbq, m):
+    from importlib import import_module
+    quant = import_module("spikingbrain-cpu_b200.quant")
+    k = 512
+    a = sbq.Int8Linear(sbq.workloads.float_weight(384, k, seed=80), torch.randn(384))
+    b = sbq.Int8Linear(sbq.workloads.float_weight(200, k, seed=81), None)
+    mlp = sbq.FusedGatedMLP(*(sbq.Int8Linear(sbq.workloads.float_weight(*sh, seed=82 + i), None)
+                              for i, sh in enumerate([(256, k), (256, k), (k, 256)])))
+    x = sbq.workloads.activation(m, k, seed=85).cuda()
+    ya, yb = torch.empty(m, 384, device="cuda"), torch.empty(m, 200, device="cuda", dtype=torch.float16)
+    h = torch.empty(m, 256, device="cuda", dtype=torch.float16)
+    quant.gemv_group([mlp.gateup_job(x, h), a.gemv_job(x, ya), b.gemv_job(x, yb)], x.dtype, m, x.device)
+    b.out_dtype = torch.float16
+    assert torch.equal(ya, a(x)) and torch.equal(yb, b(x))
+    assert torch.equal(h, mlp.gateup_into(x, torch.empty_like(h)))
