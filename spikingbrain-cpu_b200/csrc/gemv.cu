@@ -5,14 +5,18 @@
 // each 128-row block of the weight to fp32 and runs an fp32 sgemm, then multiplies by the
 // per-row scale.  Here the weight is streamed from HBM exactly once per launch:
 //
-//   * one CTA per 16-row tile of a weight; a producer warp streams the tile's contiguous K strip
-//     (ceil(k/64) KiB per matrix) with cp.async.bulk copies into a 64 KiB shared-memory ring
-//     (8 KiB chunks, mbarrier transaction counts); several CTAs share an SM;
+//   * each CTA owns a run of consecutive 16-row tiles of one weight (sized so a launch has about
+//     three CTAs per SM, each moving a similar number of bytes); a producer warp streams that
+//     contiguous byte range with cp.async.bulk copies into a 40 KiB shared-memory ring (8 KiB
+//     chunks, mbarrier transaction counts), across tile boundaries without pausing;
+//   * the consumers copy x into shared memory once (when m * k fits in 26 KiB), so the chunk
+//     loop reads its activation fragments from shared memory instead of waiting on L2;
 //   * eight consumer warps take one 1 KiB tile of each chunk: two conflict-free 16-byte shared
 //     loads per lane, int8 -> fp16 (or bf16) in registers (exact), m16n8k16 tensor-core MMAs with
 //     fp32 accumulation and the activation rows as the n dimension (8 or 16 tokens per pass);
-//   * the warps' partial sums are reduced through the drained ring, then the fp32 per-row scale
-//     (and bias, or the SiLU(gate) * up product) is applied before one store;
+//   * at the end of each tile the warps' partial sums are reduced through shared memory in a fixed
+//     order, then the fp32 per-row scale (and bias, or the SiLU(gate) * up product) is applied
+//     before one store, while the producer keeps streaming the next tile;
 //   * one launch can carry several independent projections ("jobs": e.g. q|k|v|delta_in and
 //     gate/up of one layer, which read the same x); each CTA finds its job from its block index;
 //   * programmatic dependent launch: the weights never depend on the previous kernel, so the
@@ -44,7 +48,9 @@ struct GemvJob {
     int kt_total;      // ceil(k / 64)
     int chunk_tiles;   // tiles per streamed chunk: the largest of 8, 4, 2, 1 dividing kt_total
     int out_f16;       // 1: fp16 output, 0: fp32
-    int tile_begin;    // first block index of this job in the grid
+    int n_tiles;       // 16-row tiles of the weight
+    int tiles_per_cta; // consecutive tiles one CTA streams
+    int cta_begin;     // first block index of this job in the grid
 };
 
 constexpr int kMaxJobs = 8;
@@ -146,9 +152,15 @@ __device__ __forceinline__ void store_out<__half>(void* y, int64_t idx, float v)
 
 constexpr int kGemvThreads = (kGemvWarps + 1) * 32;  // 8 consumer warps + 1 producer warp
 constexpr int kChunkTiles = 8;                         // tiles (KiB) per chunk and matrix, at most
-constexpr int kRingBytes = 64 * 1024;                  // 8 stages of 8 KiB, or 4 of 16 KiB (gate + up)
-constexpr int kMaxStages = 8;
-constexpr int kGemvSmem = kRingBytes + 2 * kMaxStages * 8;
+constexpr int kRingBytes = 40 * 1024;                  // 5 stages of 8 KiB, or 2 of 16 KiB (gate + up)
+constexpr int kMaxStages = 5;
+constexpr int kXBytes = 25 * 1024 + 512;               // x staged in shared memory when it fits (m * (k + 8) * es)
+template <int MT>
+struct GemvSmemSize {
+    static constexpr int kRed = kGemvWarps * 2 * MT * 16 * 9 * 4;  // per-warp partial sums of one tile
+    static constexpr int kBytes = kRingBytes + kXBytes + kRed + 2 * kMaxStages * 8;  // 3 CTAs per SM at MT = 1
+};
+constexpr int kCtasPerSm = 3;
 
 // Named barrier 1 over the consumer warps.
 __device__ __forceinline__ void consumers_sync() {
@@ -169,21 +181,24 @@ __device__ __forceinline__ int consumers_sync_and(int v) {
     return r;
 }
 
-// The body of one CTA: one 16-row tile `nt` of job `jb`, NMAT matrices (1, or 2 for gate/up).
+// The body of one CTA: consecutive 16-row tiles [t0, t1) of job `jb` (a contiguous byte range of the
+// packed weight, and of the up weight when NMAT = 2), NMAT matrices (1, or 2 for gate/up).
 template <int XK, int MT, int NMAT>
-__device__ __forceinline__ void gemv_tile(const GemvJob& jb, int nt, uint8_t* ring, uint64_t* full, uint64_t* empty) {
-    constexpr int S = kMaxStages / NMAT;
+__device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, uint8_t* ring, uint8_t* xs, float* red,
+                                           uint64_t* full, uint64_t* empty) {
+    constexpr int S = NMAT == 1 ? kMaxStages : kRingBytes / (2 * kChunkTiles * kTileBytes);
     constexpr int kStageBytes = NMAT * kChunkTiles * kTileBytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int C = jb.chunk_tiles;
-    const int nchunks = jb.kt_total / C;
+    const int cpt = jb.kt_total / C;  // chunks per tile
+    const int nchunks = (t1 - t0) * cpt;
 
     if (warp == kGemvWarps) {
-        // ---- producer: this tile-row's K strip, chunk by chunk
+        // ---- producer: one contiguous byte range per matrix, chunk by chunk
         if (lane == 0) {
             const uint32_t bytes = (uint32_t)C * kTileBytes;
-            const int8_t* src0 = jb.w0 + (int64_t)nt * jb.kt_total * kTileBytes;
-            const int8_t* src1 = NMAT == 2 ? jb.w1 + (int64_t)nt * jb.kt_total * kTileBytes : nullptr;
+            const int8_t* src0 = jb.w0 + (int64_t)t0 * jb.kt_total * kTileBytes;
+            const int8_t* src1 = NMAT == 2 ? jb.w1 + (int64_t)t0 * jb.kt_total * kTileBytes : nullptr;
             for (int i = 0; i < nchunks; ++i) {
                 const int s = i % S;
                 if (!tc::mbar_wait(&empty[s], ((i / S) & 1) ^ 1)) break;
@@ -196,26 +211,42 @@ __device__ __forceinline__ void gemv_tile(const GemvJob& jb, int nt, uint8_t* ri
         return;
     }
 
-    // ---- consumers
+    // ---- consumers: x into shared memory once (when it fits), so the chunk loop never waits on L2
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
+    constexpr int es = XK == kXF32 ? 4 : 2;
+    const int xrow = jb.k * es + 16;  // bytes per staged row (+16 against bank conflicts)
+    const void* xsrc = jb.x;
+    int64_t xld = jb.ldx;
+    if (jb.m * xrow <= kXBytes) {
+        const int vpr = jb.k * es / 16;
+        for (int v = threadIdx.x; v < jb.m * vpr; v += kGemvWarps * 32) {
+            const int r = v / vpr, cc = v - r * vpr;
+            *reinterpret_cast<uint4*>(xs + r * xrow + cc * 16) =
+                *reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(jb.x) + (int64_t)r * jb.ldx * es + cc * 16);
+        }
+        consumers_sync();
+        xsrc = xs;
+        xld = xrow / es;
+    }
     const int g = lane >> 2, c = lane & 3;
-    float acc[NMAT][MT][4];
-#pragma unroll
-    for (int a = 0; a < NMAT; ++a)
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[a][mt][e] = 0.0f;
-
-    bool ok = true;
     const bool mine = warp < C;
-    for (int i = 0; i < nchunks; ++i) {
+    bool ok = true;
+    float acc[NMAT][MT][4];
+    for (int i = 0, j = 0; i < nchunks; ++i) {
+        if (j == 0) {
+#pragma unroll
+            for (int a = 0; a < NMAT; ++a)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[a][mt][e] = 0.0f;
+        }
         const int s = i % S;
         XFrag<XK> xf[MT];
         if (mine) {
-            const int64_t k0 = (int64_t)(i * C + warp) * kTileCols + 16 * c;
+            const int64_t k0 = (int64_t)(j * C + warp) * kTileCols + 16 * c;
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], jb.x, jb.ldx, 8 * mt + g, jb.m, k0, jb.k);
+            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xsrc, xld, 8 * mt + g, jb.m, k0, jb.k);
         }
         // warp-uniform wait (the __syncwarp below must see every lane)
         if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (i / S) & 1))) {
@@ -234,67 +265,68 @@ __device__ __forceinline__ void gemv_tile(const GemvJob& jb, int nt, uint8_t* ri
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&empty[s]);
-    }
+        if (++j < cpt) continue;
+        j = 0;
 
-    // ---- reduce the 8 warps' partial sums through the drained ring, then the epilogue
-    consumers_sync();
-    float* red = reinterpret_cast<float*>(ring);  // [warp][mat][mt][16 rows][9]
+        // ---- tile complete: reduce the 8 warps' partial sums (fixed order), scale, store
+        const int nt = t0 + i / cpt;
 #define SBQ_RED(w, a, mt, r, col) red[((((w) * NMAT + (a)) * MT + (mt)) * 16 + (r)) * 9 + (col)]
 #pragma unroll
-    for (int a = 0; a < NMAT; ++a)
+        for (int a = 0; a < NMAT; ++a)
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-            SBQ_RED(warp, a, mt, g, 2 * c) = acc[a][mt][0];
-            SBQ_RED(warp, a, mt, g, 2 * c + 1) = acc[a][mt][1];
-            SBQ_RED(warp, a, mt, g + 8, 2 * c) = acc[a][mt][2];
-            SBQ_RED(warp, a, mt, g + 8, 2 * c + 1) = acc[a][mt][3];
-        }
-    if (!consumers_sync_and(ok)) {
-        if (threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
-        return;
-    }
-    for (int t = threadIdx.x; t < MT * 8 * 16; t += kGemvWarps * 32) {
-        const int r = t & 15, tok = t >> 4, mt = tok >> 3, col = tok & 7;
-        const int n = nt * 16 + r;
-        if (n >= jb.n || tok >= jb.m) continue;
-        float v[NMAT];
+            for (int mt = 0; mt < MT; ++mt) {
+                SBQ_RED(warp, a, mt, g, 2 * c) = acc[a][mt][0];
+                SBQ_RED(warp, a, mt, g, 2 * c + 1) = acc[a][mt][1];
+                SBQ_RED(warp, a, mt, g + 8, 2 * c) = acc[a][mt][2];
+                SBQ_RED(warp, a, mt, g + 8, 2 * c + 1) = acc[a][mt][3];
+            }
+        consumers_sync();
+        for (int t = threadIdx.x; t < MT * 8 * 16; t += kGemvWarps * 32) {
+            const int r = t & 15, tok = t >> 4, mt = tok >> 3, col = tok & 7;
+            const int n = nt * 16 + r;
+            if (n >= jb.n || tok >= jb.m) continue;
+            float v[NMAT];
 #pragma unroll
-        for (int a = 0; a < NMAT; ++a) {
-            float sum = 0.0f;
+            for (int a = 0; a < NMAT; ++a) {
+                float sum = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kGemvWarps; ++w) sum += SBQ_RED(w, a, mt, r, col);
-            v[a] = sum;
+                for (int w = 0; w < kGemvWarps; ++w) sum += SBQ_RED(w, a, mt, r, col);
+                v[a] = sum;
+            }
+            float out;
+            if (NMAT == 1) {
+                out = v[0] * jb.s0[n];
+                if (jb.bias) out += jb.bias[n];
+            } else {
+                const float gv = v[0] * jb.s0[n];
+                const float uv = v[1] * jb.s1[n];
+                out = gv / (1.0f + expf(-gv)) * uv;
+            }
+            const int64_t idx = (int64_t)tok * jb.ldy + n;
+            if (jb.out_f16)
+                static_cast<__half*>(jb.y)[idx] = __float2half_rn(out);
+            else
+                static_cast<float*>(jb.y)[idx] = out;
         }
-        float out;
-        if (NMAT == 1) {
-            out = v[0] * jb.s0[n];
-            if (jb.bias) out += jb.bias[n];
-        } else {
-            const float gv = v[0] * jb.s0[n];
-            const float uv = v[1] * jb.s1[n];
-            out = gv / (1.0f + expf(-gv)) * uv;
-        }
-        const int64_t idx = (int64_t)tok * jb.ldy + n;
-        if (jb.out_f16)
-            static_cast<__half*>(jb.y)[idx] = __float2half_rn(out);
-        else
-            static_cast<float*>(jb.y)[idx] = out;
-    }
 #undef SBQ_RED
+        consumers_sync();  // red is rewritten by the next tile
+    }
+    if (!consumers_sync_and(ok) && threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
 }
 
 template <int XK, int MT>
 __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2) gemv_w8_kernel(const __grid_constant__ GemvGroup grp) {
     extern __shared__ __align__(128) uint8_t ring[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRingBytes);
+    uint8_t* xs = ring + kRingBytes;
+    float* red = reinterpret_cast<float*>(xs + kXBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(xs + kXBytes + GemvSmemSize<MT>::kRed);
     uint64_t* empty = full + kMaxStages;
     int j = 0;
-    while (j + 1 < grp.njobs && (int)blockIdx.x >= grp.job[j + 1].tile_begin) ++j;
+    while (j + 1 < grp.njobs && (int)blockIdx.x >= grp.job[j + 1].cta_begin) ++j;
     const GemvJob& jb = grp.job[j];
     const int nmat = jb.w1 ? 2 : 1;
     if (threadIdx.x == 0) {
-        const int stages = kMaxStages / nmat;
-        for (int i = 0; i < stages; ++i) {
+        for (int i = 0; i < kMaxStages; ++i) {
             tc::mbar_init(&full[i], 1);
             tc::mbar_init(&empty[i], kGemvWarps);
         }
@@ -303,34 +335,70 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2) gemv_w8_kernel(
     __syncthreads();
     // the next launch may start its own weight stream now (it waits for this grid before reading x)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int nt = (int)blockIdx.x - jb.tile_begin;
+    const int t0 = ((int)blockIdx.x - jb.cta_begin) * jb.tiles_per_cta;
+    const int t1 = min(t0 + jb.tiles_per_cta, jb.n_tiles);
     if (nmat == 2)
-        gemv_tile<XK, MT, 2>(jb, nt, ring, full, empty);
+        gemv_tiles<XK, MT, 2>(jb, t0, t1, ring, xs, red, full, empty);
     else
-        gemv_tile<XK, MT, 1>(jb, nt, ring, full, empty);
+        gemv_tiles<XK, MT, 1>(jb, t0, t1, ring, xs, red, full, empty);
 }
 
 template <int XK, int MT>
-static void launch_group(const GemvGroup& grp, int total_tiles, cudaStream_t s) {
+static void launch_group(const GemvGroup& grp, int total_ctas, cudaStream_t s) {
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)total_tiles);
+    cfg.gridDim = dim3((unsigned)total_ctas);
     cfg.blockDim = dim3(kGemvThreads);
-    cfg.dynamicSmemBytes = kGemvSmem;
+    cfg.dynamicSmemBytes = GemvSmemSize<MT>::kBytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaFuncSetAttribute(gemv_w8_kernel<XK, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+    cudaFuncSetAttribute(gemv_w8_kernel<XK, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemvSmemSize<MT>::kBytes);
     cudaLaunchKernelEx(&cfg, gemv_w8_kernel<XK, MT>, grp);
 }
 
-static void dispatch_group(const GemvGroup& grp, int total_tiles, int xk, int mt, cudaStream_t s) {
+static int sm_count() {
+    static int count[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!count[dev]) {
+        int c = 0;
+        cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+        count[dev] = c > 0 ? c : 148;
+    }
+    return count[dev];
+}
+
+// Splits every job into runs of consecutive tiles so that the launch has about kCtasPerSm CTAs per
+// SM, each streaming a similar number of weight bytes.  Returns the number of CTAs.
+static int plan_group(GemvGroup& grp) {
+    double total = 0.0;
+    for (int i = 0; i < grp.njobs; ++i) {
+        GemvJob& j = grp.job[i];
+        j.n_tiles = (int)ceil_div(j.n, 16);
+        total += (double)j.n_tiles * (j.w1 ? 2 : 1) * j.kt_total * kTileBytes;
+    }
+    const double target = total / (double)(kCtasPerSm * sm_count());
+    int ctas = 0;
+    for (int i = 0; i < grp.njobs; ++i) {
+        GemvJob& j = grp.job[i];
+        const double tile_bytes = (double)(j.w1 ? 2 : 1) * j.kt_total * kTileBytes;
+        int t = (int)(target / tile_bytes + 0.5);
+        j.tiles_per_cta = t < 1 ? 1 : (t > j.n_tiles ? j.n_tiles : t);
+        j.cta_begin = ctas;
+        ctas += (int)ceil_div(j.n_tiles, j.tiles_per_cta);
+    }
+    return ctas;
+}
+
+static void dispatch_group(GemvGroup& grp, int xk, int mt, cudaStream_t s) {
+    const int ctas = plan_group(grp);
     switch (xk) {
-        case kXF16: mt == 2 ? launch_group<kXF16, 2>(grp, total_tiles, s) : launch_group<kXF16, 1>(grp, total_tiles, s); break;
-        case kXBF16: mt == 2 ? launch_group<kXBF16, 2>(grp, total_tiles, s) : launch_group<kXBF16, 1>(grp, total_tiles, s); break;
-        default: mt == 2 ? launch_group<kXF32, 2>(grp, total_tiles, s) : launch_group<kXF32, 1>(grp, total_tiles, s); break;
+        case kXF16: mt == 2 ? launch_group<kXF16, 2>(grp, ctas, s) : launch_group<kXF16, 1>(grp, ctas, s); break;
+        case kXBF16: mt == 2 ? launch_group<kXBF16, 2>(grp, ctas, s) : launch_group<kXBF16, 1>(grp, ctas, s); break;
+        default: mt == 2 ? launch_group<kXF32, 2>(grp, ctas, s) : launch_group<kXF32, 1>(grp, ctas, s); break;
     }
 }
 
@@ -396,9 +464,8 @@ static int run_single(GemvJob jb, int64_t m, int x_dtype, int y_dtype, cudaStrea
         q.m = (int)(m - m0 < 16 ? m - m0 : 16);
         q.x = static_cast<const char*>(jb.x) + m0 * jb.ldx * xs;
         q.y = static_cast<char*>(jb.y) + m0 * jb.ldy * ys;
-        q.tile_begin = 0;
         grp.job[0] = q;
-        dispatch_group(grp, (int)ceil_div(q.n, 16), x_kind(x_dtype), q.m > 8 ? 2 : 1, s);
+        dispatch_group(grp, x_kind(x_dtype), q.m > 8 ? 2 : 1, s);
     }
     return check_launch(what);
 }
@@ -435,7 +502,6 @@ extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtyp
     if (m < 1 || m > 16) return set_error(SBQ_ERR_UNSUPPORTED, "a grouped launch takes 1..16 rows of x (m=%lld)", (long long)m);
     GemvGroup grp{};
     grp.njobs = njobs;
-    int tiles = 0;
     for (int i = 0; i < njobs; ++i) {
         const sbq_gemv_job& j = jobs[i];
         int st = check_linear_args(j.x, x_dtype, j.ldx, j.packed, j.scale, m, j.n, j.k, j.y, j.y_dtype, j.ldy);
@@ -449,10 +515,8 @@ extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtyp
         fill_job(grp.job[i], j.x, j.ldx, j.packed, j.scale, j.packed_up, j.scale_up, j.bias, j.n, j.k, j.y, j.y_dtype,
                  j.ldy);
         grp.job[i].m = (int)m;
-        grp.job[i].tile_begin = tiles;
-        tiles += (int)ceil_div(j.n, 16);
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    dispatch_group(grp, tiles, x_kind(x_dtype), m > 8 ? 2 : 1, s);
+    dispatch_group(grp, x_kind(x_dtype), m > 8 ? 2 : 1, s);
     return check_launch("gemv_w8_group");
 }
