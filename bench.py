@@ -99,6 +99,25 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def traffic_per_launch(launches: int):
+    """DRAM bytes per launch of the grouped decode GEMV, from the committed ncu summary (or None).
+
+    profiles/gemv_w8_stack_decode_traffic.md records dram__bytes_read.sum + dram__bytes_write.sum
+    summed over every launch of a captured decode step of the stack, and the launches it covered.
+    """
+    p = ROOT / "profiles" / "gemv_w8_stack_decode_traffic.md"
+    if not p.exists():
+        return None
+    vals = {}
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_step_layer:") or line.startswith("launches_per_layer:"):
+            k, v = line.split(":", 1)
+            vals[k] = float(v)
+    if len(vals) < 2:
+        return None
+    return int(vals["traffic_bytes_per_step_layer:"[:-1]] / vals["launches_per_layer:"[:-1]])
+
+
 def dist_setup(args):
     import torch
     import torch.distributed as dist
@@ -409,6 +428,7 @@ def main() -> None:
                "sample": "reference int8 algorithm (blocked fp32 dequant + sgemm) on 2 of 36 stack layers, "
                          "batch 1, %d steps" % r["steps"]}
 
+    launches = stack.launches_per_step(1)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -421,14 +441,19 @@ def main() -> None:
                        "l2": "no flush: each step streams %.2f GB per GPU > 126 MB L2"
                              % (stack.weight_bytes() / 1e9),
                        "timing": "one CUDA graph replay per step, CUDA events, max over ranks"},
-            "roofline": {"kernel": "gemv_w8 fused gate/up (sbq_mlp_gateup_w8)", "bound": "hbm",
-                         "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk["source"],
-                         "bytes_per_launch": gu_bytes, "us_per_launch": round(gu_ms * 1e3, 3), "traffic": None},
+            "roofline": {"kernel": "gemv_w8_kernel (grouped decode GEMV; every launch of the timed step)",
+                         "bound": "hbm", "achieved": round(value, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(value / pk["hbm_gbs"], 4), "peak_source": pk["source"],
+                         "bytes_per_launch": total_bytes // launches,
+                         "us_per_launch": round(ms * 1e3 / launches, 3),
+                         "traffic": traffic_per_launch(launches),
+                         "standalone_gateup": {"achieved": round(achieved, 1),
+                                               "frac": round(achieved / pk["hbm_gbs"], 4),
+                                               "bytes_per_launch": gu_bytes, "us_per_launch": round(gu_ms * 1e3, 3)}},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 2 * hidden,
                     "d2h_bytes_per_step": 2 * hidden, "ms_per_step": round(e2e_ms, 4)},
-            "gpu_launches": stack.launches_per_step(1) * args.steps,
+            "gpu_launches": launches * args.steps,
             "clocks": clocks.summary(),
             "configs_0_3": extra,
         }

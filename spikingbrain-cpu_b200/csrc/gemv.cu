@@ -11,8 +11,8 @@
 //     chunks, mbarrier transaction counts), across tile boundaries without pausing;
 //   * the consumers copy x into shared memory once (when m * k fits in 26 KiB), so the chunk
 //     loop reads its activation fragments from shared memory instead of waiting on L2;
-//   * eight consumer warps take one 1 KiB tile of each chunk: two conflict-free 16-byte shared
-//     loads per lane, int8 -> fp16 (or bf16) in registers (exact), m16n8k16 tensor-core MMAs with
+//   * eight consumer warps (or four on gate and four on up) take one 1 KiB tile of each chunk:
+//     two conflict-free 16-byte shared loads per lane, int8 -> fp16 (or bf16) in registers (exact), m16n8k16 tensor-core MMAs with
 //     fp32 accumulation and the activation rows as the n dimension (8 or 16 tokens per pass);
 //   * at the end of each tile the warps' partial sums are reduced through shared memory in a fixed
 //     order, then the fp32 per-row scale (and bias, or the SiLU(gate) * up product) is applied
@@ -46,7 +46,7 @@ struct GemvJob {
     int n;
     int k;
     int kt_total;      // ceil(k / 64)
-    int chunk_tiles;   // tiles per streamed chunk: the largest of 8, 4, 2, 1 dividing kt_total
+    int chunk_tiles;   // tiles per chunk and matrix: the largest of 8 (4 for gate/up), 4, 2, 1 dividing kt_total
     int out_f16;       // 1: fp16 output, 0: fp32
     int n_tiles;       // 16-row tiles of the weight
     int tiles_per_cta; // consecutive tiles one CTA streams
@@ -152,15 +152,15 @@ __device__ __forceinline__ void store_out<__half>(void* y, int64_t idx, float v)
 
 constexpr int kGemvThreads = (kGemvWarps + 1) * 32;  // 8 consumer warps + 1 producer warp
 constexpr int kChunkTiles = 8;                         // tiles (KiB) per chunk and matrix, at most
-constexpr int kRingBytes = 40 * 1024;                  // 5 stages of 8 KiB, or 2 of 16 KiB (gate + up)
+constexpr int kRingBytes = 40 * 1024;                  // 5 stages of 8 KiB (8 tiles, or 4 gate + 4 up tiles)
 constexpr int kMaxStages = 5;
 constexpr int kXBytes = 25 * 1024 + 512;               // x staged in shared memory when it fits (m * (k + 8) * es)
 template <int MT>
 struct GemvSmemSize {
-    static constexpr int kRed = kGemvWarps * 2 * MT * 16 * 9 * 4;  // per-warp partial sums of one tile
+    static constexpr int kRed = kGemvWarps * MT * 16 * 9 * 4;  // per-warp partial sums of one tile
     static constexpr int kBytes = kRingBytes + kXBytes + kRed + 2 * kMaxStages * 8;  // 3 CTAs per SM at MT = 1
 };
-constexpr int kCtasPerSm = 3;
+constexpr int kCtasPerSm = 3;  // CTAs a launch is sized for (three fit per SM)
 
 // Named barrier 1 over the consumer warps.
 __device__ __forceinline__ void consumers_sync() {
@@ -182,15 +182,18 @@ __device__ __forceinline__ int consumers_sync_and(int v) {
 }
 
 // The body of one CTA: consecutive 16-row tiles [t0, t1) of job `jb` (a contiguous byte range of the
-// packed weight, and of the up weight when NMAT = 2), NMAT matrices (1, or 2 for gate/up).
+// packed weight, and of the up weight when NMAT = 2).  A chunk holds C tiles of each matrix; the
+// consumer warps are split evenly over the matrices (8 over one, or 4 on gate and 4 on up), each
+// warp taking one tile of its matrix per chunk.
 template <int XK, int MT, int NMAT>
 __device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, uint8_t* ring, uint8_t* xs, float* red,
                                            uint64_t* full, uint64_t* empty) {
-    constexpr int S = NMAT == 1 ? kMaxStages : kRingBytes / (2 * kChunkTiles * kTileBytes);
-    constexpr int kStageBytes = NMAT * kChunkTiles * kTileBytes;
+    constexpr int S = kMaxStages;
+    constexpr int kStageBytes = kChunkTiles * kTileBytes;  // 8 KiB: C tiles of each of the NMAT matrices
+    constexpr int WPM = kGemvWarps / NMAT;                   // warps per matrix
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int C = jb.chunk_tiles;
-    const int cpt = jb.kt_total / C;  // chunks per tile
+    const int C = jb.chunk_tiles;                            // tiles per chunk and matrix (<= WPM)
+    const int cpt = jb.kt_total / C;                         // chunks per tile
     const int nchunks = (t1 - t0) * cpt;
 
     if (warp == kGemvWarps) {
@@ -205,7 +208,7 @@ __device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, ui
                 uint8_t* dst = ring + s * kStageBytes;
                 tc::mbar_arrive_expect_tx(&full[s], bytes * NMAT);
                 tc::bulk_load(dst, src0 + (int64_t)i * bytes, bytes, &full[s]);
-                if (NMAT == 2) tc::bulk_load(dst + kChunkTiles * kTileBytes, src1 + (int64_t)i * bytes, bytes, &full[s]);
+                if (NMAT == 2) tc::bulk_load(dst + bytes, src1 + (int64_t)i * bytes, bytes, &full[s]);
             }
         }
         return;
@@ -229,22 +232,22 @@ __device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, ui
         xld = xrow / es;
     }
     const int g = lane >> 2, c = lane & 3;
-    const bool mine = warp < C;
+    const int mat = warp / WPM, slot = warp % WPM;  // this warp's matrix and tile within a chunk
+    const bool mine = slot < C;
+    const int mat_off = mat * C * kTileBytes;
     bool ok = true;
-    float acc[NMAT][MT][4];
+    float acc[MT][4];
     for (int i = 0, j = 0; i < nchunks; ++i) {
         if (j == 0) {
 #pragma unroll
-            for (int a = 0; a < NMAT; ++a)
+            for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) acc[a][mt][e] = 0.0f;
+                for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
         }
         const int s = i % S;
         XFrag<XK> xf[MT];
         if (mine) {
-            const int64_t k0 = (int64_t)(j * C + warp) * kTileCols + 16 * c;
+            const int64_t k0 = (int64_t)(j * C + slot) * kTileCols + 16 * c;
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xsrc, xld, 8 * mt + g, jb.m, k0, jb.k);
         }
@@ -254,32 +257,26 @@ __device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, ui
             break;
         }
         if (mine) {
-            const uint8_t* st = ring + s * kStageBytes + warp * kTileBytes + lane * 16;
-#pragma unroll
-            for (int a = 0; a < NMAT; ++a) {
-                const uint8_t* t = st + a * (kChunkTiles * kTileBytes);
-                const uint4 wa = *reinterpret_cast<const uint4*>(t);
-                const uint4 wb = *reinterpret_cast<const uint4*>(t + 512);
-                tile_mma<XK, MT>(acc[a], wa, wb, xf);
-            }
+            const uint8_t* t = ring + s * kStageBytes + mat_off + slot * kTileBytes + lane * 16;
+            const uint4 wa = *reinterpret_cast<const uint4*>(t);
+            const uint4 wb = *reinterpret_cast<const uint4*>(t + 512);
+            tile_mma<XK, MT>(acc, wa, wb, xf);
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&empty[s]);
         if (++j < cpt) continue;
         j = 0;
 
-        // ---- tile complete: reduce the 8 warps' partial sums (fixed order), scale, store
+        // ---- tile complete: reduce the warps' partial sums (fixed order), scale, store
         const int nt = t0 + i / cpt;
-#define SBQ_RED(w, a, mt, r, col) red[((((w) * NMAT + (a)) * MT + (mt)) * 16 + (r)) * 9 + (col)]
+#define SBQ_RED(w, mt, r, col) red[(((w) * MT + (mt)) * 16 + (r)) * 9 + (col)]
 #pragma unroll
-        for (int a = 0; a < NMAT; ++a)
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-                SBQ_RED(warp, a, mt, g, 2 * c) = acc[a][mt][0];
-                SBQ_RED(warp, a, mt, g, 2 * c + 1) = acc[a][mt][1];
-                SBQ_RED(warp, a, mt, g + 8, 2 * c) = acc[a][mt][2];
-                SBQ_RED(warp, a, mt, g + 8, 2 * c + 1) = acc[a][mt][3];
-            }
+        for (int mt = 0; mt < MT; ++mt) {
+            SBQ_RED(warp, mt, g, 2 * c) = acc[mt][0];
+            SBQ_RED(warp, mt, g, 2 * c + 1) = acc[mt][1];
+            SBQ_RED(warp, mt, g + 8, 2 * c) = acc[mt][2];
+            SBQ_RED(warp, mt, g + 8, 2 * c + 1) = acc[mt][3];
+        }
         consumers_sync();
         for (int t = threadIdx.x; t < MT * 8 * 16; t += kGemvWarps * 32) {
             const int r = t & 15, tok = t >> 4, mt = tok >> 3, col = tok & 7;
@@ -290,7 +287,7 @@ __device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, ui
             for (int a = 0; a < NMAT; ++a) {
                 float sum = 0.0f;
 #pragma unroll
-                for (int w = 0; w < kGemvWarps; ++w) sum += SBQ_RED(w, a, mt, r, col);
+                for (int w = 0; w < WPM; ++w) sum += SBQ_RED(a * WPM + w, mt, r, col);
                 v[a] = sum;
             }
             float out;
@@ -450,7 +447,8 @@ static void fill_job(GemvJob& jb, const void* x, int64_t ldx, const void* w0, co
     jb.n = (int)n;
     jb.k = (int)k;
     jb.kt_total = (int)ceil_div(k, kTileCols);
-    jb.chunk_tiles = jb.kt_total % 8 == 0 ? 8 : jb.kt_total % 4 == 0 ? 4 : jb.kt_total % 2 == 0 ? 2 : 1;
+    const int cmax = w1 ? 4 : 8;  // a chunk is 8 KiB: 8 tiles of one matrix or 4 of each of two
+    jb.chunk_tiles = jb.kt_total % cmax == 0 ? cmax : jb.kt_total % 4 == 0 ? 4 : jb.kt_total % 2 == 0 ? 2 : 1;
     jb.out_f16 = y_dtype == SBQ_F16;
 }
 
