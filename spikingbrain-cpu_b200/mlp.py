@@ -20,7 +20,10 @@ FUSED_MAX_ROWS = 64
 
 
 class FusedGatedMLP(nn.Module):
-    def __init__(self, gate: Int8Linear, up: Int8Linear, down: Int8Linear, h_dtype: torch.dtype = torch.float16):
+    def __init__(self, gate: Int8Linear, up: Int8Linear, down: Int8Linear, h_dtype: torch.dtype = torch.float16,
+                 shards: int = 1):
+        """``shards`` > 1: gate/up hold one output-channel shard each and down consumes the gathered
+        activation of all ``shards`` of them (the sharded stack); ``forward`` is then unavailable."""
         super().__init__()
         if not all(isinstance(mod, Int8Linear) for mod in (gate, up, down)):
             raise ValueError("FusedGatedMLP needs int8 gate, up and down projections")
@@ -28,14 +31,17 @@ class FusedGatedMLP(nn.Module):
             raise ValueError("the fused gate/up epilogue has no bias term")
         if gate.out_features != up.out_features or gate.in_features != up.in_features:
             raise ValueError("gate and up projections must have the same shape")
-        if down.in_features != gate.out_features:
+        if down.in_features != gate.out_features * shards:
             raise ValueError("down projection input must match the gate/up output")
+        self.shards = shards
         if h_dtype not in (torch.float16, torch.float32):
             raise ValueError("hidden activation dtype must be float16 or float32")
         self.gate_proj, self.up_proj, self.down_proj = gate, up, down
         self.h_dtype = h_dtype
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.shards != 1:
+            raise RuntimeError("a sharded FusedGatedMLP needs the gather between gate/up and down; use the stack")
         shape = x.shape
         dev = self.gate_proj.scale.device
         x2, k16, on_host = _prepare_x(x, self.gate_proj.in_features, dev)

@@ -78,7 +78,7 @@ class StackLayer(nn.Module):
         down = Int8Linear(shard(hidden, inter, 8), None, device=dev)
         down.scale.mul_(_fold(inter, _h_moment(hidden)))
         down.out_dtype = torch.float16
-        self.mlp = FusedGatedMLP(gate, up, down)
+        self.mlp = FusedGatedMLP(gate, up, down, shards=world)
         del qkvd_w
 
     def weight_bytes(self) -> int:
