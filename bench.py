@@ -428,7 +428,7 @@ def main() -> None:
                "sample": "reference int8 algorithm (blocked fp32 dequant + sgemm) on 2 of 36 stack layers, "
                          "batch 1, %d steps" % r["steps"]}
 
-    launches = stack.launches_per_step(1)
+    launches = stack.launches_per_step(1, program=runner.program is not None)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,

@@ -145,6 +145,20 @@ typedef struct sbq_gemv_job {
  * such a group. */
 SBQ_API int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m, void* stream);
 
+/* A decode program: groups of jobs run as stages of ONE persistent launch, stage s + 1 starting after
+ * every output of stage s is written (a grid-wide barrier inside the kernel instead of a kernel
+ * boundary); the weight stream continues across the barriers.  jobs[i] belongs to stage job_stage[i]
+ * (non-decreasing); later stages may read earlier stages' outputs.  Requirements: 1 <= m <= 8 and
+ * m * (k + 8) activation elements of every job fit in 25.5 KiB (m = 1 for k up to 12288 at fp16).
+ * sbq_gemv_program_build lays the program out in `program` (sbq_gemv_program_bytes(nstages) bytes,
+ * device memory, 256-byte aligned) and synchronises (a set-up call; the job pointers are baked in).
+ * sbq_gemv_program_run clears `counters` (nstages ints of device memory) and launches; it is
+ * capturable in a CUDA graph.  The buffers named by the jobs must stay allocated. */
+SBQ_API size_t sbq_gemv_program_bytes(int nstages);
+SBQ_API int sbq_gemv_program_build(const sbq_gemv_job* jobs, const int* job_stage, int njobs, int x_dtype, int64_t m,
+                                   void* program, size_t program_bytes);
+SBQ_API int sbq_gemv_program_run(const void* program, int nstages, int x_dtype, int* counters, void* stream);
+
 /* ---- int8-dyn: dynamic activation quantisation + int8 x int8 -> int32 GEMM ------------- */
 
 /* Bytes of workspace sbq_linear_dyn / sbq_quant_act_* need for an [m, k] activation. */

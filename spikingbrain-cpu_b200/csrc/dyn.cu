@@ -348,8 +348,11 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
     __syncwarp();
 
     // ---- epilogue: wait for the accumulator, then TMEM -> registers -> global
-    // warp-uniform decision: tcgen05.ld below is a warp-collective instruction
-    const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(done, 0) && !*(volatile int*)abort_flag);
+    // one lane per warp polls (with back-off) so idle threads do not compete with the producer and
+    // MMA threads for the barrier; the decision is warp-uniform (tcgen05.ld is warp-collective)
+    int waited = 1;
+    if (lane == 0) waited = tc::mbar_wait_backoff(done, 0) && !*(volatile int*)abort_flag;
+    const bool ok = __shfl_sync(0xffffffffu, waited, 0) != 0;
     tc::fence_after_sync();
     if (ok) {
         const int row = m0 + warp * 32 + lane;
@@ -364,16 +367,30 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
             const int nb = n0 + c * 32;
             float* yrow = p.y + (int64_t)row * p.ldy;
             int32_t* arow = p.acc_out ? p.acc_out + (int64_t)row * p.n : nullptr;
+            float v[32];
+            int32_t a[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-                const int n = nb + j;
-                if (n >= p.n) break;
                 const int i = c * 32 + j;
-                const int32_t a = (int32_t)r[j] - zp * s_rowsum[i];
+                a[j] = (int32_t)r[j] - zp * s_rowsum[i];
                 const float f = __fmul_rn(sx, s_scale[i]);
-                const float af = __int2float_rn(a);
-                yrow[n] = p.bias ? __fmaf_rn(af, f, s_bias[i]) : __fmul_rn(af, f);
-                if (arow) arow[n] = a;
+                const float af = __int2float_rn(a[j]);
+                v[j] = p.bias ? __fmaf_rn(af, f, s_bias[i]) : __fmul_rn(af, f);
+            }
+            if (nb + 32 <= p.n && (p.ldy % 4) == 0 && (p.n % 4) == 0) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    *reinterpret_cast<float4*>(yrow + nb + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    if (arow) *reinterpret_cast<int4*>(arow + nb + j) = make_int4(a[j], a[j + 1], a[j + 2], a[j + 3]);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (nb + j < p.n) {
+                        yrow[nb + j] = v[j];
+                        if (arow) arow[nb + j] = a[j];
+                    }
+                }
             }
         }
     }

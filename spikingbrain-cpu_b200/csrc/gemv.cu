@@ -25,6 +25,9 @@
 //
 // fp32 activations are split into a bf16 high and low part (two MMAs, ~16 mantissa bits kept);
 // the dot product of int8 weights and fp16/bf16 activations is exact up to fp32 accumulation.
+#include <cmath>
+#include <vector>
+
 #include "tc.cuh"
 
 namespace sbq {
@@ -181,13 +184,63 @@ __device__ __forceinline__ int consumers_sync_and(int v) {
     return r;
 }
 
-// The body of one CTA: consecutive 16-row tiles [t0, t1) of job `jb` (a contiguous byte range of the
-// packed weight, and of the up weight when NMAT = 2).  A chunk holds C tiles of each matrix; the
+// A CTA's work on one job is a run of consecutive 16-row tiles [t0, t1): a contiguous byte range of
+// the packed weight (and of the up weight when NMAT = 2).  A chunk holds C tiles of each matrix; the
 // consumer warps are split evenly over the matrices (8 over one, or 4 on gate and 4 on up), each
-// warp taking one tile of its matrix per chunk.
+// warp taking one tile of its matrix per chunk.  `ci` counts chunks through the ring across runs,
+// so a CTA can stream several runs back to back (the decode program kernel does).
+
+// Producer (one thread): streams the run's chunks.  False if a wait timed out.
+template <int NMAT>
+__device__ __forceinline__ bool produce_run(const GemvJob& jb, int t0, int t1, uint8_t* ring, uint64_t* full,
+                                            uint64_t* empty, uint32_t& ci) {
+    constexpr int S = kMaxStages;
+    constexpr int kStageBytes = kChunkTiles * kTileBytes;
+    const int C = jb.chunk_tiles;
+    const int nchunks = (t1 - t0) * (jb.kt_total / C);
+    const uint32_t bytes = (uint32_t)C * kTileBytes;
+    const int8_t* src0 = jb.w0 + (int64_t)t0 * jb.kt_total * kTileBytes;
+    const int8_t* src1 = NMAT == 2 ? jb.w1 + (int64_t)t0 * jb.kt_total * kTileBytes : nullptr;
+    for (int i = 0; i < nchunks; ++i, ++ci) {
+        const int s = ci % S;
+        if (!tc::mbar_wait(&empty[s], ((ci / S) & 1) ^ 1)) return false;
+        uint8_t* dst = ring + s * kStageBytes;
+        tc::mbar_arrive_expect_tx(&full[s], bytes * NMAT);
+        tc::bulk_load(dst, src0 + (int64_t)i * bytes, bytes, &full[s]);
+        if (NMAT == 2) tc::bulk_load(dst + bytes, src1 + (int64_t)i * bytes, bytes, &full[s]);
+    }
+    return true;
+}
+
+// Consumers: copy x into shared memory when it fits (m * (k + 8) elements), else read it in place.
+// `coherent` loads bypass L1 (x written earlier in the same kernel by other SMs).
+template <int XK>
+__device__ __forceinline__ void stage_x(const GemvJob& jb, uint8_t* xs, bool coherent, const void*& xsrc,
+                                        int64_t& xld) {
+    constexpr int es = XK == kXF32 ? 4 : 2;
+    const int xrow = jb.k * es + 16;  // bytes per staged row (+16 against bank conflicts)
+    xsrc = jb.x;
+    xld = jb.ldx;
+    if (jb.m * xrow <= kXBytes) {
+        const int vpr = jb.k * es / 16;
+        for (int v = threadIdx.x; v < jb.m * vpr; v += kGemvWarps * 32) {
+            const int r = v / vpr, cc = v - r * vpr;
+            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(jb.x) +
+                                                              (int64_t)r * jb.ldx * es + cc * 16);
+            *reinterpret_cast<uint4*>(xs + r * xrow + cc * 16) = coherent ? __ldcg(src) : *src;
+        }
+        consumers_sync();
+        xsrc = xs;
+        xld = xrow / es;
+    }
+}
+
+// Consumers (8 warps): the run's chunks, a fixed-order reduction and the epilogue per tile.
+// Returns false (warp-uniformly) if a wait timed out.
 template <int XK, int MT, int NMAT>
-__device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, uint8_t* ring, uint8_t* xs, float* red,
-                                           uint64_t* full, uint64_t* empty) {
+__device__ __forceinline__ bool consume_run(const GemvJob& jb, int t0, int t1, const void* xsrc, int64_t xld,
+                                            uint8_t* ring, float* red, uint64_t* full, uint64_t* empty,
+                                            uint32_t& ci) {
     constexpr int S = kMaxStages;
     constexpr int kStageBytes = kChunkTiles * kTileBytes;  // 8 KiB: C tiles of each of the NMAT matrices
     constexpr int WPM = kGemvWarps / NMAT;                   // warps per matrix
@@ -195,56 +248,19 @@ __device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, ui
     const int C = jb.chunk_tiles;                            // tiles per chunk and matrix (<= WPM)
     const int cpt = jb.kt_total / C;                         // chunks per tile
     const int nchunks = (t1 - t0) * cpt;
-
-    if (warp == kGemvWarps) {
-        // ---- producer: one contiguous byte range per matrix, chunk by chunk
-        if (lane == 0) {
-            const uint32_t bytes = (uint32_t)C * kTileBytes;
-            const int8_t* src0 = jb.w0 + (int64_t)t0 * jb.kt_total * kTileBytes;
-            const int8_t* src1 = NMAT == 2 ? jb.w1 + (int64_t)t0 * jb.kt_total * kTileBytes : nullptr;
-            for (int i = 0; i < nchunks; ++i) {
-                const int s = i % S;
-                if (!tc::mbar_wait(&empty[s], ((i / S) & 1) ^ 1)) break;
-                uint8_t* dst = ring + s * kStageBytes;
-                tc::mbar_arrive_expect_tx(&full[s], bytes * NMAT);
-                tc::bulk_load(dst, src0 + (int64_t)i * bytes, bytes, &full[s]);
-                if (NMAT == 2) tc::bulk_load(dst + bytes, src1 + (int64_t)i * bytes, bytes, &full[s]);
-            }
-        }
-        return;
-    }
-
-    // ---- consumers: x into shared memory once (when it fits), so the chunk loop never waits on L2
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
-    constexpr int es = XK == kXF32 ? 4 : 2;
-    const int xrow = jb.k * es + 16;  // bytes per staged row (+16 against bank conflicts)
-    const void* xsrc = jb.x;
-    int64_t xld = jb.ldx;
-    if (jb.m * xrow <= kXBytes) {
-        const int vpr = jb.k * es / 16;
-        for (int v = threadIdx.x; v < jb.m * vpr; v += kGemvWarps * 32) {
-            const int r = v / vpr, cc = v - r * vpr;
-            *reinterpret_cast<uint4*>(xs + r * xrow + cc * 16) =
-                *reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(jb.x) + (int64_t)r * jb.ldx * es + cc * 16);
-        }
-        consumers_sync();
-        xsrc = xs;
-        xld = xrow / es;
-    }
     const int g = lane >> 2, c = lane & 3;
     const int mat = warp / WPM, slot = warp % WPM;  // this warp's matrix and tile within a chunk
     const bool mine = slot < C;
     const int mat_off = mat * C * kTileBytes;
-    bool ok = true;
     float acc[MT][4];
-    for (int i = 0, j = 0; i < nchunks; ++i) {
+    for (int i = 0, j = 0; i < nchunks; ++i, ++ci) {
         if (j == 0) {
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
         }
-        const int s = i % S;
+        const int s = ci % S;
         XFrag<XK> xf[MT];
         if (mine) {
             const int64_t k0 = (int64_t)(j * C + slot) * kTileCols + 16 * c;
@@ -252,10 +268,7 @@ __device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, ui
             for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xsrc, xld, 8 * mt + g, jb.m, k0, jb.k);
         }
         // warp-uniform wait (the __syncwarp below must see every lane)
-        if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (i / S) & 1))) {
-            ok = false;
-            break;
-        }
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (ci / S) & 1))) return false;
         if (mine) {
             const uint8_t* t = ring + s * kStageBytes + mat_off + slot * kTileBytes + lane * 16;
             const uint4 wa = *reinterpret_cast<const uint4*>(t);
@@ -308,6 +321,23 @@ __device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, ui
 #undef SBQ_RED
         consumers_sync();  // red is rewritten by the next tile
     }
+    return true;
+}
+
+template <int XK, int MT, int NMAT>
+__device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, uint8_t* ring, uint8_t* xs, float* red,
+                                           uint64_t* full, uint64_t* empty) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint32_t ci = 0;
+    if (warp == kGemvWarps) {
+        if (lane == 0) produce_run<NMAT>(jb, t0, t1, ring, full, empty, ci);
+        return;
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
+    const void* xsrc;
+    int64_t xld;
+    stage_x<XK>(jb, xs, false, xsrc, xld);
+    const bool ok = consume_run<XK, MT, NMAT>(jb, t0, t1, xsrc, xld, ring, red, full, empty, ci);
     if (!consumers_sync_and(ok) && threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
 }
 
@@ -338,6 +368,119 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2) gemv_w8_kernel(
         gemv_tiles<XK, MT, 2>(jb, t0, t1, ring, xs, red, full, empty);
     else
         gemv_tiles<XK, MT, 1>(jb, t0, t1, ring, xs, red, full, empty);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Decode program: a whole sequence of grouped stages in one persistent cooperative launch.
+//
+// Stage s may read what stages < s wrote.  Every CTA owns at most one run per stage; when its
+// consumers finish that run (or have none) they publish with a fence and an atomic increment of
+// counters[s]; before stage s + 1 a CTA's consumers wait until counters[s] equals the grid size.
+// The producer never waits on a stage: it streams the next stages' weights (which depend on
+// nothing) as fast as the ring drains, so HBM stays busy across the barriers.  All CTAs are
+// co-resident (cooperative launch), every wait is bounded, and activations are read with L2-only
+// loads (they were written during this launch by other SMs).
+// ---------------------------------------------------------------------------------------------
+struct ProgItem {
+    int job;
+    int t0;
+    int t1;
+};
+
+struct ProgStage {
+    GemvJob job[kMaxJobs];
+    int njobs;
+    int pad;
+};
+
+struct ProgParams {
+    const ProgStage* stages;
+    const ProgItem* items;  // [stage][cta]
+    int nstages;
+    int* counters;          // [stage], zero at launch
+};
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+template <int XK>
+__global__ void __launch_bounds__(kGemvThreads, 3) gemv_program_kernel(const ProgParams p) {
+    constexpr int MT = 1;
+    extern __shared__ __align__(128) uint8_t ring[];
+    uint8_t* xs = ring + kRingBytes;
+    float* red = reinterpret_cast<float*>(xs + kXBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(xs + kXBytes + GemvSmemSize<MT>::kRed);
+    uint64_t* empty = full + kMaxStages;
+    __shared__ int abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nctas = gridDim.x, cta = blockIdx.x;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kMaxStages; ++i) {
+            tc::mbar_init(&full[i], 1);
+            tc::mbar_init(&empty[i], kGemvWarps);
+        }
+        tc::fence_mbar_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    uint32_t ci = 0;
+    if (warp == kGemvWarps) {
+        if (lane == 0) {
+            for (int st = 0; st < p.nstages; ++st) {
+                const ProgItem it = p.items[(int64_t)st * nctas + cta];
+                if (it.t1 <= it.t0) continue;
+                const GemvJob jb = p.stages[st].job[it.job];
+                const bool ok = jb.w1 ? produce_run<2>(jb, it.t0, it.t1, ring, full, empty, ci)
+                                      : produce_run<1>(jb, it.t0, it.t1, ring, full, empty, ci);
+                if (!ok) break;
+            }
+        }
+        return;
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the first stage's x comes from the previous kernel
+    for (int st = 0; st < p.nstages; ++st) {
+        if (st > 0) {
+            if (threadIdx.x == 0) {
+                const int* ctr = p.counters + (st - 1);
+                if (ld_acquire(ctr) < nctas) {
+                    const uint64_t t0 = tc::now_ns();
+                    for (uint32_t i = 1; ld_acquire(ctr) < nctas; ++i) {
+                        if ((i & 63) == 0 && tc::now_ns() - t0 > tc::kWaitLimitNs) {
+                            tc::raise_error(SBQ_ERR_TIMEOUT);
+                            abort_flag = 1;
+                            break;
+                        }
+                    }
+                }
+            }
+            consumers_sync();
+            if (abort_flag) return;
+        }
+        const ProgItem it = p.items[(int64_t)st * nctas + cta];
+        if (it.t1 > it.t0) {
+            const GemvJob jb = p.stages[st].job[it.job];
+            const void* xsrc;
+            int64_t xld;
+            stage_x<XK>(jb, xs, true, xsrc, xld);
+            const bool ok = jb.w1 ? consume_run<XK, MT, 2>(jb, it.t0, it.t1, xsrc, xld, ring, red, full, empty, ci)
+                                  : consume_run<XK, MT, 1>(jb, it.t0, it.t1, xsrc, xld, ring, red, full, empty, ci);
+            if (!ok) {
+                if (lane == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
+                abort_flag = 1;
+            }
+        }
+        // publish this CTA's part of stage st: every consumer's stores precede the barrier, the fence
+        // of the publishing thread orders them before its increment
+        consumers_sync();
+        if (abort_flag) return;
+        if (threadIdx.x == 0) {
+            __threadfence();
+            atomicAdd(p.counters + st, 1);
+        }
+    }
 }
 
 template <int XK, int MT>
@@ -517,4 +660,127 @@ extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtyp
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     dispatch_group(grp, x_kind(x_dtype), m > 8 ? 2 : 1, s);
     return check_launch("gemv_w8_group");
+}
+
+// ---- decode program: build (once, synchronous) and run (per step, capturable) ---------------------
+static int program_ctas() { return kCtasPerSm * sm_count(); }
+
+static size_t program_bytes_for(int nstages, int nctas) {
+    return 256 + (size_t)nstages * sizeof(ProgStage) + (size_t)nstages * nctas * sizeof(ProgItem);
+}
+
+extern "C" size_t sbq_gemv_program_bytes(int nstages) {
+    if (nstages < 1) return 0;
+    return program_bytes_for(nstages, program_ctas());
+}
+
+extern "C" int sbq_gemv_program_build(const sbq_gemv_job* jobs, const int* job_stage, int njobs, int x_dtype, int64_t m,
+                                      void* program, size_t program_bytes) {
+    if (!jobs || !job_stage || njobs < 1 || !program) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null argument");
+    if (x_kind(x_dtype) < 0) return set_error(SBQ_ERR_UNSUPPORTED, "activation dtype %d", x_dtype);
+    if (reinterpret_cast<uintptr_t>(program) % 256) return set_error(SBQ_ERR_ALIGNMENT, "program must be 256-byte aligned");
+    int nstages = 0;
+    for (int i = 0; i < njobs; ++i) {
+        if (job_stage[i] < 0 || (i > 0 && job_stage[i] < job_stage[i - 1]))
+            return set_error(SBQ_ERR_INVALID_ARGUMENT, "job stages must be non-negative and non-decreasing");
+        if (job_stage[i] + 1 > nstages) nstages = job_stage[i] + 1;
+    }
+    const int nctas = program_ctas();
+    if (program_bytes < program_bytes_for(nstages, nctas))
+        return set_error(SBQ_ERR_WORKSPACE, "program needs %zu bytes", program_bytes_for(nstages, nctas));
+    const int es = elem_size(x_dtype);
+    std::vector<uint8_t> host(program_bytes_for(nstages, nctas), 0);
+    ProgStage* stages = reinterpret_cast<ProgStage*>(host.data() + 256);
+    ProgItem* items = reinterpret_cast<ProgItem*>(host.data() + 256 + (size_t)nstages * sizeof(ProgStage));
+    for (int i = 0; i < njobs; ++i) {
+        const sbq_gemv_job& j = jobs[i];
+        int st = check_linear_args(j.x, x_dtype, j.ldx, j.packed, j.scale, m, j.n, j.k, j.y, j.y_dtype, j.ldy);
+        if (st) return set_error(st, "job %d: %s", i, sbq_last_error());
+        if (m > 8 || m * (j.k * es + 16) > kXBytes)
+            return set_error(SBQ_ERR_UNSUPPORTED, "job %d: a program needs m * (k + 8) activation elements to fit in "
+                             "%d bytes (m=%lld k=%lld)", i, kXBytes, (long long)m, (long long)j.k);
+        if (j.packed_up && (!j.scale_up || j.bias))
+            return set_error(SBQ_ERR_INVALID_ARGUMENT, "job %d: fused gate/up job needs scale_up and no bias", i);
+        ProgStage& ps = stages[job_stage[i]];
+        if (ps.njobs >= kMaxJobs) return set_error(SBQ_ERR_UNSUPPORTED, "more than %d jobs in one stage", kMaxJobs);
+        GemvJob& jb = ps.job[ps.njobs++];
+        fill_job(jb, j.x, j.ldx, j.packed, j.scale, j.packed_up, j.scale_up, j.bias, j.n, j.k, j.y, j.y_dtype, j.ldy);
+        jb.m = (int)m;
+        jb.n_tiles = (int)ceil_div(j.n, 16);
+    }
+    // per stage: CTAs in proportion to each job's weight bytes, consecutive tiles per CTA
+    for (int st = 0; st < nstages; ++st) {
+        ProgStage& ps = stages[st];
+        ProgItem* row = items + (size_t)st * nctas;
+        for (int c = 0; c < nctas; ++c) row[c] = ProgItem{0, 0, 0};
+        if (ps.njobs == 0) continue;
+        double total = 0.0;
+        for (int i = 0; i < ps.njobs; ++i)
+            total += (double)ps.job[i].n_tiles * (ps.job[i].w1 ? 2 : 1) * ps.job[i].kt_total;
+        const double per_cta = total / nctas;
+        int c = 0;
+        for (int i = 0; i < ps.njobs && c < nctas; ++i) {
+            GemvJob& jb = ps.job[i];
+            const double tile_cost = (double)(jb.w1 ? 2 : 1) * jb.kt_total;
+            int t = (int)std::ceil(per_cta / tile_cost - 1e-9);
+            if (t < 1) t = 1;
+            // leave at least one CTA for every later job
+            const int later = ps.njobs - 1 - i;
+            while ((int)ceil_div(jb.n_tiles, t) > nctas - c - later) ++t;
+            jb.tiles_per_cta = t;
+            for (int t0 = 0; t0 < jb.n_tiles && c < nctas; t0 += t, ++c)
+                row[c] = ProgItem{i, t0, t0 + t < jb.n_tiles ? t0 + t : jb.n_tiles};
+        }
+    }
+    int* header = reinterpret_cast<int*>(host.data());
+    header[0] = nstages;
+    header[1] = nctas;
+    header[2] = x_dtype;
+    header[3] = (int)m;
+    if (cudaMemcpy(program, host.data(), host.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        return check_launch("copy decode program");
+    return SBQ_OK;
+}
+
+extern "C" int sbq_gemv_program_run(const void* program, int nstages, int x_dtype, int* counters, void* stream) {
+    if (!program || !counters || nstages < 1) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null argument");
+    const int xk = x_kind(x_dtype);
+    if (xk < 0) return set_error(SBQ_ERR_UNSUPPORTED, "activation dtype %d", x_dtype);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaMemsetAsync(counters, 0, sizeof(int) * nstages, s) != cudaSuccess) return check_launch("clear counters");
+    ProgParams pp{};
+    const uint8_t* base = static_cast<const uint8_t*>(program);
+    const int nctas = program_ctas();
+    pp.stages = reinterpret_cast<const ProgStage*>(base + 256);
+    pp.items = reinterpret_cast<const ProgItem*>(base + 256 + (size_t)nstages * sizeof(ProgStage));
+    pp.nstages = nstages;
+    pp.counters = counters;
+    const int smem = GemvSmemSize<1>::kBytes;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)nctas);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // every CTA co-resident: the stage barriers rely on it
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    switch (xk) {
+        case kXF16:
+            cudaFuncSetAttribute(gemv_program_kernel<kXF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            e = cudaLaunchKernelEx(&cfg, gemv_program_kernel<kXF16>, pp);
+            break;
+        case kXBF16:
+            cudaFuncSetAttribute(gemv_program_kernel<kXBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            e = cudaLaunchKernelEx(&cfg, gemv_program_kernel<kXBF16>, pp);
+            break;
+        default:
+            cudaFuncSetAttribute(gemv_program_kernel<kXF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            e = cudaLaunchKernelEx(&cfg, gemv_program_kernel<kXF32>, pp);
+            break;
+    }
+    if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "decode program launch: %s", cudaGetErrorString(e));
+    return check_launch("gemv_program");
 }

@@ -85,6 +85,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// Same as mbar_wait for threads that only wait (no work to overlap): sleeps between polls.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = now_ns();
+    for (uint32_t i = 1;; ++i) {
+        __nanosleep(256);
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63) == 0 && now_ns() - t0 > kWaitLimitNs) {
+            raise_error(SBQ_ERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
 // ---- TMA --------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
     asm volatile(

@@ -22,6 +22,7 @@ NVLink) assembles the full activation before its consumer.  x is replicated.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -160,11 +161,73 @@ class ProjectionStack(nn.Module):
             x = self._gather(xn)
         return x
 
-    def launches_per_step(self, m: int) -> int:
-        """Kernels of this library one forward launches (grouped decode path for m <= 16)."""
+    def decode_program(self, x: torch.Tensor) -> "DecodeProgram":
+        """The whole batch-1 decode step as one persistent launch reading ``x`` (see DecodeProgram)."""
+        return DecodeProgram(self, x)
+
+    def launches_per_step(self, m: int, program: bool = False) -> int:
+        """Kernels of this library one forward launches (one decode program, else grouped launches
+        for m <= 16, else one launch per projection)."""
+        if program:
+            return 1
         if m <= 16:
             return len(self.layers) * 2
         return len(self.layers) * 5
+
+
+class DecodeProgram:
+    """A single-GPU batch-1 decode step of the stack as one launch of the decode program kernel.
+
+    Two stages per layer: [gate/up, q|k|v|delta_in] read the layer input, [down, o, delta_out] read
+    their outputs; a grid-wide barrier inside the kernel separates them and the weight stream never
+    pauses.  Every layer gets its own activation buffers (written once per step).  ``run()`` reads
+    the fixed input buffer ``x`` and returns the fixed output buffer (the last layer's down output).
+    """
+
+    def __init__(self, stack: ProjectionStack, x: torch.Tensor):
+        from . import _lib as L
+        from .quant import _DTYPE_CODE
+
+        if stack.world != 1:
+            raise ValueError("the decode program runs on one GPU (no gathers inside a launch)")
+        if x.shape != (1, stack.hidden) or x.dtype != torch.float16 or not x.is_contiguous():
+            raise ValueError("the decode program takes a contiguous fp16 [1, hidden] input")
+        hd, dev = stack.hidden, x.device
+        self.stack, self.x = stack, x
+        self.buffers = []
+        jobs, stage = [], []
+        cur = x
+        for i, layer in enumerate(stack.layers):
+            qkvd = torch.empty(1, 4 * hd, dtype=torch.float16, device=dev)
+            h = torch.empty(1, stack.inter, dtype=torch.float16, device=dev)
+            od = torch.empty(1, 2 * hd, dtype=torch.float16, device=dev)
+            nxt = torch.empty(1, hd, dtype=torch.float16, device=dev)
+            self.buffers += [qkvd, h, od, nxt]
+            jobs += [layer.mlp.gateup_job(cur, h), layer.qkvd.gemv_job(cur, qkvd)]
+            stage += [2 * i, 2 * i]
+            jobs += [layer.mlp.down_proj.gemv_job(h, nxt), layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], od[:, :hd]),
+                     layer.dout.gemv_job(qkvd[:, 3 * hd:], od[:, hd:])]
+            stage += [2 * i + 1] * 3
+            cur = nxt
+        self.y = cur
+        self.nstages = 2 * len(stack.layers)
+        lib = L.load()
+        nbytes = int(lib.sbq_gemv_program_bytes(self.nstages))
+        self.program = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.counters = torch.zeros(self.nstages, dtype=torch.int32, device=dev)
+        arr = (L.GemvJob * len(jobs))(*jobs)
+        st = (ctypes.c_int * len(stage))(*stage)
+        self._code = _DTYPE_CODE[torch.float16]
+        L.call("sbq_gemv_program_build", arr, st, len(jobs), self._code, 1, ctypes.c_void_p(self.program.data_ptr()),
+               nbytes)
+
+    def run(self) -> torch.Tensor:
+        from . import _lib as L
+        from .quant import _stream
+
+        L.call("sbq_gemv_program_run", ctypes.c_void_p(self.program.data_ptr()), self.nstages, self._code,
+               ctypes.c_void_p(self.counters.data_ptr()), _stream(self.x.device))
+        return self.y
 
 
 class CapturedStack:
@@ -176,16 +239,21 @@ class CapturedStack:
     Launch overhead of the per-projection kernels disappears inside the graph.
     """
 
-    def __init__(self, stack: ProjectionStack, m: int = 1, stream: torch.cuda.Stream | None = None):
+    def __init__(self, stack: ProjectionStack, m: int = 1, stream: torch.cuda.Stream | None = None,
+                 use_program: bool = False):
         self.stack = stack
         self.stream = stream or torch.cuda.Stream(stack.device)
         self.x = torch.zeros(m, stack.hidden, dtype=torch.float16, device=stack.device)
+        # grouped launches by default; use_program=True runs a batch-1 single-GPU step as one
+        # decode-program launch (bit-identical; measured slower than the grouped launches so far)
+        self.program = stack.decode_program(self.x) if (m == 1 and stack.world == 1 and use_program) else None
+        step = self.program.run if self.program is not None else (lambda: stack(self.x))
         with torch.cuda.stream(self.stream):
-            stack(self.x)  # warm-up outside the capture (allocator, communicators)
+            step()  # warm-up outside the capture (allocator, communicators)
         self.stream.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=self.stream):
-            self.y = stack(self.x)
+            self.y = step()
         self.x_host = torch.empty(m, stack.hidden, dtype=torch.float16).pin_memory()
         self.y_host = torch.empty(m, stack.hidden, dtype=torch.float16).pin_memory()
 

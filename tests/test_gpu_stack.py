@@ -63,3 +63,22 @@ def test_stack_activations_stay_bounded(sbq):
     y = stack(sbq.workloads.activation(1, 4096, seed=5, device="cuda")).float()
     assert torch.isfinite(y).all()
     assert 0.2 < float(y.std()) < 5.0
+
+
+@pytest.mark.parametrize("layers,hidden,inter", [(3, 512, 1024), (2, 4096, 12288)])
+def test_decode_program_matches_grouped_launches(sbq, layers, hidden, inter):
+    # the one-launch decode program computes every tile exactly as the grouped launches do
+    stack = sbq.stack.ProjectionStack(layers=layers, hidden=hidden, inter=inter, seed=6)
+    x = sbq.workloads.activation(1, hidden, seed=7, device="cuda")
+    want = stack(x)
+    prog = stack.decode_program(x.clone())
+    for _ in range(2):  # the counters are cleared by every run
+        got = prog.run()
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+    assert sbq._lib.load().sbq_check_device_error() == 0
+    # and the captured runner (which uses it) agrees with eager
+    runner = sbq.stack.CapturedStack(stack, m=1, use_program=True)
+    assert runner.program is not None
+    assert torch.equal(runner(x.cpu()).cuda(), want)
+    runner.release()
