@@ -191,8 +191,10 @@ def _graph_time(fn, stream, reps: int, warmup: int) -> float:
         fn()
     stream.synchronize()
     g, _ = capture(fn, stream)
-    for _ in range(warmup):
-        g.replay()
+    with torch.cuda.stream(stream):  # warm-up replays on the timed stream, finished before timing
+        for _ in range(warmup):
+            g.replay()
+    stream.synchronize()
     ms = timed_graph(g, reps, stream)
     del g
     return ms
@@ -294,6 +296,37 @@ def kernel_cases(sbq, dev, stream, steps: int, warmup: int, which=("gemv", "mlp"
         ops = 2 * m * n * k
         out["cfg3_dyn"] = {"us": round(ms * 1e3, 2), "tops": round(ops / ms / 1e9, 1),
                            "frac_int8_spec_4500": round(ops / ms / 1e9 / 4500.0, 4)}
+    return out
+
+
+def stack_cases(sbq, stack, dev, stream, warmup: int) -> dict:
+    """Configuration 4's other points on the same stack: decode at batch 8 and 64, prefill of 8192
+    tokens (weight GB/s for decode, TFLOPS for prefill; CUDA graph per step, CUDA events)."""
+    import torch
+
+    out = {}
+    total = stack.weight_bytes()
+    for m in (8, 64):
+        x = sbq.workloads.activation(m, stack.hidden, seed=m, device=dev)
+        ms = _graph_time(lambda: stack(x), stream, 10, warmup)
+        out["decode_b%d" % m] = {"ms": round(ms, 3), "gbs": round(total / ms / 1e6, 1),
+                                 "frac_hbm": round(total / ms / 1e6 / peaks()["hbm_gbs"], 4)}
+    m = 8192
+    x = sbq.workloads.activation(m, stack.hidden, seed=m, device=dev)
+    with torch.cuda.stream(stream):
+        stack(x)  # warm-up (allocator)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        reps = 2
+        for _ in range(reps):
+            stack(x)
+        end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end) / reps
+    fl = 2.0 * m * total
+    out["prefill_8192"] = {"ms": round(ms, 2), "tflops": round(fl / ms / 1e9, 1),
+                           "frac_bf16_peak": round(fl / ms / 1e9 / peaks()["bf16_tflops"], 4),
+                           "note": "per-projection GEMMs plus torch SiLU*mul between gate/up and down"}
     return out
 
 
@@ -406,8 +439,10 @@ def main() -> None:
                    n_inter, hidden, c_void_p(h_buf.data_ptr()), L.F16, n_inter, st)
 
     g2, _ = capture(gateup_all, stream)
-    for _ in range(3):
-        g2.replay()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g2.replay()
+    stream.synchronize()
     reps = max(5, min(50, args.steps // 20))
     gu_ms = timed_graph(g2, reps, stream) / len(stack.layers)
     gu_bytes = 2 * n_inter * hidden + 2 * 4 * n_inter + 2 * hidden + 2 * n_inter
@@ -418,6 +453,7 @@ def main() -> None:
     extra = None
     if world == 1 and not args.no_extra:
         extra = kernel_cases(sbq, dev, stream, args.steps, args.warmup)
+        extra["cfg4_stack"] = stack_cases(sbq, stack, dev, stream, args.warmup)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

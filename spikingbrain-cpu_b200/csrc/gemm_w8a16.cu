@@ -7,12 +7,14 @@
 //   * warp 0 (one thread) streams 256 x 64 fp16 activation tiles (TMA, 128-byte swizzle) and the
 //     matching 128 x 64 int8 weight tiles (TMA over the packed layout, 64-byte swizzle) into a
 //     5-stage ring;
-//   * warps 4-7 (one weight row per thread) convert each int8 row to fp16 in registers (exact) and
-//     write it straight into tensor memory with tcgen05.st - the MMA's A operand - in a 4-deep ring;
+//   * warps 4-7 and 8-11 (two warpgroups taking alternate k-blocks; one weight row per thread)
+//     convert each int8 row to fp16 in registers (exact) and write it straight into tensor memory
+//     with tcgen05.st - the MMA's A operand - in a 4-deep ring;
 //   * warp 1 (one thread) issues tcgen05.mma.cta_group::1.kind::f16 with A from tensor memory and
 //     the activation tile from shared memory (128 x 256 x 16, fp32 accumulators in TMEM);
-//   * warps 4-7 finally read their channel's accumulators (tcgen05.ld), apply the fp32 per-row
-//     scale (and bias) and store fp16 or fp32 output, consecutive channels per warp store.
+//   * both warpgroups finally read their channel's accumulators (tcgen05.ld; one half of the
+//     tokens each), apply the fp32 per-row scale (and bias) and store fp16 or fp32 output,
+//     consecutive channels per warp store.
 // The scale stays in the fp32 epilogue, as in the reference: int8 values are exact in fp16.
 #include "tc.cuh"
 
@@ -31,7 +33,7 @@ constexpr int kWTok = 256;     // activation rows per CTA (MMA N)
 constexpr int kWBK = 64;       // k per stage (one 128-byte fp16 row, one packed tile column)
 constexpr int kWStages = 5;    // TMA stages
 constexpr int kWABufs = 4;     // weight operand buffers in TMEM (32 columns each)
-constexpr int kWThreads = 256; // 8 warps
+constexpr int kWThreads = 384; // 12 warps: producer, MMA, TMEM, idle, then two converter warpgroups
 constexpr uint32_t kWTmemCols = 512;
 constexpr uint32_t kWAccCol = 0;    // accumulator: columns [0, 256)
 constexpr uint32_t kWACol = 256;    // weight buffers: 32 columns each from 256
@@ -125,11 +127,12 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
             tc::mma_commit(done);
         }
     } else if (warp >= 4) {
-        const int wq = warp - 4;                  // lanes 32 wq .. 32 wq + 31 of tensor memory
+        const int grp = (warp - 4) >> 2;          // converter warpgroup: even (0) or odd (1) k-blocks
+        const int wq = (warp - 4) & 3;            // lanes 32 wq .. 32 wq + 31 of tensor memory
         const int row = wq * 32 + lane;           // weight row (output channel) of this thread
         const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
         bool ok = true;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = grp; kb < p.num_kb; kb += 2) {
             const int s = kb % kWStages, d = kb % kWABufs;
             const uint32_t ph = (kb / kWStages) & 1, phd = (kb / kWABufs) & 1;
             // warp-uniform waits: tcgen05.st below is warp-collective
@@ -164,7 +167,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
             const float sc = s_scale[row], bi = s_bias[row];
             const bool has_bias = p.bias != nullptr;
 #pragma unroll 1
-            for (int c = 0; c < kWTok / 32; ++c) {
+            for (int c = grp * (kWTok / 64); c < (grp + 1) * (kWTok / 64); ++c) {  // this group's token half
                 uint32_t r[32];
                 tc::tmem_ld_32x32b_x32(tmem + lane_addr + kWAccCol + c * 32, r);
                 tc::tmem_wait_ld();
