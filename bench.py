@@ -352,6 +352,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline measurement")
     ap.add_argument("--no-extra", action="store_true", help="skip the per-configuration kernel timings")
     ap.add_argument("--kernel", choices=("gemv", "mlp", "gemm", "dyn"), help="time one configuration's kernel alone")
+    ap.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
+                    help="how sharded ranks assemble activations (N > 1): peer stores over NVLink or NCCL all-gather")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
@@ -371,7 +373,7 @@ def main() -> None:
 
     dev = torch.device("cuda", torch.cuda.current_device())
     group = dist.group.WORLD if world > 1 else None
-    stack = sbq.stack.ProjectionStack(layers=args.layers, device=dev, group=group)
+    stack = sbq.stack.ProjectionStack(layers=args.layers, device=dev, group=group, exchange=args.exchange)
     torch.cuda.synchronize()
     hidden = stack.hidden
     total_bytes = sbq.workloads.stack_bytes(args.layers)  # whole job, all ranks
@@ -465,6 +467,14 @@ def main() -> None:
                          "batch 1, %d steps" % r["steps"]}
 
     launches = stack.launches_per_step(1, program=runner.program is not None)
+    per_gpu = value / world  # each rank streams 1/world of the weights per step
+    if world == 1:
+        parallelism = "single"
+    elif stack.exchange == "peer":
+        parallelism = ("output-channel tp%d; GEMV outputs stored to every rank over NVLink (peer memory), "
+                       "per-launch arrival counters" % world)
+    else:
+        parallelism = "output-channel tp%d + NCCL all-gather" % world
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -473,16 +483,17 @@ def main() -> None:
                                                                      "per-channel int8; N(0,1) fp16 input)",
             "config": {"workload": "cfg4-stack36-decode-b1", "layers": args.layers, "hidden": hidden,
                        "intermediate": stack.inter, "batch": 1, "weight_bytes_per_step": total_bytes,
-                       "parallelism": "output-channel tp%d + NCCL all-gather" % world if world > 1 else "single",
+                       "parallelism": parallelism,
                        "l2": "no flush: each step streams %.2f GB per GPU > 126 MB L2"
                              % (stack.weight_bytes() / 1e9),
                        "timing": "one CUDA graph replay per step, CUDA events, max over ranks"},
             "roofline": {"kernel": "gemv_w8_kernel (grouped decode GEMV; every launch of the timed step)",
-                         "bound": "hbm", "achieved": round(value, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(value / pk["hbm_gbs"], 4), "peak_source": pk["source"],
-                         "bytes_per_launch": total_bytes // launches,
+                         "bound": "hbm", "achieved": round(per_gpu, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(per_gpu / pk["hbm_gbs"], 4), "peak_source": pk["source"],
+                         "per": "GPU" if world > 1 else "job",
+                         "bytes_per_launch": total_bytes // world // launches,
                          "us_per_launch": round(ms * 1e3 / launches, 3),
-                         "traffic": traffic_per_launch(launches),
+                         "traffic": traffic_per_launch(launches) if world == 1 else None,
                          "standalone_gateup": {"achieved": round(achieved, 1),
                                                "frac": round(achieved / pk["hbm_gbs"], 4),
                                                "bytes_per_launch": gu_bytes, "us_per_launch": round(gu_ms * 1e3, 3)}},
@@ -497,6 +508,8 @@ def main() -> None:
     runner.release()
     if world > 1:
         dist.barrier()
+        if stack.peer is not None:
+            stack.peer.close()
         dist.destroy_process_group()
 
 

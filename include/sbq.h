@@ -159,6 +159,46 @@ SBQ_API int sbq_gemv_program_build(const sbq_gemv_job* jobs, const int* job_stag
                                    void* program, size_t program_bytes);
 SBQ_API int sbq_gemv_program_run(const void* program, int nstages, int x_dtype, int* counters, void* stream);
 
+/* ---- output-channel shards across the GPUs of one node (peer memory over NVLink) -------------
+ *
+ * Replaces the all-gather that follows each sharded projection (the output-channel sharding of
+ * the model's projections, quant.py:32-53 run per shard; the reference has no multi-GPU path).
+ * Every rank allocates one arena with sbq_peer_alloc, exports it with sbq_peer_handle, and maps
+ * the other ranks' arenas with sbq_peer_open (the handles travel over any host channel).  All
+ * ranks lay their arenas out identically, so a buffer or counter at offset o is at base_p + o on
+ * rank p.  The ranks must be different GPUs of one node with peer access (NVLink). */
+SBQ_API int sbq_peer_alloc(size_t bytes, void** ptr);          /* zero-filled device memory */
+SBQ_API int sbq_peer_free(void* ptr);
+SBQ_API int sbq_peer_handle(const void* ptr, void* handle);      /* SBQ_PEER_HANDLE_BYTES out */
+SBQ_API int sbq_peer_open(const void* handle, void** ptr);       /* another process's arena */
+SBQ_API int sbq_peer_close(void* ptr);
+#define SBQ_PEER_HANDLE_BYTES 64
+#define SBQ_MAX_PEERS 8
+
+/* One grouped decode launch of a sharded step (see sbq_gemv_w8_group).  Job j's output slice is
+ * stored to y[j][p] on every rank p (this rank's slice inside rank p's full-width buffer, as
+ * mapped in this process; row stride = the job's ldy; jobs[j].y must be this rank's own entry).
+ * When a CTA has stored its tiles it adds their count (16-row tiles) to signal[p] on every rank.
+ * If wait_count is set, the launch first waits until that local counter (the previous launch's
+ * signal) has received wait_expected more increments than at its previous step (all ranks' tiles of
+ * that launch), so x may be an earlier peer launch's output.  wait_state: two zero-initialised
+ * words of this rank's memory used only by this launch position.  Every wait is bounded (10 s, so
+ * ranks may drift apart on the host by that much; then SBQ_ERR_TIMEOUT through
+ * sbq_check_device_error).  Ranks must issue the same launches in the same order. */
+typedef struct sbq_peer_group {
+    int nranks;
+    void* y[8][SBQ_MAX_PEERS];
+    unsigned* signal[SBQ_MAX_PEERS];
+    const unsigned* wait_count;
+    unsigned* wait_state;
+    unsigned wait_expected;
+} sbq_peer_group;
+SBQ_API int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m,
+                                   const sbq_peer_group* peers, void* stream);
+/* The same wait as a one-CTA launch: the end of a sharded step, before anything else reads the
+ * last launch's gathered output. */
+SBQ_API int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned expected, void* stream);
+
 /* ---- int8-dyn: dynamic activation quantisation + int8 x int8 -> int32 GEMM ------------- */
 
 /* Bytes of workspace sbq_linear_dyn / sbq_quant_act_* need for an [m, k] activation. */

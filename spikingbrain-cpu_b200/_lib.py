@@ -29,6 +29,18 @@ class GemvJob(ctypes.Structure):
                 ("y_dtype", ctypes.c_int), ("ldy", ctypes.c_int64)]
 
 
+MAX_PEERS = 8
+PEER_HANDLE_BYTES = 64
+
+
+class PeerGroup(ctypes.Structure):
+    """struct sbq_peer_group of include/sbq.h."""
+
+    _fields_ = [("nranks", ctypes.c_int), ("y", (ctypes.c_void_p * MAX_PEERS) * 8),
+                ("signal", ctypes.c_void_p * MAX_PEERS), ("wait_count", ctypes.c_void_p),
+                ("wait_state", ctypes.c_void_p), ("wait_expected", ctypes.c_uint)]
+
+
 # name -> (restype, argtypes); kept in the order of include/sbq.h
 SIGNATURES = {
     "sbq_version": (_c_int, []),
@@ -49,6 +61,14 @@ SIGNATURES = {
     "sbq_gemv_program_build": (_c_int, [ctypes.POINTER(GemvJob), ctypes.POINTER(ctypes.c_int), _c_int, _c_int, _c_i64,
                                         _vp, _sz]),
     "sbq_gemv_program_run": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
+    "sbq_peer_alloc": (_c_int, [_sz, ctypes.POINTER(_vp)]),
+    "sbq_peer_free": (_c_int, [_vp]),
+    "sbq_peer_handle": (_c_int, [_vp, _vp]),
+    "sbq_peer_open": (_c_int, [_vp, ctypes.POINTER(_vp)]),
+    "sbq_peer_close": (_c_int, [_vp]),
+    "sbq_gemv_w8_group_peer": (_c_int, [ctypes.POINTER(GemvJob), _c_int, _c_int, _c_i64, ctypes.POINTER(PeerGroup),
+                                        _vp]),
+    "sbq_peer_wait": (_c_int, [_vp, _vp, ctypes.c_uint, _vp]),
     "sbq_dyn_workspace_bytes": (_sz, [_c_i64, _c_i64, _c_int]),
     "sbq_quant_act_per_tensor": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "sbq_quant_act_per_token": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp]),

@@ -63,6 +63,59 @@ struct GemvGroup {
     int njobs;
 };
 
+// Output-channel shards on several GPUs of one node (sbq_gemv_w8_group_peer).  Every rank computes
+// its slice of each job's output and stores it straight into every rank's full-width buffer over
+// NVLink (peer pointers); when a CTA's stores are done it adds its tile count to this launch's
+// arrival counter on every rank.  A launch that reads such outputs first waits (bounded) until its
+// local copy of the producing launch's counter has received the increments of a whole step.
+constexpr int kMaxPeers = 8;
+
+struct PeerSync {
+    void* y[kMaxJobs][kMaxPeers];  // job j's output slice as mapped on rank p (same ldy as the job)
+    unsigned* signal[kMaxPeers];   // this launch's arrival counter on rank p
+    const unsigned* wait_count;    // local arrival counter of the launch whose outputs x comes from, or null
+    unsigned* wait_state;          // [generation, arrivals] of this launch's wait (local)
+    unsigned wait_expected;        // increments wait_count receives per step (16-row tiles, all ranks)
+    int nranks;
+};
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_add_sys(unsigned* p, unsigned v) {
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// One thread per CTA: waits until `count` has received this step's `expected` increments (targets
+// grow by `expected` per step; state[0] counts completed steps of this waiter), then records the
+// CTA's arrival; the last CTA of the grid advances the generation for the next step.  Bounded (ranks
+// may drift apart on the host by up to kPeerWaitLimitNs): on expiry the error word is set and the
+// kernel carries on (its outputs are then invalid, the host sees SBQ_ERR_TIMEOUT); after an earlier
+// failure it does not wait at all.
+constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;
+
+__device__ __forceinline__ void peer_wait(const unsigned* count, unsigned* state, unsigned expected) {
+    const unsigned gen = *reinterpret_cast<volatile unsigned*>(state);
+    const unsigned target = (gen + 1u) * expected;
+    if (*reinterpret_cast<volatile int*>(&g_device_error) == 0 && (int)(ld_acquire_sys(count) - target) < 0) {
+        const uint64_t t0 = tc::now_ns();
+        for (uint32_t i = 1; (int)(ld_acquire_sys(count) - target) < 0; ++i) {
+            if ((i & 63) == 0 && tc::now_ns() - t0 > kPeerWaitLimitNs) {
+                tc::raise_error(SBQ_ERR_TIMEOUT);
+                break;
+            }
+        }
+    }
+    if (atomicAdd(state + 1, 1u) == gridDim.x - 1) {
+        state[1] = 0;
+        __threadfence();
+        atomicAdd(state, 1u);
+    }
+}
+
 constexpr int kGemvWarps = 8;  // consumer warps
 
 template <int XK>
@@ -73,16 +126,18 @@ struct XFrag {
 
 // Loads the 16 activation values lane (g, c) needs for k0 .. k0 + 15 of row `row` as MMA B fragments
 // b[s][0..1] (s = the four k16 steps).  Rows beyond m (or spans beyond k) read as zero.
+// `coh`: x is in global memory and was written by other GPUs during this launch (L2-only loads).
 template <int XK>
-__device__ __forceinline__ void load_x(XFrag<XK>& f, const void* xv, int64_t ldx, int row, int m, int64_t k0, int k) {
+__device__ __forceinline__ void load_x(XFrag<XK>& f, const void* xv, int64_t ldx, int row, int m, int64_t k0, int k,
+                                       bool coh = false) {
     const uint8_t* x = static_cast<const uint8_t*>(xv);
     const bool ok = row < m && k0 < k;
     if (XK == kXF16 || XK == kXBF16) {
         uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
         if (ok) {
             const uint4* q = reinterpret_cast<const uint4*>(x + ((int64_t)row * ldx + k0) * 2);
-            v0 = q[0];
-            v1 = q[1];
+            v0 = coh ? __ldcg(q) : q[0];
+            v1 = coh ? __ldcg(q + 1) : q[1];
         }
         f.b[0][0] = v0.x; f.b[0][1] = v0.y; f.b[1][0] = v0.z; f.b[1][1] = v0.w;
         f.b[2][0] = v1.x; f.b[2][1] = v1.y; f.b[3][0] = v1.z; f.b[3][1] = v1.w;
@@ -94,7 +149,7 @@ __device__ __forceinline__ void load_x(XFrag<XK>& f, const void* xv, int64_t ldx
             const uint4* q = reinterpret_cast<const uint4*>(x + ((int64_t)row * ldx + k0) * 4);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const uint4 t = q[i];
+                const uint4 t = coh ? __ldcg(q + i) : q[i];
                 v[4 * i + 0] = __uint_as_float(t.x);
                 v[4 * i + 1] = __uint_as_float(t.y);
                 v[4 * i + 2] = __uint_as_float(t.z);
@@ -237,10 +292,12 @@ __device__ __forceinline__ void stage_x(const GemvJob& jb, uint8_t* xs, bool coh
 
 // Consumers (8 warps): the run's chunks, a fixed-order reduction and the epilogue per tile.
 // Returns false (warp-uniformly) if a wait timed out.
-template <int XK, int MT, int NMAT>
+// PEER: every output is stored to each rank's copy (ps->y[jidx][p]) instead of jb.y.
+template <int XK, int MT, int NMAT, bool PEER = false>
 __device__ __forceinline__ bool consume_run(const GemvJob& jb, int t0, int t1, const void* xsrc, int64_t xld,
                                             uint8_t* ring, float* red, uint64_t* full, uint64_t* empty,
-                                            uint32_t& ci) {
+                                            uint32_t& ci, const PeerSync* ps = nullptr, int jidx = 0,
+                                            bool xcoh = false) {
     constexpr int S = kMaxStages;
     constexpr int kStageBytes = kChunkTiles * kTileBytes;  // 8 KiB: C tiles of each of the NMAT matrices
     constexpr int WPM = kGemvWarps / NMAT;                   // warps per matrix
@@ -265,7 +322,7 @@ __device__ __forceinline__ bool consume_run(const GemvJob& jb, int t0, int t1, c
         if (mine) {
             const int64_t k0 = (int64_t)(j * C + slot) * kTileCols + 16 * c;
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xsrc, xld, 8 * mt + g, jb.m, k0, jb.k);
+            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xsrc, xld, 8 * mt + g, jb.m, k0, jb.k, xcoh);
         }
         // warp-uniform wait (the __syncwarp below must see every lane)
         if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (ci / S) & 1))) return false;
@@ -313,10 +370,19 @@ __device__ __forceinline__ bool consume_run(const GemvJob& jb, int t0, int t1, c
                 out = gv / (1.0f + expf(-gv)) * uv;
             }
             const int64_t idx = (int64_t)tok * jb.ldy + n;
-            if (jb.out_f16)
+            if (PEER) {
+                // consecutive threads store consecutive rows: one coalesced NVLink write per rank
+                for (int p = 0; p < ps->nranks; ++p) {
+                    if (jb.out_f16)
+                        static_cast<__half*>(ps->y[jidx][p])[idx] = __float2half_rn(out);
+                    else
+                        static_cast<float*>(ps->y[jidx][p])[idx] = out;
+                }
+            } else if (jb.out_f16) {
                 static_cast<__half*>(jb.y)[idx] = __float2half_rn(out);
-            else
+            } else {
                 static_cast<float*>(jb.y)[idx] = out;
+            }
         }
 #undef SBQ_RED
         consumers_sync();  // red is rewritten by the next tile
@@ -324,9 +390,9 @@ __device__ __forceinline__ bool consume_run(const GemvJob& jb, int t0, int t1, c
     return true;
 }
 
-template <int XK, int MT, int NMAT>
+template <int XK, int MT, int NMAT, bool PEER>
 __device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, uint8_t* ring, uint8_t* xs, float* red,
-                                           uint64_t* full, uint64_t* empty) {
+                                           uint64_t* full, uint64_t* empty, const PeerSync& ps, int jidx) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint32_t ci = 0;
     if (warp == kGemvWarps) {
@@ -334,15 +400,31 @@ __device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, ui
         return;
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
+    if (PEER && ps.wait_count) {
+        // x also holds the other ranks' slices, stored by their previous launch
+        if (threadIdx.x == 0) peer_wait(ps.wait_count, ps.wait_state, ps.wait_expected);
+        consumers_sync();
+    }
     const void* xsrc;
     int64_t xld;
-    stage_x<XK>(jb, xs, false, xsrc, xld);
-    const bool ok = consume_run<XK, MT, NMAT>(jb, t0, t1, xsrc, xld, ring, red, full, empty, ci);
+    stage_x<XK>(jb, xs, PEER, xsrc, xld);
+    const bool staged = xsrc != jb.x;
+    const bool ok =
+        consume_run<XK, MT, NMAT, PEER>(jb, t0, t1, xsrc, xld, ring, red, full, empty, ci, &ps, jidx, PEER && !staged);
     if (!consumers_sync_and(ok) && threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
+    if (PEER) {
+        // publish: every consumer's peer stores are ordered before the barrier, the barrier before
+        // the increments (sent even after a timeout, so that the other ranks do not wait in vain)
+        __threadfence_system();
+        consumers_sync();
+        if (threadIdx.x == 0)
+            for (int p = 0; p < ps.nranks; ++p) red_add_sys(ps.signal[p], (unsigned)(t1 - t0));
+    }
 }
 
-template <int XK, int MT>
-__global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2) gemv_w8_kernel(const __grid_constant__ GemvGroup grp) {
+template <int XK, int MT, bool PEER>
+__global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2)
+    gemv_w8_kernel(const __grid_constant__ GemvGroup grp, const __grid_constant__ PeerSync ps) {
     extern __shared__ __align__(128) uint8_t ring[];
     uint8_t* xs = ring + kRingBytes;
     float* red = reinterpret_cast<float*>(xs + kXBytes);
@@ -365,9 +447,16 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2) gemv_w8_kernel(
     const int t0 = ((int)blockIdx.x - jb.cta_begin) * jb.tiles_per_cta;
     const int t1 = min(t0 + jb.tiles_per_cta, jb.n_tiles);
     if (nmat == 2)
-        gemv_tiles<XK, MT, 2>(jb, t0, t1, ring, xs, red, full, empty);
+        gemv_tiles<XK, MT, 2, PEER>(jb, t0, t1, ring, xs, red, full, empty, ps, j);
     else
-        gemv_tiles<XK, MT, 1>(jb, t0, t1, ring, xs, red, full, empty);
+        gemv_tiles<XK, MT, 1, PEER>(jb, t0, t1, ring, xs, red, full, empty, ps, j);
+}
+
+// Waits (one CTA) for a peer launch's outputs: the end of a sharded decode step, before the host
+// or another stream reads the gathered result.
+__global__ void peer_wait_kernel(const unsigned* count, unsigned* state, unsigned expected) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (threadIdx.x == 0) peer_wait(count, state, expected);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -483,8 +572,8 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_program_kernel(const Pro
     }
 }
 
-template <int XK, int MT>
-static void launch_group(const GemvGroup& grp, int total_ctas, cudaStream_t s) {
+template <int XK, int MT, bool PEER>
+static void launch_group(const GemvGroup& grp, const PeerSync& ps, int total_ctas, cudaStream_t s) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)total_ctas);
     cfg.blockDim = dim3(kGemvThreads);
@@ -495,8 +584,9 @@ static void launch_group(const GemvGroup& grp, int total_ctas, cudaStream_t s) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaFuncSetAttribute(gemv_w8_kernel<XK, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemvSmemSize<MT>::kBytes);
-    cudaLaunchKernelEx(&cfg, gemv_w8_kernel<XK, MT>, grp);
+    cudaFuncSetAttribute(gemv_w8_kernel<XK, MT, PEER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         GemvSmemSize<MT>::kBytes);
+    cudaLaunchKernelEx(&cfg, gemv_w8_kernel<XK, MT, PEER>, grp, ps);
 }
 
 static int sm_count() {
@@ -533,13 +623,25 @@ static int plan_group(GemvGroup& grp) {
     return ctas;
 }
 
-static void dispatch_group(GemvGroup& grp, int xk, int mt, cudaStream_t s) {
+template <bool PEER>
+static void dispatch_group_t(GemvGroup& grp, const PeerSync& ps, int xk, int mt, cudaStream_t s) {
     const int ctas = plan_group(grp);
     switch (xk) {
-        case kXF16: mt == 2 ? launch_group<kXF16, 2>(grp, ctas, s) : launch_group<kXF16, 1>(grp, ctas, s); break;
-        case kXBF16: mt == 2 ? launch_group<kXBF16, 2>(grp, ctas, s) : launch_group<kXBF16, 1>(grp, ctas, s); break;
-        default: mt == 2 ? launch_group<kXF32, 2>(grp, ctas, s) : launch_group<kXF32, 1>(grp, ctas, s); break;
+        case kXF16:
+            mt == 2 ? launch_group<kXF16, 2, PEER>(grp, ps, ctas, s) : launch_group<kXF16, 1, PEER>(grp, ps, ctas, s);
+            break;
+        case kXBF16:
+            mt == 2 ? launch_group<kXBF16, 2, PEER>(grp, ps, ctas, s) : launch_group<kXBF16, 1, PEER>(grp, ps, ctas, s);
+            break;
+        default:
+            mt == 2 ? launch_group<kXF32, 2, PEER>(grp, ps, ctas, s) : launch_group<kXF32, 1, PEER>(grp, ps, ctas, s);
+            break;
     }
+}
+
+static void dispatch_group(GemvGroup& grp, int xk, int mt, cudaStream_t s) {
+    const PeerSync none{};
+    dispatch_group_t<false>(grp, none, xk, mt, s);
 }
 
 SBQ_DEFINE_ERROR_POLL(poll_error_gemv)
@@ -660,6 +762,73 @@ extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtyp
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     dispatch_group(grp, x_kind(x_dtype), m > 8 ? 2 : 1, s);
     return check_launch("gemv_w8_group");
+}
+
+extern "C" int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m,
+                                      const sbq_peer_group* peers, void* stream) {
+    if (!peers) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null peer description");
+    if (!jobs || njobs < 1 || njobs > kMaxJobs)
+        return set_error(SBQ_ERR_INVALID_ARGUMENT, "njobs must be 1..%d", kMaxJobs);
+    if (m < 1 || m > 16) return set_error(SBQ_ERR_UNSUPPORTED, "a grouped launch takes 1..16 rows of x (m=%lld)", (long long)m);
+    const sbq_peer_group& pg = *peers;
+    if (pg.nranks < 1 || pg.nranks > kMaxPeers)
+        return set_error(SBQ_ERR_INVALID_ARGUMENT, "nranks must be 1..%d (got %d)", kMaxPeers, pg.nranks);
+    if (pg.wait_count && (!pg.wait_state || pg.wait_expected == 0))
+        return set_error(SBQ_ERR_INVALID_ARGUMENT, "a wait needs wait_state and a positive wait_expected");
+    if (reinterpret_cast<uintptr_t>(pg.wait_count) % 4 || reinterpret_cast<uintptr_t>(pg.wait_state) % 8)
+        return set_error(SBQ_ERR_ALIGNMENT, "wait counter must be 4-byte and wait state 8-byte aligned");
+    PeerSync ps{};
+    ps.nranks = pg.nranks;
+    ps.wait_count = pg.wait_count;
+    ps.wait_state = pg.wait_state;
+    ps.wait_expected = pg.wait_expected;
+    for (int p = 0; p < pg.nranks; ++p) {
+        if (!pg.signal[p] || reinterpret_cast<uintptr_t>(pg.signal[p]) % 4)
+            return set_error(SBQ_ERR_INVALID_ARGUMENT, "signal[%d] must be a 4-byte aligned device pointer", p);
+        ps.signal[p] = pg.signal[p];
+    }
+    GemvGroup grp{};
+    grp.njobs = njobs;
+    for (int i = 0; i < njobs; ++i) {
+        const sbq_gemv_job& j = jobs[i];
+        int st = check_linear_args(j.x, x_dtype, j.ldx, j.packed, j.scale, m, j.n, j.k, j.y, j.y_dtype, j.ldy);
+        if (st) return set_error(st, "job %d: %s", i, sbq_last_error());
+        if (j.packed_up) {
+            if (!j.scale_up) return set_error(SBQ_ERR_INVALID_ARGUMENT, "job %d: null up-projection scale", i);
+            if (reinterpret_cast<uintptr_t>(j.packed_up) % 256)
+                return set_error(SBQ_ERR_ALIGNMENT, "job %d: packed weight must be 256-byte aligned", i);
+            if (j.bias) return set_error(SBQ_ERR_UNSUPPORTED, "job %d: a fused gate/up job takes no bias", i);
+        }
+        bool local = false;
+        for (int p = 0; p < pg.nranks; ++p) {
+            if (!pg.y[i][p]) return set_error(SBQ_ERR_INVALID_ARGUMENT, "job %d: null destination for rank %d", i, p);
+            local = local || pg.y[i][p] == j.y;
+            ps.y[i][p] = pg.y[i][p];
+        }
+        if (!local) return set_error(SBQ_ERR_INVALID_ARGUMENT, "job %d: y must be one of its rank destinations", i);
+        fill_job(grp.job[i], j.x, j.ldx, j.packed, j.scale, j.packed_up, j.scale_up, j.bias, j.n, j.k, j.y, j.y_dtype,
+                 j.ldy);
+        grp.job[i].m = (int)m;
+    }
+    dispatch_group_t<true>(grp, ps, x_kind(x_dtype), m > 8 ? 2 : 1, static_cast<cudaStream_t>(stream));
+    return check_launch("gemv_w8_group_peer");
+}
+
+extern "C" int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned expected, void* stream) {
+    if (!count || !state || expected == 0) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null counter/state or zero expected");
+    if (reinterpret_cast<uintptr_t>(count) % 4 || reinterpret_cast<uintptr_t>(state) % 8)
+        return set_error(SBQ_ERR_ALIGNMENT, "counter must be 4-byte and state 8-byte aligned");
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, peer_wait_kernel, count, state, expected);
+    return check_launch("peer_wait");
 }
 
 // ---- decode program: build (once, synchronous) and run (per step, capturable) ---------------------

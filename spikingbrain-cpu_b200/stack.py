@@ -16,8 +16,15 @@ the activations stay near unit variance over 36 layers; the int8 weights themsel
 reference quantiser on ``N(0, 0.02)`` weights.
 
 Sharding (``world > 1``): rank r owns rows [r n / world, (r+1) n / world) of every projection and
-produces that slice of each output; ``torch.distributed.all_gather_into_tensor`` (NCCL over
-NVLink) assembles the full activation before its consumer.  x is replicated.
+produces that slice of each output; x is replicated.  Two ways assemble the full activation before
+its consumer:
+
+* ``exchange="peer"`` (decode, m <= 16): every GEMV stores its slice straight into every rank's
+  full-width buffer over NVLink and signals a per-launch arrival counter on every rank; the next
+  launch waits on its local counter (``PeerExchange``).  Two synchronisation points per layer and
+  no collective launches.
+* ``exchange="nccl"`` (and every prefill size): ``torch.distributed.all_gather_into_tensor`` after
+  each sharded projection.
 """
 
 from __future__ import annotations
@@ -87,14 +94,157 @@ class StackLayer(nn.Module):
         return sum(m.out_features * m.in_features for m in mods)
 
 
+class _DeviceBytes:
+    """``__cuda_array_interface__`` of raw device memory, so torch can view it without owning it."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "strides": None, "version": 2}
+
+
+class PeerExchange:
+    """Rank-symmetric arena of a sharded stack's decode activations and arrival counters.
+
+    Every rank allocates the same layout (``libsbq`` peer arena), exports it with a CUDA IPC handle
+    and maps every other rank's arena, so that a GEMV can store its output slice into all ranks'
+    full-width buffers and signal their counters (``sbq_gemv_w8_group_peer``).  Per layer: the full
+    ``qkvd`` [m_max, 4 hidden], ``h`` [m_max, inter], ``od`` [m_max, 2 hidden] and ``x'`` [m_max, hidden]
+    buffers (fp16), one arrival counter per launch and one wait state per waiting launch.
+    The ranks must be distinct GPUs of one node with peer access.
+    """
+
+    def __init__(self, stack: "ProjectionStack", m_max: int = 16):
+        import torch.distributed as dist
+
+        from . import _lib as L
+
+        self.L, self.lib = L, L.load()
+        self.stack, self.m_max = stack, m_max
+        w, rank, dev = stack.world, stack.rank, stack.device
+        if w > L.MAX_PEERS:
+            raise ValueError("at most %d ranks share a peer exchange" % L.MAX_PEERS)
+        props = torch.cuda.get_device_properties(dev)
+        ident = str(getattr(props, "uuid", "")) or "%s:%s" % (getattr(props, "pci_bus_id", ""), dev.index)
+        ids = [None] * w
+        dist.all_gather_object(ids, ident, group=stack.group)
+        if len(set(ids)) != w:
+            raise ValueError("peer exchange needs one GPU per rank (ranks share a device)")
+        hd, it = stack.hidden, stack.inter
+        off = 0
+
+        def take(nbytes: int) -> int:
+            nonlocal off
+            o = off
+            off += (nbytes + 255) // 256 * 256
+            return o
+
+        self.buf = []  # per layer: offsets of qkvd, h, od, x'
+        for _ in stack.layers:
+            self.buf.append([take(m_max * n * 2) for n in (4 * hd, it, 2 * hd, hd)])
+        self.cnt = [[take(128), take(128)] for _ in stack.layers]   # arrival counter of launch 1 / 2
+        self.state = [[take(128), take(128)] for _ in stack.layers]  # wait state of launch 1 / 2
+        self.final_state = take(128)
+        self.nbytes = off
+        base = ctypes.c_void_p()
+        L.call("sbq_peer_alloc", off, ctypes.byref(base))
+        self.base = base.value
+        handle = (ctypes.c_uint8 * L.PEER_HANDLE_BYTES)()
+        L.call("sbq_peer_handle", ctypes.c_void_p(self.base), handle)
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=dev)
+        every = torch.empty(w * L.PEER_HANDLE_BYTES, dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(every, mine, group=stack.group)
+        every = every.cpu().view(w, L.PEER_HANDLE_BYTES)
+        self.peers = []
+        for p in range(w):
+            if p == rank:
+                self.peers.append(self.base)
+                continue
+            h = (ctypes.c_uint8 * L.PEER_HANDLE_BYTES)(*every[p].tolist())
+            ptr = ctypes.c_void_p()
+            L.call("sbq_peer_open", h, ctypes.byref(ptr))
+            self.peers.append(ptr.value)
+        self.arena = torch.as_tensor(_DeviceBytes(self.base, self.nbytes), device=dev)
+        dist.barrier(group=stack.group)
+
+    def view(self, layer: int, which: int, m: int) -> torch.Tensor:
+        """Local full-width fp16 buffer ``which`` (0 qkvd, 1 h, 2 od, 3 x') of a layer, first m rows."""
+        n = (4 * self.stack.hidden, self.stack.inter, 2 * self.stack.hidden, self.stack.hidden)[which]
+        o = self.buf[layer][which]
+        return self.arena[o:o + self.m_max * n * 2].view(torch.float16).view(self.m_max, n)[:m]
+
+    def _group(self, dests, signal_off: int, wait_off, state_off: int, expected: int):
+        L = self.L
+        pg = L.PeerGroup()
+        pg.nranks = self.stack.world
+        for j, (off, col) in enumerate(dests):
+            for p, b in enumerate(self.peers):
+                pg.y[j][p] = b + off + col * 2
+        for p, b in enumerate(self.peers):
+            pg.signal[p] = b + signal_off
+        pg.wait_count = None if wait_off is None else self.base + wait_off
+        pg.wait_state = self.base + state_off
+        pg.wait_expected = expected
+        return pg
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """The sharded decode step on fp16 x [m, hidden] (m <= m_max, replicated); returns the local
+        full-width output buffer after every rank's slice of it has arrived."""
+        from .quant import _DTYPE_CODE, _stream
+
+        L, st = self.L, self.stack
+        m = x.shape[0]
+        if m > self.m_max:
+            raise ValueError("the peer exchange was laid out for %d rows (got %d)" % (self.m_max, m))
+        hd, it, w, r = st.hidden, st.inter, st.world, st.rank
+        code, stream = _DTYPE_CODE[x.dtype], _stream(x.device)
+        e1 = w * (-(-it // (16 * w)) + -(-4 * hd // (16 * w)))   # 16-row tiles of launch 1, all ranks
+        e2 = w * 3 * -(-hd // (16 * w))
+        cur = x
+        for i, layer in enumerate(st.layers):
+            q_off, h_off, od_off, x_off = self.buf[i]
+            qkvd, h, od, xn = (self.view(i, k, m) for k in range(4))
+            hs, qs = it // w, 4 * hd // w
+            jobs = [layer.mlp.gateup_job(cur, h[:, r * hs:(r + 1) * hs]), layer.qkvd.gemv_job(cur, qkvd[:, r * qs:(r + 1) * qs])]
+            pg = self._group([(h_off, r * hs), (q_off, r * qs)], self.cnt[i][0],
+                             None if i == 0 else self.cnt[i - 1][1], self.state[i][0], e2)
+            L.call("sbq_gemv_w8_group_peer", (L.GemvJob * 2)(*jobs), 2, code, m, ctypes.byref(pg), stream)
+            s = hd // w
+            jobs = [layer.mlp.down_proj.gemv_job(h, xn[:, r * s:(r + 1) * s]),
+                    layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], od[:, r * s:(r + 1) * s]),
+                    layer.dout.gemv_job(qkvd[:, 3 * hd:], od[:, hd + r * s:hd + (r + 1) * s])]
+            pg = self._group([(x_off, r * s), (od_off, r * s), (od_off, hd + r * s)], self.cnt[i][1],
+                             self.cnt[i][0], self.state[i][1], e1)
+            L.call("sbq_gemv_w8_group_peer", (L.GemvJob * 3)(*jobs), 3, code, m, ctypes.byref(pg), stream)
+            cur = xn
+        L.call("sbq_peer_wait", ctypes.c_void_p(self.base + self.cnt[-1][1]),
+               ctypes.c_void_p(self.base + self.final_state), e2, stream)
+        return cur
+
+    def close(self) -> None:
+        """Unmap the other ranks' arenas and free this one (every rank, after its last step)."""
+        import torch.distributed as dist
+
+        if self.base is None:
+            return
+        dist.barrier(group=self.stack.group)
+        for p, b in enumerate(self.peers):
+            if b != self.base:
+                self.L.call("sbq_peer_close", ctypes.c_void_p(b))
+        self.arena = None
+        self.L.call("sbq_peer_free", ctypes.c_void_p(self.base))
+        self.base = None
+
+
 class ProjectionStack(nn.Module):
     """The stack; ``forward(x)`` maps fp16 [m, hidden] to fp16 [m, hidden] on the device."""
 
     def __init__(self, layers: int = W.LAYERS, hidden: int = W.HIDDEN, inter: int = W.INTER, seed: int = 4,
-                 device=None, group=None):
+                 device=None, group=None, exchange: str = "peer"):
         super().__init__()
         import torch.distributed as dist
 
+        if exchange not in ("peer", "nccl"):
+            raise ValueError("exchange must be 'peer' or 'nccl'")
         self.group = group
         self.world = dist.get_world_size(group) if group is not None else 1
         self.rank = dist.get_rank(group) if group is not None else 0
@@ -105,6 +255,8 @@ class ProjectionStack(nn.Module):
         self.device, self.hidden, self.inter = dev, hidden, inter
         self.layers = nn.ModuleList(StackLayer(i, hidden, inter, seed, dev, self.rank, self.world)
                                     for i in range(layers))
+        self.exchange = exchange if self.world > 1 else "none"
+        self.peer = PeerExchange(self) if self.exchange == "peer" else None
 
     def weight_bytes(self) -> int:
         """int8 weight bytes this rank streams per decode step."""
@@ -130,6 +282,8 @@ class ProjectionStack(nn.Module):
         (both read x) and [down, o, delta_out] (after their inputs are gathered).
         """
         if x.shape[0] <= 16:
+            if self.peer is not None:
+                return self.peer.forward(x)
             return self._forward_grouped(x)
         hd, w = self.hidden, self.world
         m = x.shape[0]
@@ -171,7 +325,7 @@ class ProjectionStack(nn.Module):
         if program:
             return 1
         if m <= 16:
-            return len(self.layers) * 2
+            return len(self.layers) * 2 + (1 if self.peer is not None else 0)
         return len(self.layers) * 5
 
 

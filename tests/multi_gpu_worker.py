@@ -1,0 +1,69 @@
+"""One rank of the sharded-stack parity check (run by tests/test_gpu_multi.py under torchrun).
+
+Every rank builds the unsharded stack on its own GPU as the reference (the seeded weights are the
+same on every rank), then the output-channel sharded stack with each exchange ("peer": GEMV outputs
+stored to every rank over NVLink; "nccl": all-gather), and checks that every sharded result is
+bit-identical to the unsharded one: eager decode (m = 1, 3, 16), the captured decode step replayed
+on several inputs, and an m = 80 prefill (NCCL gathers).  Exits non-zero on the first mismatch.
+"""
+
+from __future__ import annotations
+
+import datetime
+import importlib
+import os
+import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+import torch
+import torch.distributed as dist
+
+
+def main() -> int:
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
+    sbq = importlib.import_module("spikingbrain-cpu_b200")
+    dev = torch.device("cuda", local)
+    shape = dict(layers=3, hidden=1024, inter=2048, seed=11, device=dev)
+    ref = sbq.stack.ProjectionStack(**shape)
+    failures = []
+
+    def check(name, got, want):
+        if not torch.equal(got.cpu(), want.cpu()):
+            d = (got.float() - want.float()).abs().max().item()
+            failures.append("%s: max |diff| %g" % (name, d))
+
+    for exchange in ("peer", "nccl"):
+        st = sbq.stack.ProjectionStack(group=dist.group.WORLD, exchange=exchange, **shape)
+        for m in (1, 3, 16):
+            x = sbq.workloads.activation(m, shape["hidden"], seed=20 + m, device=dev)
+            check("%s eager m=%d" % (exchange, m), st(x).clone(), ref(x))
+        x = sbq.workloads.activation(80, shape["hidden"], seed=3, device=dev)
+        check("%s prefill m=80" % exchange, st(x).clone(), ref(x))
+        run = sbq.stack.CapturedStack(st, m=1)
+        for i in range(4):
+            x = sbq.workloads.activation(1, shape["hidden"], seed=40 + i, device=dev)
+            check("%s graph replay %d" % (exchange, i), run(x).clone(), ref(x))
+            xh = x.cpu()
+            check("%s graph host call %d" % (exchange, i), run(xh).clone(), ref(x))
+        torch.cuda.synchronize()
+        status = sbq._lib.load().sbq_check_device_error()
+        if status:
+            failures.append("%s: device error %d" % (exchange, status))
+        run.release()
+        dist.barrier()
+        if st.peer is not None:
+            st.peer.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    for f in failures:
+        print("rank %d: %s" % (rank, f), flush=True)
+    print("rank %d: %s" % (rank, "ok" if not failures else "FAILED"), flush=True)
+    return 1 if failures else 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
