@@ -178,17 +178,23 @@ SBQ_API int sbq_peer_close(void* ptr);
 /* One grouped decode launch of a sharded step (see sbq_gemv_w8_group).  Job j's output slice is
  * stored to y[j][p] on every rank p (this rank's slice inside rank p's full-width buffer, as
  * mapped in this process; row stride = the job's ldy; jobs[j].y must be this rank's own entry).
- * When a CTA has stored its tiles it adds their count (16-row tiles) to signal[p] on every rank.
- * If wait_count is set, the launch first waits until that local counter (the previous launch's
- * signal) has received wait_expected more increments than at its previous step (all ranks' tiles of
- * that launch), so x may be an earlier peer launch's output.  wait_state: two zero-initialised
- * words of this rank's memory used only by this launch position.  Every wait is bounded (10 s, so
- * ranks may drift apart on the host by that much; then SBQ_ERR_TIMEOUT through
- * sbq_check_device_error).  Ranks must issue the same launches in the same order. */
+ * The launch's CTAs count themselves out on `done` (one word of this rank's memory, zero at first
+ * use); the last one adds 1 to the launch's signal on every rank (signal[p], as mapped here).  A
+ * signal is SBQ_PEER_SIGNAL_COPIES words 128 bytes apart (a 4 KiB region, 128-byte aligned, zero
+ * at first use), all incremented together so that waiting CTAs poll different lines.  If
+ * wait_count is set (this rank's signal of the launch whose output x is), the launch first waits
+ * until that signal has received wait_expected (= the number of ranks) more increments than at its
+ * previous step.  wait_state: two zero-initialised words of this rank's memory used only by this
+ * launch position.  Every wait is bounded (10 s, so ranks may drift apart on the host by that
+ * much; then SBQ_ERR_TIMEOUT through sbq_check_device_error).  Ranks must issue the same launches
+ * in the same order. */
+#define SBQ_PEER_SIGNAL_COPIES 32
+#define SBQ_PEER_SIGNAL_BYTES 4096
 typedef struct sbq_peer_group {
     int nranks;
     void* y[8][SBQ_MAX_PEERS];
     unsigned* signal[SBQ_MAX_PEERS];
+    unsigned* done;
     const unsigned* wait_count;
     unsigned* wait_state;
     unsigned wait_expected;

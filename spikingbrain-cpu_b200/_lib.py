@@ -31,13 +31,14 @@ class GemvJob(ctypes.Structure):
 
 MAX_PEERS = 8
 PEER_HANDLE_BYTES = 64
+PEER_SIGNAL_BYTES = 4096
 
 
 class PeerGroup(ctypes.Structure):
     """struct sbq_peer_group of include/sbq.h."""
 
     _fields_ = [("nranks", ctypes.c_int), ("y", (ctypes.c_void_p * MAX_PEERS) * 8),
-                ("signal", ctypes.c_void_p * MAX_PEERS), ("wait_count", ctypes.c_void_p),
+                ("signal", ctypes.c_void_p * MAX_PEERS), ("done", ctypes.c_void_p), ("wait_count", ctypes.c_void_p),
                 ("wait_state", ctypes.c_void_p), ("wait_expected", ctypes.c_uint)]
 
 

@@ -65,17 +65,23 @@ struct GemvGroup {
 
 // Output-channel shards on several GPUs of one node (sbq_gemv_w8_group_peer).  Every rank computes
 // its slice of each job's output and stores it straight into every rank's full-width buffer over
-// NVLink (peer pointers); when a CTA's stores are done it adds its tile count to this launch's
-// arrival counter on every rank.  A launch that reads such outputs first waits (bounded) until its
-// local copy of the producing launch's counter has received the increments of a whole step.
+// NVLink (peer pointers).  The CTAs of a launch count themselves out on a local counter; the last
+// one adds 1 to this launch's signal on every rank.  A launch that reads such outputs first waits
+// (bounded) until its local copy of the producing launch's signal has received one increment per
+// rank for this step.  Signals are kept in kSignalCopies copies 128 bytes apart (the last CTA's
+// warp writes all of them at once) so that the CTAs of the waiting launch poll different L2 lines.
 constexpr int kMaxPeers = 8;
+constexpr int kSignalCopies = SBQ_PEER_SIGNAL_COPIES;
+constexpr int kSignalStride = 32;  // u32 words between copies
+static_assert(kSignalCopies == 32, "one warp writes the signal copies");
 
 struct PeerSync {
     void* y[kMaxJobs][kMaxPeers];  // job j's output slice as mapped on rank p (same ldy as the job)
-    unsigned* signal[kMaxPeers];   // this launch's arrival counter on rank p
-    const unsigned* wait_count;    // local arrival counter of the launch whose outputs x comes from, or null
+    unsigned* signal[kMaxPeers];   // this launch's signal copies on rank p
+    unsigned* done;                // local: CTAs of this launch that have published their stores
+    const unsigned* wait_count;    // local signal copies of the launch whose outputs x comes from, or null
     unsigned* wait_state;          // [generation, arrivals] of this launch's wait (local)
-    unsigned wait_expected;        // increments wait_count receives per step (16-row tiles, all ranks)
+    unsigned wait_expected;        // increments a signal copy receives per step (one per rank)
     int nranks;
 };
 
@@ -89,20 +95,22 @@ __device__ __forceinline__ void red_add_sys(unsigned* p, unsigned v) {
     asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// One thread per CTA: waits until `count` has received this step's `expected` increments (targets
-// grow by `expected` per step; state[0] counts completed steps of this waiter), then records the
-// CTA's arrival; the last CTA of the grid advances the generation for the next step.  Bounded (ranks
-// may drift apart on the host by up to kPeerWaitLimitNs): on expiry the error word is set and the
-// kernel carries on (its outputs are then invalid, the host sees SBQ_ERR_TIMEOUT); after an earlier
-// failure it does not wait at all.
+// One thread per CTA: waits until its copy of the signal has received this step's `expected`
+// increments (targets grow by `expected` per step; state[0] counts completed steps of this
+// waiter), then records the CTA's arrival; the last CTA of the grid advances the generation for
+// the next step.  Bounded (ranks may drift apart on the host by up to kPeerWaitLimitNs): on expiry
+// the error word is set and the kernel carries on (its outputs are then invalid, the host sees
+// SBQ_ERR_TIMEOUT); after an earlier failure it does not wait at all.
 constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;
 
-__device__ __forceinline__ void peer_wait(const unsigned* count, unsigned* state, unsigned expected) {
+__device__ __forceinline__ void peer_wait(const unsigned* signal, unsigned* state, unsigned expected) {
+    const unsigned* count = signal + (blockIdx.x % kSignalCopies) * kSignalStride;
     const unsigned gen = *reinterpret_cast<volatile unsigned*>(state);
     const unsigned target = (gen + 1u) * expected;
     if (*reinterpret_cast<volatile int*>(&g_device_error) == 0 && (int)(ld_acquire_sys(count) - target) < 0) {
         const uint64_t t0 = tc::now_ns();
         for (uint32_t i = 1; (int)(ld_acquire_sys(count) - target) < 0; ++i) {
+            __nanosleep(64);
             if ((i & 63) == 0 && tc::now_ns() - t0 > kPeerWaitLimitNs) {
                 tc::raise_error(SBQ_ERR_TIMEOUT);
                 break;
@@ -113,6 +121,27 @@ __device__ __forceinline__ void peer_wait(const unsigned* count, unsigned* state
         state[1] = 0;
         __threadfence();
         atomicAdd(state, 1u);
+    }
+}
+
+// Warp 0 of every CTA, after the consumers' barrier that follows their last output stores.
+// Ordering: the barrier orders every consumer's (local and peer) output stores before lane 0's
+// GPU-scope release (fence + count-out); the last CTA's count-out reads the whole release sequence,
+// and its system-scope fence is cumulative, so all CTAs' stores are ordered before the signal the
+// other ranks acquire.  One system-scope fence per launch: a per-CTA system fence measured about
+// 8 us per launch on B200.
+__device__ __forceinline__ void peer_publish(const PeerSync& ps, int lane) {
+    unsigned last = 0;
+    if (lane == 0) {
+        __threadfence();
+        last = atomicAdd(ps.done, 1u) == gridDim.x - 1;
+        if (last) *ps.done = 0;  // next used by this launch position of the next step
+    }
+    __syncwarp();
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+        __threadfence_system();
+        for (int p = 0; p < ps.nranks; ++p) red_add_sys(ps.signal[p] + lane * kSignalStride, 1u);
     }
 }
 
@@ -413,12 +442,9 @@ __device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, ui
         consume_run<XK, MT, NMAT, PEER>(jb, t0, t1, xsrc, xld, ring, red, full, empty, ci, &ps, jidx, PEER && !staged);
     if (!consumers_sync_and(ok) && threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
     if (PEER) {
-        // publish: every consumer's peer stores are ordered before the barrier, the barrier before
-        // the increments (sent even after a timeout, so that the other ranks do not wait in vain)
-        __threadfence_system();
+        // publish (also after a timeout, so that the other ranks do not wait in vain)
         consumers_sync();
-        if (threadIdx.x == 0)
-            for (int p = 0; p < ps.nranks; ++p) red_add_sys(ps.signal[p], (unsigned)(t1 - t0));
+        if (warp == 0) peer_publish(ps, lane);
     }
 }
 
@@ -775,16 +801,19 @@ extern "C" int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x
         return set_error(SBQ_ERR_INVALID_ARGUMENT, "nranks must be 1..%d (got %d)", kMaxPeers, pg.nranks);
     if (pg.wait_count && (!pg.wait_state || pg.wait_expected == 0))
         return set_error(SBQ_ERR_INVALID_ARGUMENT, "a wait needs wait_state and a positive wait_expected");
-    if (reinterpret_cast<uintptr_t>(pg.wait_count) % 4 || reinterpret_cast<uintptr_t>(pg.wait_state) % 8)
-        return set_error(SBQ_ERR_ALIGNMENT, "wait counter must be 4-byte and wait state 8-byte aligned");
+    if (reinterpret_cast<uintptr_t>(pg.wait_count) % 128 || reinterpret_cast<uintptr_t>(pg.wait_state) % 8)
+        return set_error(SBQ_ERR_ALIGNMENT, "wait signal must be 128-byte and wait state 8-byte aligned");
+    if (!pg.done || reinterpret_cast<uintptr_t>(pg.done) % 4)
+        return set_error(SBQ_ERR_INVALID_ARGUMENT, "done must be a 4-byte aligned device pointer");
     PeerSync ps{};
     ps.nranks = pg.nranks;
+    ps.done = pg.done;
     ps.wait_count = pg.wait_count;
     ps.wait_state = pg.wait_state;
     ps.wait_expected = pg.wait_expected;
     for (int p = 0; p < pg.nranks; ++p) {
-        if (!pg.signal[p] || reinterpret_cast<uintptr_t>(pg.signal[p]) % 4)
-            return set_error(SBQ_ERR_INVALID_ARGUMENT, "signal[%d] must be a 4-byte aligned device pointer", p);
+        if (!pg.signal[p] || reinterpret_cast<uintptr_t>(pg.signal[p]) % 128)
+            return set_error(SBQ_ERR_INVALID_ARGUMENT, "signal[%d] must be a 128-byte aligned device pointer", p);
         ps.signal[p] = pg.signal[p];
     }
     GemvGroup grp{};
@@ -816,8 +845,8 @@ extern "C" int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x
 
 extern "C" int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned expected, void* stream) {
     if (!count || !state || expected == 0) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null counter/state or zero expected");
-    if (reinterpret_cast<uintptr_t>(count) % 4 || reinterpret_cast<uintptr_t>(state) % 8)
-        return set_error(SBQ_ERR_ALIGNMENT, "counter must be 4-byte and state 8-byte aligned");
+    if (reinterpret_cast<uintptr_t>(count) % 128 || reinterpret_cast<uintptr_t>(state) % 8)
+        return set_error(SBQ_ERR_ALIGNMENT, "signal must be 128-byte and state 8-byte aligned");
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(32);

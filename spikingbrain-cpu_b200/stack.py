@@ -109,7 +109,8 @@ class PeerExchange:
     and maps every other rank's arena, so that a GEMV can store its output slice into all ranks'
     full-width buffers and signal their counters (``sbq_gemv_w8_group_peer``).  Per layer: the full
     ``qkvd`` [m_max, 4 hidden], ``h`` [m_max, inter], ``od`` [m_max, 2 hidden] and ``x'`` [m_max, hidden]
-    buffers (fp16), one arrival counter per launch and one wait state per waiting launch.
+    buffers (fp16), one signal (32 counter copies) and one count-out word per launch and one wait
+    state per waiting launch.
     The ranks must be distinct GPUs of one node with peer access.
     """
 
@@ -141,7 +142,9 @@ class PeerExchange:
         self.buf = []  # per layer: offsets of qkvd, h, od, x'
         for _ in stack.layers:
             self.buf.append([take(m_max * n * 2) for n in (4 * hd, it, 2 * hd, hd)])
-        self.cnt = [[take(128), take(128)] for _ in stack.layers]   # arrival counter of launch 1 / 2
+        sig = L.PEER_SIGNAL_BYTES
+        self.cnt = [[take(sig), take(sig)] for _ in stack.layers]    # signal of launch 1 / 2
+        self.done = [[take(128), take(128)] for _ in stack.layers]   # CTA count-out of launch 1 / 2
         self.state = [[take(128), take(128)] for _ in stack.layers]  # wait state of launch 1 / 2
         self.final_state = take(128)
         self.nbytes = off
@@ -172,7 +175,7 @@ class PeerExchange:
         o = self.buf[layer][which]
         return self.arena[o:o + self.m_max * n * 2].view(torch.float16).view(self.m_max, n)[:m]
 
-    def _group(self, dests, signal_off: int, wait_off, state_off: int, expected: int):
+    def _group(self, dests, signal_off: int, done_off: int, wait_off, state_off: int):
         L = self.L
         pg = L.PeerGroup()
         pg.nranks = self.stack.world
@@ -181,9 +184,10 @@ class PeerExchange:
                 pg.y[j][p] = b + off + col * 2
         for p, b in enumerate(self.peers):
             pg.signal[p] = b + signal_off
+        pg.done = self.base + done_off
         pg.wait_count = None if wait_off is None else self.base + wait_off
         pg.wait_state = self.base + state_off
-        pg.wait_expected = expected
+        pg.wait_expected = self.stack.world  # one increment per rank and step
         return pg
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -197,27 +201,25 @@ class PeerExchange:
             raise ValueError("the peer exchange was laid out for %d rows (got %d)" % (self.m_max, m))
         hd, it, w, r = st.hidden, st.inter, st.world, st.rank
         code, stream = _DTYPE_CODE[x.dtype], _stream(x.device)
-        e1 = w * (-(-it // (16 * w)) + -(-4 * hd // (16 * w)))   # 16-row tiles of launch 1, all ranks
-        e2 = w * 3 * -(-hd // (16 * w))
         cur = x
         for i, layer in enumerate(st.layers):
             q_off, h_off, od_off, x_off = self.buf[i]
             qkvd, h, od, xn = (self.view(i, k, m) for k in range(4))
             hs, qs = it // w, 4 * hd // w
             jobs = [layer.mlp.gateup_job(cur, h[:, r * hs:(r + 1) * hs]), layer.qkvd.gemv_job(cur, qkvd[:, r * qs:(r + 1) * qs])]
-            pg = self._group([(h_off, r * hs), (q_off, r * qs)], self.cnt[i][0],
-                             None if i == 0 else self.cnt[i - 1][1], self.state[i][0], e2)
+            pg = self._group([(h_off, r * hs), (q_off, r * qs)], self.cnt[i][0], self.done[i][0],
+                             None if i == 0 else self.cnt[i - 1][1], self.state[i][0])
             L.call("sbq_gemv_w8_group_peer", (L.GemvJob * 2)(*jobs), 2, code, m, ctypes.byref(pg), stream)
             s = hd // w
             jobs = [layer.mlp.down_proj.gemv_job(h, xn[:, r * s:(r + 1) * s]),
                     layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], od[:, r * s:(r + 1) * s]),
                     layer.dout.gemv_job(qkvd[:, 3 * hd:], od[:, hd + r * s:hd + (r + 1) * s])]
             pg = self._group([(x_off, r * s), (od_off, r * s), (od_off, hd + r * s)], self.cnt[i][1],
-                             self.cnt[i][0], self.state[i][1], e1)
+                             self.done[i][1], self.cnt[i][0], self.state[i][1])
             L.call("sbq_gemv_w8_group_peer", (L.GemvJob * 3)(*jobs), 3, code, m, ctypes.byref(pg), stream)
             cur = xn
         L.call("sbq_peer_wait", ctypes.c_void_p(self.base + self.cnt[-1][1]),
-               ctypes.c_void_p(self.base + self.final_state), e2, stream)
+               ctypes.c_void_p(self.base + self.final_state), w, stream)
         return cur
 
     def close(self) -> None:

@@ -4,7 +4,7 @@ Every rank builds the unsharded stack on its own GPU as the reference (the seede
 same on every rank), then the output-channel sharded stack with each exchange ("peer": GEMV outputs
 stored to every rank over NVLink; "nccl": all-gather), and checks that every sharded result is
 bit-identical to the unsharded one: eager decode (m = 1, 3, 16), the captured decode step replayed
-on several inputs, and an m = 80 prefill (NCCL gathers).  Exits non-zero on the first mismatch.
+back to back on 24 inputs and called with device and host inputs, and an m = 80 prefill (NCCL gathers).  Exits non-zero on the first mismatch.
 """
 
 from __future__ import annotations
@@ -44,6 +44,14 @@ def main() -> int:
         x = sbq.workloads.activation(80, shape["hidden"], seed=3, device=dev)
         check("%s prefill m=80" % exchange, st(x).clone(), ref(x))
         run = sbq.stack.CapturedStack(st, m=1)
+        # back-to-back replays with a new input each: a stale slice from an earlier step would show
+        xs = [sbq.workloads.activation(1, shape["hidden"], seed=100 + i, device=dev) for i in range(24)]
+        outs = []
+        for x in xs:
+            run.x.copy_(x)
+            outs.append(run.run().clone())
+        for i, (x, y) in enumerate(zip(xs, outs)):
+            check("%s back-to-back replay %d" % (exchange, i), y, ref(x))
         for i in range(4):
             x = sbq.workloads.activation(1, shape["hidden"], seed=40 + i, device=dev)
             check("%s graph replay %d" % (exchange, i), run(x).clone(), ref(x))
