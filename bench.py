@@ -352,6 +352,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline measurement")
     ap.add_argument("--no-extra", action="store_true", help="skip the per-configuration kernel timings")
     ap.add_argument("--kernel", choices=("gemv", "mlp", "gemm", "dyn"), help="time one configuration's kernel alone")
+    ap.add_argument("--program", action="store_true",
+                    help="run the decode step as one persistent decode-program launch instead of grouped launches")
     ap.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
                     help="how sharded ranks assemble activations (N > 1): peer stores over NVLink or NCCL all-gather")
     args = ap.parse_args()
@@ -380,7 +382,7 @@ def main() -> None:
     stream = torch.cuda.Stream(dev)
 
     # ---- device-resident timing: one graph replay per step
-    runner = sbq.stack.CapturedStack(stack, m=1, stream=stream)
+    runner = sbq.stack.CapturedStack(stack, m=1, stream=stream, use_program=args.program)
     x_static = runner.x
     x_static.copy_(sbq.workloads.activation(1, hidden, seed=5, device=dev))
     torch.cuda.synchronize()

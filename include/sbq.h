@@ -148,16 +148,18 @@ SBQ_API int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtype, 
 /* A decode program: groups of jobs run as stages of ONE persistent launch, stage s + 1 starting after
  * every output of stage s is written (a grid-wide barrier inside the kernel instead of a kernel
  * boundary); the weight stream continues across the barriers.  jobs[i] belongs to stage job_stage[i]
- * (non-decreasing); later stages may read earlier stages' outputs.  Requirements: 1 <= m <= 8 and
- * m * (k + 8) activation elements of every job fit in 25.5 KiB (m = 1 for k up to 12288 at fp16).
+ * (non-decreasing); later stages may read earlier stages' outputs.  Requirement: 1 <= m <= 8.
  * sbq_gemv_program_build lays the program out in `program` (sbq_gemv_program_bytes(nstages) bytes,
  * device memory, 256-byte aligned) and synchronises (a set-up call; the job pointers are baked in).
- * sbq_gemv_program_run clears `counters` (nstages ints of device memory) and launches; it is
- * capturable in a CUDA graph.  The buffers named by the jobs must stay allocated. */
+ * sbq_gemv_program_run launches it; `sync` is sbq_gemv_program_sync_bytes(nstages) bytes of device
+ * memory, 128-byte aligned, zero before the first run and left to the program afterwards (its
+ * counters only grow, so no run clears anything).  The run is capturable in a CUDA graph.  The
+ * buffers named by the jobs must stay allocated. */
 SBQ_API size_t sbq_gemv_program_bytes(int nstages);
+SBQ_API size_t sbq_gemv_program_sync_bytes(int nstages);
 SBQ_API int sbq_gemv_program_build(const sbq_gemv_job* jobs, const int* job_stage, int njobs, int x_dtype, int64_t m,
                                    void* program, size_t program_bytes);
-SBQ_API int sbq_gemv_program_run(const void* program, int nstages, int x_dtype, int* counters, void* stream);
+SBQ_API int sbq_gemv_program_run(const void* program, int nstages, int x_dtype, void* sync, void* stream);
 
 /* ---- output-channel shards across the GPUs of one node (peer memory over NVLink) -------------
  *
@@ -204,6 +206,16 @@ SBQ_API int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x_dt
 /* The same wait as a one-CTA launch: the end of a sharded step, before anything else reads the
  * last launch's gathered output. */
 SBQ_API int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned expected, void* stream);
+
+/* A sharded decode program (see sbq_gemv_program_build): the stages' barriers span every rank, and
+ * job i's output slice is stored to ydest[i * nranks + p] on every rank p (as mapped here; jobs[i].y
+ * must be this rank's own entry).  peer_sync[p]: rank p's sync region (the `sync` it passes to
+ * sbq_gemv_program_run, inside its peer arena), as mapped here.  Every rank builds the same stage
+ * structure and runs its program once per step; the launch ends when every rank's last-stage
+ * outputs have arrived.  Waits are bounded (10 s). */
+SBQ_API int sbq_gemv_program_build_peer(const sbq_gemv_job* jobs, const int* job_stage, int njobs, int x_dtype,
+                                        int64_t m, void* const* ydest, int nranks, void* const* peer_sync,
+                                        void* program, size_t program_bytes);
 
 /* ---- int8-dyn: dynamic activation quantisation + int8 x int8 -> int32 GEMM ------------- */
 

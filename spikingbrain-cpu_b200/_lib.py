@@ -59,6 +59,7 @@ SIGNATURES = {
                                    _c_i64, _vp]),
     "sbq_gemv_w8_group": (_c_int, [ctypes.POINTER(GemvJob), _c_int, _c_int, _c_i64, _vp]),
     "sbq_gemv_program_bytes": (_sz, [_c_int]),
+    "sbq_gemv_program_sync_bytes": (_sz, [_c_int]),
     "sbq_gemv_program_build": (_c_int, [ctypes.POINTER(GemvJob), ctypes.POINTER(ctypes.c_int), _c_int, _c_int, _c_i64,
                                         _vp, _sz]),
     "sbq_gemv_program_run": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
@@ -70,6 +71,8 @@ SIGNATURES = {
     "sbq_gemv_w8_group_peer": (_c_int, [ctypes.POINTER(GemvJob), _c_int, _c_int, _c_i64, ctypes.POINTER(PeerGroup),
                                         _vp]),
     "sbq_peer_wait": (_c_int, [_vp, _vp, ctypes.c_uint, _vp]),
+    "sbq_gemv_program_build_peer": (_c_int, [ctypes.POINTER(GemvJob), ctypes.POINTER(ctypes.c_int), _c_int, _c_int,
+                                             _c_i64, ctypes.POINTER(_vp), _c_int, ctypes.POINTER(_vp), _vp, _sz]),
     "sbq_dyn_workspace_bytes": (_sz, [_c_i64, _c_i64, _c_int]),
     "sbq_quant_act_per_tensor": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "sbq_quant_act_per_token": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp]),

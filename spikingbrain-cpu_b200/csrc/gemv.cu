@@ -5,12 +5,12 @@
 // each 128-row block of the weight to fp32 and runs an fp32 sgemm, then multiplies by the
 // per-row scale.  Here the weight is streamed from HBM exactly once per launch:
 //
-//   * each CTA owns a run of consecutive 16-row tiles of one weight (sized so a launch has about
-//     three CTAs per SM, each moving a similar number of bytes); a producer warp streams that
-//     contiguous byte range with cp.async.bulk copies into a 40 KiB shared-memory ring (8 KiB
+//   * each CTA owns a run of consecutive 16-row tiles of one weight; a launch fills every CTA slot
+//     of the GPU once (three per SM) with runs of near-equal bytes; a producer warp streams its
+//     contiguous byte range with cp.async.bulk copies into a 48 KiB shared-memory ring (8 KiB
 //     chunks, mbarrier transaction counts), across tile boundaries without pausing;
-//   * the consumers copy x into shared memory once (when m * k fits in 26 KiB), so the chunk
-//     loop reads its activation fragments from shared memory instead of waiting on L2;
+//   * the consumers read their activation fragments in place (L1-cached) before waiting for each
+//     chunk, so the load overlaps the wait;
 //   * eight consumer warps (or four on gate and four on up) take one 1 KiB tile of each chunk:
 //     two conflict-free 16-byte shared loads per lane, int8 -> fp16 (or bf16) in registers (exact), m16n8k16 tensor-core MMAs with
 //     fp32 accumulation and the activation rows as the n dimension (8 or 16 tokens per pass);
@@ -25,7 +25,10 @@
 //
 // fp32 activations are split into a bf16 high and low part (two MMAs, ~16 mantissa bits kept);
 // the dot product of int8 weights and fp16/bf16 activations is exact up to fp32 accumulation.
+#include <atomic>
 #include <cmath>
+#include <mutex>
+#include <unordered_set>
 #include <vector>
 
 #include "tc.cuh"
@@ -52,7 +55,7 @@ struct GemvJob {
     int chunk_tiles;   // tiles per chunk and matrix: the largest of 8 (4 for gate/up), 4, 2, 1 dividing kt_total
     int out_f16;       // 1: fp16 output, 0: fp32
     int n_tiles;       // 16-row tiles of the weight
-    int tiles_per_cta; // consecutive tiles one CTA streams
+    int cta_count;     // CTAs of this job; CTA c streams tiles [c n_tiles / cta_count, (c + 1) n_tiles / cta_count)
     int cta_begin;     // first block index of this job in the grid
 };
 
@@ -61,6 +64,9 @@ constexpr int kMaxJobs = 8;
 struct GemvGroup {
     GemvJob job[kMaxJobs];
     int njobs;
+    int total_units;                 // 16-row tiles of all jobs
+    int unit_begin[kMaxJobs + 1];    // first unit of each job
+    unsigned* claim;                 // this launch's work counter pair (g_claim slot)
 };
 
 // Output-channel shards on several GPUs of one node (sbq_gemv_w8_group_peer).  Every rank computes
@@ -239,13 +245,15 @@ __device__ __forceinline__ void store_out<__half>(void* y, int64_t idx, float v)
 
 constexpr int kGemvThreads = (kGemvWarps + 1) * 32;  // 8 consumer warps + 1 producer warp
 constexpr int kChunkTiles = 8;                         // tiles (KiB) per chunk and matrix, at most
-constexpr int kRingBytes = 40 * 1024;                  // 5 stages of 8 KiB (8 tiles, or 4 gate + 4 up tiles)
-constexpr int kMaxStages = 5;
-constexpr int kXBytes = 25 * 1024 + 512;               // x staged in shared memory when it fits (m * (k + 8) * es)
+#ifndef SBQ_GEMV_STAGES
+#define SBQ_GEMV_STAGES 6
+#endif
+constexpr int kMaxStages = SBQ_GEMV_STAGES;            // ring stages of 8 KiB (8 tiles, or 4 gate + 4 up tiles)
+constexpr int kRingBytes = kMaxStages * 8 * 1024;
 template <int MT>
 struct GemvSmemSize {
-    static constexpr int kRed = kGemvWarps * MT * 16 * 9 * 4;  // per-warp partial sums of one tile
-    static constexpr int kBytes = kRingBytes + kXBytes + kRed + 2 * kMaxStages * 8;  // 3 CTAs per SM at MT = 1
+    static constexpr int kRed = 2 * kGemvWarps * MT * 16 * 9 * 4;  // per-warp partial sums of two tiles
+    static constexpr int kBytes = kRingBytes + kRed + 2 * kMaxStages * 8;  // 3 CTAs per SM at MT = 1
 };
 constexpr int kCtasPerSm = 3;  // CTAs a launch is sized for (three fit per SM)
 
@@ -296,29 +304,6 @@ __device__ __forceinline__ bool produce_run(const GemvJob& jb, int t0, int t1, u
     return true;
 }
 
-// Consumers: copy x into shared memory when it fits (m * (k + 8) elements), else read it in place.
-// `coherent` loads bypass L1 (x written earlier in the same kernel by other SMs).
-template <int XK>
-__device__ __forceinline__ void stage_x(const GemvJob& jb, uint8_t* xs, bool coherent, const void*& xsrc,
-                                        int64_t& xld) {
-    constexpr int es = XK == kXF32 ? 4 : 2;
-    const int xrow = jb.k * es + 16;  // bytes per staged row (+16 against bank conflicts)
-    xsrc = jb.x;
-    xld = jb.ldx;
-    if (jb.m * xrow <= kXBytes) {
-        const int vpr = jb.k * es / 16;
-        for (int v = threadIdx.x; v < jb.m * vpr; v += kGemvWarps * 32) {
-            const int r = v / vpr, cc = v - r * vpr;
-            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(jb.x) +
-                                                              (int64_t)r * jb.ldx * es + cc * 16);
-            *reinterpret_cast<uint4*>(xs + r * xrow + cc * 16) = coherent ? __ldcg(src) : *src;
-        }
-        consumers_sync();
-        xsrc = xs;
-        xld = xrow / es;
-    }
-}
-
 // Consumers (8 warps): the run's chunks, a fixed-order reduction and the epilogue per tile.
 // Returns false (warp-uniformly) if a wait timed out.
 // PEER: every output is stored to each rank's copy (ps->y[jidx][p]) instead of jb.y.
@@ -338,13 +323,26 @@ __device__ __forceinline__ bool consume_run(const GemvJob& jb, int t0, int t1, c
     const int mat = warp / WPM, slot = warp % WPM;  // this warp's matrix and tile within a chunk
     const bool mine = slot < C;
     const int mat_off = mat * C * kTileBytes;
+    constexpr int kEntries = MT * 8 * 16;  // (row, token) outputs of one tile, one per epilogue thread
+    constexpr int kRedFloats = kGemvWarps * MT * 16 * 9;
     float acc[MT][4];
+    float sc0 = 0.0f, sc1 = 0.0f, bz = 0.0f;  // the epilogue thread's scale(s) and bias, loaded early
+    int vt = 0;
     for (int i = 0, j = 0; i < nchunks; ++i, ++ci) {
         if (j == 0) {
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
+            // this tile's epilogue runs on warp (tile % 8) onwards: its threads fetch the scales now
+            const int tile_seq = i / cpt;
+            vt = (threadIdx.x + kGemvWarps * 32 - (tile_seq % kGemvWarps) * 32) % (kGemvWarps * 32);
+            const int n = (t0 + tile_seq) * 16 + (vt & 15);
+            if (vt < kEntries && n < jb.n) {
+                sc0 = jb.s0[n];
+                if (NMAT == 2) sc1 = jb.s1[n];
+                if (NMAT == 1 && jb.bias) bz = jb.bias[n];
+            }
         }
         const int s = ci % S;
         XFrag<XK> xf[MT];
@@ -366,9 +364,14 @@ __device__ __forceinline__ bool consume_run(const GemvJob& jb, int t0, int t1, c
         if (++j < cpt) continue;
         j = 0;
 
-        // ---- tile complete: reduce the warps' partial sums (fixed order), scale, store
-        const int nt = t0 + i / cpt;
-#define SBQ_RED(w, mt, r, col) red[(((w) * MT + (mt)) * 16 + (r)) * 9 + (col)]
+        // ---- tile complete: the warps' partial sums go to a double-buffered reduction area, one
+        // barrier, then the tile's epilogue threads reduce (fixed order), scale and store while the
+        // other warps go on with the next tile.  A buffer is written again two tiles later, after
+        // the next tile's barrier, which its epilogue threads reach only when done reading.
+        const int tile_seq = i / cpt;
+        const int nt = t0 + tile_seq;
+        float* rb = red + (tile_seq & 1) * kRedFloats;
+#define SBQ_RED(w, mt, r, col) rb[(((w) * MT + (mt)) * 16 + (r)) * 9 + (col)]
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
             SBQ_RED(warp, mt, g, 2 * c) = acc[mt][0];
@@ -377,89 +380,236 @@ __device__ __forceinline__ bool consume_run(const GemvJob& jb, int t0, int t1, c
             SBQ_RED(warp, mt, g + 8, 2 * c + 1) = acc[mt][3];
         }
         consumers_sync();
-        for (int t = threadIdx.x; t < MT * 8 * 16; t += kGemvWarps * 32) {
-            const int r = t & 15, tok = t >> 4, mt = tok >> 3, col = tok & 7;
+        if (vt < kEntries) {
+            const int r = vt & 15, tok = vt >> 4, mt = tok >> 3, col = tok & 7;
             const int n = nt * 16 + r;
-            if (n >= jb.n || tok >= jb.m) continue;
-            float v[NMAT];
+            if (n < jb.n && tok < jb.m) {
+                float v[NMAT];
 #pragma unroll
-            for (int a = 0; a < NMAT; ++a) {
-                float sum = 0.0f;
+                for (int a = 0; a < NMAT; ++a) {
+                    float sum = 0.0f;
 #pragma unroll
-                for (int w = 0; w < WPM; ++w) sum += SBQ_RED(a * WPM + w, mt, r, col);
-                v[a] = sum;
-            }
-            float out;
-            if (NMAT == 1) {
-                out = v[0] * jb.s0[n];
-                if (jb.bias) out += jb.bias[n];
-            } else {
-                const float gv = v[0] * jb.s0[n];
-                const float uv = v[1] * jb.s1[n];
-                out = gv / (1.0f + expf(-gv)) * uv;
-            }
-            const int64_t idx = (int64_t)tok * jb.ldy + n;
-            if (PEER) {
-                // consecutive threads store consecutive rows: one coalesced NVLink write per rank
-                for (int p = 0; p < ps->nranks; ++p) {
-                    if (jb.out_f16)
-                        static_cast<__half*>(ps->y[jidx][p])[idx] = __float2half_rn(out);
-                    else
-                        static_cast<float*>(ps->y[jidx][p])[idx] = out;
+                    for (int w = 0; w < WPM; ++w) sum += SBQ_RED(a * WPM + w, mt, r, col);
+                    v[a] = sum;
                 }
-            } else if (jb.out_f16) {
-                static_cast<__half*>(jb.y)[idx] = __float2half_rn(out);
-            } else {
-                static_cast<float*>(jb.y)[idx] = out;
+                float out;
+                if (NMAT == 1) {
+                    out = v[0] * sc0;
+                    if (jb.bias) out += bz;
+                } else {
+                    const float gv = v[0] * sc0;
+                    const float uv = v[1] * sc1;
+                    out = gv / (1.0f + expf(-gv)) * uv;
+                }
+                const int64_t idx = (int64_t)tok * jb.ldy + n;
+                if (PEER) {
+                    // consecutive threads store consecutive rows: one coalesced NVLink write per rank
+                    for (int p = 0; p < ps->nranks; ++p) {
+                        if (jb.out_f16)
+                            static_cast<__half*>(ps->y[jidx][p])[idx] = __float2half_rn(out);
+                        else
+                            static_cast<float*>(ps->y[jidx][p])[idx] = out;
+                    }
+                } else if (jb.out_f16) {
+                    static_cast<__half*>(jb.y)[idx] = __float2half_rn(out);
+                } else {
+                    static_cast<float*>(jb.y)[idx] = out;
+                }
             }
         }
 #undef SBQ_RED
-        consumers_sync();  // red is rewritten by the next tile
     }
+    consumers_sync();  // the last epilogue has read its buffer (a later run starts over at buffer 0)
     return true;
 }
 
-template <int XK, int MT, int NMAT, bool PEER>
-__device__ __forceinline__ void gemv_tiles(const GemvJob& jb, int t0, int t1, uint8_t* ring, uint8_t* xs, float* red,
-                                           uint64_t* full, uint64_t* empty, const PeerSync& ps, int jidx) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// ---------------------------------------------------------------------------------------------
+// Grouped launch with dynamic work: the units of a launch are the 16-row tiles of all its jobs
+// (largest tiles first), claimed one at a time from a per-launch counter by each CTA's producer.
+// A CTA that runs ahead (the warp schedulers favour some CTAs of an SM over others) simply takes
+// more units, so every CTA slot stays busy until the work runs out and the launch ends within about
+// one unit of its ideal time.  Each ring stage carries its unit's (job, tile, chunk, chunks) in
+// shared memory; x is read in place, so a CTA may take units of different jobs.
+// ---------------------------------------------------------------------------------------------
+constexpr int kClaimSlots = 1024;  // per-launch counters, used round-robin by consecutive launches
+static __device__ unsigned g_claim[kClaimSlots][2];  // [next unit, CTAs finished]; reset by the last CTA
+
+// Producer (one thread).  Claims the next unit while the last ring-full of the current one is
+// still to be issued, so the claim's latency is hidden.  False if a wait timed out.
+__device__ __forceinline__ bool produce_units(const GemvGroup& grp, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                              int4* meta) {
+    constexpr int S = kMaxStages;
+    constexpr int kStageBytes = kChunkTiles * kTileBytes;
     uint32_t ci = 0;
-    if (warp == kGemvWarps) {
-        if (lane == 0) produce_run<NMAT>(jb, t0, t1, ring, full, empty, ci);
-        return;
+    int u = (int)atomicAdd(grp.claim, 1u);
+    for (;;) {
+        if (u >= grp.total_units) {
+            const int s = ci % S;
+            if (!tc::mbar_wait(&empty[s], ((ci / S) & 1) ^ 1)) return false;
+            meta[s] = make_int4(-1, 0, 0, 0);
+            tc::mbar_arrive(&full[s]);  // the end marker: a phase with no bytes
+            return true;
+        }
+        int j = 0;
+        while (j + 1 < grp.njobs && u >= grp.unit_begin[j + 1]) ++j;
+        const GemvJob& jb = grp.job[j];
+        const int tile = u - grp.unit_begin[j];
+        const int C = jb.chunk_tiles, cpt = jb.kt_total / C, nmat = jb.w1 ? 2 : 1;
+        const uint32_t bytes = (uint32_t)C * kTileBytes;
+        const int8_t* src0 = jb.w0 + (int64_t)tile * jb.kt_total * kTileBytes;
+        const int8_t* src1 = jb.w1 ? jb.w1 + (int64_t)tile * jb.kt_total * kTileBytes : nullptr;
+        const int claim_at = cpt > S ? cpt - S : 0;
+        int next = 0;
+        for (int i = 0; i < cpt; ++i, ++ci) {
+            if (i == claim_at) next = (int)atomicAdd(grp.claim, 1u);
+            const int s = ci % S;
+            if (!tc::mbar_wait(&empty[s], ((ci / S) & 1) ^ 1)) return false;
+            meta[s] = make_int4(j, tile, i, cpt);
+            uint8_t* dst = ring + s * kStageBytes;
+            tc::mbar_arrive_expect_tx(&full[s], bytes * nmat);
+            tc::bulk_load(dst, src0 + (int64_t)i * bytes, bytes, &full[s]);
+            if (nmat == 2) tc::bulk_load(dst + bytes, src1 + (int64_t)i * bytes, bytes, &full[s]);
+        }
+        u = next;
     }
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
-    if (PEER && ps.wait_count) {
-        // x also holds the other ranks' slices, stored by their previous launch
-        if (threadIdx.x == 0) peer_wait(ps.wait_count, ps.wait_state, ps.wait_expected);
+}
+
+// Consumers (8 warps): per unit, its chunks, the fixed-order reduction and the epilogue (as
+// consume_run; the job and the warp split are read once per unit from the first chunk's stage).
+// `xcoh`: x was written by other GPUs during this step (L2-only loads).  False (warp-uniformly)
+// on a timeout.
+template <int XK, int MT, bool PEER>
+__device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* ring, float* red, uint64_t* full,
+                                              uint64_t* empty, const int4* meta, const PeerSync& ps, bool xcoh) {
+    constexpr int S = kMaxStages;
+    constexpr int kStageBytes = kChunkTiles * kTileBytes;
+    constexpr int kEntries = MT * 8 * 16;
+    constexpr int kRedFloats = kGemvWarps * MT * 16 * 9;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    uint32_t ci = 0;
+    for (int units = 0;; ++units) {
+        int s = ci % S;
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (ci / S) & 1))) return false;
+        const int4 md = meta[s];
+        if (md.x < 0) break;
+        const int j = md.x, tile = md.y, cpt = md.w;
+        const GemvJob& jb = grp.job[j];
+        const bool two = jb.w1 != nullptr;
+        const int C = jb.chunk_tiles;
+        const int mat = two ? warp >> 2 : 0, slot = two ? warp & 3 : warp;
+        const bool mine = slot < C;
+        const void* xj = jb.x;
+        const int64_t ldx = jb.ldx;
+        const int xm = jb.m, xk = jb.k;
+        const uint32_t toff = (uint32_t)((mat * C + slot) * kTileBytes + lane * 16);
+        float acc[MT][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
+        // this unit's epilogue runs on warp (unit % 8) onwards: its threads fetch the scales now
+        const int vt = (threadIdx.x + kGemvWarps * 32 - (units % kGemvWarps) * 32) % (kGemvWarps * 32);
+        float sc0 = 0.0f, sc1 = 0.0f, bz = 0.0f;
+        {
+            const int n = tile * 16 + (vt & 15);
+            if (vt < kEntries && n < jb.n) {
+                sc0 = jb.s0[n];
+                if (two) sc1 = jb.s1[n];
+                else if (jb.bias) bz = jb.bias[n];
+            }
+        }
+        XFrag<XK> xf[MT];
+        if (mine) {
+            const int64_t k0 = (int64_t)slot * kTileCols + 16 * c;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xj, ldx, 8 * mt + g, xm, k0, xk, xcoh);
+        }
+        for (int i = 0;;) {
+            if (mine) {
+                const uint8_t* t = ring + s * kStageBytes + toff;
+                const uint4 wa = *reinterpret_cast<const uint4*>(t);
+                const uint4 wb = *reinterpret_cast<const uint4*>(t + 512);
+                tile_mma<XK, MT>(acc, wa, wb, xf);
+            }
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&empty[s]);
+            ++ci;
+            if (++i == cpt) break;
+            // the next chunk of this unit: load its x, then wait for its weights
+            if (mine) {
+                const int64_t k0 = (int64_t)(i * C + slot) * kTileCols + 16 * c;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xj, ldx, 8 * mt + g, xm, k0, xk, xcoh);
+            }
+            s = ci % S;
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (ci / S) & 1))) return false;
+        }
+
+        // ---- unit complete: partial sums to a double-buffered area, one barrier, then the unit's
+        // epilogue threads reduce (fixed order), scale and store while the other warps go on
+        float* rb = red + (units & 1) * kRedFloats;
+#define SBQ_RED(w, mt, r, col) rb[(((w) * MT + (mt)) * 16 + (r)) * 9 + (col)]
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            SBQ_RED(warp, mt, g, 2 * c) = acc[mt][0];
+            SBQ_RED(warp, mt, g, 2 * c + 1) = acc[mt][1];
+            SBQ_RED(warp, mt, g + 8, 2 * c) = acc[mt][2];
+            SBQ_RED(warp, mt, g + 8, 2 * c + 1) = acc[mt][3];
+        }
         consumers_sync();
+        if (vt < kEntries) {
+            const int r = vt & 15, tok = vt >> 4, mt = tok >> 3, col = tok & 7;
+            const int n = tile * 16 + r;
+            if (n < jb.n && tok < xm) {
+                float out;
+                if (!two) {
+                    float v0 = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < 8; ++w) v0 += SBQ_RED(w, mt, r, col);
+                    out = v0 * sc0;
+                    if (jb.bias) out += bz;
+                } else {
+                    float v0 = 0.0f, v1 = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) v0 += SBQ_RED(w, mt, r, col);
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) v1 += SBQ_RED(4 + w, mt, r, col);
+                    const float gv = v0 * sc0;
+                    const float uv = v1 * sc1;
+                    out = gv / (1.0f + expf(-gv)) * uv;
+                }
+                const int64_t idx = (int64_t)tok * jb.ldy + n;
+                if (PEER) {
+                    // consecutive threads store consecutive rows: one coalesced NVLink write per rank
+                    for (int p = 0; p < ps.nranks; ++p) {
+                        if (jb.out_f16)
+                            static_cast<__half*>(ps.y[j][p])[idx] = __float2half_rn(out);
+                        else
+                            static_cast<float*>(ps.y[j][p])[idx] = out;
+                    }
+                } else if (jb.out_f16) {
+                    static_cast<__half*>(jb.y)[idx] = __float2half_rn(out);
+                } else {
+                    static_cast<float*>(jb.y)[idx] = out;
+                }
+            }
+        }
+#undef SBQ_RED
     }
-    const void* xsrc;
-    int64_t xld;
-    stage_x<XK>(jb, xs, PEER, xsrc, xld);
-    const bool staged = xsrc != jb.x;
-    const bool ok =
-        consume_run<XK, MT, NMAT, PEER>(jb, t0, t1, xsrc, xld, ring, red, full, empty, ci, &ps, jidx, PEER && !staged);
-    if (!consumers_sync_and(ok) && threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
-    if (PEER) {
-        // publish (also after a timeout, so that the other ranks do not wait in vain)
-        consumers_sync();
-        if (warp == 0) peer_publish(ps, lane);
-    }
+    consumers_sync();  // the last epilogue is done
+    return true;
 }
 
 template <int XK, int MT, bool PEER>
 __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2)
     gemv_w8_kernel(const __grid_constant__ GemvGroup grp, const __grid_constant__ PeerSync ps) {
     extern __shared__ __align__(128) uint8_t ring[];
-    uint8_t* xs = ring + kRingBytes;
-    float* red = reinterpret_cast<float*>(xs + kXBytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(xs + kXBytes + GemvSmemSize<MT>::kRed);
+    float* red = reinterpret_cast<float*>(ring + kRingBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRingBytes + GemvSmemSize<MT>::kRed);
     uint64_t* empty = full + kMaxStages;
-    int j = 0;
-    while (j + 1 < grp.njobs && (int)blockIdx.x >= grp.job[j + 1].cta_begin) ++j;
-    const GemvJob& jb = grp.job[j];
-    const int nmat = jb.w1 ? 2 : 1;
+    __shared__ int4 meta[kMaxStages];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < kMaxStages; ++i) {
             tc::mbar_init(&full[i], 1);
@@ -470,12 +620,33 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2)
     __syncthreads();
     // the next launch may start its own weight stream now (it waits for this grid before reading x)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int t0 = ((int)blockIdx.x - jb.cta_begin) * jb.tiles_per_cta;
-    const int t1 = min(t0 + jb.tiles_per_cta, jb.n_tiles);
-    if (nmat == 2)
-        gemv_tiles<XK, MT, 2, PEER>(jb, t0, t1, ring, xs, red, full, empty, ps, j);
-    else
-        gemv_tiles<XK, MT, 1, PEER>(jb, t0, t1, ring, xs, red, full, empty, ps, j);
+    if (warp == kGemvWarps) {
+        if (lane == 0 && !produce_units(grp, ring, full, empty, meta)) tc::raise_error(SBQ_ERR_TIMEOUT);
+        return;
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
+    if (PEER && ps.wait_count) {
+        // x also holds the other ranks' slices, stored by their previous launch
+        if (threadIdx.x == 0) peer_wait(ps.wait_count, ps.wait_state, ps.wait_expected);
+        consumers_sync();
+    }
+    const bool ok = consume_units<XK, MT, PEER>(grp, ring, red, full, empty, meta, ps, PEER);
+    if (!consumers_sync_and(ok) && threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
+    if (warp == 0) {
+        // count out; the last CTA resets the launch's counter for the next launch that uses it
+        // (every producer has made its last claim before its consumers saw the end marker)
+        unsigned last = 0;
+        if (lane == 0) {
+            __threadfence();
+            last = atomicAdd(grp.claim + 1, 1u) == gridDim.x - 1;
+            if (last) {
+                grp.claim[0] = 0;
+                grp.claim[1] = 0;
+            }
+        }
+        __syncwarp();
+        if (PEER) peer_publish(ps, lane);  // also after a timeout, so that the other ranks do not wait in vain
+    }
 }
 
 // Waits (one CTA) for a peer launch's outputs: the end of a sharded decode step, before the host
@@ -488,13 +659,16 @@ __global__ void peer_wait_kernel(const unsigned* count, unsigned* state, unsigne
 // ---------------------------------------------------------------------------------------------
 // Decode program: a whole sequence of grouped stages in one persistent cooperative launch.
 //
-// Stage s may read what stages < s wrote.  Every CTA owns at most one run per stage; when its
-// consumers finish that run (or have none) they publish with a fence and an atomic increment of
-// counters[s]; before stage s + 1 a CTA's consumers wait until counters[s] equals the grid size.
-// The producer never waits on a stage: it streams the next stages' weights (which depend on
-// nothing) as fast as the ring drains, so HBM stays busy across the barriers.  All CTAs are
-// co-resident (cooperative launch), every wait is bounded, and activations are read with L2-only
-// loads (they were written during this launch by other SMs).
+// Stage s may read what stages < s wrote (on this rank and, in a sharded program, on every rank).
+// Every CTA owns at most one run per stage.  When its consumers finish that run (or have none) the
+// CTA counts itself in on the stage's arrival counter (GPU-scope fence + 64-bit atomic; the
+// counters only grow, so a run's epoch E is the first return value / grid size and nothing is ever
+// cleared); the last CTA of the stage on each rank adds 1 to the stage's flag on every rank, in
+// 32 copies on separate L2 lines.  Before stage s + 1 a CTA's consumers poll their copy (with
+// backoff) until it reaches (E + 1) * ranks.  The producer never waits on a stage: it streams the
+// next stages' weights (which depend on nothing) as fast as the ring drains, so HBM stays busy
+// across the barriers.  All CTAs are co-resident (cooperative launch), every wait is bounded, and
+// activations are read with L2-only loads (they were written during this launch).
 // ---------------------------------------------------------------------------------------------
 struct ProgItem {
     int job;
@@ -504,30 +678,44 @@ struct ProgItem {
 
 struct ProgStage {
     GemvJob job[kMaxJobs];
+    PeerSync peer;  // sharded program: output destinations on every rank (y, nranks)
     int njobs;
     int pad;
 };
 
-struct ProgParams {
-    const ProgStage* stages;
-    const ProgItem* items;  // [stage][cta]
+// Synchronisation region per stage: one line for the arrival counter, 32 lines of flag copies.
+constexpr int kSyncStageBytes = 128 + kSignalCopies * 128;
+
+// Header at the start of a program buffer (256 bytes).
+struct ProgHeader {
     int nstages;
-    int* counters;          // [stage], zero at launch
+    int nctas;
+    int x_dtype;
+    int m;
+    int nranks;                        // 1: single GPU; > 1: sharded program
+    int pad[3];
+    uint8_t* peer_sync[kMaxPeers];     // every rank's synchronisation region as mapped here
+};
+static_assert(sizeof(ProgHeader) <= 256, "program header");
+
+struct ProgParams {
+    const ProgHeader* hdr;
+    const ProgStage* stages;
+    const ProgItem* items;             // [stage][cta]
+    int nstages;
+    uint8_t* sync;                     // this rank's synchronisation region
 };
 
-__device__ __forceinline__ int ld_acquire(const int* p) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+__device__ __forceinline__ unsigned* prog_flag(uint8_t* sync, int st, int copy) {
+    return reinterpret_cast<unsigned*>(sync + (size_t)st * kSyncStageBytes + 128 + copy * 128);
 }
 
-template <int XK>
-__global__ void __launch_bounds__(kGemvThreads, 3) gemv_program_kernel(const ProgParams p) {
+template <int XK, bool PEER>
+__global__ void __launch_bounds__(kGemvThreads, 3) gemv_program_kernel(const __grid_constant__ ProgParams p) {
     constexpr int MT = 1;
     extern __shared__ __align__(128) uint8_t ring[];
-    uint8_t* xs = ring + kRingBytes;
-    float* red = reinterpret_cast<float*>(xs + kXBytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(xs + kXBytes + GemvSmemSize<MT>::kRed);
+    float* red = reinterpret_cast<float*>(ring + kRingBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRingBytes + GemvSmemSize<MT>::kRed);
     uint64_t* empty = full + kMaxStages;
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -556,14 +744,22 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_program_kernel(const Pro
         return;
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the first stage's x comes from the previous kernel
-    for (int st = 0; st < p.nstages; ++st) {
-        if (st > 0) {
+    const int nranks = PEER ? p.hdr->nranks : 1;
+    constexpr bool peer = PEER;
+    const uint64_t limit = peer ? kPeerWaitLimitNs : tc::kWaitLimitNs;
+    unsigned long long epoch = 0;  // thread 0: this run's epoch, from its first arrival
+    for (int st = 0; st <= p.nstages; ++st) {
+        if (st > 0 && (st < p.nstages || (peer && cta == 0))) {
+            // wait for stage st - 1 on every rank (after the last stage: one CTA, so that the
+            // kernel ends only when every rank's final outputs have arrived)
             if (threadIdx.x == 0) {
-                const int* ctr = p.counters + (st - 1);
-                if (ld_acquire(ctr) < nctas) {
+                const unsigned* flag = prog_flag(p.sync, st - 1, cta % kSignalCopies);
+                const unsigned target = (unsigned)(epoch + 1) * (unsigned)nranks;
+                if ((int)(ld_acquire_sys(flag) - target) < 0) {
                     const uint64_t t0 = tc::now_ns();
-                    for (uint32_t i = 1; ld_acquire(ctr) < nctas; ++i) {
-                        if ((i & 63) == 0 && tc::now_ns() - t0 > tc::kWaitLimitNs) {
+                    for (uint32_t i = 1; (int)(ld_acquire_sys(flag) - target) < 0; ++i) {
+                        __nanosleep(32);
+                        if ((i & 63) == 0 && tc::now_ns() - t0 > limit) {
                             tc::raise_error(SBQ_ERR_TIMEOUT);
                             abort_flag = 1;
                             break;
@@ -574,26 +770,45 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_program_kernel(const Pro
             consumers_sync();
             if (abort_flag) return;
         }
+        if (st == p.nstages) break;
         const ProgItem it = p.items[(int64_t)st * nctas + cta];
         if (it.t1 > it.t0) {
-            const GemvJob jb = p.stages[st].job[it.job];
-            const void* xsrc;
-            int64_t xld;
-            stage_x<XK>(jb, xs, true, xsrc, xld);
-            const bool ok = jb.w1 ? consume_run<XK, MT, 2>(jb, it.t0, it.t1, xsrc, xld, ring, red, full, empty, ci)
-                                  : consume_run<XK, MT, 1>(jb, it.t0, it.t1, xsrc, xld, ring, red, full, empty, ci);
+            const ProgStage& ps = p.stages[st];
+            const GemvJob jb = ps.job[it.job];
+            // x was written during this launch (by other CTAs, or other GPUs): L2-only loads
+            const bool ok = jb.w1 ? consume_run<XK, MT, 2, PEER>(jb, it.t0, it.t1, jb.x, jb.ldx, ring, red, full,
+                                                                 empty, ci, &ps.peer, it.job, true)
+                                  : consume_run<XK, MT, 1, PEER>(jb, it.t0, it.t1, jb.x, jb.ldx, ring, red, full,
+                                                                 empty, ci, &ps.peer, it.job, true);
             if (!ok) {
                 if (lane == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
                 abort_flag = 1;
             }
         }
-        // publish this CTA's part of stage st: every consumer's stores precede the barrier, the fence
-        // of the publishing thread orders them before its increment
+        // count in: every consumer's stores precede the barrier, the fence of the counting thread
+        // orders them before its increment (and the last one's system fence before the flags)
         consumers_sync();
         if (abort_flag) return;
-        if (threadIdx.x == 0) {
-            __threadfence();
-            atomicAdd(p.counters + st, 1);
+        if (warp == 0) {
+            unsigned last = 0;
+            if (lane == 0) {
+                __threadfence();
+                unsigned long long* ctr = reinterpret_cast<unsigned long long*>(p.sync + (size_t)st * kSyncStageBytes);
+                const unsigned long long old = atomicAdd(ctr, 1ull);
+                if (st == 0) epoch = old / (unsigned long long)nctas;
+                last = old + 1 == (epoch + 1) * (unsigned long long)nctas;
+            }
+            __syncwarp();
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                if (peer) {
+                    __threadfence_system();
+                    for (int r = 0; r < nranks; ++r) red_add_sys(prog_flag(p.hdr->peer_sync[r], st, lane), 1u);
+                } else {
+                    __threadfence();
+                    atomicAdd(prog_flag(p.sync, st, lane), 1u);
+                }
+            }
         }
     }
 }
@@ -627,31 +842,117 @@ static int sm_count() {
     return count[dev];
 }
 
-// Splits every job into runs of consecutive tiles so that the launch has about kCtasPerSm CTAs per
-// SM, each streaming a similar number of weight bytes.  Returns the number of CTAs.
-static int plan_group(GemvGroup& grp) {
+// Splits every job into runs of consecutive tiles so that the launch fills every CTA slot of the GPU
+// once (`slots` = CTAs per SM x SMs): the slots are shared out in proportion to the jobs' weight
+// bytes and a job's tiles as evenly as possible over its CTAs.  A launch that leaves slots empty,
+// or spills into a second wave, streams measurably slower (the weight stream is bound by the bytes
+// in flight per SM).  Returns the number of CTAs.
+static int plan_jobs(GemvJob* job, int njobs, int slots) {
     double total = 0.0;
-    for (int i = 0; i < grp.njobs; ++i) {
-        GemvJob& j = grp.job[i];
+    int tiles = 0;
+    for (int i = 0; i < njobs; ++i) {
+        GemvJob& j = job[i];
         j.n_tiles = (int)ceil_div(j.n, 16);
-        total += (double)j.n_tiles * (j.w1 ? 2 : 1) * j.kt_total * kTileBytes;
+        tiles += j.n_tiles;
+        total += (double)j.n_tiles * (j.w1 ? 2 : 1) * j.kt_total;
     }
-    const double target = total / (double)(kCtasPerSm * sm_count());
+    int used = 0;
+    for (int i = 0; i < njobs; ++i) {
+        GemvJob& j = job[i];
+        int c = j.n_tiles;
+        if (tiles > slots) {
+            c = (int)((double)slots * ((double)j.n_tiles * (j.w1 ? 2 : 1) * j.kt_total) / total);
+            c = c < 1 ? 1 : (c > j.n_tiles ? j.n_tiles : c);
+        }
+        j.cta_count = c;
+        used += c;
+    }
+    // the one-CTA minimum may overshoot: take CTAs back from the jobs with the least bytes per CTA
+    while (used > slots) {
+        int best = -1;
+        double least = 0.0;
+        for (int i = 0; i < njobs; ++i) {
+            const GemvJob& j = job[i];
+            if (j.cta_count <= 1) continue;
+            const double per = (double)j.n_tiles * (j.w1 ? 2 : 1) * j.kt_total / j.cta_count;
+            if (best < 0 || per < least) least = per, best = i;
+        }
+        if (best < 0) break;  // more jobs than slots: one CTA each
+        --job[best].cta_count;
+        --used;
+    }
+    // rounding may leave slots over: give them to the jobs with the most bytes per CTA
+    while (tiles > slots && used < slots) {
+        int best = -1;
+        double most = 0.0;
+        for (int i = 0; i < njobs; ++i) {
+            const GemvJob& j = job[i];
+            if (j.cta_count >= j.n_tiles) continue;
+            const double per = (double)j.n_tiles * (j.w1 ? 2 : 1) * j.kt_total / j.cta_count;
+            if (per > most) most = per, best = i;
+        }
+        if (best < 0) break;
+        ++job[best].cta_count;
+        ++used;
+    }
     int ctas = 0;
-    for (int i = 0; i < grp.njobs; ++i) {
-        GemvJob& j = grp.job[i];
-        const double tile_bytes = (double)(j.w1 ? 2 : 1) * j.kt_total * kTileBytes;
-        int t = (int)(target / tile_bytes + 0.5);
-        j.tiles_per_cta = t < 1 ? 1 : (t > j.n_tiles ? j.n_tiles : t);
-        j.cta_begin = ctas;
-        ctas += (int)ceil_div(j.n_tiles, j.tiles_per_cta);
+    for (int i = 0; i < njobs; ++i) {
+        job[i].cta_begin = ctas;
+        ctas += job[i].cta_count;
     }
     return ctas;
 }
 
+// Device address of this device's claim counters (cached per device).
+static unsigned* claim_base() {
+    static unsigned* base[64] = {};
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!base[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_claim) != cudaSuccess) return nullptr;
+        base[dev] = static_cast<unsigned*>(p);
+    }
+    return base[dev];
+}
+
+static std::atomic<unsigned> g_claim_next{0};
+
+// Orders the jobs by unit size (largest first, so the last units claimed are the small ones),
+// permuting the peer destinations alike, numbers the units and picks this launch's counter.
+// Returns the grid size (every CTA slot, or one CTA per unit if there are fewer), 0 on failure.
+static int plan_units(GemvGroup& grp, PeerSync& ps, int slots) {
+    int perm[kMaxJobs];
+    for (int i = 0; i < grp.njobs; ++i) perm[i] = i;
+    auto unit_bytes = [&](int i) { return (int64_t)grp.job[i].kt_total * (grp.job[i].w1 ? 2 : 1); };
+    for (int i = 1; i < grp.njobs; ++i)  // stable insertion sort by decreasing unit bytes
+        for (int k = i; k > 0 && unit_bytes(perm[k]) > unit_bytes(perm[k - 1]); --k) std::swap(perm[k], perm[k - 1]);
+    GemvGroup sorted = grp;
+    PeerSync pss = ps;
+    int units = 0;
+    for (int i = 0; i < grp.njobs; ++i) {
+        sorted.job[i] = grp.job[perm[i]];
+        for (int p = 0; p < kMaxPeers; ++p) pss.y[i][p] = ps.y[perm[i]][p];
+        sorted.job[i].n_tiles = (int)ceil_div(sorted.job[i].n, 16);
+        sorted.unit_begin[i] = units;
+        units += sorted.job[i].n_tiles;
+    }
+    sorted.unit_begin[grp.njobs] = units;
+    sorted.total_units = units;
+    unsigned* base = claim_base();
+    if (!base) return 0;
+    sorted.claim = base + 2 * (g_claim_next.fetch_add(1) % kClaimSlots);
+    grp = sorted;
+    ps = pss;
+    return units < slots ? units : slots;
+}
+
 template <bool PEER>
-static void dispatch_group_t(GemvGroup& grp, const PeerSync& ps, int xk, int mt, cudaStream_t s) {
-    const int ctas = plan_group(grp);
+static int dispatch_group_t(GemvGroup& grp, PeerSync ps, int xk, int mt, cudaStream_t s) {
+    const int ctas = plan_units(grp, ps, (mt == 2 ? 2 : kCtasPerSm) * sm_count());
+    if (ctas <= 0) return set_error(SBQ_ERR_CUDA, "grouped GEMV: no work counter on this device");
     switch (xk) {
         case kXF16:
             mt == 2 ? launch_group<kXF16, 2, PEER>(grp, ps, ctas, s) : launch_group<kXF16, 1, PEER>(grp, ps, ctas, s);
@@ -663,11 +964,12 @@ static void dispatch_group_t(GemvGroup& grp, const PeerSync& ps, int xk, int mt,
             mt == 2 ? launch_group<kXF32, 2, PEER>(grp, ps, ctas, s) : launch_group<kXF32, 1, PEER>(grp, ps, ctas, s);
             break;
     }
+    return SBQ_OK;
 }
 
-static void dispatch_group(GemvGroup& grp, int xk, int mt, cudaStream_t s) {
+static int dispatch_group(GemvGroup& grp, int xk, int mt, cudaStream_t s) {
     const PeerSync none{};
-    dispatch_group_t<false>(grp, none, xk, mt, s);
+    return dispatch_group_t<false>(grp, none, xk, mt, s);
 }
 
 SBQ_DEFINE_ERROR_POLL(poll_error_gemv)
@@ -734,7 +1036,8 @@ static int run_single(GemvJob jb, int64_t m, int x_dtype, int y_dtype, cudaStrea
         q.x = static_cast<const char*>(jb.x) + m0 * jb.ldx * xs;
         q.y = static_cast<char*>(jb.y) + m0 * jb.ldy * ys;
         grp.job[0] = q;
-        dispatch_group(grp, x_kind(x_dtype), q.m > 8 ? 2 : 1, s);
+        const int st = dispatch_group(grp, x_kind(x_dtype), q.m > 8 ? 2 : 1, s);
+        if (st) return st;
     }
     return check_launch(what);
 }
@@ -786,7 +1089,8 @@ extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtyp
         grp.job[i].m = (int)m;
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    dispatch_group(grp, x_kind(x_dtype), m > 8 ? 2 : 1, s);
+    const int st = dispatch_group(grp, x_kind(x_dtype), m > 8 ? 2 : 1, s);
+    if (st) return st;
     return check_launch("gemv_w8_group");
 }
 
@@ -839,7 +1143,8 @@ extern "C" int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x
                  j.ldy);
         grp.job[i].m = (int)m;
     }
-    dispatch_group_t<true>(grp, ps, x_kind(x_dtype), m > 8 ? 2 : 1, static_cast<cudaStream_t>(stream));
+    const int st = dispatch_group_t<true>(grp, ps, x_kind(x_dtype), m > 8 ? 2 : 1, static_cast<cudaStream_t>(stream));
+    if (st) return st;
     return check_launch("gemv_w8_group_peer");
 }
 
@@ -863,6 +1168,10 @@ extern "C" int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned ex
 // ---- decode program: build (once, synchronous) and run (per step, capturable) ---------------------
 static int program_ctas() { return kCtasPerSm * sm_count(); }
 
+// Programs built by sbq_gemv_program_build_peer (the run picks the sharded kernel for them).
+static std::mutex g_peer_programs_mu;
+static std::unordered_set<const void*> g_peer_programs;
+
 static size_t program_bytes_for(int nstages, int nctas) {
     return 256 + (size_t)nstages * sizeof(ProgStage) + (size_t)nstages * nctas * sizeof(ProgItem);
 }
@@ -872,8 +1181,14 @@ extern "C" size_t sbq_gemv_program_bytes(int nstages) {
     return program_bytes_for(nstages, program_ctas());
 }
 
-extern "C" int sbq_gemv_program_build(const sbq_gemv_job* jobs, const int* job_stage, int njobs, int x_dtype, int64_t m,
-                                      void* program, size_t program_bytes) {
+extern "C" size_t sbq_gemv_program_sync_bytes(int nstages) {
+    if (nstages < 1) return 0;
+    return (size_t)nstages * kSyncStageBytes;
+}
+
+// Shared by the single-GPU and the sharded build.  ydest: null, or [njobs][nranks] destinations.
+static int program_build(const sbq_gemv_job* jobs, const int* job_stage, int njobs, int x_dtype, int64_t m,
+                         void* const* ydest, int nranks, void* const* peer_sync, void* program, size_t program_bytes) {
     if (!jobs || !job_stage || njobs < 1 || !program) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null argument");
     if (x_kind(x_dtype) < 0) return set_error(SBQ_ERR_UNSUPPORTED, "activation dtype %d", x_dtype);
     if (reinterpret_cast<uintptr_t>(program) % 256) return set_error(SBQ_ERR_ALIGNMENT, "program must be 256-byte aligned");
@@ -886,73 +1201,105 @@ extern "C" int sbq_gemv_program_build(const sbq_gemv_job* jobs, const int* job_s
     const int nctas = program_ctas();
     if (program_bytes < program_bytes_for(nstages, nctas))
         return set_error(SBQ_ERR_WORKSPACE, "program needs %zu bytes", program_bytes_for(nstages, nctas));
-    const int es = elem_size(x_dtype);
     std::vector<uint8_t> host(program_bytes_for(nstages, nctas), 0);
+    ProgHeader* hdr = reinterpret_cast<ProgHeader*>(host.data());
     ProgStage* stages = reinterpret_cast<ProgStage*>(host.data() + 256);
     ProgItem* items = reinterpret_cast<ProgItem*>(host.data() + 256 + (size_t)nstages * sizeof(ProgStage));
     for (int i = 0; i < njobs; ++i) {
         const sbq_gemv_job& j = jobs[i];
         int st = check_linear_args(j.x, x_dtype, j.ldx, j.packed, j.scale, m, j.n, j.k, j.y, j.y_dtype, j.ldy);
         if (st) return set_error(st, "job %d: %s", i, sbq_last_error());
-        if (m > 8 || m * (j.k * es + 16) > kXBytes)
-            return set_error(SBQ_ERR_UNSUPPORTED, "job %d: a program needs m * (k + 8) activation elements to fit in "
-                             "%d bytes (m=%lld k=%lld)", i, kXBytes, (long long)m, (long long)j.k);
+        if (m > 8) return set_error(SBQ_ERR_UNSUPPORTED, "job %d: a program takes 1..8 rows of x (m=%lld)", i, (long long)m);
         if (j.packed_up && (!j.scale_up || j.bias))
             return set_error(SBQ_ERR_INVALID_ARGUMENT, "job %d: fused gate/up job needs scale_up and no bias", i);
         ProgStage& ps = stages[job_stage[i]];
         if (ps.njobs >= kMaxJobs) return set_error(SBQ_ERR_UNSUPPORTED, "more than %d jobs in one stage", kMaxJobs);
-        GemvJob& jb = ps.job[ps.njobs++];
+        const int jj = ps.njobs++;
+        GemvJob& jb = ps.job[jj];
         fill_job(jb, j.x, j.ldx, j.packed, j.scale, j.packed_up, j.scale_up, j.bias, j.n, j.k, j.y, j.y_dtype, j.ldy);
         jb.m = (int)m;
         jb.n_tiles = (int)ceil_div(j.n, 16);
+        ps.peer.nranks = nranks;
+        if (ydest) {
+            bool local = false;
+            for (int r = 0; r < nranks; ++r) {
+                void* d = ydest[(size_t)i * nranks + r];
+                if (!d) return set_error(SBQ_ERR_INVALID_ARGUMENT, "job %d: null destination for rank %d", i, r);
+                local = local || d == j.y;
+                ps.peer.y[jj][r] = d;
+            }
+            if (!local) return set_error(SBQ_ERR_INVALID_ARGUMENT, "job %d: y must be one of its rank destinations", i);
+        }
     }
-    // per stage: CTAs in proportion to each job's weight bytes, consecutive tiles per CTA
+    // per stage: the stage's jobs share the grid as a grouped launch would (every CTA slot filled)
     for (int st = 0; st < nstages; ++st) {
         ProgStage& ps = stages[st];
         ProgItem* row = items + (size_t)st * nctas;
         for (int c = 0; c < nctas; ++c) row[c] = ProgItem{0, 0, 0};
         if (ps.njobs == 0) continue;
-        double total = 0.0;
-        for (int i = 0; i < ps.njobs; ++i)
-            total += (double)ps.job[i].n_tiles * (ps.job[i].w1 ? 2 : 1) * ps.job[i].kt_total;
-        const double per_cta = total / nctas;
-        int c = 0;
-        for (int i = 0; i < ps.njobs && c < nctas; ++i) {
-            GemvJob& jb = ps.job[i];
-            const double tile_cost = (double)(jb.w1 ? 2 : 1) * jb.kt_total;
-            int t = (int)std::ceil(per_cta / tile_cost - 1e-9);
-            if (t < 1) t = 1;
-            // leave at least one CTA for every later job
-            const int later = ps.njobs - 1 - i;
-            while ((int)ceil_div(jb.n_tiles, t) > nctas - c - later) ++t;
-            jb.tiles_per_cta = t;
-            for (int t0 = 0; t0 < jb.n_tiles && c < nctas; t0 += t, ++c)
-                row[c] = ProgItem{i, t0, t0 + t < jb.n_tiles ? t0 + t : jb.n_tiles};
+        if (plan_jobs(ps.job, ps.njobs, nctas) > nctas)
+            return set_error(SBQ_ERR_UNSUPPORTED, "stage %d has more jobs than the grid has CTAs", st);
+        for (int i = 0; i < ps.njobs; ++i) {
+            const GemvJob& jb = ps.job[i];
+            for (int c = 0; c < jb.cta_count; ++c)
+                row[jb.cta_begin + c] = ProgItem{i, (int)((int64_t)c * jb.n_tiles / jb.cta_count),
+                                                 (int)((int64_t)(c + 1) * jb.n_tiles / jb.cta_count)};
         }
     }
-    int* header = reinterpret_cast<int*>(host.data());
-    header[0] = nstages;
-    header[1] = nctas;
-    header[2] = x_dtype;
-    header[3] = (int)m;
+    hdr->nstages = nstages;
+    hdr->nctas = nctas;
+    hdr->x_dtype = x_dtype;
+    hdr->m = (int)m;
+    hdr->nranks = nranks;
+    for (int r = 0; r < nranks && peer_sync; ++r) hdr->peer_sync[r] = static_cast<uint8_t*>(peer_sync[r]);
     if (cudaMemcpy(program, host.data(), host.size(), cudaMemcpyHostToDevice) != cudaSuccess)
         return check_launch("copy decode program");
+    std::lock_guard<std::mutex> lock(g_peer_programs_mu);
+    if (nranks > 1)
+        g_peer_programs.insert(program);
+    else
+        g_peer_programs.erase(program);
     return SBQ_OK;
 }
 
-extern "C" int sbq_gemv_program_run(const void* program, int nstages, int x_dtype, int* counters, void* stream) {
-    if (!program || !counters || nstages < 1) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null argument");
+extern "C" int sbq_gemv_program_build(const sbq_gemv_job* jobs, const int* job_stage, int njobs, int x_dtype, int64_t m,
+                                      void* program, size_t program_bytes) {
+    return program_build(jobs, job_stage, njobs, x_dtype, m, nullptr, 1, nullptr, program, program_bytes);
+}
+
+extern "C" int sbq_gemv_program_build_peer(const sbq_gemv_job* jobs, const int* job_stage, int njobs, int x_dtype,
+                                           int64_t m, void* const* ydest, int nranks, void* const* peer_sync,
+                                           void* program, size_t program_bytes) {
+    if (!ydest || !peer_sync) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null destination or sync table");
+    if (nranks < 2 || nranks > kMaxPeers)
+        return set_error(SBQ_ERR_INVALID_ARGUMENT, "a sharded program has 2..%d ranks (got %d)", kMaxPeers, nranks);
+    for (int r = 0; r < nranks; ++r)
+        if (!peer_sync[r] || reinterpret_cast<uintptr_t>(peer_sync[r]) % 128)
+            return set_error(SBQ_ERR_ALIGNMENT, "sync region of rank %d must be 128-byte aligned", r);
+    return program_build(jobs, job_stage, njobs, x_dtype, m, ydest, nranks, peer_sync, program, program_bytes);
+}
+
+template <int XK, bool PEER>
+static cudaError_t launch_program(const cudaLaunchConfig_t& cfg, const ProgParams& pp) {
+    cudaFuncSetAttribute(gemv_program_kernel<XK, PEER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)cfg.dynamicSmemBytes);
+    return cudaLaunchKernelEx(&cfg, gemv_program_kernel<XK, PEER>, pp);
+}
+
+extern "C" int sbq_gemv_program_run(const void* program, int nstages, int x_dtype, void* sync, void* stream) {
+    if (!program || !sync || nstages < 1) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null argument");
+    if (reinterpret_cast<uintptr_t>(sync) % 128) return set_error(SBQ_ERR_ALIGNMENT, "sync region must be 128-byte aligned");
     const int xk = x_kind(x_dtype);
     if (xk < 0) return set_error(SBQ_ERR_UNSUPPORTED, "activation dtype %d", x_dtype);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (cudaMemsetAsync(counters, 0, sizeof(int) * nstages, s) != cudaSuccess) return check_launch("clear counters");
     ProgParams pp{};
     const uint8_t* base = static_cast<const uint8_t*>(program);
     const int nctas = program_ctas();
+    pp.hdr = reinterpret_cast<const ProgHeader*>(base);
     pp.stages = reinterpret_cast<const ProgStage*>(base + 256);
     pp.items = reinterpret_cast<const ProgItem*>(base + 256 + (size_t)nstages * sizeof(ProgStage));
     pp.nstages = nstages;
-    pp.counters = counters;
+    pp.sync = static_cast<uint8_t*>(sync);
     const int smem = GemvSmemSize<1>::kBytes;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)nctas);
@@ -964,20 +1311,16 @@ extern "C" int sbq_gemv_program_run(const void* program, int nstages, int x_dtyp
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    bool peer;
+    {
+        std::lock_guard<std::mutex> lock(g_peer_programs_mu);
+        peer = g_peer_programs.count(program) != 0;
+    }
     cudaError_t e;
     switch (xk) {
-        case kXF16:
-            cudaFuncSetAttribute(gemv_program_kernel<kXF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            e = cudaLaunchKernelEx(&cfg, gemv_program_kernel<kXF16>, pp);
-            break;
-        case kXBF16:
-            cudaFuncSetAttribute(gemv_program_kernel<kXBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            e = cudaLaunchKernelEx(&cfg, gemv_program_kernel<kXBF16>, pp);
-            break;
-        default:
-            cudaFuncSetAttribute(gemv_program_kernel<kXF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            e = cudaLaunchKernelEx(&cfg, gemv_program_kernel<kXF32>, pp);
-            break;
+        case kXF16: e = peer ? launch_program<kXF16, true>(cfg, pp) : launch_program<kXF16, false>(cfg, pp); break;
+        case kXBF16: e = peer ? launch_program<kXBF16, true>(cfg, pp) : launch_program<kXBF16, false>(cfg, pp); break;
+        default: e = peer ? launch_program<kXF32, true>(cfg, pp) : launch_program<kXF32, false>(cfg, pp); break;
     }
     if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "decode program launch: %s", cudaGetErrorString(e));
     return check_launch("gemv_program");

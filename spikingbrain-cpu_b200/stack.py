@@ -147,6 +147,8 @@ class PeerExchange:
         self.done = [[take(128), take(128)] for _ in stack.layers]   # CTA count-out of launch 1 / 2
         self.state = [[take(128), take(128)] for _ in stack.layers]  # wait state of launch 1 / 2
         self.final_state = take(128)
+        self.nstages = 2 * len(stack.layers)
+        self.prog_sync = take(int(self.lib.sbq_gemv_program_sync_bytes(self.nstages)))  # sharded decode program
         self.nbytes = off
         base = ctypes.c_void_p()
         L.call("sbq_peer_alloc", off, ctypes.byref(base))
@@ -332,37 +334,52 @@ class ProjectionStack(nn.Module):
 
 
 class DecodeProgram:
-    """A single-GPU batch-1 decode step of the stack as one launch of the decode program kernel.
+    """A batch-1 decode step of the stack as one launch of the decode program kernel.
 
     Two stages per layer: [gate/up, q|k|v|delta_in] read the layer input, [down, o, delta_out] read
     their outputs; a grid-wide barrier inside the kernel separates them and the weight stream never
-    pauses.  Every layer gets its own activation buffers (written once per step).  ``run()`` reads
-    the fixed input buffer ``x`` and returns the fixed output buffer (the last layer's down output).
+    pauses.  On one GPU every layer gets its own activation buffers (written once per step); a
+    sharded stack uses its peer arena (outputs stored to every rank, barriers spanning the ranks).
+    ``run()`` reads the fixed input buffer ``x`` and returns the fixed output buffer (the last
+    layer's down output, full width).
     """
 
     def __init__(self, stack: ProjectionStack, x: torch.Tensor):
         from . import _lib as L
         from .quant import _DTYPE_CODE
 
-        if stack.world != 1:
-            raise ValueError("the decode program runs on one GPU (no gathers inside a launch)")
+        if stack.world != 1 and stack.peer is None:
+            raise ValueError("a sharded decode program needs the peer exchange")
         if x.shape != (1, stack.hidden) or x.dtype != torch.float16 or not x.is_contiguous():
             raise ValueError("the decode program takes a contiguous fp16 [1, hidden] input")
-        hd, dev = stack.hidden, x.device
+        hd, dev, w, r = stack.hidden, x.device, stack.world, stack.rank
         self.stack, self.x = stack, x
         self.buffers = []
-        jobs, stage = [], []
+        jobs, stage, dests = [], [], []
+        px = stack.peer
         cur = x
         for i, layer in enumerate(stack.layers):
-            qkvd = torch.empty(1, 4 * hd, dtype=torch.float16, device=dev)
-            h = torch.empty(1, stack.inter, dtype=torch.float16, device=dev)
-            od = torch.empty(1, 2 * hd, dtype=torch.float16, device=dev)
-            nxt = torch.empty(1, hd, dtype=torch.float16, device=dev)
-            self.buffers += [qkvd, h, od, nxt]
-            jobs += [layer.mlp.gateup_job(cur, h), layer.qkvd.gemv_job(cur, qkvd)]
+            if px is None:
+                qkvd = torch.empty(1, 4 * hd, dtype=torch.float16, device=dev)
+                h = torch.empty(1, stack.inter, dtype=torch.float16, device=dev)
+                od = torch.empty(1, 2 * hd, dtype=torch.float16, device=dev)
+                nxt = torch.empty(1, hd, dtype=torch.float16, device=dev)
+                self.buffers += [qkvd, h, od, nxt]
+                sl = lambda t, a, b: t[:, a:b]  # noqa: E731
+                hs, qs, s = stack.inter, 4 * hd, hd
+            else:
+                qkvd, h, od, nxt = (px.view(i, k, 1) for k in range(4))
+                sl = lambda t, a, b: t[:, a:b]  # noqa: E731
+                hs, qs, s = stack.inter // w, 4 * hd // w, hd // w
+            q_off, h_off, od_off, x_off = px.buf[i] if px is not None else (0, 0, 0, 0)
+            jobs += [layer.mlp.gateup_job(cur, sl(h, r * hs, (r + 1) * hs)),
+                     layer.qkvd.gemv_job(cur, sl(qkvd, r * qs, (r + 1) * qs))]
+            dests += [(h_off, r * hs), (q_off, r * qs)]
             stage += [2 * i, 2 * i]
-            jobs += [layer.mlp.down_proj.gemv_job(h, nxt), layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], od[:, :hd]),
-                     layer.dout.gemv_job(qkvd[:, 3 * hd:], od[:, hd:])]
+            jobs += [layer.mlp.down_proj.gemv_job(h, sl(nxt, r * s, (r + 1) * s)),
+                     layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], sl(od, r * s, (r + 1) * s)),
+                     layer.dout.gemv_job(qkvd[:, 3 * hd:], sl(od, hd + r * s, hd + (r + 1) * s))]
+            dests += [(x_off, r * s), (od_off, r * s), (od_off, hd + r * s)]
             stage += [2 * i + 1] * 3
             cur = nxt
         self.y = cur
@@ -370,19 +387,27 @@ class DecodeProgram:
         lib = L.load()
         nbytes = int(lib.sbq_gemv_program_bytes(self.nstages))
         self.program = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-        self.counters = torch.zeros(self.nstages, dtype=torch.int32, device=dev)
         arr = (L.GemvJob * len(jobs))(*jobs)
         st = (ctypes.c_int * len(stage))(*stage)
         self._code = _DTYPE_CODE[torch.float16]
-        L.call("sbq_gemv_program_build", arr, st, len(jobs), self._code, 1, ctypes.c_void_p(self.program.data_ptr()),
-               nbytes)
+        if px is None:
+            self.sync = torch.zeros(int(lib.sbq_gemv_program_sync_bytes(self.nstages)), dtype=torch.uint8, device=dev)
+            self._sync_ptr = self.sync.data_ptr()
+            L.call("sbq_gemv_program_build", arr, st, len(jobs), self._code, 1,
+                   ctypes.c_void_p(self.program.data_ptr()), nbytes)
+        else:
+            yd = (ctypes.c_void_p * (len(jobs) * w))(*[b + off + col * 2 for off, col in dests for b in px.peers])
+            ps = (ctypes.c_void_p * w)(*[b + px.prog_sync for b in px.peers])
+            self._sync_ptr = px.base + px.prog_sync
+            L.call("sbq_gemv_program_build_peer", arr, st, len(jobs), self._code, 1, yd, w, ps,
+                   ctypes.c_void_p(self.program.data_ptr()), nbytes)
 
     def run(self) -> torch.Tensor:
         from . import _lib as L
         from .quant import _stream
 
         L.call("sbq_gemv_program_run", ctypes.c_void_p(self.program.data_ptr()), self.nstages, self._code,
-               ctypes.c_void_p(self.counters.data_ptr()), _stream(self.x.device))
+               ctypes.c_void_p(self._sync_ptr), _stream(self.x.device))
         return self.y
 
 
@@ -400,9 +425,9 @@ class CapturedStack:
         self.stack = stack
         self.stream = stream or torch.cuda.Stream(stack.device)
         self.x = torch.zeros(m, stack.hidden, dtype=torch.float16, device=stack.device)
-        # grouped launches by default; use_program=True runs a batch-1 single-GPU step as one
-        # decode-program launch (bit-identical; measured slower than the grouped launches so far)
-        self.program = stack.decode_program(self.x) if (m == 1 and stack.world == 1 and use_program) else None
+        # grouped launches by default; use_program=True runs a batch-1 step as one decode-program
+        # launch (bit-identical)
+        self.program = stack.decode_program(self.x) if (m == 1 and use_program) else None
         step = self.program.run if self.program is not None else (lambda: stack(self.x))
         with torch.cuda.stream(self.stream):
             step()  # warm-up outside the capture (allocator, communicators)

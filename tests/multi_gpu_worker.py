@@ -57,6 +57,14 @@ def main() -> int:
             check("%s graph replay %d" % (exchange, i), run(x).clone(), ref(x))
             xh = x.cpu()
             check("%s graph host call %d" % (exchange, i), run(xh).clone(), ref(x))
+        if exchange == "peer":
+            # the whole sharded step as one decode-program launch per rank
+            prog = sbq.stack.CapturedStack(st, m=1, use_program=True)
+            assert prog.program is not None
+            for i in range(12):
+                x = sbq.workloads.activation(1, shape["hidden"], seed=200 + i, device=dev)
+                check("peer program replay %d" % i, prog(x).clone(), ref(x))
+            prog.release()
         torch.cuda.synchronize()
         status = sbq._lib.load().sbq_check_device_error()
         if status:
