@@ -441,7 +441,7 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, uint8_t* rin
     constexpr int S = kMaxStages;
     constexpr int kStageBytes = kChunkTiles * kTileBytes;
     uint32_t ci = 0;
-    int u = (int)atomicAdd(grp.claim, 1u);
+    int u = blockIdx.x;  // the first unit of every CTA is its own; later ones are claimed
     for (;;) {
         if (u >= grp.total_units) {
             const int s = ci % S;
@@ -461,7 +461,7 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, uint8_t* rin
         const int claim_at = cpt > S ? cpt - S : 0;
         int next = 0;
         for (int i = 0; i < cpt; ++i, ++ci) {
-            if (i == claim_at) next = (int)atomicAdd(grp.claim, 1u);
+            if (i == claim_at) next = (int)(gridDim.x + atomicAdd(grp.claim, 1u));
             const int s = ci % S;
             if (!tc::mbar_wait(&empty[s], ((ci / S) & 1) ^ 1)) return false;
             meta[s] = make_int4(j, tile, i, cpt);
@@ -536,7 +536,8 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
             if (lane == 0) tc::mbar_arrive(&empty[s]);
             ++ci;
             if (++i == cpt) break;
-            // the next chunk of this unit: load its x, then wait for its weights
+            // the next chunk of this unit: load its x, then wait for its weights (loading x a whole
+            // chunk ahead instead measured slower)
             if (mine) {
                 const int64_t k0 = (int64_t)(i * C + slot) * kTileCols + 16 * c;
 #pragma unroll
