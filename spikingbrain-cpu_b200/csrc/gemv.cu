@@ -25,9 +25,12 @@
 //
 // fp32 activations are split into a bf16 high and low part (two MMAs, ~16 mantissa bits kept);
 // the dot product of int8 weights and fp16/bf16 activations is exact up to fp32 accumulation.
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <mutex>
+#include <queue>
+#include <unordered_map>
 #include <unordered_set>
 #include <vector>
 
@@ -64,9 +67,15 @@ constexpr int kMaxJobs = 8;
 struct GemvGroup {
     GemvJob job[kMaxJobs];
     int njobs;
-    int total_units;                 // 16-row tiles of all jobs
+    int total_units;                 // units of all jobs (a unit = one K part of one 16-row tile)
     int unit_begin[kMaxJobs + 1];    // first unit of each job
+    int parts[kMaxJobs];             // K parts per tile of each job (1: a tile is one unit)
+    int split_base[kMaxJobs];        // first split-tile counter of each job (jobs with parts > 1)
+    int64_t split_fbase[kMaxJobs];   // first scratch float of each job: [tile][part][split_stride]
+    int split_stride;                // floats per part partial (entries x matrices)
     unsigned* claim;                 // this launch's work counter pair (g_claim slot)
+    float* split_scratch;            // part partials [split tile][part][split_stride]
+    unsigned* split_count;           // parts completed per split tile (reset by the combining CTA)
 };
 
 // Output-channel shards on several GPUs of one node (sbq_gemv_w8_group_peer).  Every rank computes
@@ -434,6 +443,16 @@ __device__ __forceinline__ bool consume_run(const GemvJob& jb, int t0, int t1, c
 constexpr int kClaimSlots = 1024;  // per-launch counters, used round-robin by consecutive launches
 static __device__ unsigned g_claim[kClaimSlots][2];  // [next unit, CTAs finished]; reset by the last CTA
 
+// Split-K scratch: when a launch has too few tiles to keep every CTA busy (a sharded step on several
+// GPUs), tiles are cut into K parts; each part's partial sums go here and the CTA that completes a
+// tile's last part adds them in part order (deterministic).  Two regions, used alternately by
+// consecutive launches.
+constexpr int kSplitRegions = 2;
+constexpr int kSplitFloats = 512 * 1024;  // per region (2 MiB)
+constexpr int kSplitTiles = 8192;         // split tiles per region
+static __device__ float g_split[kSplitRegions][kSplitFloats];
+static __device__ unsigned g_split_count[kSplitRegions][kSplitTiles];
+
 // Producer (one thread).  Claims the next unit while the last ring-full of the current one is
 // still to be issued, so the claim's latency is hidden.  False if a wait timed out.
 __device__ __forceinline__ bool produce_units(const GemvGroup& grp, uint8_t* ring, uint64_t* full, uint64_t* empty,
@@ -453,18 +472,20 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, uint8_t* rin
         int j = 0;
         while (j + 1 < grp.njobs && u >= grp.unit_begin[j + 1]) ++j;
         const GemvJob& jb = grp.job[j];
-        const int tile = u - grp.unit_begin[j];
+        const int P = grp.parts[j];
+        const int tile = (u - grp.unit_begin[j]) / P, part = (u - grp.unit_begin[j]) % P;
         const int C = jb.chunk_tiles, cpt = jb.kt_total / C, nmat = jb.w1 ? 2 : 1;
+        const int i0 = part * cpt / P, i1 = (part + 1) * cpt / P;  // this part's chunks
         const uint32_t bytes = (uint32_t)C * kTileBytes;
         const int8_t* src0 = jb.w0 + (int64_t)tile * jb.kt_total * kTileBytes;
         const int8_t* src1 = jb.w1 ? jb.w1 + (int64_t)tile * jb.kt_total * kTileBytes : nullptr;
-        const int claim_at = cpt > S ? cpt - S : 0;
+        const int claim_at = i1 - i0 > S ? i1 - S : i0;
         int next = 0;
-        for (int i = 0; i < cpt; ++i, ++ci) {
+        for (int i = i0; i < i1; ++i, ++ci) {
             if (i == claim_at) next = (int)(gridDim.x + atomicAdd(grp.claim, 1u));
             const int s = ci % S;
             if (!tc::mbar_wait(&empty[s], ((ci / S) & 1) ^ 1)) return false;
-            meta[s] = make_int4(j, tile, i, cpt);
+            meta[s] = make_int4(j | (part << 8), tile, i, i1 - i0);
             uint8_t* dst = ring + s * kStageBytes;
             tc::mbar_arrive_expect_tx(&full[s], bytes * nmat);
             tc::bulk_load(dst, src0 + (int64_t)i * bytes, bytes, &full[s]);
@@ -493,7 +514,7 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
         if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (ci / S) & 1))) return false;
         const int4 md = meta[s];
         if (md.x < 0) break;
-        const int j = md.x, tile = md.y, cpt = md.w;
+        const int j = md.x & 0xff, part = md.x >> 8, tile = md.y, i0 = md.z, cpt = md.w;
         const GemvJob& jb = grp.job[j];
         const bool two = jb.w1 != nullptr;
         const int C = jb.chunk_tiles;
@@ -521,7 +542,7 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
         }
         XFrag<XK> xf[MT];
         if (mine) {
-            const int64_t k0 = (int64_t)slot * kTileCols + 16 * c;
+            const int64_t k0 = (int64_t)(i0 * C + slot) * kTileCols + 16 * c;
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xj, ldx, 8 * mt + g, xm, k0, xk, xcoh);
         }
@@ -539,7 +560,7 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
             // the next chunk of this unit: load its x, then wait for its weights (loading x a whole
             // chunk ahead instead measured slower)
             if (mine) {
-                const int64_t k0 = (int64_t)(i * C + slot) * kTileCols + 16 * c;
+                const int64_t k0 = (int64_t)((i0 + i) * C + slot) * kTileCols + 16 * c;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xj, ldx, 8 * mt + g, xm, k0, xk, xcoh);
             }
@@ -559,7 +580,79 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
             SBQ_RED(warp, mt, g + 8, 2 * c + 1) = acc[mt][3];
         }
         consumers_sync();
-        if (vt < kEntries) {
+        const int P = grp.parts[j];
+        if (P > 1) {
+            // a K part of a split tile: one warp writes the part's partial sums to the scratch; the
+            // CTA completing the tile's last part sums the parts in order and runs the epilogue
+            if (warp == units % kGemvWarps) {
+                const int st = grp.split_base[j] + tile;
+                const int stride = grp.split_stride;
+                float* const tp = grp.split_scratch + grp.split_fbase[j] + (int64_t)tile * P * stride;
+                float* mp = tp + (int64_t)part * stride;
+                for (int e = lane; e < kEntries; e += 32) {
+                    const int r = e & 15, tok = e >> 4, mt = tok >> 3, col = tok & 7;
+                    float v0 = 0.0f, v1 = 0.0f;
+                    if (!two) {
+#pragma unroll
+                        for (int w = 0; w < 8; ++w) v0 += SBQ_RED(w, mt, r, col);
+                    } else {
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) v0 += SBQ_RED(w, mt, r, col);
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) v1 += SBQ_RED(4 + w, mt, r, col);
+                        mp[kEntries + e] = v1;
+                    }
+                    mp[e] = v0;
+                }
+                __syncwarp();
+                unsigned last = 0;
+                if (lane == 0) {
+                    __threadfence();  // this part's partial before the count
+                    last = atomicAdd(grp.split_count + st, 1u) == (unsigned)(P - 1);
+                    if (last) {
+                        grp.split_count[st] = 0;  // for the next launch that uses this slot
+                        __threadfence();          // every part's partial before the reads below
+                    }
+                }
+                __syncwarp();
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    const float* base = tp;
+                    for (int e = lane; e < kEntries; e += 32) {
+                        const int r = e & 15, tok = e >> 4;
+                        const int n = tile * 16 + r;
+                        if (n >= jb.n || tok >= xm) continue;
+                        float v0 = 0.0f, v1 = 0.0f;
+                        for (int q = 0; q < P; ++q) {
+                            v0 += __ldcg(base + (int64_t)q * stride + e);
+                            if (two) v1 += __ldcg(base + (int64_t)q * stride + kEntries + e);
+                        }
+                        float out;
+                        if (!two) {
+                            out = v0 * jb.s0[n];
+                            if (jb.bias) out += jb.bias[n];
+                        } else {
+                            const float gv = v0 * jb.s0[n];
+                            const float uv = v1 * jb.s1[n];
+                            out = gv / (1.0f + expf(-gv)) * uv;
+                        }
+                        const int64_t idx = (int64_t)tok * jb.ldy + n;
+                        if (PEER) {
+                            for (int p = 0; p < ps.nranks; ++p) {
+                                if (jb.out_f16)
+                                    static_cast<__half*>(ps.y[j][p])[idx] = __float2half_rn(out);
+                                else
+                                    static_cast<float*>(ps.y[j][p])[idx] = out;
+                            }
+                        } else if (jb.out_f16) {
+                            static_cast<__half*>(jb.y)[idx] = __float2half_rn(out);
+                        } else {
+                            static_cast<float*>(jb.y)[idx] = out;
+                        }
+                    }
+                }
+            }
+        } else if (vt < kEntries) {
             const int r = vt & 15, tok = vt >> 4, mt = tok >> 3, col = tok & 7;
             const int n = tile * 16 + r;
             if (n < jb.n && tok < xm) {
@@ -904,47 +997,196 @@ static int plan_jobs(GemvJob* job, int njobs, int slots) {
     return ctas;
 }
 
-// Device address of this device's claim counters (cached per device).
-static unsigned* claim_base() {
-    static unsigned* base[64] = {};
+// Device addresses of this device's claim counters and split scratch (cached per device).
+struct UnitBuffers {
+    unsigned* claim = nullptr;
+    float* split = nullptr;
+    unsigned* split_count = nullptr;
+};
+
+static const UnitBuffers* unit_buffers() {
+    static UnitBuffers per_dev[64];
     static std::mutex mu;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
     std::lock_guard<std::mutex> lock(mu);
-    if (!base[dev]) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_claim) != cudaSuccess) return nullptr;
-        base[dev] = static_cast<unsigned*>(p);
+    UnitBuffers& b = per_dev[dev];
+    if (!b.claim) {
+        void *c = nullptr, *sp = nullptr, *sc = nullptr;
+        if (cudaGetSymbolAddress(&c, g_claim) != cudaSuccess || cudaGetSymbolAddress(&sp, g_split) != cudaSuccess ||
+            cudaGetSymbolAddress(&sc, g_split_count) != cudaSuccess)
+            return nullptr;
+        b.split = static_cast<float*>(sp);
+        b.split_count = static_cast<unsigned*>(sc);
+        b.claim = static_cast<unsigned*>(c);
     }
-    return base[dev];
+    return &b;
 }
 
 static std::atomic<unsigned> g_claim_next{0};
 
-// Orders the jobs by unit size (largest first, so the last units claimed are the small ones),
-// permuting the peer destinations alike, numbers the units and picks this launch's counter.
-// Returns the grid size (every CTA slot, or one CTA per unit if there are fewer), 0 on failure.
-static int plan_units(GemvGroup& grp, PeerSync& ps, int slots) {
+// Launch time of units claimed greedily by `slots` equally fast CTAs, in bytes per CTA: the units
+// are taken in order, each by the CTA that is free first.
+static double greedy_makespan(const std::vector<double>& unit_bytes, int slots) {
+    std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+    for (int i = 0; i < slots; ++i) free_at.push(0.0);
+    double end = 0.0;
+    for (double b : unit_bytes) {
+        const double t = free_at.top() + b;
+        free_at.pop();
+        free_at.push(t);
+        end = std::max(end, t);
+    }
+    return end;
+}
+
+// K parts per tile for a launch shape.  Launch time model: the larger of the GPU's streaming time
+// (all bytes at the HBM rate) and the busiest CTA's bytes at one CTA's own rate (a CTA streams
+// about 1/kCtaShare of the HBM rate: its ring holds a fixed number of bytes in flight), with units
+// claimed greedily.  Tiles are cut into K parts (at least 32 KiB and whole chunks each, partial sums
+// added in part order) only while that lowers the modelled time by more than 2 %: a sharded step
+// on several GPUs, whose launches have few tiles, cuts its large tiles; a one-GPU launch does not.
+// Cached per shape: eager callers plan each shape once.
+constexpr double kCtaShare = 200.0;
+struct PartsKey {
+    int slots, m, nj;
+    int64_t shape[kMaxJobs][3];  // tiles, tile bytes, chunks per tile
+    bool operator==(const PartsKey& o) const {
+        if (slots != o.slots || m != o.m || nj != o.nj) return false;
+        for (int i = 0; i < nj; ++i)
+            for (int f = 0; f < 3; ++f)
+                if (shape[i][f] != o.shape[i][f]) return false;
+        return true;
+    }
+};
+struct PartsKeyHash {
+    size_t operator()(const PartsKey& k) const {
+        size_t h = (size_t)k.slots * 1000003u ^ (size_t)k.m * 7919u ^ (size_t)k.nj;
+        for (int i = 0; i < k.nj; ++i)
+            for (int f = 0; f < 3; ++f) h = h * 1099511628211ull ^ (size_t)k.shape[i][f];
+        return h;
+    }
+};
+
+static void unit_order(int nj, const int64_t* tile_bytes, const int* parts, int* perm) {
+    for (int i = 0; i < nj; ++i) perm[i] = i;
+    for (int i = 1; i < nj; ++i)  // stable insertion sort by decreasing unit bytes
+        for (int k = i; k > 0 && tile_bytes[perm[k]] * parts[perm[k - 1]] > tile_bytes[perm[k - 1]] * parts[perm[k]]; --k)
+            std::swap(perm[k], perm[k - 1]);
+}
+
+static void choose_parts(const PartsKey& key, int* parts_out) {
+    static std::mutex mu;
+    static std::unordered_map<PartsKey, std::vector<int>, PartsKeyHash> cache;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            for (int i = 0; i < key.nj; ++i) parts_out[i] = it->second[i];
+            return;
+        }
+    }
+    const int nj = key.nj;
+    int tiles[kMaxJobs], parts[kMaxJobs], max_parts[kMaxJobs];
+    int64_t tile_bytes[kMaxJobs];
+    double total = 0.0;
+    for (int i = 0; i < nj; ++i) {
+        tiles[i] = (int)key.shape[i][0];
+        tile_bytes[i] = key.shape[i][1];
+        max_parts[i] = std::max(1, (int)std::min<int64_t>(std::min<int64_t>(8, key.shape[i][2]), tile_bytes[i] >> 15));
+        parts[i] = 1;
+        total += (double)tiles[i] * tile_bytes[i];
+    }
+    const int stride = 2 * (key.m > 8 ? 2 : 1) * 128;
+    auto makespan = [&]() {
+        int perm[kMaxJobs];
+        unit_order(nj, tile_bytes, parts, perm);
+        std::vector<double> ub;
+        for (int i = 0; i < nj; ++i)
+            for (int t = 0; t < tiles[perm[i]] * parts[perm[i]]; ++t) ub.push_back((double)tile_bytes[perm[i]] / parts[perm[i]]);
+        return greedy_makespan(ub, key.slots);
+    };
+    auto scratch_ok = [&]() {
+        int64_t f = 0, t = 0;
+        for (int i = 0; i < nj; ++i)
+            if (parts[i] > 1) f += (int64_t)tiles[i] * parts[i] * stride, t += tiles[i];
+        return f <= kSplitFloats && t <= kSplitTiles;
+    };
+    const double stream = total / kCtaShare;  // the streaming time, in bytes of one CTA
+    auto model = [&]() { return std::max(stream, makespan()); };
+    double best_t = model();
+    int best[kMaxJobs];
+    for (int i = 0; i < nj; ++i) best[i] = parts[i];
+    for (;;) {
+        int cut = -1;  // the job with the largest units that can still be cut
+        for (int i = 0; i < nj; ++i)
+            if (parts[i] < max_parts[i] && (cut < 0 || tile_bytes[i] * parts[cut] > tile_bytes[cut] * parts[i])) cut = i;
+        if (cut < 0) break;
+        ++parts[cut];
+        if (!scratch_ok()) break;
+        const double t = model();
+        if (t < 0.98 * best_t) {
+            best_t = t;
+            for (int i = 0; i < nj; ++i) best[i] = parts[i];
+        }
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    cache.emplace(key, std::vector<int>(best, best + nj));
+    for (int i = 0; i < nj; ++i) parts_out[i] = best[i];
+}
+
+// Plans a grouped launch: K parts per tile (choose_parts), jobs ordered by unit size (largest
+// first, so that the last units claimed are the small ones; the peer destinations are permuted
+// alike), unit numbering, this launch's counter and scratch.  Returns the grid size (every CTA slot,
+// or one CTA per unit if there are fewer), 0 if the device buffers are unavailable.
+static int plan_units(GemvGroup& grp, PeerSync& ps, int slots, int m) {
+    const int nj = grp.njobs;
+    int parts[kMaxJobs], tiles[kMaxJobs];
+    int64_t tile_bytes[kMaxJobs];
+    PartsKey key{};
+    key.slots = slots;
+    key.m = m;
+    key.nj = nj;
+    for (int i = 0; i < nj; ++i) {
+        const GemvJob& jb = grp.job[i];
+        tiles[i] = (int)ceil_div(jb.n, 16);
+        tile_bytes[i] = (int64_t)jb.kt_total * (jb.w1 ? 2 : 1) * kTileBytes;
+        key.shape[i][0] = tiles[i];
+        key.shape[i][1] = tile_bytes[i];
+        key.shape[i][2] = jb.kt_total / jb.chunk_tiles;
+    }
+    choose_parts(key, parts);
+    const int stride = 2 * (m > 8 ? 2 : 1) * 128;  // floats per part partial (entries of both matrices)
     int perm[kMaxJobs];
-    for (int i = 0; i < grp.njobs; ++i) perm[i] = i;
-    auto unit_bytes = [&](int i) { return (int64_t)grp.job[i].kt_total * (grp.job[i].w1 ? 2 : 1); };
-    for (int i = 1; i < grp.njobs; ++i)  // stable insertion sort by decreasing unit bytes
-        for (int k = i; k > 0 && unit_bytes(perm[k]) > unit_bytes(perm[k - 1]); --k) std::swap(perm[k], perm[k - 1]);
+    unit_order(nj, tile_bytes, parts, perm);
     GemvGroup sorted = grp;
     PeerSync pss = ps;
-    int units = 0;
-    for (int i = 0; i < grp.njobs; ++i) {
-        sorted.job[i] = grp.job[perm[i]];
-        for (int p = 0; p < kMaxPeers; ++p) pss.y[i][p] = ps.y[perm[i]][p];
-        sorted.job[i].n_tiles = (int)ceil_div(sorted.job[i].n, 16);
+    int units = 0, split_tiles = 0;
+    int64_t split_floats = 0;
+    for (int i = 0; i < nj; ++i) {
+        const int q = perm[i];
+        sorted.job[i] = grp.job[q];
+        for (int p = 0; p < kMaxPeers; ++p) pss.y[i][p] = ps.y[q][p];
+        sorted.job[i].n_tiles = tiles[q];
+        sorted.parts[i] = parts[q];
+        sorted.split_base[i] = split_tiles;
+        sorted.split_fbase[i] = split_floats;
+        if (parts[q] > 1) {
+            split_tiles += tiles[q];
+            split_floats += (int64_t)tiles[q] * parts[q] * stride;
+        }
         sorted.unit_begin[i] = units;
-        units += sorted.job[i].n_tiles;
+        units += tiles[q] * parts[q];
     }
-    sorted.unit_begin[grp.njobs] = units;
+    sorted.unit_begin[nj] = units;
     sorted.total_units = units;
-    unsigned* base = claim_base();
-    if (!base) return 0;
-    sorted.claim = base + 2 * (g_claim_next.fetch_add(1) % kClaimSlots);
+    sorted.split_stride = stride;
+    const UnitBuffers* ub = unit_buffers();
+    if (!ub) return 0;
+    const unsigned slot = g_claim_next.fetch_add(1);
+    sorted.claim = ub->claim + 2 * (slot % kClaimSlots);
+    sorted.split_scratch = ub->split + (size_t)(slot % kSplitRegions) * kSplitFloats;
+    sorted.split_count = ub->split_count + (size_t)(slot % kSplitRegions) * kSplitTiles;
     grp = sorted;
     ps = pss;
     return units < slots ? units : slots;
@@ -952,7 +1194,7 @@ static int plan_units(GemvGroup& grp, PeerSync& ps, int slots) {
 
 template <bool PEER>
 static int dispatch_group_t(GemvGroup& grp, PeerSync ps, int xk, int mt, cudaStream_t s) {
-    const int ctas = plan_units(grp, ps, (mt == 2 ? 2 : kCtasPerSm) * sm_count());
+    const int ctas = plan_units(grp, ps, (mt == 2 ? 2 : kCtasPerSm) * sm_count(), grp.job[0].m);
     if (ctas <= 0) return set_error(SBQ_ERR_CUDA, "grouped GEMV: no work counter on this device");
     switch (xk) {
         case kXF16:

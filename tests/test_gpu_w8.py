@@ -177,3 +177,47 @@ def test_grouped_launch_matches_single_calls(sbq, m):
     b.out_dtype = torch.float16
     assert torch.equal(ya, a(x)) and torch.equal(yb, b(x))
     assert torch.equal(h, mlp.gateup_into(x, torch.empty_like(h)))
+
+
+@pytest.mark.parametrize("n,k,m", [(64, 12288, 1), (256, 12288, 3), (1024, 8192, 12), (96, 4096, 5)])
+@pytest.mark.parametrize("out", [torch.float32, torch.float16])
+def test_split_k_gemv_vs_oracle(sbq, n, k, m, out):
+    # few row tiles with long K: the launch cuts each tile into K parts whose partial sums are
+    # added in part order by the CTA that completes the tile (deterministic)
+    w = sbq.workloads.float_weight(n, k, seed=n + 3 * k)
+    b = torch.randn(n)
+    x = sbq.workloads.activation(m, k, seed=m + 40)
+    q, s = R.quantize_per_channel(w.numpy())
+    mod = sbq.Int8Linear(w, b)
+    mod.out_dtype = out
+    y1 = mod(x.cuda())
+    y2 = mod(x.cuda())
+    assert torch.equal(y1, y2)
+    assert R.rel_l2(_np(y1), R.int8_linear(x.float().numpy(), q, s, b.numpy())) < REL_L2
+
+
+@pytest.mark.parametrize("xdtype", [torch.bfloat16, torch.float32])
+def test_split_k_other_activation_types(sbq, xdtype):
+    n, k, m = 128, 12288, 2
+    w = sbq.workloads.float_weight(n, k, seed=51)
+    x = sbq.workloads.activation(m, k, seed=52, dtype=xdtype)
+    q, s = R.quantize_per_channel(w.numpy())
+    y = sbq.Int8Linear(w, None)(x.cuda())
+    tol = 2e-5 if xdtype == torch.float32 else REL_L2
+    assert R.rel_l2(_np(y), R.int8_linear(x.float().numpy(), q, s)) < tol
+
+
+@pytest.mark.parametrize("m", [1, 6])
+def test_split_k_fused_gateup(sbq, m):
+    n, k = 64, 8192
+    wg = sbq.workloads.float_weight(n, k, seed=60)
+    wu = sbq.workloads.float_weight(n, k, seed=61)
+    wd = sbq.workloads.float_weight(k, n, seed=62)
+    x = sbq.workloads.activation(m, k, seed=63)
+    mlp = sbq.FusedGatedMLP(*(sbq.Int8Linear(w, None) for w in (wg, wu, wd)))
+    h1 = mlp.gateup_into(x.cuda(), torch.empty(m, n, device="cuda"))
+    h2 = mlp.gateup_into(x.cuda(), torch.empty(m, n, device="cuda"))
+    assert torch.equal(h1, h2)
+    g, u = (R.int8_linear(x.float().numpy(), *R.quantize_per_channel(w.numpy())) for w in (wg, wu))
+    want = g / (1.0 + np.exp(-g)) * u
+    assert R.rel_l2(_np(h1), want) < REL_L2
