@@ -97,7 +97,7 @@ SBQ_API int sbq_unpack_int8(const void* packed, int64_t n, int64_t k, int8_t* q,
 /* Int8Linear.forward (quant.py:41-53): y[m, n] = (x[m, :] . q[n, :]) * scale[n] (+ bias[n]).
  * x dtype SBQ_F16, SBQ_BF16 or SBQ_F32 (fp32 is split into two bf16 terms, ~16 mantissa bits);
  * y dtype SBQ_F32 (the reference's output type) or SBQ_F16.  bias may be NULL.  Chooses the
- * decode GEMV for small m and the tensor-memory GEMM otherwise. */
+ * decode GEMV up to 32 rows (and for bf16/fp32 x) and the tensor-memory GEMM above. */
 SBQ_API int sbq_linear_w8(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                   const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
                   void* stream);
@@ -107,8 +107,11 @@ SBQ_API int sbq_gemv_w8(const void* x, int x_dtype, int64_t ldx, const void* pac
                 const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
                 void* stream);
 
-/* The prefill GEMM alone: TMA-fed, int8 tiles dequantised to fp16 in shared memory, tcgen05 MMA
- * with fp32 accumulators in tensor memory, scale epilogue.  x must be SBQ_F16. */
+/* The tensor-memory GEMM alone: TMA-fed, int8 rows dequantised to fp16 straight into tensor memory
+ * (the MMA's A operand), tcgen05 MMA with fp32 accumulators in tensor memory, scale epilogue.
+ * Up to 128 rows of x: 64-token tiles, with the K range split over a thread-block cluster when the
+ * tiles are too few for the GPU (partials added through distributed shared memory in part order);
+ * more rows: 256-token tiles.  x must be SBQ_F16. */
 SBQ_API int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                    const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
                    void* stream);

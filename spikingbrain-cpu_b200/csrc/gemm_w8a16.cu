@@ -195,6 +195,265 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Small-batch variant (17..128 activation rows, e.g. batched decode): 128-channel x 64-token tiles,
+// 6-stage TMA ring (2 CTAs per SM), and split-K over a thread-block cluster when the tiles alone
+// cannot fill the GPU: the S CTAs of a cluster (one K part each) keep their fp32 partial tile in
+// shared memory and each reduces 1/S of the channels by reading all S partials through distributed
+// shared memory in part order (deterministic), then scales and stores.  Roles as above.
+// ---------------------------------------------------------------------------------------------
+constexpr int kSTok = 64;      // activation rows per CTA (MMA N)
+constexpr int kSStages = 6;
+constexpr uint32_t kSTmemCols = 256;  // accumulator [0, 64), six weight buffers of 32 columns from 64
+constexpr uint32_t kSACol = 64;
+constexpr int kSABufs = 6;
+constexpr int kSPad = 68;      // floats per row of the partial tile in shared memory (16-byte rows)
+
+struct SmallSmem {
+    static constexpr int kX = kSTok * kWBK * 2;  // 8 KiB fp16 activation tile
+    static constexpr int kW8 = kWCh * kWBK;      // 8 KiB int8 weight tile
+    static constexpr int kStage = kX + kW8;
+    static constexpr int kBarOff = kSStages * kStage;
+    static constexpr int kBytes = kBarOff + 256 + kWCh * 8 + 1024;
+    static_assert(kWCh * kSPad * 4 <= kSStages * kStage, "partial tile fits in the ring");
+};
+
+struct GemmSmallParams {
+    int m, n, k, num_kb, parts;
+    const float* scale;
+    const float* bias;
+    void* y;
+    int64_t ldy;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Shared-memory address `a` of this CTA mapped into cluster CTA `rank`'s shared memory.
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t a, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ float4 ld_dsmem4(uint32_t cluster_addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cluster_addr)
+                 : "memory");
+    return v;
+}
+
+template <bool OUT_F16>
+__global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                                        const __grid_constant__ CUtensorMap tmap_w,
+                                                                        const GemmSmallParams p) {
+    using S = SmallSmem;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
+    uint64_t* empty = full + kSStages;
+    uint64_t* a_full = empty + kSStages;
+    uint64_t* a_empty = a_full + kSABufs;
+    uint64_t* done = a_empty + kSABufs;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    float* s_scale = reinterpret_cast<float*>(smem + S::kBarOff + 256);
+    float* s_bias = s_scale + kWCh;
+    float* part_tile = reinterpret_cast<float*>(smem);  // [128][kSPad], after the main loop
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kWCh, t0 = blockIdx.y * kSTok;
+    const int part = p.parts > 1 ? (int)cluster_rank() : 0;
+    const int kb0 = part * p.num_kb / p.parts, kb1 = (part + 1) * p.num_kb / p.parts;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kSStages; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 4 + 1);
+        }
+        for (int d = 0; d < kSABufs; ++d) {
+            tc::mbar_init(&a_full[d], 4);
+            tc::mbar_init(&a_empty[d], 1);
+        }
+        tc::mbar_init(done, 1);
+        tc::fence_mbar_init();
+        tc::prefetch_tmap(&tmap_x);
+        tc::prefetch_tmap(&tmap_w);
+    }
+    if (warp == 2) {
+        tc::tmem_alloc(tmem_slot, kSTmemCols);
+        tc::tmem_relinquish();
+    }
+    for (int i = threadIdx.x; i < kWCh; i += blockDim.x) {
+        const int n = n0 + i;
+        s_scale[i] = n < p.n ? p.scale[n] : 0.0f;
+        s_bias[i] = (p.bias && n < p.n) ? p.bias[n] : 0.0f;
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const int nkb = kb1 - kb0;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % kSStages;
+                const uint32_t ph = (i / kSStages) & 1;
+                if (!tc::mbar_wait(&empty[s], ph ^ 1)) break;
+                uint8_t* xs = smem + s * S::kStage;
+                tc::mbar_arrive_expect_tx(&full[s], S::kStage);
+                tc::tma_load_2d(xs, &tmap_x, &full[s], (kb0 + i) * kWBK, t0);
+                tc::tma_load_4d(xs + S::kX, &tmap_w, &full[s], 0, 0, kb0 + i, n0 / 16);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_f16(kWCh, kSTok);
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % kSStages, d = i % kSABufs;
+                const uint32_t ph = (i / kSStages) & 1, phd = (i / kSABufs) & 1;
+                if (!tc::mbar_wait(&full[s], ph)) break;
+                if (!tc::mbar_wait(&a_full[d], phd)) break;
+                tc::fence_after_sync();
+                const uint8_t* xs = smem + s * S::kStage;
+                const uint32_t a_col = tmem + kSACol + d * (kWBK / 2);
+#pragma unroll
+                for (int j = 0; j < kWBK / 16; ++j) {
+                    const uint64_t bd = tc::smem_desc(xs + j * 32, tc::kSwizzle128B, 1024);
+                    tc::mma_f16_ts(tmem, a_col + j * 8, bd, idesc, (i | j) != 0);
+                }
+                tc::mma_commit(&empty[s]);
+                tc::mma_commit(&a_empty[d]);
+            }
+            tc::mma_commit(done);
+        }
+    } else if (warp >= 4) {
+        const int grp = (warp - 4) >> 2;
+        const int wq = (warp - 4) & 3;
+        const int row = wq * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
+        // each group converts two consecutive k-blocks per turn (pairs alternate between the
+        // groups): two tensor-memory stores share one wait, which halves the conversion latency
+        // per k-block (the MMA of a 64-token tile is short, so that latency sets the pace)
+        bool ok = true;
+        for (int i = 2 * grp; i < nkb; i += 4) {
+            const int cnt = nkb - i >= 2 ? 2 : 1;
+            uint32_t h[2][32];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                if (u >= cnt) break;
+                const int kb = i + u, s = kb % kSStages, d = kb % kSABufs;
+                const uint32_t ph = (kb / kSStages) & 1, phd = (kb / kSABufs) & 1;
+                if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], ph))) { ok = false; break; }
+                if (!__all_sync(0xffffffffu, tc::mbar_wait(&a_empty[d], phd ^ 1))) { ok = false; break; }
+                tc::fence_after_sync();
+                const uint8_t* w8 = smem + s * S::kStage + S::kX + row * 64;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(w8 + ((c ^ ((row >> 1) & 3)) << 4));
+                    i8x4_to_half2x2(v.x, h[u][8 * c + 0], h[u][8 * c + 1]);
+                    i8x4_to_half2x2(v.y, h[u][8 * c + 2], h[u][8 * c + 3]);
+                    i8x4_to_half2x2(v.z, h[u][8 * c + 4], h[u][8 * c + 5]);
+                    i8x4_to_half2x2(v.w, h[u][8 * c + 6], h[u][8 * c + 7]);
+                }
+                tc::tmem_st_32x32b_x32(tmem + lane_addr + kSACol + d * (kWBK / 2), h[u]);
+            }
+            if (!ok) break;
+            tc::tmem_wait_st();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) {
+                for (int u = 0; u < cnt; ++u) {
+                    const int kb = i + u;
+                    tc::mbar_arrive(&a_full[kb % kSABufs]);
+                    tc::mbar_arrive(&empty[kb % kSStages]);
+                }
+            }
+        }
+        // ---- this thread's channel, this group's 32 tokens of accumulators
+        ok = __all_sync(0xffffffffu, ok && tc::mbar_wait(done, 0));
+        tc::fence_after_sync();
+        uint32_t r[32];
+        tc::tmem_ld_32x32b_x32(tmem + lane_addr + grp * 32, r);
+        tc::tmem_wait_ld();
+        if (!ok) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+        if (p.parts == 1) {
+            const int n = n0 + row;
+            if (n < p.n) {
+                const float sc = s_scale[row], bi = s_bias[row];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = t0 + grp * 32 + j;
+                    if (t >= p.m) break;
+                    float v = __fmul_rn(__uint_as_float(r[j]), sc);
+                    if (p.bias) v = __fadd_rn(v, bi);
+                    if (OUT_F16)
+                        static_cast<__half*>(p.y)[(int64_t)t * p.ldy + n] = __float2half_rn(v);
+                    else
+                        static_cast<float*>(p.y)[(int64_t)t * p.ldy + n] = v;
+                }
+            }
+        } else {
+            // the ring is idle (every stage consumed): keep the raw partial tile there
+#pragma unroll
+            for (int j = 0; j < 32; ++j) part_tile[row * kSPad + grp * 32 + j] = __uint_as_float(r[j]);
+        }
+    }
+    if (p.parts > 1) {
+        // every part's partial tile is in its CTA's shared memory; this CTA reduces its share of
+        // the channels over all parts, in part order: four tokens per load, all parts' loads issued
+        // before the sum
+        cluster_sync_all();
+        const int r0 = part * kWCh / p.parts, r1 = (part + 1) * kWCh / p.parts, nr = r1 - r0;
+        for (int e = threadIdx.x; e < nr * (kSTok / 4); e += blockDim.x) {
+            const int row = r0 + e % nr, tq = (e / nr) * 4;
+            const uint32_t a = tc::smem_u32(part_tile + row * kSPad + tq);
+            float4 v[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                if (q < p.parts) v[q] = ld_dsmem4(dsmem_map(a, (uint32_t)q));
+            float4 acc = v[0];
+#pragma unroll
+            for (int q = 1; q < 8; ++q)
+                if (q < p.parts) acc.x += v[q].x, acc.y += v[q].y, acc.z += v[q].z, acc.w += v[q].w;
+            const int n = n0 + row;
+            if (n >= p.n) continue;
+            const float sc = s_scale[row], bi = s_bias[row];
+            const float r4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int t = t0 + tq + j;
+                if (t >= p.m) break;
+                float o = __fmul_rn(r4[j], sc);
+                if (p.bias) o = __fadd_rn(o, bi);
+                if (OUT_F16)
+                    static_cast<__half*>(p.y)[(int64_t)t * p.ldy + n] = __float2half_rn(o);
+                else
+                    static_cast<float*>(p.y)[(int64_t)t * p.ldy + n] = o;
+            }
+        }
+        cluster_sync_all();  // no CTA leaves while another may still read its shared memory
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 2) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kSTmemCols);
+    }
+}
+
 SBQ_DEFINE_ERROR_POLL(poll_error_w8a16)
 
 int check_linear_args(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale, int64_t m,
@@ -203,6 +462,79 @@ int check_linear_args(const void* x, int x_dtype, int64_t ldx, const void* packe
 }  // namespace sbq
 
 using namespace sbq;
+
+constexpr int64_t kSmallMaxRows = 128;  // up to this many activation rows: the 64-token kernel
+
+static int sm_count_w16() {
+    static int count[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!count[dev]) {
+        int c = 0;
+        cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+        count[dev] = c > 0 ? c : 148;
+    }
+    return count[dev];
+}
+
+static int gemm_small(const void* x, int64_t ldx, const void* packed, const float* scale, const float* bias, int64_t m,
+                      int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream) {
+    CUtensorMap mx, mw;
+    int st;
+    {
+        const uint64_t dims[2] = {(uint64_t)k, (uint64_t)m};
+        const uint64_t strides[1] = {(uint64_t)ldx * 2};
+        const uint32_t box[2] = {kWBK, kSTok};
+        st = encode_tmap(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+    }
+    {
+        const uint64_t kt = (uint64_t)ceil_div(k, kTileCols), nt = (uint64_t)ceil_div(n, kTileRows);
+        const uint64_t dims[4] = {64, 16, kt, nt};
+        const uint64_t strides[3] = {64, 1024, kt * 1024};
+        const uint32_t box[4] = {64, 16, 1, kWCh / 16};
+        st = encode_tmap(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, packed, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+        if (st) return st;
+    }
+    GemmSmallParams p{};
+    p.m = (int)m;
+    p.n = (int)n;
+    p.k = (int)k;
+    p.num_kb = (int)ceil_div(k, kWBK);
+    p.scale = scale;
+    p.bias = bias;
+    p.y = y;
+    p.ldy = ldy;
+    // K parts per tile: as many as fill the GPU's CTA slots (2 per SM) once, at most 8 (a portable
+    // cluster) and at least 2 k-blocks each
+    const int tiles = (int)(ceil_div(n, kWCh) * ceil_div(m, kSTok));
+    int parts = 2 * sm_count_w16() / tiles;
+    parts = parts < 1 ? 1 : (parts > 8 ? 8 : parts);
+    while (parts > 1 && p.num_kb / parts < 2) --parts;
+    p.parts = parts;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)ceil_div(n, kWCh), (unsigned)ceil_div(m, kSTok), (unsigned)parts);
+    cfg.blockDim = dim3(kWThreads);
+    cfg.dynamicSmemBytes = SmallSmem::kBytes;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = (unsigned)parts;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    if (y_dtype == SBQ_F16) {
+        cudaFuncSetAttribute(gemm_w8a16_small_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SmallSmem::kBytes);
+        e = cudaLaunchKernelEx(&cfg, gemm_w8a16_small_kernel<true>, mx, mw, p);
+    } else {
+        cudaFuncSetAttribute(gemm_w8a16_small_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SmallSmem::kBytes);
+        e = cudaLaunchKernelEx(&cfg, gemm_w8a16_small_kernel<false>, mx, mw, p);
+    }
+    if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "gemm_w8a16 (small batch) launch: %s", cudaGetErrorString(e));
+    return check_launch("gemm_w8a16_small");
+}
 
 extern "C" int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                               const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
@@ -226,6 +558,7 @@ extern "C" int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const voi
         st = encode_tmap(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, packed, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
         if (st) return st;
     }
+    if (m <= kSmallMaxRows) return gemm_small(x, ldx, packed, scale, bias, m, n, k, y, y_dtype, ldy, stream);
     GemmW16Params p{};
     p.m = (int)m;
     p.n = (int)n;

@@ -8,9 +8,9 @@ int check_linear_args(const void* x, int x_dtype, int64_t ldx, const void* packe
 
 using namespace sbq;
 
-// Rows of x above which the tensor-memory GEMM replaces the weight-streaming GEMV (which re-reads
-// the weight once per 16 rows).
-constexpr int64_t kGemmMinRows = 64;
+// Rows of x above which the tensor-memory GEMM (64-token tiles up to 128 rows, 256-token tiles
+// beyond) replaces the weight-streaming GEMV, which re-reads the weight once per 16 rows.
+constexpr int64_t kGemmMinRows = 32;
 
 extern "C" int sbq_linear_w8(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                              const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,

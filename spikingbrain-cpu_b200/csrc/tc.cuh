@@ -73,14 +73,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase of the given parity to complete; false (and the error word set) on timeout.
+// The wall clock is read only after 256 unsuccessful polls (each poll may suspend the thread for a
+// while), so a wait that completes soon costs no timer read.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = now_ns();
+    uint64_t t0 = 0;
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 0 && now_ns() - t0 > kWaitLimitNs) {
-            raise_error(SBQ_ERR_TIMEOUT);
-            return false;
+        if ((i & 255) == 0) {
+            if (t0 == 0) {
+                t0 = now_ns();
+            } else if (now_ns() - t0 > kWaitLimitNs) {
+                raise_error(SBQ_ERR_TIMEOUT);
+                return false;
+            }
         }
     }
 }

@@ -92,3 +92,22 @@ def test_prefill_mlp_through_gemm(sbq):
     o = [R.quantize_per_channel(w.numpy()) for w in ws]
     want = R.gated_mlp(x.float().numpy(), o[0], o[1], o[2], h_dtype=np.float16)
     assert R.rel_l2(y.cpu().numpy(), want) < REL_L2
+
+
+@pytest.mark.parametrize("m,n,k", [(64, 256, 4096), (100, 4096, 4096), (33, 1000, 12288), (17, 130, 320),
+                                   (128, 12288, 4096), (50, 4096, 12288)])
+@pytest.mark.parametrize("out", [torch.float32, torch.float16])
+def test_gemm_small_batch_split_k(sbq, m, n, k, out):
+    # up to 128 rows: 64-token tiles; few tiles: the K range is split over a thread-block cluster
+    # whose CTAs add their partial tiles through distributed shared memory in part order
+    w = sbq.workloads.float_weight(n, k, seed=m * 7 + n)
+    x = sbq.workloads.activation(m, k, seed=k + 3)
+    b = torch.randn(n) if n % 3 else None
+    q, s = R.quantize_per_channel(w.numpy())
+    mod = sbq.Int8Linear(w, b)
+    y1 = _gemm(sbq, mod, x.cuda(), torch.empty(m, n, dtype=out, device="cuda"))
+    y2 = _gemm(sbq, mod, x.cuda(), torch.empty(m, n, dtype=out, device="cuda"))
+    assert torch.equal(y1, y2)
+    want = R.int8_linear(x.float().numpy(), q, s, None if b is None else b.numpy())
+    assert R.rel_l2(y1.float().cpu().numpy(), want) < REL_L2
+    assert sbq._lib.load().sbq_check_device_error() == 0
