@@ -190,8 +190,9 @@ SBQ_API int sbq_peer_close(void* ptr);
  * wait_count is set (this rank's signal of the launch whose output x is), the launch first waits
  * until that signal has received wait_expected (= the number of ranks) more increments than at its
  * previous step.  wait_state: two zero-initialised words of this rank's memory used only by this
- * launch position.  Every wait is bounded (10 s, so ranks may drift apart on the host by that
- * much; then SBQ_ERR_TIMEOUT through sbq_check_device_error).  Ranks must issue the same launches
+ * launch position.  Every wait is bounded (wait_limit_ns, 10 s by default, so ranks may drift apart
+ * on the host by that much; then SBQ_ERR_TIMEOUT through sbq_check_device_error, and later waits
+ * are skipped until that error has been read).  Ranks must issue the same launches
  * in the same order. */
 #define SBQ_PEER_SIGNAL_COPIES 32
 #define SBQ_PEER_SIGNAL_BYTES 4096
@@ -203,12 +204,14 @@ typedef struct sbq_peer_group {
     const unsigned* wait_count;
     unsigned* wait_state;
     unsigned wait_expected;
+    unsigned long long wait_limit_ns; /* bound of the wait; 0 = 10 s */
 } sbq_peer_group;
 SBQ_API int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m,
                                    const sbq_peer_group* peers, void* stream);
 /* The same wait as a one-CTA launch: the end of a sharded step, before anything else reads the
- * last launch's gathered output. */
-SBQ_API int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned expected, void* stream);
+ * last launch's gathered output.  limit_ns: bound of the wait (0 = 10 s). */
+SBQ_API int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned expected, unsigned long long limit_ns,
+                          void* stream);
 
 /* A sharded decode program (see sbq_gemv_program_build): the stages' barriers span every rank, and
  * job i's output slice is stored to ydest[i * nranks + p] on every rank p (as mapped here; jobs[i].y

@@ -39,7 +39,7 @@ class PeerGroup(ctypes.Structure):
 
     _fields_ = [("nranks", ctypes.c_int), ("y", (ctypes.c_void_p * MAX_PEERS) * 8),
                 ("signal", ctypes.c_void_p * MAX_PEERS), ("done", ctypes.c_void_p), ("wait_count", ctypes.c_void_p),
-                ("wait_state", ctypes.c_void_p), ("wait_expected", ctypes.c_uint)]
+                ("wait_state", ctypes.c_void_p), ("wait_expected", ctypes.c_uint), ("wait_limit_ns", ctypes.c_ulonglong)]
 
 
 # name -> (restype, argtypes); kept in the order of include/sbq.h
@@ -70,7 +70,7 @@ SIGNATURES = {
     "sbq_peer_close": (_c_int, [_vp]),
     "sbq_gemv_w8_group_peer": (_c_int, [ctypes.POINTER(GemvJob), _c_int, _c_int, _c_i64, ctypes.POINTER(PeerGroup),
                                         _vp]),
-    "sbq_peer_wait": (_c_int, [_vp, _vp, ctypes.c_uint, _vp]),
+    "sbq_peer_wait": (_c_int, [_vp, _vp, ctypes.c_uint, ctypes.c_ulonglong, _vp]),
     "sbq_gemv_program_build_peer": (_c_int, [ctypes.POINTER(GemvJob), ctypes.POINTER(ctypes.c_int), _c_int, _c_int,
                                              _c_i64, ctypes.POINTER(_vp), _c_int, ctypes.POINTER(_vp), _vp, _sz]),
     "sbq_dyn_workspace_bytes": (_sz, [_c_i64, _c_i64, _c_int]),

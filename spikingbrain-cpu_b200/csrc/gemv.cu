@@ -98,6 +98,7 @@ struct PeerSync {
     unsigned* wait_state;          // [generation, arrivals] of this launch's wait (local)
     unsigned wait_expected;        // increments a signal copy receives per step (one per rank)
     int nranks;
+    unsigned long long wait_limit_ns;  // bound of the wait
 };
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
@@ -113,12 +114,13 @@ __device__ __forceinline__ void red_add_sys(unsigned* p, unsigned v) {
 // One thread per CTA: waits until its copy of the signal has received this step's `expected`
 // increments (targets grow by `expected` per step; state[0] counts completed steps of this
 // waiter), then records the CTA's arrival; the last CTA of the grid advances the generation for
-// the next step.  Bounded (ranks may drift apart on the host by up to kPeerWaitLimitNs): on expiry
+// the next step.  Bounded (by default ranks may drift apart on the host by up to kPeerWaitLimitNs): on expiry
 // the error word is set and the kernel carries on (its outputs are then invalid, the host sees
 // SBQ_ERR_TIMEOUT); after an earlier failure it does not wait at all.
 constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;
 
-__device__ __forceinline__ void peer_wait(const unsigned* signal, unsigned* state, unsigned expected) {
+__device__ __forceinline__ void peer_wait(const unsigned* signal, unsigned* state, unsigned expected,
+                                          unsigned long long limit_ns) {
     const unsigned* count = signal + (blockIdx.x % kSignalCopies) * kSignalStride;
     const unsigned gen = *reinterpret_cast<volatile unsigned*>(state);
     const unsigned target = (gen + 1u) * expected;
@@ -126,7 +128,7 @@ __device__ __forceinline__ void peer_wait(const unsigned* signal, unsigned* stat
         const uint64_t t0 = tc::now_ns();
         for (uint32_t i = 1; (int)(ld_acquire_sys(count) - target) < 0; ++i) {
             __nanosleep(64);
-            if ((i & 63) == 0 && tc::now_ns() - t0 > kPeerWaitLimitNs) {
+            if ((i & 63) == 0 && tc::now_ns() - t0 > limit_ns) {
                 tc::raise_error(SBQ_ERR_TIMEOUT);
                 break;
             }
@@ -721,7 +723,7 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2)
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
     if (PEER && ps.wait_count) {
         // x also holds the other ranks' slices, stored by their previous launch
-        if (threadIdx.x == 0) peer_wait(ps.wait_count, ps.wait_state, ps.wait_expected);
+        if (threadIdx.x == 0) peer_wait(ps.wait_count, ps.wait_state, ps.wait_expected, ps.wait_limit_ns);
         consumers_sync();
     }
     const bool ok = consume_units<XK, MT, PEER>(grp, ring, red, full, empty, meta, ps, PEER);
@@ -745,9 +747,10 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2)
 
 // Waits (one CTA) for a peer launch's outputs: the end of a sharded decode step, before the host
 // or another stream reads the gathered result.
-__global__ void peer_wait_kernel(const unsigned* count, unsigned* state, unsigned expected) {
+__global__ void peer_wait_kernel(const unsigned* count, unsigned* state, unsigned expected,
+                                 unsigned long long limit_ns) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (threadIdx.x == 0) peer_wait(count, state, expected);
+    if (threadIdx.x == 0) peer_wait(count, state, expected, limit_ns);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -1358,6 +1361,7 @@ extern "C" int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x
     ps.wait_count = pg.wait_count;
     ps.wait_state = pg.wait_state;
     ps.wait_expected = pg.wait_expected;
+    ps.wait_limit_ns = pg.wait_limit_ns ? pg.wait_limit_ns : kPeerWaitLimitNs;
     for (int p = 0; p < pg.nranks; ++p) {
         if (!pg.signal[p] || reinterpret_cast<uintptr_t>(pg.signal[p]) % 128)
             return set_error(SBQ_ERR_INVALID_ARGUMENT, "signal[%d] must be a 128-byte aligned device pointer", p);
@@ -1391,7 +1395,8 @@ extern "C" int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x
     return check_launch("gemv_w8_group_peer");
 }
 
-extern "C" int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned expected, void* stream) {
+extern "C" int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned expected, unsigned long long limit_ns,
+                             void* stream) {
     if (!count || !state || expected == 0) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null counter/state or zero expected");
     if (reinterpret_cast<uintptr_t>(count) % 128 || reinterpret_cast<uintptr_t>(state) % 8)
         return set_error(SBQ_ERR_ALIGNMENT, "signal must be 128-byte and state 8-byte aligned");
@@ -1404,7 +1409,7 @@ extern "C" int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned ex
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, peer_wait_kernel, count, state, expected);
+    cudaLaunchKernelEx(&cfg, peer_wait_kernel, count, state, expected, limit_ns ? limit_ns : kPeerWaitLimitNs);
     return check_launch("peer_wait");
 }
 

@@ -221,7 +221,7 @@ class PeerExchange:
             L.call("sbq_gemv_w8_group_peer", (L.GemvJob * 3)(*jobs), 3, code, m, ctypes.byref(pg), stream)
             cur = xn
         L.call("sbq_peer_wait", ctypes.c_void_p(self.base + self.cnt[-1][1]),
-               ctypes.c_void_p(self.base + self.final_state), w, stream)
+               ctypes.c_void_p(self.base + self.final_state), w, 0, stream)
         return cur
 
     def close(self) -> None:

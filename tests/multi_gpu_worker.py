@@ -4,7 +4,9 @@ Every rank builds the unsharded stack on its own GPU as the reference (the seede
 same on every rank), then the output-channel sharded stack with each exchange ("peer": GEMV outputs
 stored to every rank over NVLink; "nccl": all-gather), and checks that every sharded result is
 bit-identical to the unsharded one: eager decode (m = 1, 3, 16), the captured decode step replayed
-back to back on 24 inputs and called with device and host inputs, and an m = 80 prefill (NCCL gathers).  Exits non-zero on the first mismatch.
+back to back on 24 inputs and called with device and host inputs, and the decode program.  An
+m = 80 prefill (NCCL gathers) is checked against the int8 format's 1e-3 relative L2 instead: the
+sharded GEMMs split K differently.  Exits non-zero on any mismatch.
 """
 
 from __future__ import annotations
@@ -36,13 +38,21 @@ def main() -> int:
             d = (got.float() - want.float()).abs().max().item()
             failures.append("%s: max |diff| %g" % (name, d))
 
+    def check_close(name, got, want, rel=1e-3):
+        # prefill GEMMs split K by the shape of each rank's slice (fewer tiles per rank, more K parts),
+        # so sharded and unsharded sums are rounded differently: compare with the format's tolerance
+        g, w = got.float().cpu(), want.float().cpu()
+        err = ((g - w).norm() / w.norm()).item()
+        if not err < rel:
+            failures.append("%s: relative L2 %g" % (name, err))
+
     for exchange in ("peer", "nccl"):
         st = sbq.stack.ProjectionStack(group=dist.group.WORLD, exchange=exchange, **shape)
         for m in (1, 3, 16):
             x = sbq.workloads.activation(m, shape["hidden"], seed=20 + m, device=dev)
             check("%s eager m=%d" % (exchange, m), st(x).clone(), ref(x))
         x = sbq.workloads.activation(80, shape["hidden"], seed=3, device=dev)
-        check("%s prefill m=80" % exchange, st(x).clone(), ref(x))
+        check_close("%s prefill m=80" % exchange, st(x).clone(), ref(x))
         run = sbq.stack.CapturedStack(st, m=1)
         # back-to-back replays with a new input each: a stale slice from an earlier step would show
         xs = [sbq.workloads.activation(1, shape["hidden"], seed=100 + i, device=dev) for i in range(24)]

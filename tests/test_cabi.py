@@ -69,3 +69,25 @@ def test_package_surface(sbq):
         assert hasattr(sbq, name), name
     assert sbq.FORMATS == ("float32", "bfloat16", "float16", "int8", "int8-dyn")
     assert hasattr(sbq.stack, "ProjectionStack") and hasattr(sbq.stack, "CapturedStack")
+
+
+def test_peer_group_arguments_rejected_on_the_host(sbq):
+    """Argument checks of the sharded launch run before any CUDA call (no GPU needed)."""
+    import ctypes
+
+    L = sbq._lib
+    lib = L.load()
+    job = L.GemvJob(16, 64, 256, 256, None, None, None, 16, 64, 512, L.F32, 16)
+    jobs = (L.GemvJob * 1)(job)
+    assert lib.sbq_gemv_w8_group_peer(jobs, 1, L.F16, 1, None, None) == L.ERR_INVALID_ARGUMENT
+    pg = L.PeerGroup()
+    pg.nranks = 0
+    assert lib.sbq_gemv_w8_group_peer(jobs, 1, L.F16, 1, ctypes.byref(pg), None) == L.ERR_INVALID_ARGUMENT
+    pg.nranks = 9
+    assert lib.sbq_gemv_w8_group_peer(jobs, 1, L.F16, 1, ctypes.byref(pg), None) == L.ERR_INVALID_ARGUMENT
+    pg.nranks = 1
+    pg.wait_count = 4096
+    pg.wait_state = None
+    assert lib.sbq_gemv_w8_group_peer(jobs, 1, L.F16, 1, ctypes.byref(pg), None) == L.ERR_INVALID_ARGUMENT
+    assert lib.sbq_peer_wait(None, None, 1, 0, None) == L.ERR_INVALID_ARGUMENT
+    assert lib.sbq_peer_wait(4100, 4096, 1, 0, None) == L.ERR_ALIGNMENT
