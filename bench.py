@@ -39,6 +39,11 @@ METRIC = "int8 decode GEMV HBM GB/s and prefill GEMM TFLOPS, % of B200 roofline"
 FALLBACK_HBM_GBS = 6650.0
 
 
+SPEC_HBM_GBS = 8000.0       # B200 HBM3e, nominal
+SPEC_F16_TFLOPS = 2250.0    # dense fp16/bf16 tensor, nominal
+SPEC_I8_TOPS = 4500.0       # dense int8 tensor, nominal
+
+
 def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -238,7 +243,8 @@ def kernel_cases(sbq, dev, stream, steps: int, warmup: int, which=("gemv", "mlp"
         ms = _graph_time(f, stream, max(20, steps // 10), warmup) / copies
         b = n * k + 4 * n + 2 * k + 4 * n
         out["cfg0_gemv"] = {"us": round(ms * 1e3, 3), "gbs": round(b / ms / 1e6, 1),
-                            "frac_hbm": round(b / ms / 1e6 / pk["hbm_gbs"], 4), "bytes": b}
+                            "frac_hbm": round(b / ms / 1e6 / pk["hbm_gbs"], 4),
+                            "frac_hbm_spec": round(b / ms / 1e6 / SPEC_HBM_GBS, 4), "bytes": b}
         del ws
 
     if "mlp" in which:  # configuration 1: fused gate/up + down at m in {1, 4, 16}
@@ -261,7 +267,8 @@ def kernel_cases(sbq, dev, stream, steps: int, warmup: int, which=("gemv", "mlp"
             ms = _graph_time(f, stream, max(20, steps // 10), warmup) / 2
             b = 3 * n * k + 12 * n + 4 * k + 2 * m * k + 4 * m * n + 4 * m * k
             res[str(m)] = {"us": round(ms * 1e3, 3), "gbs": round(b / ms / 1e6, 1),
-                           "frac_hbm": round(b / ms / 1e6 / pk["hbm_gbs"], 4)}
+                           "frac_hbm": round(b / ms / 1e6 / pk["hbm_gbs"], 4),
+                           "frac_hbm_spec": round(b / ms / 1e6 / SPEC_HBM_GBS, 4)}
         out["cfg1_mlp"] = res
         del gs, us_, ds
 
@@ -278,7 +285,8 @@ def kernel_cases(sbq, dev, stream, steps: int, warmup: int, which=("gemv", "mlp"
         ms = _graph_time(f, stream, max(20, steps // 10), warmup)
         fl = 2 * m * n * k
         out["cfg2_prefill_gemm"] = {"us": round(ms * 1e3, 2), "tflops": round(fl / ms / 1e9, 1),
-                                    "frac_bf16_peak": round(fl / ms / 1e9 / pk["bf16_tflops"], 4)}
+                                    "frac_bf16_peak": round(fl / ms / 1e9 / pk["bf16_tflops"], 4),
+                                    "frac_f16_spec": round(fl / ms / 1e9 / SPEC_F16_TFLOPS, 4)}
 
     if "dyn" in which:  # configuration 3: int8-dyn, m=512, k=n=4096
         m, k, n = 512, W.HIDDEN, W.HIDDEN
@@ -295,7 +303,7 @@ def kernel_cases(sbq, dev, stream, steps: int, warmup: int, which=("gemv", "mlp"
         ms = _graph_time(f, stream, max(20, steps // 10), warmup)
         ops = 2 * m * n * k
         out["cfg3_dyn"] = {"us": round(ms * 1e3, 2), "tops": round(ops / ms / 1e9, 1),
-                           "frac_int8_spec_4500": round(ops / ms / 1e9 / 4500.0, 4)}
+                           "frac_int8_spec_4500": round(ops / ms / 1e9 / SPEC_I8_TOPS, 4)}
     return out
 
 
@@ -310,7 +318,8 @@ def stack_cases(sbq, stack, dev, stream, warmup: int) -> dict:
         x = sbq.workloads.activation(m, stack.hidden, seed=m, device=dev)
         ms = _graph_time(lambda: stack(x), stream, 10, warmup)
         out["decode_b%d" % m] = {"ms": round(ms, 3), "gbs": round(total / ms / 1e6, 1),
-                                 "frac_hbm": round(total / ms / 1e6 / peaks()["hbm_gbs"], 4)}
+                                 "frac_hbm": round(total / ms / 1e6 / peaks()["hbm_gbs"], 4),
+                                 "frac_hbm_spec": round(total / ms / 1e6 / SPEC_HBM_GBS, 4)}
     m = 8192
     x = sbq.workloads.activation(m, stack.hidden, seed=m, device=dev)
     with torch.cuda.stream(stream):
@@ -326,6 +335,7 @@ def stack_cases(sbq, stack, dev, stream, warmup: int) -> dict:
     fl = 2.0 * m * total
     out["prefill_8192"] = {"ms": round(ms, 2), "tflops": round(fl / ms / 1e9, 1),
                            "frac_bf16_peak": round(fl / ms / 1e9 / peaks()["bf16_tflops"], 4),
+                           "frac_f16_spec": round(fl / ms / 1e9 / SPEC_F16_TFLOPS, 4),
                            "note": "per-projection GEMMs plus torch SiLU*mul between gate/up and down"}
     return out
 
@@ -492,6 +502,7 @@ def main() -> None:
             "roofline": {"kernel": "gemv_w8_kernel (grouped decode GEMV; every launch of the timed step)",
                          "bound": "hbm", "achieved": round(per_gpu, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(per_gpu / pk["hbm_gbs"], 4), "peak_source": pk["source"],
+                         "frac_of_spec_8000": round(per_gpu / SPEC_HBM_GBS, 4),
                          "per": "GPU" if world > 1 else "job",
                          "bytes_per_launch": total_bytes // world // launches,
                          "us_per_launch": round(ms * 1e3 / launches, 3),

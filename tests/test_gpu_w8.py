@@ -221,3 +221,59 @@ def test_split_k_fused_gateup(sbq, m):
     g, u = (R.int8_linear(x.float().numpy(), *R.quantize_per_channel(w.numpy())) for w in (wg, wu))
     want = g / (1.0 + np.exp(-g)) * u
     assert R.rel_l2(_np(h1), want) < REL_L2
+
+
+# The checkpoint's projection shapes (hidden 2560, 32 heads of 128, 8 key/value heads, MLP 9728,
+# vocabulary 151936; spikingbrain_cpu/model.py:232-301 and the tied head, loader.py:94), as [N, K].
+REAL_SHAPES = [(9728, 2560), (2560, 9728), (4096, 2560), (1024, 2560), (2560, 4096), (128, 2560), (4096, 128),
+               (64, 2560), (4, 2560)]
+
+
+@pytest.mark.parametrize("n,k", REAL_SHAPES)
+@pytest.mark.parametrize("m", [1, 7, 100])
+def test_real_model_shapes_vs_oracle(sbq, n, k, m):
+    # fp32 activations, as the reference's model passes them (quant.py:47)
+    w = sbq.workloads.float_weight(n, k, seed=n * 7 + k)
+    x = sbq.workloads.activation(m, k, seed=m + n, dtype=torch.float32)
+    q, s = R.quantize_per_channel(w.numpy())
+    y = sbq.Int8Linear(w, None)(x.cuda())
+    assert R.rel_l2(_np(y), R.int8_linear(x.numpy(), q, s)) < 2e-5
+
+
+def test_tied_head_shape(sbq):
+    # the [151936 x 2560] int8 head at decode, checked on the first and last 1024 rows
+    n, k = 151936, 2560
+    w = sbq.workloads.float_weight(n, k, seed=9)
+    x = sbq.workloads.activation(1, k, seed=10)
+    y = _np(sbq.Int8Linear(w, None)(x.cuda()))
+    for rows in (slice(0, 1024), slice(n - 1024, n)):
+        q, s = R.quantize_per_channel(w[rows].numpy())
+        assert R.rel_l2(y[:, rows], R.int8_linear(x.float().numpy(), q, s)) < REL_L2
+
+
+def test_shared_input_projection_group(sbq):
+    # sse_q/k/v and swa_q/k/v of one hybrid block read the same x (model.py:317-321, :363-365): one
+    # grouped launch gives what six separate calls give
+    from importlib import import_module
+    quant = import_module("spikingbrain-cpu_b200.quant")
+    hid = 2560
+    mods = [sbq.Int8Linear(sbq.workloads.float_weight(n, hid, seed=90 + i), None)
+            for i, n in enumerate((4096, 4096, 4096, 4096, 1024, 1024))]
+    x = sbq.workloads.activation(1, hid, seed=99).cuda()
+    outs = [torch.empty(1, mod.out_features, device="cuda") for mod in mods]
+    quant.gemv_group([mod.gemv_job(x, o) for mod, o in zip(mods, outs)], x.dtype, 1, x.device)
+    for mod, o in zip(mods, outs):
+        assert torch.equal(o, mod(x))
+
+
+def test_lora_projection_pair(sbq):
+    # lora_q_proj = Linear(2560 -> 128) then Linear(128 -> 4096) (model.py:287)
+    a = sbq.workloads.float_weight(128, 2560, seed=77)
+    b = sbq.workloads.float_weight(4096, 128, seed=78)
+    x = sbq.workloads.activation(3, 2560, seed=79, dtype=torch.float32)
+    la, lb = sbq.Int8Linear(a, None), sbq.Int8Linear(b, None)
+    y = lb(la(x.cuda()))
+    qa, sa = R.quantize_per_channel(a.numpy())
+    qb, sb = R.quantize_per_channel(b.numpy())
+    want = R.int8_linear(R.int8_linear(x.numpy(), qa, sa).astype(np.float32), qb, sb)
+    assert R.rel_l2(_np(y), want) < 1e-4
