@@ -266,7 +266,10 @@ struct GemvSmemSize {
     static constexpr int kRed = 2 * kGemvWarps * MT * 16 * 9 * 4;  // per-warp partial sums of two tiles
     static constexpr int kBytes = kRingBytes + kRed + 2 * kMaxStages * 8;  // 3 CTAs per SM at MT = 1
 };
-constexpr int kCtasPerSm = 3;  // CTAs a launch is sized for (three fit per SM)
+#ifndef SBQ_GEMV_CTAS_PER_SM
+#define SBQ_GEMV_CTAS_PER_SM 3
+#endif
+constexpr int kCtasPerSm = SBQ_GEMV_CTAS_PER_SM;  // CTAs a launch is sized for (three fit per SM)
 
 // Named barrier 1 over the consumer warps.
 __device__ __forceinline__ void consumers_sync() {
@@ -698,7 +701,7 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
 }
 
 template <int XK, int MT, bool PEER>
-__global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2)
+__global__ void __launch_bounds__(kGemvThreads, MT == 1 ? kCtasPerSm : 2)
     gemv_w8_kernel(const __grid_constant__ GemvGroup grp, const __grid_constant__ PeerSync ps) {
     extern __shared__ __align__(128) uint8_t ring[];
     float* red = reinterpret_cast<float*>(ring + kRingBytes);
@@ -808,7 +811,7 @@ __device__ __forceinline__ unsigned* prog_flag(uint8_t* sync, int st, int copy) 
 }
 
 template <int XK, bool PEER>
-__global__ void __launch_bounds__(kGemvThreads, 3) gemv_program_kernel(const __grid_constant__ ProgParams p) {
+__global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_program_kernel(const __grid_constant__ ProgParams p) {
     constexpr int MT = 1;
     extern __shared__ __align__(128) uint8_t ring[];
     float* red = reinterpret_cast<float*>(ring + kRingBytes);
