@@ -28,6 +28,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstring>
 #include <mutex>
 #include <queue>
 #include <unordered_map>
@@ -172,18 +173,18 @@ struct XFrag {
 
 // Loads the 16 activation values lane (g, c) needs for k0 .. k0 + 15 of row `row` as MMA B fragments
 // b[s][0..1] (s = the four k16 steps).  Rows beyond m (or spans beyond k) read as zero.
-// `coh`: x is in global memory and was written by other GPUs during this launch (L2-only loads).
+// x written earlier in the same launch (or by other GPUs) is read with these ordinary loads too: the
+// reading CTA has passed an acquire (one thread) and a CTA barrier since, the grid-barrier pattern.
 template <int XK>
-__device__ __forceinline__ void load_x(XFrag<XK>& f, const void* xv, int64_t ldx, int row, int m, int64_t k0, int k,
-                                       bool coh = false) {
+__device__ __forceinline__ void load_x(XFrag<XK>& f, const void* xv, int64_t ldx, int row, int m, int64_t k0, int k) {
     const uint8_t* x = static_cast<const uint8_t*>(xv);
     const bool ok = row < m && k0 < k;
     if (XK == kXF16 || XK == kXBF16) {
         uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
         if (ok) {
             const uint4* q = reinterpret_cast<const uint4*>(x + ((int64_t)row * ldx + k0) * 2);
-            v0 = coh ? __ldcg(q) : q[0];
-            v1 = coh ? __ldcg(q + 1) : q[1];
+            v0 = q[0];
+            v1 = q[1];
         }
         f.b[0][0] = v0.x; f.b[0][1] = v0.y; f.b[1][0] = v0.z; f.b[1][1] = v0.w;
         f.b[2][0] = v1.x; f.b[2][1] = v1.y; f.b[3][0] = v1.z; f.b[3][1] = v1.w;
@@ -195,7 +196,7 @@ __device__ __forceinline__ void load_x(XFrag<XK>& f, const void* xv, int64_t ldx
             const uint4* q = reinterpret_cast<const uint4*>(x + ((int64_t)row * ldx + k0) * 4);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const uint4 t = coh ? __ldcg(q + i) : q[i];
+                const uint4 t = q[i];
                 v[4 * i + 0] = __uint_as_float(t.x);
                 v[4 * i + 1] = __uint_as_float(t.y);
                 v[4 * i + 2] = __uint_as_float(t.z);
@@ -290,153 +291,6 @@ __device__ __forceinline__ int consumers_sync_and(int v) {
     return r;
 }
 
-// A CTA's work on one job is a run of consecutive 16-row tiles [t0, t1): a contiguous byte range of
-// the packed weight (and of the up weight when NMAT = 2).  A chunk holds C tiles of each matrix; the
-// consumer warps are split evenly over the matrices (8 over one, or 4 on gate and 4 on up), each
-// warp taking one tile of its matrix per chunk.  `ci` counts chunks through the ring across runs,
-// so a CTA can stream several runs back to back (the decode program kernel does).
-
-// Producer (one thread): streams the run's chunks.  False if a wait timed out.
-template <int NMAT>
-__device__ __forceinline__ bool produce_run(const GemvJob& jb, int t0, int t1, uint8_t* ring, uint64_t* full,
-                                            uint64_t* empty, uint32_t& ci) {
-    constexpr int S = kMaxStages;
-    constexpr int kStageBytes = kChunkTiles * kTileBytes;
-    const int C = jb.chunk_tiles;
-    const int nchunks = (t1 - t0) * (jb.kt_total / C);
-    const uint32_t bytes = (uint32_t)C * kTileBytes;
-    const int8_t* src0 = jb.w0 + (int64_t)t0 * jb.kt_total * kTileBytes;
-    const int8_t* src1 = NMAT == 2 ? jb.w1 + (int64_t)t0 * jb.kt_total * kTileBytes : nullptr;
-    for (int i = 0; i < nchunks; ++i, ++ci) {
-        const int s = ci % S;
-        if (!tc::mbar_wait(&empty[s], ((ci / S) & 1) ^ 1)) return false;
-        uint8_t* dst = ring + s * kStageBytes;
-        tc::mbar_arrive_expect_tx(&full[s], bytes * NMAT);
-        tc::bulk_load(dst, src0 + (int64_t)i * bytes, bytes, &full[s]);
-        if (NMAT == 2) tc::bulk_load(dst + bytes, src1 + (int64_t)i * bytes, bytes, &full[s]);
-    }
-    return true;
-}
-
-// Consumers (8 warps): the run's chunks, a fixed-order reduction and the epilogue per tile.
-// Returns false (warp-uniformly) if a wait timed out.
-// PEER: every output is stored to each rank's copy (ps->y[jidx][p]) instead of jb.y.
-template <int XK, int MT, int NMAT, bool PEER = false>
-__device__ __forceinline__ bool consume_run(const GemvJob& jb, int t0, int t1, const void* xsrc, int64_t xld,
-                                            uint8_t* ring, float* red, uint64_t* full, uint64_t* empty,
-                                            uint32_t& ci, const PeerSync* ps = nullptr, int jidx = 0,
-                                            bool xcoh = false) {
-    constexpr int S = kMaxStages;
-    constexpr int kStageBytes = kChunkTiles * kTileBytes;  // 8 KiB: C tiles of each of the NMAT matrices
-    constexpr int WPM = kGemvWarps / NMAT;                   // warps per matrix
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int C = jb.chunk_tiles;                            // tiles per chunk and matrix (<= WPM)
-    const int cpt = jb.kt_total / C;                         // chunks per tile
-    const int nchunks = (t1 - t0) * cpt;
-    const int g = lane >> 2, c = lane & 3;
-    const int mat = warp / WPM, slot = warp % WPM;  // this warp's matrix and tile within a chunk
-    const bool mine = slot < C;
-    const int mat_off = mat * C * kTileBytes;
-    constexpr int kEntries = MT * 8 * 16;  // (row, token) outputs of one tile, one per epilogue thread
-    constexpr int kRedFloats = kGemvWarps * MT * 16 * 9;
-    float acc[MT][4];
-    float sc0 = 0.0f, sc1 = 0.0f, bz = 0.0f;  // the epilogue thread's scale(s) and bias, loaded early
-    int vt = 0;
-    for (int i = 0, j = 0; i < nchunks; ++i, ++ci) {
-        if (j == 0) {
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
-            // this tile's epilogue runs on warp (tile % 8) onwards: its threads fetch the scales now
-            const int tile_seq = i / cpt;
-            vt = (threadIdx.x + kGemvWarps * 32 - (tile_seq % kGemvWarps) * 32) % (kGemvWarps * 32);
-            const int n = (t0 + tile_seq) * 16 + (vt & 15);
-            if (vt < kEntries && n < jb.n) {
-                sc0 = jb.s0[n];
-                if (NMAT == 2) sc1 = jb.s1[n];
-                if (NMAT == 1 && jb.bias) bz = jb.bias[n];
-            }
-        }
-        const int s = ci % S;
-        XFrag<XK> xf[MT];
-        if (mine) {
-            const int64_t k0 = (int64_t)(j * C + slot) * kTileCols + 16 * c;
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xsrc, xld, 8 * mt + g, jb.m, k0, jb.k, xcoh);
-        }
-        // warp-uniform wait (the __syncwarp below must see every lane)
-        if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (ci / S) & 1))) return false;
-        if (mine) {
-            const uint8_t* t = ring + s * kStageBytes + mat_off + slot * kTileBytes + lane * 16;
-            const uint4 wa = *reinterpret_cast<const uint4*>(t);
-            const uint4 wb = *reinterpret_cast<const uint4*>(t + 512);
-            tile_mma<XK, MT>(acc, wa, wb, xf);
-        }
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&empty[s]);
-        if (++j < cpt) continue;
-        j = 0;
-
-        // ---- tile complete: the warps' partial sums go to a double-buffered reduction area, one
-        // barrier, then the tile's epilogue threads reduce (fixed order), scale and store while the
-        // other warps go on with the next tile.  A buffer is written again two tiles later, after
-        // the next tile's barrier, which its epilogue threads reach only when done reading.
-        const int tile_seq = i / cpt;
-        const int nt = t0 + tile_seq;
-        float* rb = red + (tile_seq & 1) * kRedFloats;
-#define SBQ_RED(w, mt, r, col) rb[(((w) * MT + (mt)) * 16 + (r)) * 9 + (col)]
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-            SBQ_RED(warp, mt, g, 2 * c) = acc[mt][0];
-            SBQ_RED(warp, mt, g, 2 * c + 1) = acc[mt][1];
-            SBQ_RED(warp, mt, g + 8, 2 * c) = acc[mt][2];
-            SBQ_RED(warp, mt, g + 8, 2 * c + 1) = acc[mt][3];
-        }
-        consumers_sync();
-        if (vt < kEntries) {
-            const int r = vt & 15, tok = vt >> 4, mt = tok >> 3, col = tok & 7;
-            const int n = nt * 16 + r;
-            if (n < jb.n && tok < jb.m) {
-                float v[NMAT];
-#pragma unroll
-                for (int a = 0; a < NMAT; ++a) {
-                    float sum = 0.0f;
-#pragma unroll
-                    for (int w = 0; w < WPM; ++w) sum += SBQ_RED(a * WPM + w, mt, r, col);
-                    v[a] = sum;
-                }
-                float out;
-                if (NMAT == 1) {
-                    out = v[0] * sc0;
-                    if (jb.bias) out += bz;
-                } else {
-                    const float gv = v[0] * sc0;
-                    const float uv = v[1] * sc1;
-                    out = gv / (1.0f + expf(-gv)) * uv;
-                }
-                const int64_t idx = (int64_t)tok * jb.ldy + n;
-                if (PEER) {
-                    // consecutive threads store consecutive rows: one coalesced NVLink write per rank
-                    for (int p = 0; p < ps->nranks; ++p) {
-                        if (jb.out_f16)
-                            static_cast<__half*>(ps->y[jidx][p])[idx] = __float2half_rn(out);
-                        else
-                            static_cast<float*>(ps->y[jidx][p])[idx] = out;
-                    }
-                } else if (jb.out_f16) {
-                    static_cast<__half*>(jb.y)[idx] = __float2half_rn(out);
-                } else {
-                    static_cast<float*>(jb.y)[idx] = out;
-                }
-            }
-        }
-#undef SBQ_RED
-    }
-    consumers_sync();  // the last epilogue has read its buffer (a later run starts over at buffer 0)
-    return true;
-}
-
 // ---------------------------------------------------------------------------------------------
 // Grouped launch with dynamic work: the units of a launch are the 16-row tiles of all its jobs
 // (largest tiles first), claimed one at a time from a per-launch counter by each CTA's producer.
@@ -460,11 +314,12 @@ static __device__ unsigned g_split_count[kSplitRegions][kSplitTiles];
 
 // Producer (one thread).  Claims the next unit while the last ring-full of the current one is
 // still to be issued, so the claim's latency is hidden.  False if a wait timed out.
-__device__ __forceinline__ bool produce_units(const GemvGroup& grp, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                                              int4* meta) {
+// `claim`: the work counter pair; `ci`: ring position (continues across calls, the decode program
+// streams one group per stage through the same ring).  The end marker takes a ring slot too.
+__device__ __forceinline__ bool produce_units(const GemvGroup& grp, unsigned* claim, uint8_t* ring, uint64_t* full,
+                                              uint64_t* empty, int4* meta, uint32_t& ci) {
     constexpr int S = kMaxStages;
     constexpr int kStageBytes = kChunkTiles * kTileBytes;
-    uint32_t ci = 0;
     int u = blockIdx.x;  // the first unit of every CTA is its own; later ones are claimed
     for (;;) {
         if (u >= grp.total_units) {
@@ -472,6 +327,7 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, uint8_t* rin
             if (!tc::mbar_wait(&empty[s], ((ci / S) & 1) ^ 1)) return false;
             meta[s] = make_int4(-1, 0, 0, 0);
             tc::mbar_arrive(&full[s]);  // the end marker: a phase with no bytes
+            ++ci;
             return true;
         }
         int j = 0;
@@ -487,7 +343,7 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, uint8_t* rin
         const int claim_at = i1 - i0 > S ? i1 - S : i0;
         int next = 0;
         for (int i = i0; i < i1; ++i, ++ci) {
-            if (i == claim_at) next = (int)(gridDim.x + atomicAdd(grp.claim, 1u));
+            if (i == claim_at) next = (int)(gridDim.x + atomicAdd(claim, 1u));
             const int s = ci % S;
             if (!tc::mbar_wait(&empty[s], ((ci / S) & 1) ^ 1)) return false;
             meta[s] = make_int4(j | (part << 8), tile, i, i1 - i0);
@@ -500,25 +356,33 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, uint8_t* rin
     }
 }
 
-// Consumers (8 warps): per unit, its chunks, the fixed-order reduction and the epilogue (as
-// consume_run; the job and the warp split are read once per unit from the first chunk's stage).
-// `xcoh`: x was written by other GPUs during this step (L2-only loads).  False (warp-uniformly)
-// on a timeout.
+// Consumers (8 warps): per unit, its chunks (each warp takes one 1 KiB tile of each chunk: two
+// conflict-free 16-byte shared loads per lane, int8 -> fp16/bf16 in registers, m16n8k16 MMAs with
+// the activation rows as the n dimension), then the fixed-order reduction and the epilogue.  The
+// job and the warp split are read once per unit from the first chunk's stage.
+// False (warp-uniformly) on a timeout.
+// `ci` / `units`: ring position and units done so far (both continue across calls).
 template <int XK, int MT, bool PEER>
 __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* ring, float* red, uint64_t* full,
-                                              uint64_t* empty, const int4* meta, const PeerSync& ps, bool xcoh) {
+                                              uint64_t* empty, const int4* meta, const PeerSync& ps,
+                                              uint32_t& ci, int& units) {
     constexpr int S = kMaxStages;
     constexpr int kStageBytes = kChunkTiles * kTileBytes;
     constexpr int kEntries = MT * 8 * 16;
     constexpr int kRedFloats = kGemvWarps * MT * 16 * 9;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
-    uint32_t ci = 0;
-    for (int units = 0;; ++units) {
+    for (;; ++units) {
         int s = ci % S;
         if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (ci / S) & 1))) return false;
         const int4 md = meta[s];
-        if (md.x < 0) break;
+        if (md.x < 0) {
+            // the end marker: release its slot (the producer may go on with another group)
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&empty[s]);
+            ++ci;
+            break;
+        }
         const int j = md.x & 0xff, part = md.x >> 8, tile = md.y, i0 = md.z, cpt = md.w;
         const GemvJob& jb = grp.job[j];
         const bool two = jb.w1 != nullptr;
@@ -549,7 +413,7 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
         if (mine) {
             const int64_t k0 = (int64_t)(i0 * C + slot) * kTileCols + 16 * c;
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xj, ldx, 8 * mt + g, xm, k0, xk, xcoh);
+            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xj, ldx, 8 * mt + g, xm, k0, xk);
         }
         for (int i = 0;;) {
             if (mine) {
@@ -567,7 +431,7 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
             if (mine) {
                 const int64_t k0 = (int64_t)((i0 + i) * C + slot) * kTileCols + 16 * c;
 #pragma unroll
-                for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xj, ldx, 8 * mt + g, xm, k0, xk, xcoh);
+                for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xj, ldx, 8 * mt + g, xm, k0, xk);
             }
             s = ci % S;
             if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (ci / S) & 1))) return false;
@@ -720,7 +584,8 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? kCtasPerSm : 2)
     // the next launch may start its own weight stream now (it waits for this grid before reading x)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (warp == kGemvWarps) {
-        if (lane == 0 && !produce_units(grp, ring, full, empty, meta)) tc::raise_error(SBQ_ERR_TIMEOUT);
+        uint32_t pci = 0;
+        if (lane == 0 && !produce_units(grp, grp.claim, ring, full, empty, meta, pci)) tc::raise_error(SBQ_ERR_TIMEOUT);
         return;
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
@@ -729,7 +594,9 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? kCtasPerSm : 2)
         if (threadIdx.x == 0) peer_wait(ps.wait_count, ps.wait_state, ps.wait_expected, ps.wait_limit_ns);
         consumers_sync();
     }
-    const bool ok = consume_units<XK, MT, PEER>(grp, ring, red, full, empty, meta, ps, PEER);
+    uint32_t ci = 0;
+    int units = 0;
+    const bool ok = consume_units<XK, MT, PEER>(grp, ring, red, full, empty, meta, ps, ci, units);
     if (!consumers_sync_and(ok) && threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
     if (warp == 0) {
         // count out; the last CTA resets the launch's counter for the next launch that uses it
@@ -760,31 +627,25 @@ __global__ void peer_wait_kernel(const unsigned* count, unsigned* state, unsigne
 // Decode program: a whole sequence of grouped stages in one persistent cooperative launch.
 //
 // Stage s may read what stages < s wrote (on this rank and, in a sharded program, on every rank).
-// Every CTA owns at most one run per stage.  When its consumers finish that run (or have none) the
-// CTA counts itself in on the stage's arrival counter (GPU-scope fence + 64-bit atomic; the
-// counters only grow, so a run's epoch E is the first return value / grid size and nothing is ever
-// cleared); the last CTA of the stage on each rank adds 1 to the stage's flag on every rank, in
-// 32 copies on separate L2 lines.  Before stage s + 1 a CTA's consumers poll their copy (with
-// backoff) until it reaches (E + 1) * ranks.  The producer never waits on a stage: it streams the
-// next stages' weights (which depend on nothing) as fast as the ring drains, so HBM stays busy
-// across the barriers.  All CTAs are co-resident (cooperative launch), every wait is bounded, and
-// activations are read with L2-only loads (they were written during this launch).
+// Each stage is a grouped launch's work (dynamic units, K parts), streamed through the CTA's ring
+// by its producer, which moves on to the next stage's units as soon as the current stage's are all
+// claimed: the weight stream never waits for a stage barrier.  When its consumers have finished
+// the stage's units (its end marker), the CTA counts itself in on the stage's arrival counter
+// (GPU-scope fence + 64-bit atomic; the counters only grow, so a run's epoch E is the first return
+// value / grid size); the last CTA of the stage on each rank resets the stage's claim counter and
+// adds 1 to the stage's flag on every rank, in 32 copies on separate L2 lines.  Before stage s + 1
+// a CTA's consumers poll their copy (with backoff) until it reaches (E + 1) * ranks.  All CTAs are
+// co-resident (cooperative launch) and every wait is bounded.
 // ---------------------------------------------------------------------------------------------
-struct ProgItem {
-    int job;
-    int t0;
-    int t1;
-};
-
 struct ProgStage {
-    GemvJob job[kMaxJobs];
+    GemvGroup grp;  // the stage's jobs, planned as a grouped launch (claim counter: in the sync region)
     PeerSync peer;  // sharded program: output destinations on every rank (y, nranks)
-    int njobs;
-    int pad;
 };
 
-// Synchronisation region per stage: one line for the arrival counter, 32 lines of flag copies.
-constexpr int kSyncStageBytes = 128 + kSignalCopies * 128;
+// Synchronisation region per stage: the arrival counter, 32 lines of flag copies, the claim pair.
+constexpr int kSyncFlagOff = 128;
+constexpr int kSyncClaimOff = 128 + kSignalCopies * 128;
+constexpr int kSyncStageBytes = kSyncClaimOff + 128;
 
 // Header at the start of a program buffer (256 bytes).
 struct ProgHeader {
@@ -801,13 +662,16 @@ static_assert(sizeof(ProgHeader) <= 256, "program header");
 struct ProgParams {
     const ProgHeader* hdr;
     const ProgStage* stages;
-    const ProgItem* items;             // [stage][cta]
     int nstages;
     uint8_t* sync;                     // this rank's synchronisation region
 };
 
 __device__ __forceinline__ unsigned* prog_flag(uint8_t* sync, int st, int copy) {
-    return reinterpret_cast<unsigned*>(sync + (size_t)st * kSyncStageBytes + 128 + copy * 128);
+    return reinterpret_cast<unsigned*>(sync + (size_t)st * kSyncStageBytes + kSyncFlagOff + copy * 128);
+}
+
+__device__ __forceinline__ unsigned* prog_claim(uint8_t* sync, int st) {
+    return reinterpret_cast<unsigned*>(sync + (size_t)st * kSyncStageBytes + kSyncClaimOff);
 }
 
 template <int XK, bool PEER>
@@ -817,6 +681,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_program_kernel(
     float* red = reinterpret_cast<float*>(ring + kRingBytes);
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRingBytes + GemvSmemSize<MT>::kRed);
     uint64_t* empty = full + kMaxStages;
+    __shared__ int4 meta[kMaxStages];
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nctas = gridDim.x, cta = blockIdx.x;
@@ -829,27 +694,25 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_program_kernel(
         abort_flag = 0;
     }
     __syncthreads();
-    uint32_t ci = 0;
     if (warp == kGemvWarps) {
         if (lane == 0) {
-            for (int st = 0; st < p.nstages; ++st) {
-                const ProgItem it = p.items[(int64_t)st * nctas + cta];
-                if (it.t1 <= it.t0) continue;
-                const GemvJob jb = p.stages[st].job[it.job];
-                const bool ok = jb.w1 ? produce_run<2>(jb, it.t0, it.t1, ring, full, empty, ci)
-                                      : produce_run<1>(jb, it.t0, it.t1, ring, full, empty, ci);
-                if (!ok) break;
-            }
+            uint32_t pci = 0;
+            for (int st = 0; st < p.nstages; ++st)
+                if (!produce_units(p.stages[st].grp, prog_claim(p.sync, st), ring, full, empty, meta, pci)) {
+                    tc::raise_error(SBQ_ERR_TIMEOUT);
+                    break;
+                }
         }
         return;
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the first stage's x comes from the previous kernel
     const int nranks = PEER ? p.hdr->nranks : 1;
-    constexpr bool peer = PEER;
-    const uint64_t limit = peer ? kPeerWaitLimitNs : tc::kWaitLimitNs;
+    const uint64_t limit = PEER ? kPeerWaitLimitNs : tc::kWaitLimitNs;
     unsigned long long epoch = 0;  // thread 0: this run's epoch, from its first arrival
+    uint32_t ci = 0;
+    int units = 0;
     for (int st = 0; st <= p.nstages; ++st) {
-        if (st > 0 && (st < p.nstages || (peer && cta == 0))) {
+        if (st > 0 && (st < p.nstages || (PEER && cta == 0))) {
             // wait for stage st - 1 on every rank (after the last stage: one CTA, so that the
             // kernel ends only when every rank's final outputs have arrived)
             if (threadIdx.x == 0) {
@@ -871,19 +734,10 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_program_kernel(
             if (abort_flag) return;
         }
         if (st == p.nstages) break;
-        const ProgItem it = p.items[(int64_t)st * nctas + cta];
-        if (it.t1 > it.t0) {
-            const ProgStage& ps = p.stages[st];
-            const GemvJob jb = ps.job[it.job];
-            // x was written during this launch (by other CTAs, or other GPUs): L2-only loads
-            const bool ok = jb.w1 ? consume_run<XK, MT, 2, PEER>(jb, it.t0, it.t1, jb.x, jb.ldx, ring, red, full,
-                                                                 empty, ci, &ps.peer, it.job, true)
-                                  : consume_run<XK, MT, 1, PEER>(jb, it.t0, it.t1, jb.x, jb.ldx, ring, red, full,
-                                                                 empty, ci, &ps.peer, it.job, true);
-            if (!ok) {
-                if (lane == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
-                abort_flag = 1;
-            }
+        const ProgStage& ps = p.stages[st];
+        if (!consume_units<XK, MT, PEER>(ps.grp, ring, red, full, empty, meta, ps.peer, ci, units)) {
+            if (lane == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
+            abort_flag = 1;
         }
         // count in: every consumer's stores precede the barrier, the fence of the counting thread
         // orders them before its increment (and the last one's system fence before the flags)
@@ -897,11 +751,18 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_program_kernel(
                 const unsigned long long old = atomicAdd(ctr, 1ull);
                 if (st == 0) epoch = old / (unsigned long long)nctas;
                 last = old + 1 == (epoch + 1) * (unsigned long long)nctas;
+                if (last) {
+                    // every producer has made its last claim of this stage (before the end marker
+                    // its consumers have seen): the claim counter starts over for the next run
+                    unsigned* claim = prog_claim(p.sync, st);
+                    claim[0] = 0;
+                    claim[1] = 0;
+                }
             }
             __syncwarp();
             last = __shfl_sync(0xffffffffu, last, 0);
             if (last) {
-                if (peer) {
+                if (PEER) {
                     __threadfence_system();
                     for (int r = 0; r < nranks; ++r) red_add_sys(prog_flag(p.hdr->peer_sync[r], st, lane), 1u);
                 } else {
@@ -940,67 +801,6 @@ static int sm_count() {
         count[dev] = c > 0 ? c : 148;
     }
     return count[dev];
-}
-
-// Splits every job into runs of consecutive tiles so that the launch fills every CTA slot of the GPU
-// once (`slots` = CTAs per SM x SMs): the slots are shared out in proportion to the jobs' weight
-// bytes and a job's tiles as evenly as possible over its CTAs.  A launch that leaves slots empty,
-// or spills into a second wave, streams measurably slower (the weight stream is bound by the bytes
-// in flight per SM).  Returns the number of CTAs.
-static int plan_jobs(GemvJob* job, int njobs, int slots) {
-    double total = 0.0;
-    int tiles = 0;
-    for (int i = 0; i < njobs; ++i) {
-        GemvJob& j = job[i];
-        j.n_tiles = (int)ceil_div(j.n, 16);
-        tiles += j.n_tiles;
-        total += (double)j.n_tiles * (j.w1 ? 2 : 1) * j.kt_total;
-    }
-    int used = 0;
-    for (int i = 0; i < njobs; ++i) {
-        GemvJob& j = job[i];
-        int c = j.n_tiles;
-        if (tiles > slots) {
-            c = (int)((double)slots * ((double)j.n_tiles * (j.w1 ? 2 : 1) * j.kt_total) / total);
-            c = c < 1 ? 1 : (c > j.n_tiles ? j.n_tiles : c);
-        }
-        j.cta_count = c;
-        used += c;
-    }
-    // the one-CTA minimum may overshoot: take CTAs back from the jobs with the least bytes per CTA
-    while (used > slots) {
-        int best = -1;
-        double least = 0.0;
-        for (int i = 0; i < njobs; ++i) {
-            const GemvJob& j = job[i];
-            if (j.cta_count <= 1) continue;
-            const double per = (double)j.n_tiles * (j.w1 ? 2 : 1) * j.kt_total / j.cta_count;
-            if (best < 0 || per < least) least = per, best = i;
-        }
-        if (best < 0) break;  // more jobs than slots: one CTA each
-        --job[best].cta_count;
-        --used;
-    }
-    // rounding may leave slots over: give them to the jobs with the most bytes per CTA
-    while (tiles > slots && used < slots) {
-        int best = -1;
-        double most = 0.0;
-        for (int i = 0; i < njobs; ++i) {
-            const GemvJob& j = job[i];
-            if (j.cta_count >= j.n_tiles) continue;
-            const double per = (double)j.n_tiles * (j.w1 ? 2 : 1) * j.kt_total / j.cta_count;
-            if (per > most) most = per, best = i;
-        }
-        if (best < 0) break;
-        ++job[best].cta_count;
-        ++used;
-    }
-    int ctas = 0;
-    for (int i = 0; i < njobs; ++i) {
-        job[i].cta_begin = ctas;
-        ctas += job[i].cta_count;
-    }
-    return ctas;
 }
 
 // Device addresses of this device's claim counters and split scratch (cached per device).
@@ -1419,17 +1219,11 @@ extern "C" int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned ex
 // ---- decode program: build (once, synchronous) and run (per step, capturable) ---------------------
 static int program_ctas() { return kCtasPerSm * sm_count(); }
 
-// Programs built by sbq_gemv_program_build_peer (the run picks the sharded kernel for them).
-static std::mutex g_peer_programs_mu;
-static std::unordered_set<const void*> g_peer_programs;
-
-static size_t program_bytes_for(int nstages, int nctas) {
-    return 256 + (size_t)nstages * sizeof(ProgStage) + (size_t)nstages * nctas * sizeof(ProgItem);
-}
+static size_t program_bytes_for(int nstages) { return 256 + (size_t)nstages * sizeof(ProgStage); }
 
 extern "C" size_t sbq_gemv_program_bytes(int nstages) {
     if (nstages < 1) return 0;
-    return program_bytes_for(nstages, program_ctas());
+    return program_bytes_for(nstages);
 }
 
 extern "C" size_t sbq_gemv_program_sync_bytes(int nstages) {
@@ -1437,40 +1231,46 @@ extern "C" size_t sbq_gemv_program_sync_bytes(int nstages) {
     return (size_t)nstages * kSyncStageBytes;
 }
 
+// Programs built by sbq_gemv_program_build_peer (the run picks the sharded kernel for them).
+static std::mutex g_peer_programs_mu;
+static std::unordered_set<const void*> g_peer_programs;
+
 // Shared by the single-GPU and the sharded build.  ydest: null, or [njobs][nranks] destinations.
 static int program_build(const sbq_gemv_job* jobs, const int* job_stage, int njobs, int x_dtype, int64_t m,
                          void* const* ydest, int nranks, void* const* peer_sync, void* program, size_t program_bytes) {
     if (!jobs || !job_stage || njobs < 1 || !program) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null argument");
     if (x_kind(x_dtype) < 0) return set_error(SBQ_ERR_UNSUPPORTED, "activation dtype %d", x_dtype);
     if (reinterpret_cast<uintptr_t>(program) % 256) return set_error(SBQ_ERR_ALIGNMENT, "program must be 256-byte aligned");
+    if (m < 1 || m > 8) return set_error(SBQ_ERR_UNSUPPORTED, "a program takes 1..8 rows of x (m=%lld)", (long long)m);
     int nstages = 0;
     for (int i = 0; i < njobs; ++i) {
         if (job_stage[i] < 0 || (i > 0 && job_stage[i] < job_stage[i - 1]))
             return set_error(SBQ_ERR_INVALID_ARGUMENT, "job stages must be non-negative and non-decreasing");
         if (job_stage[i] + 1 > nstages) nstages = job_stage[i] + 1;
     }
+    if (program_bytes < program_bytes_for(nstages))
+        return set_error(SBQ_ERR_WORKSPACE, "program needs %zu bytes", program_bytes_for(nstages));
     const int nctas = program_ctas();
-    if (program_bytes < program_bytes_for(nstages, nctas))
-        return set_error(SBQ_ERR_WORKSPACE, "program needs %zu bytes", program_bytes_for(nstages, nctas));
-    std::vector<uint8_t> host(program_bytes_for(nstages, nctas), 0);
+    std::vector<uint8_t> host(program_bytes_for(nstages), 0);
     ProgHeader* hdr = reinterpret_cast<ProgHeader*>(host.data());
-    ProgStage* stages = reinterpret_cast<ProgStage*>(host.data() + 256);
-    ProgItem* items = reinterpret_cast<ProgItem*>(host.data() + 256 + (size_t)nstages * sizeof(ProgStage));
+    std::vector<ProgStage> stages(nstages);
+    for (auto& ps : stages) {
+        ps.grp = GemvGroup{};
+        ps.peer = PeerSync{};
+        ps.peer.nranks = nranks;
+    }
     for (int i = 0; i < njobs; ++i) {
         const sbq_gemv_job& j = jobs[i];
         int st = check_linear_args(j.x, x_dtype, j.ldx, j.packed, j.scale, m, j.n, j.k, j.y, j.y_dtype, j.ldy);
         if (st) return set_error(st, "job %d: %s", i, sbq_last_error());
-        if (m > 8) return set_error(SBQ_ERR_UNSUPPORTED, "job %d: a program takes 1..8 rows of x (m=%lld)", i, (long long)m);
         if (j.packed_up && (!j.scale_up || j.bias))
             return set_error(SBQ_ERR_INVALID_ARGUMENT, "job %d: fused gate/up job needs scale_up and no bias", i);
         ProgStage& ps = stages[job_stage[i]];
-        if (ps.njobs >= kMaxJobs) return set_error(SBQ_ERR_UNSUPPORTED, "more than %d jobs in one stage", kMaxJobs);
-        const int jj = ps.njobs++;
-        GemvJob& jb = ps.job[jj];
-        fill_job(jb, j.x, j.ldx, j.packed, j.scale, j.packed_up, j.scale_up, j.bias, j.n, j.k, j.y, j.y_dtype, j.ldy);
-        jb.m = (int)m;
-        jb.n_tiles = (int)ceil_div(j.n, 16);
-        ps.peer.nranks = nranks;
+        if (ps.grp.njobs >= kMaxJobs) return set_error(SBQ_ERR_UNSUPPORTED, "more than %d jobs in one stage", kMaxJobs);
+        const int jj = ps.grp.njobs++;
+        fill_job(ps.grp.job[jj], j.x, j.ldx, j.packed, j.scale, j.packed_up, j.scale_up, j.bias, j.n, j.k, j.y,
+                 j.y_dtype, j.ldy);
+        ps.grp.job[jj].m = (int)m;
         if (ydest) {
             bool local = false;
             for (int r = 0; r < nranks; ++r) {
@@ -1482,21 +1282,20 @@ static int program_build(const sbq_gemv_job* jobs, const int* job_stage, int njo
             if (!local) return set_error(SBQ_ERR_INVALID_ARGUMENT, "job %d: y must be one of its rank destinations", i);
         }
     }
-    // per stage: the stage's jobs share the grid as a grouped launch would (every CTA slot filled)
+    // each stage is planned as a grouped launch over the program's grid (units, K parts, largest
+    // first); its split scratch alternates between the two regions stage by stage (stage s + 2
+    // starts only after stage s + 1's barrier, so after every use of stage s's region)
+    const UnitBuffers* ub = unit_buffers();
+    if (!ub) return set_error(SBQ_ERR_CUDA, "decode program: no device work buffers");
     for (int st = 0; st < nstages; ++st) {
         ProgStage& ps = stages[st];
-        ProgItem* row = items + (size_t)st * nctas;
-        for (int c = 0; c < nctas; ++c) row[c] = ProgItem{0, 0, 0};
-        if (ps.njobs == 0) continue;
-        if (plan_jobs(ps.job, ps.njobs, nctas) > nctas)
-            return set_error(SBQ_ERR_UNSUPPORTED, "stage %d has more jobs than the grid has CTAs", st);
-        for (int i = 0; i < ps.njobs; ++i) {
-            const GemvJob& jb = ps.job[i];
-            for (int c = 0; c < jb.cta_count; ++c)
-                row[jb.cta_begin + c] = ProgItem{i, (int)((int64_t)c * jb.n_tiles / jb.cta_count),
-                                                 (int)((int64_t)(c + 1) * jb.n_tiles / jb.cta_count)};
-        }
+        if (ps.grp.njobs == 0) continue;
+        if (plan_units(ps.grp, ps.peer, nctas, (int)m) <= 0) return set_error(SBQ_ERR_CUDA, "decode program plan");
+        ps.grp.claim = nullptr;  // the stage's claim pair lives in the run's sync region
+        ps.grp.split_scratch = ub->split + (size_t)(st % kSplitRegions) * kSplitFloats;
+        ps.grp.split_count = ub->split_count + (size_t)(st % kSplitRegions) * kSplitTiles;
     }
+    std::memcpy(host.data() + 256, stages.data(), (size_t)nstages * sizeof(ProgStage));
     hdr->nstages = nstages;
     hdr->nctas = nctas;
     hdr->x_dtype = x_dtype;
@@ -1548,7 +1347,6 @@ extern "C" int sbq_gemv_program_run(const void* program, int nstages, int x_dtyp
     const int nctas = program_ctas();
     pp.hdr = reinterpret_cast<const ProgHeader*>(base);
     pp.stages = reinterpret_cast<const ProgStage*>(base + 256);
-    pp.items = reinterpret_cast<const ProgItem*>(base + 256 + (size_t)nstages * sizeof(ProgStage));
     pp.nstages = nstages;
     pp.sync = static_cast<uint8_t*>(sync);
     const int smem = GemvSmemSize<1>::kBytes;
