@@ -588,11 +588,14 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? kCtasPerSm : 2)
         if (lane == 0 && !produce_units(grp, grp.claim, ring, full, empty, meta, pci)) tc::raise_error(SBQ_ERR_TIMEOUT);
         return;
     }
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
     if (PEER && ps.wait_count) {
-        // x also holds the other ranks' slices, stored by their previous launch
+        // x is the previous launch's output on every rank (this one included): its signal, not
+        // the end of the previous grid, is what the consumers need, so they start as soon as the
+        // last rank's last CTA has published (the release/acquire pair orders every store before)
         if (threadIdx.x == 0) peer_wait(ps.wait_count, ps.wait_state, ps.wait_expected, ps.wait_limit_ns);
         consumers_sync();
+    } else {
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
     }
     uint32_t ci = 0;
     int units = 0;
