@@ -205,7 +205,8 @@ def _graph_time(fn, stream, reps: int, warmup: int) -> float:
     return ms
 
 
-def kernel_cases(sbq, dev, stream, steps: int, warmup: int, which=("gemv", "mlp", "gemm", "dyn")) -> dict:
+def kernel_cases(sbq, dev, stream, steps: int, warmup: int,
+                 which=("gemv", "mlp", "gemm", "gemm_small", "dyn")) -> dict:
     """Configurations 0-3 at their own shapes, each kernel timed alone (CUDA graph, CUDA events).
 
     HBM-bound cases rotate over enough distinct weight copies that every launch reads its weight
@@ -288,6 +289,26 @@ def kernel_cases(sbq, dev, stream, steps: int, warmup: int, which=("gemv", "mlp"
                                     "frac_bf16_peak": round(fl / ms / 1e9 / pk["bf16_tflops"], 4),
                                     "frac_f16_spec": round(fl / ms / 1e9 / SPEC_F16_TFLOPS, 4)}
 
+    if "gemm_small" in which:  # configuration 4 at decode batch 64: the small-batch GEMM per projection
+        res = {}
+        for name, n, k in (("qkvd", 4 * W.HIDDEN, W.HIDDEN), ("o", W.HIDDEN, W.HIDDEN), ("down", W.HIDDEN, W.INTER)):
+            copies = max(2, int(2 * 126e6 / (n * k)) + 1)
+            ws = int8_weights(n, k, copies)
+            x = W.activation(64, k, seed=4, device=dev)
+            y = torch.empty(64, n, dtype=torch.float16, device=dev)
+
+            def f():
+                for p_, s_, _ in ws:
+                    L.call("sbq_gemm_w8a16", vp(x.data_ptr()), L.F16, k, vp(p_.data_ptr()), vp(s_.data_ptr()), None, 64,
+                           n, k, vp(y.data_ptr()), L.F16, n, st)
+
+            ms = _graph_time(f, stream, max(20, steps // 10), warmup) / copies
+            b = n * k
+            res[name] = {"n": n, "k": k, "us": round(ms * 1e3, 2), "gbs": round(b / ms / 1e6, 1),
+                         "frac_hbm": round(b / ms / 1e6 / pk["hbm_gbs"], 4)}
+            del ws
+        out["cfg4_b64_gemm_small"] = res
+
     if "dyn" in which:  # configuration 3: int8-dyn, m=512, k=n=4096
         m, k, n = 512, W.HIDDEN, W.HIDDEN
         (p_, s_, rs), = int8_weights(n, k, 1)
@@ -361,7 +382,8 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline measurement")
     ap.add_argument("--no-extra", action="store_true", help="skip the per-configuration kernel timings")
-    ap.add_argument("--kernel", choices=("gemv", "mlp", "gemm", "dyn"), help="time one configuration's kernel alone")
+    ap.add_argument("--kernel", choices=("gemv", "mlp", "gemm", "gemm_small", "dyn"),
+                    help="time one configuration's kernel alone")
     ap.add_argument("--program", action="store_true",
                     help="run the decode step as one persistent decode-program launch instead of grouped launches")
     ap.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
