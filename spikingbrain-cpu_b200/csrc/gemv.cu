@@ -1098,6 +1098,29 @@ static int run_single(GemvJob jb, int64_t m, int x_dtype, int y_dtype, cudaStrea
 
 using namespace sbq;
 
+extern "C" int sbq_gemv_plan_parts(const int64_t* shapes, int njobs, int slots, int64_t m, int* parts) {
+    if (!shapes || !parts || njobs < 1 || njobs > kMaxJobs || slots < 1 || m < 1 || m > 16)
+        return set_error(SBQ_ERR_INVALID_ARGUMENT, "plan: 1..%d jobs, slots >= 1, 1 <= m <= 16", kMaxJobs);
+    PartsKey key{};
+    key.slots = slots;
+    key.m = (int)m;
+    key.nj = njobs;
+    for (int i = 0; i < njobs; ++i) {
+        const int64_t n = shapes[3 * i], k = shapes[3 * i + 1], nmat = shapes[3 * i + 2];
+        if (n < 1 || k < 1 || k % 16 || (nmat != 1 && nmat != 2))
+            return set_error(SBQ_ERR_INVALID_ARGUMENT, "plan: job %d needs n >= 1, k a positive multiple of 16, "
+                             "1 or 2 matrices", i);
+        GemvJob jb;
+        fill_job(jb, nullptr, k, nullptr, nullptr, nmat == 2 ? reinterpret_cast<const void*>(1) : nullptr, nullptr,
+                 nullptr, n, k, nullptr, SBQ_F32, n);
+        key.shape[i][0] = ceil_div(n, 16);
+        key.shape[i][1] = (int64_t)jb.kt_total * nmat * kTileBytes;
+        key.shape[i][2] = jb.kt_total / jb.chunk_tiles;
+    }
+    choose_parts(key, parts);
+    return SBQ_OK;
+}
+
 extern "C" int sbq_gemv_w8(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                            const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
                            void* stream) {
