@@ -357,7 +357,7 @@ def stack_cases(sbq, stack, dev, stream, warmup: int) -> dict:
     out["prefill_8192"] = {"ms": round(ms, 2), "tflops": round(fl / ms / 1e9, 1),
                            "frac_bf16_peak": round(fl / ms / 1e9 / peaks()["bf16_tflops"], 4),
                            "frac_f16_spec": round(fl / ms / 1e9 / SPEC_F16_TFLOPS, 4),
-                           "note": "per-projection GEMMs plus torch SiLU*mul between gate/up and down"}
+                           "note": "per-projection GEMMs; gate GEMM then up GEMM with the SiLU*mul epilogue"}
     return out
 
 

@@ -116,9 +116,11 @@ SBQ_API int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const void* 
                    const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
                    void* stream);
 
-/* GatedMLP.forward's first half (model.py:239-240): h = silu(x q_gate^T * s_gate) * (x q_up^T * s_up),
- * computed in one pass over both weights ([n, k] each) with h written as h_dtype (SBQ_F16 or
- * SBQ_F32).  The down projection is a separate sbq_linear_w8 call on h. */
+/* GatedMLP.forward's first half (model.py:239-240): h = silu(x q_gate^T * s_gate) * (x q_up^T * s_up)
+ * with h written as h_dtype (SBQ_F16 or SBQ_F32).  Up to 32 rows (or bf16/fp32 x): one pass over
+ * both weights ([n, k] each) in the decode GEMV.  More fp16 rows: the gate projection goes into h
+ * (rounded to h_dtype) and the up projection's GEMM epilogue replaces it by silu(gate) * up.  The
+ * down projection is a separate sbq_linear_w8 call on h. */
 SBQ_API int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const void* packed_gate,
                       const float* scale_gate, const void* packed_up, const float* scale_up, int64_t m,
                       int64_t n, int64_t k, void* h, int h_dtype, int64_t ldh, void* stream);

@@ -26,7 +26,38 @@ struct GemmW16Params {
     const float* bias;
     void* y;
     int64_t ldy;
+    int gated;  // y already holds the gate projection: store silu(gate) * result in its place
 };
+
+// One output element.  With `gated`, y holds the gate projection of the same rows (written by an
+// earlier launch into this buffer) and receives silu(gate) * v (GatedMLP.forward, model.py:239-240).
+template <bool OUT_F16, class P>
+__device__ __forceinline__ float load_y(const P& p, int t, int n) {
+    const int64_t idx = (int64_t)t * p.ldy + n;
+    return OUT_F16 ? __half2float(static_cast<const __half*>(p.y)[idx]) : static_cast<const float*>(p.y)[idx];
+}
+
+template <bool OUT_F16, class P>
+__device__ __forceinline__ void put_y(const P& p, int t, int n, float v) {
+    const int64_t idx = (int64_t)t * p.ldy + n;
+    if (OUT_F16)
+        static_cast<__half*>(p.y)[idx] = __float2half_rn(v);
+    else
+        static_cast<float*>(p.y)[idx] = v;
+}
+
+template <bool OUT_F16, class P>
+__device__ __forceinline__ void store_y(const P& p, int t, int n, float v) {
+    const int64_t idx = (int64_t)t * p.ldy + n;
+    if (p.gated) {
+        const float g = OUT_F16 ? __half2float(static_cast<const __half*>(p.y)[idx]) : static_cast<const float*>(p.y)[idx];
+        v = g / (1.0f + expf(-g)) * v;
+    }
+    if (OUT_F16)
+        static_cast<__half*>(p.y)[idx] = __float2half_rn(v);
+    else
+        static_cast<float*>(p.y)[idx] = v;
+}
 
 constexpr int kWCh = 128;      // output channels per CTA (MMA M, one per TMEM lane)
 constexpr int kWTok = 256;     // activation rows per CTA (MMA N)
@@ -173,16 +204,27 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
                 tc::tmem_wait_ld();
                 if (n >= p.n) continue;
                 const int tb = t0 + c * 32;
+                if (p.gated) {
+                    // all 32 gate values are loaded before any is used (independent loads)
+                    float gv[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) gv[j] = tb + j < p.m ? load_y<OUT_F16>(p, tb + j, n) : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (tb + j >= p.m) break;
+                        float v = __fmul_rn(__uint_as_float(r[j]), sc);
+                        if (has_bias) v = __fadd_rn(v, bi);
+                        put_y<OUT_F16>(p, tb + j, n, gv[j] / (1.0f + expf(-gv[j])) * v);
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int t = tb + j;
                     if (t >= p.m) break;
                     float v = __fmul_rn(__uint_as_float(r[j]), sc);
                     if (has_bias) v = __fadd_rn(v, bi);
-                    if (OUT_F16)
-                        static_cast<__half*>(p.y)[(int64_t)t * p.ldy + n] = __float2half_rn(v);
-                    else
-                        static_cast<float*>(p.y)[(int64_t)t * p.ldy + n] = v;
+                    store_y<OUT_F16>(p, t, n, v);
                 }
             }
         }
@@ -220,6 +262,7 @@ struct SmallSmem {
 
 struct GemmSmallParams {
     int m, n, k, num_kb, parts;
+    int gated;             // as GemmW16Params::gated
     const float* scale;
     const float* bias;
     void* y;
@@ -399,10 +442,7 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
                     if (t >= p.m) break;
                     float v = __fmul_rn(__uint_as_float(r[j]), sc);
                     if (p.bias) v = __fadd_rn(v, bi);
-                    if (OUT_F16)
-                        static_cast<__half*>(p.y)[(int64_t)t * p.ldy + n] = __float2half_rn(v);
-                    else
-                        static_cast<float*>(p.y)[(int64_t)t * p.ldy + n] = v;
+                    store_y<OUT_F16>(p, t, n, v);
                 }
             }
         } else {
@@ -438,10 +478,7 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
                 if (t >= p.m) break;
                 float o = __fmul_rn(r4[j], sc);
                 if (p.bias) o = __fadd_rn(o, bi);
-                if (OUT_F16)
-                    static_cast<__half*>(p.y)[(int64_t)t * p.ldy + n] = __float2half_rn(o);
-                else
-                    static_cast<float*>(p.y)[(int64_t)t * p.ldy + n] = o;
+                store_y<OUT_F16>(p, t, n, o);
             }
         }
         cluster_sync_all();  // no CTA leaves while another may still read its shared memory
@@ -478,7 +515,7 @@ static int sm_count_w16() {
 }
 
 static int gemm_small(const void* x, int64_t ldx, const void* packed, const float* scale, const float* bias, int64_t m,
-                      int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream) {
+                      int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream, int gated) {
     CUtensorMap mx, mw;
     int st;
     {
@@ -497,6 +534,7 @@ static int gemm_small(const void* x, int64_t ldx, const void* packed, const floa
         if (st) return st;
     }
     GemmSmallParams p{};
+    p.gated = gated;
     p.m = (int)m;
     p.n = (int)n;
     p.k = (int)k;
@@ -536,9 +574,22 @@ static int gemm_small(const void* x, int64_t ldx, const void* packed, const floa
     return check_launch("gemm_w8a16_small");
 }
 
+namespace sbq {
+// The tensor-memory GEMM of both tile sizes; `gated`: see GemmW16Params (sbq_mlp_gateup_w8 runs the
+// gate projection into h, then the up projection with gated = 1).
+int gemm_w8a16_run(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale, const float* bias,
+                   int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream, int gated);
+}
+
 extern "C" int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                               const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
                               void* stream) {
+    return gemm_w8a16_run(x, x_dtype, ldx, packed, scale, bias, m, n, k, y, y_dtype, ldy, stream, 0);
+}
+
+int sbq::gemm_w8a16_run(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
+                        const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
+                        void* stream, int gated) {
     int st = check_linear_args(x, x_dtype, ldx, packed, scale, m, n, k, y, y_dtype, ldy);
     if (st) return st;
     if (x_dtype != SBQ_F16) return set_error(SBQ_ERR_UNSUPPORTED, "sbq_gemm_w8a16 takes fp16 activations");
@@ -558,8 +609,9 @@ extern "C" int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const voi
         st = encode_tmap(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, packed, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
         if (st) return st;
     }
-    if (m <= kSmallMaxRows) return gemm_small(x, ldx, packed, scale, bias, m, n, k, y, y_dtype, ldy, stream);
+    if (m <= kSmallMaxRows) return gemm_small(x, ldx, packed, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
     GemmW16Params p{};
+    p.gated = gated;
     p.m = (int)m;
     p.n = (int)n;
     p.k = (int)k;

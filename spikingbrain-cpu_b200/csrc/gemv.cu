@@ -1131,6 +1131,15 @@ extern "C" int sbq_gemv_w8(const void* x, int x_dtype, int64_t ldx, const void* 
     return run_single(jb, m, x_dtype, y_dtype, static_cast<cudaStream_t>(stream), "gemv_w8");
 }
 
+namespace sbq {
+int gemm_w8a16_run(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale, const float* bias,
+                   int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream, int gated);
+}
+
+// Rows of x above which the gate/up pair runs as two tensor-memory GEMMs (the gate projection into
+// h, then the up projection whose epilogue turns h into silu(gate) * up) instead of the fused GEMV.
+constexpr int64_t kGateUpGemmMinRows = 32;
+
 extern "C" int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const void* packed_gate,
                                  const float* scale_gate, const void* packed_up, const float* scale_up, int64_t m,
                                  int64_t n, int64_t k, void* h, int h_dtype, int64_t ldh, void* stream) {
@@ -1138,6 +1147,11 @@ extern "C" int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const 
     if (st) return st;
     if (!packed_up || !scale_up) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null up-projection pointer");
     if (reinterpret_cast<uintptr_t>(packed_up) % 256) return set_error(SBQ_ERR_ALIGNMENT, "packed weight must be 256-byte aligned");
+    if (m > kGateUpGemmMinRows && x_dtype == SBQ_F16) {
+        st = gemm_w8a16_run(x, x_dtype, ldx, packed_gate, scale_gate, nullptr, m, n, k, h, h_dtype, ldh, stream, 0);
+        if (st) return st;
+        return gemm_w8a16_run(x, x_dtype, ldx, packed_up, scale_up, nullptr, m, n, k, h, h_dtype, ldh, stream, 1);
+    }
     GemvJob jb;
     fill_job(jb, x, ldx, packed_gate, scale_gate, packed_up, scale_up, nullptr, n, k, h, h_dtype, ldh);
     return run_single(jb, m, x_dtype, h_dtype, static_cast<cudaStream_t>(stream), "mlp_gateup_w8");

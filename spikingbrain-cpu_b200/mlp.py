@@ -15,10 +15,6 @@ import torch.nn as nn
 from . import _lib as L
 from .quant import _DTYPE_CODE, Int8Linear, _prepare_x, _ptr, _stream
 
-# Above this many rows the gate/up products go through the GEMM path instead of the fused GEMV (the
-# GEMV streams the weights once per 16 rows; the small-batch GEMM once).
-FUSED_MAX_ROWS = 32
-
 
 class FusedGatedMLP(nn.Module):
     def __init__(self, gate: Int8Linear, up: Int8Linear, down: Int8Linear, h_dtype: torch.dtype = torch.float16,
@@ -61,14 +57,12 @@ class FusedGatedMLP(nn.Module):
     def gateup_into(self, x2: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
         """Low-level device call: silu(gate(x2)) * up(x2) into ``h`` [m, n] (fp16/fp32, unit column stride).
 
-        x2 is [m, k'] with 16-byte aligned rows (k' = in_features rounded up to 16).  Rows beyond
-        FUSED_MAX_ROWS go through the unfused GEMM composition.
+        x2 is [m, k'] with 16-byte aligned rows (k' = in_features rounded up to 16).  The library
+        picks the kernel: the fused gate/up GEMV up to 32 rows (or for bf16/fp32 x); above, the gate
+        GEMM into ``h`` and the up GEMM whose epilogue replaces it by silu(gate) * up.
         """
         m, n = x2.shape[0], self.gate_proj.out_features
-        if m > FUSED_MAX_ROWS:
-            xk = x2[:, :self.gate_proj.in_features]
-            h.copy_(torch.nn.functional.silu(self.gate_proj(xk)) * self.up_proj(xk))
-        elif m > 0:
+        if m > 0:
             L.call("sbq_mlp_gateup_w8", _ptr(x2), _DTYPE_CODE[x2.dtype], x2.stride(0), _ptr(self.gate_proj.packed),
                    _ptr(self.gate_proj.scale), _ptr(self.up_proj.packed), _ptr(self.up_proj.scale), m, n,
                    x2.shape[1], _ptr(h), L.F16 if h.dtype == torch.float16 else L.F32, h.stride(0),

@@ -111,3 +111,22 @@ def test_gemm_small_batch_split_k(sbq, m, n, k, out):
     want = R.int8_linear(x.float().numpy(), q, s, None if b is None else b.numpy())
     assert R.rel_l2(y1.float().cpu().numpy(), want) < REL_L2
     assert sbq._lib.load().sbq_check_device_error() == 0
+
+
+@pytest.mark.parametrize("m", [40, 64, 300])
+@pytest.mark.parametrize("h_dtype", [torch.float16, torch.float32])
+def test_gated_gemm_gateup(sbq, m, h_dtype):
+    # above 32 rows the gate/up pair runs as two GEMMs: the gate projection into h, then the up
+    # projection whose epilogue replaces it by silu(gate) * up (the gate is rounded to h's dtype)
+    n, k = 1536, 1024
+    wg = sbq.workloads.float_weight(n, k, seed=m + 1)
+    wu = sbq.workloads.float_weight(n, k, seed=m + 2)
+    wd = sbq.workloads.float_weight(k, n, seed=m + 3)
+    mlp = sbq.FusedGatedMLP(*(sbq.Int8Linear(w, None) for w in (wg, wu, wd)), h_dtype=h_dtype)
+    x = sbq.workloads.activation(m, k, seed=m + 4)
+    h = mlp.gateup_into(x.cuda(), torch.empty(m, n, dtype=h_dtype, device="cuda"))
+    g, u = (R.int8_linear(x.float().numpy(), *R.quantize_per_channel(w.numpy())) for w in (wg, wu))
+    if h_dtype == torch.float16:
+        g = g.astype(np.float16).astype(np.float64)
+    want = g / (1.0 + np.exp(-g)) * u
+    assert R.rel_l2(h.float().cpu().numpy(), want) < REL_L2
