@@ -77,7 +77,7 @@ struct W16Smem {
     static constexpr int kBytes = kBarOff + 256 + kWCh * 8 + 1024;
 };
 
-template <bool OUT_F16>
+template <bool OUT_F16, bool GATED>
 __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                                   const __grid_constant__ CUtensorMap tmap_w,
                                                                   const GemmW16Params p) {
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
                 tc::tmem_wait_ld();
                 if (n >= p.n) continue;
                 const int tb = t0 + c * 32;
-                if (p.gated) {
+                if (GATED) {
                     // all 32 gate values are loaded before any is used (independent loads)
                     float gv[32];
 #pragma unroll
@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
                     if (t >= p.m) break;
                     float v = __fmul_rn(__uint_as_float(r[j]), sc);
                     if (has_bias) v = __fadd_rn(v, bi);
-                    store_y<OUT_F16>(p, t, n, v);
+                    put_y<OUT_F16>(p, t, n, v);
                 }
             }
         }
@@ -624,11 +624,21 @@ int sbq::gemm_w8a16_run(const void* x, int x_dtype, int64_t ldx, const void* pac
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int smem = W16Smem::kBytes;
     if (y_dtype == SBQ_F16) {
-        cudaFuncSetAttribute(gemm_w8a16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        gemm_w8a16_kernel<true><<<grid, kWThreads, smem, s>>>(mx, mw, p);
+        if (gated) {
+            cudaFuncSetAttribute(gemm_w8a16_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            gemm_w8a16_kernel<true, true><<<grid, kWThreads, smem, s>>>(mx, mw, p);
+        } else {
+            cudaFuncSetAttribute(gemm_w8a16_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            gemm_w8a16_kernel<true, false><<<grid, kWThreads, smem, s>>>(mx, mw, p);
+        }
     } else {
-        cudaFuncSetAttribute(gemm_w8a16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        gemm_w8a16_kernel<false><<<grid, kWThreads, smem, s>>>(mx, mw, p);
+        if (gated) {
+            cudaFuncSetAttribute(gemm_w8a16_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            gemm_w8a16_kernel<false, true><<<grid, kWThreads, smem, s>>>(mx, mw, p);
+        } else {
+            cudaFuncSetAttribute(gemm_w8a16_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            gemm_w8a16_kernel<false, false><<<grid, kWThreads, smem, s>>>(mx, mw, p);
+        }
     }
     return check_launch("gemm_w8a16");
 }
