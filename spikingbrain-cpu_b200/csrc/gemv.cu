@@ -5,23 +5,27 @@
 // each 128-row block of the weight to fp32 and runs an fp32 sgemm, then multiplies by the
 // per-row scale.  Here the weight is streamed from HBM exactly once per launch:
 //
-//   * each CTA owns a run of consecutive 16-row tiles of one weight; a launch fills every CTA slot
-//     of the GPU once (three per SM) with runs of near-equal bytes; a producer warp streams its
-//     contiguous byte range with cp.async.bulk copies into a 48 KiB shared-memory ring (8 KiB
-//     chunks, mbarrier transaction counts), across tile boundaries without pausing;
-//   * the consumers read their activation fragments in place (L1-cached) before waiting for each
-//     chunk, so the load overlaps the wait;
+//   * a launch's work is a list of units - one 16-row tile of one job (its contiguous K strip in
+//     the packed layout), or one K part of such a tile when the tiles are too few for the GPU -
+//     and every CTA slot of the GPU (three per SM) runs one CTA; each CTA's producer thread takes
+//     its first unit by block index and claims the next ones from a per-launch counter, largest
+//     units first, and streams them with cp.async.bulk copies into a 48 KiB shared-memory ring
+//     (8 KiB chunks, mbarrier transaction counts; each chunk's unit described beside it);
 //   * eight consumer warps (or four on gate and four on up) take one 1 KiB tile of each chunk:
-//     two conflict-free 16-byte shared loads per lane, int8 -> fp16 (or bf16) in registers (exact), m16n8k16 tensor-core MMAs with
-//     fp32 accumulation and the activation rows as the n dimension (8 or 16 tokens per pass);
-//   * at the end of each tile the warps' partial sums are reduced through shared memory in a fixed
-//     order, then the fp32 per-row scale (and bias, or the SiLU(gate) * up product) is applied
-//     before one store, while the producer keeps streaming the next tile;
+//     two conflict-free 16-byte shared loads per lane, int8 -> fp16 (or bf16) in registers
+//     (exact), m16n8k16 tensor-core MMAs with fp32 accumulation and the activation rows as the n
+//     dimension (8 or 16 tokens per pass); activation fragments are read in place (L1-cached)
+//     before waiting for the chunk, so the load overlaps the wait;
+//   * at the end of each unit the warps' partial sums go to a double-buffered shared-memory area
+//     and one rotating warp reduces them in a fixed order and applies the fp32 per-row scale (and
+//     bias, or the SiLU(gate) * up product) while the others continue; K parts are added in part
+//     order by the CTA that completes a tile's last part (deterministic);
 //   * one launch can carry several independent projections ("jobs": e.g. q|k|v|delta_in and
-//     gate/up of one layer, which read the same x); each CTA finds its job from its block index;
+//     gate/up of one layer, which read the same x);
 //   * programmatic dependent launch: the weights never depend on the previous kernel, so the
-//     producer starts streaming at once; only the consumers wait (griddepcontrol.wait) before
-//     reading x, and each CTA releases the next launch as soon as it starts.
+//     producer starts streaming at once; only the consumers wait (griddepcontrol.wait, or the
+//     peer signal of a sharded step) before reading x, and each CTA releases the next launch as
+//     soon as it starts.
 //
 // fp32 activations are split into a bf16 high and low part (two MMAs, ~16 mantissa bits kept);
 // the dot product of int8 weights and fp16/bf16 activations is exact up to fp32 accumulation.
@@ -59,8 +63,6 @@ struct GemvJob {
     int chunk_tiles;   // tiles per chunk and matrix: the largest of 8 (4 for gate/up), 4, 2, 1 dividing kt_total
     int out_f16;       // 1: fp16 output, 0: fp32
     int n_tiles;       // 16-row tiles of the weight
-    int cta_count;     // CTAs of this job; CTA c streams tiles [c n_tiles / cta_count, (c + 1) n_tiles / cta_count)
-    int cta_begin;     // first block index of this job in the grid
 };
 
 constexpr int kMaxJobs = 8;
@@ -246,14 +248,6 @@ __device__ __forceinline__ void tile_mma(float (&acc)[MT][4], const uint4& wa, c
     }
 }
 
-template <typename T>
-__device__ __forceinline__ void store_out(void* y, int64_t idx, float v);
-template <>
-__device__ __forceinline__ void store_out<float>(void* y, int64_t idx, float v) { static_cast<float*>(y)[idx] = v; }
-template <>
-__device__ __forceinline__ void store_out<__half>(void* y, int64_t idx, float v) {
-    static_cast<__half*>(y)[idx] = __float2half_rn(v);
-}
 
 constexpr int kGemvThreads = (kGemvWarps + 1) * 32;  // 8 consumer warps + 1 producer warp
 constexpr int kChunkTiles = 8;                         // tiles (KiB) per chunk and matrix, at most
