@@ -11,6 +11,8 @@
 // accumulators in tensor memory) and applies the zero-point correction acc - zp * rowsum[n] in the
 // epilogue, which is exact integer arithmetic.  The per-token mode (symmetric int8, one scale per
 // row, no reference counterpart) shares the GEMM with a signed A operand.
+#include <cstring>
+
 #include "tc.cuh"
 
 namespace sbq {
@@ -55,23 +57,41 @@ struct Vec<__nv_bfloat16> {
 };
 
 constexpr int kQuantThreads = 256;
+constexpr int kQuantVecs = 4;  // vectors a thread loads at once (kept in registers across a wait)
 constexpr int kMaxPartials = 1024;
 
-// Step 1: per-CTA (min, max) of x [m, k] (row stride ldx; k a multiple of the vector width).
+// Element offset of vector v (V elements) of x [m, k] with row stride ldx.
+__device__ __forceinline__ int64_t vec_offset(int64_t v, int64_t per_row, int V, int64_t ldx) {
+    if (ldx == per_row * V) return v * V;
+    const int64_t row = v / per_row;
+    return row * ldx + (v - row * per_row) * V;
+}
+
+// Step 1: per-CTA (min, max) of x [m, k] (row stride ldx; k a multiple of the vector width).  Each
+// thread requests kQuantVecs vectors before folding any, so one memory latency covers them.
 template <typename T>
 __global__ void __launch_bounds__(kQuantThreads) minmax_partial_kernel(const T* __restrict__ x, int64_t ldx, int m,
                                                                       int k, float2* __restrict__ partials) {
+    // the quantisation kernel may start now: it loads x (complete before this grid started) and
+    // waits for this grid before reading the partials
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     constexpr int V = Vec<T>::kN;
     const int64_t per_row = k / V, total = (int64_t)m * per_row;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     float mn = INFINITY, mx = -INFINITY;
-    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t row = v / per_row, col = (v - row * per_row) * V;
-        float e[V];
-        Vec<T>::load(x + row * ldx + col, e);
+    for (int64_t v0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v0 < total; v0 += kQuantVecs * stride) {
+        float e[kQuantVecs][V];
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-            mn = fminf(mn, e[i]);
-            mx = fmaxf(mx, e[i]);
+        for (int j = 0; j < kQuantVecs; ++j)
+            if (v0 + j * stride < total) Vec<T>::load(x + vec_offset(v0 + j * stride, per_row, V, ldx), e[j]);
+#pragma unroll
+        for (int j = 0; j < kQuantVecs; ++j) {
+            if (v0 + j * stride >= total) continue;
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                mn = fminf(mn, e[j][i]);
+                mx = fmaxf(mx, e[j][i]);
+            }
         }
     }
 #pragma unroll
@@ -125,14 +145,50 @@ __device__ void choose_qparams(float mn, float mx, float* scale_out, int* zp_out
     *zp_out = zp;
 }
 
-// Step 3.  Every CTA folds the partials and derives the parameters itself (identical result, no
-// grid-wide synchronisation or counters); CTA 0 publishes them.
+// Quantise V elements to V/4 packed bytes: clamp(rint(fma(x, inv, zp)), 0, 255).
+template <int V>
+__device__ __forceinline__ void quant_u8(const float (&e)[V], float inv, float fzp, uint8_t* dst) {
+    uint32_t packed[V / 4];
+#pragma unroll
+    for (int w = 0; w < V / 4; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float t = rintf(__fmaf_rn(e[4 * w + i], inv, fzp));
+            t = fminf(fmaxf(t, 0.0f), 255.0f);
+            word |= (uint32_t)t << (8 * i);
+        }
+        packed[w] = word;
+    }
+    if (V == 4) {
+        *reinterpret_cast<uint32_t*>(dst) = packed[0];
+    } else {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[V / 4 - 1]);
+    }
+}
+
+// Step 3, launched as a programmatic dependent of step 1.  Every CTA loads its first vectors of x
+// while step 1 still runs, then waits for it, folds the partials and derives the parameters itself
+// (identical result, no grid-wide synchronisation or counters); CTA 0 publishes them.
 template <typename T>
 __global__ void __launch_bounds__(kQuantThreads) quantize_per_tensor_kernel(const T* __restrict__ x, int64_t ldx, int m,
                                                                            int k, const float2* __restrict__ partials,
                                                                            int nparts, uint8_t* __restrict__ xq,
                                                                            float* __restrict__ s_out,
                                                                            int32_t* __restrict__ zp_out) {
+    // the GEMM launched next prepares its pipeline and streams its first weight tiles meanwhile; it
+    // waits for this grid before reading xq and the parameters
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    constexpr int V = Vec<T>::kN;
+    const int64_t per_row = k / V, total = (int64_t)m * per_row;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    float e[kQuantVecs][V];
+#pragma unroll
+    for (int j = 0; j < kQuantVecs; ++j)
+        if (first + j * stride < total) Vec<T>::load(x + vec_offset(first + j * stride, per_row, V, ldx), e[j]);
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the partials are step 1's output
+
     __shared__ float2 red[kQuantThreads / 32];
     __shared__ float s_inv, s_zp;
     float mn = INFINITY, mx = -INFINITY;
@@ -165,76 +221,94 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_per_tensor_kernel(cons
     }
     __syncthreads();
     const float inv = s_inv, fzp = s_zp;
-    constexpr int V = Vec<T>::kN;
-    const int64_t per_row = k / V, total = (int64_t)m * per_row;
-    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t row = v / per_row, col = (v - row * per_row) * V;
-        float e[V];
-        Vec<T>::load(x + row * ldx + col, e);
-        uint32_t packed[V / 4];
+    for (int64_t v0 = first; v0 < total; v0 += kQuantVecs * stride) {
+        if (v0 != first) {
 #pragma unroll
-        for (int w = 0; w < V / 4; ++w) {
-            uint32_t word = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float t = rintf(__fmaf_rn(e[4 * w + i], inv, fzp));
-                t = fminf(fmaxf(t, 0.0f), 255.0f);
-                word |= (uint32_t)t << (8 * i);
-            }
-            packed[w] = word;
+            for (int j = 0; j < kQuantVecs; ++j)
+                if (v0 + j * stride < total) Vec<T>::load(x + vec_offset(v0 + j * stride, per_row, V, ldx), e[j]);
         }
-        uint8_t* dst = xq + row * (int64_t)k + col;
-        if (V == 4) {
-            *reinterpret_cast<uint32_t*>(dst) = packed[0];
-        } else {
-            *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[V / 4 - 1]);
+#pragma unroll
+        for (int j = 0; j < kQuantVecs; ++j) {
+            const int64_t v = v0 + j * stride;
+            if (v >= total) continue;
+            const int64_t row = v / per_row;
+            quant_u8<V>(e[j], inv, fzp, xq + row * (int64_t)k + (v - row * per_row) * V);
         }
     }
 }
 
-// Per-token symmetric mode: one warp per row, s_t = max(max|x_t|, 1e-8) / 127, xq = clamp(rint(x / s_t)).
+// Per-token symmetric mode: one CTA per row, s_t = max(max|x_t|, 1e-8) / 127, xq = clamp(rint(x / s_t)).
+// Rows of up to kQuantVecs * kTokThreads vectors stay in registers between the two passes.
+constexpr int kTokThreads = 128;
+
 template <typename T>
-__global__ void __launch_bounds__(kQuantThreads) quantize_per_token_kernel(const T* __restrict__ x, int64_t ldx, int m,
-                                                                          int k, int8_t* __restrict__ xq,
-                                                                          float* __restrict__ s_tok) {
+__global__ void __launch_bounds__(kTokThreads) quantize_per_token_kernel(const T* __restrict__ x, int64_t ldx, int m,
+                                                                        int k, int8_t* __restrict__ xq,
+                                                                        float* __restrict__ s_tok) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // as in the per-tensor step 3
     constexpr int V = Vec<T>::kN;
-    const int row = blockIdx.x * (kQuantThreads / 32) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (row >= m) return;
+    const int row = blockIdx.x;
+    const int per_row = k / V;
+    const bool cached = per_row <= kQuantVecs * kTokThreads;
     const T* xr = x + (int64_t)row * ldx;
+    float e[kQuantVecs][V];
     float amax = 0.0f;
-    for (int c = lane * V; c < k; c += 32 * V) {
-        float e[V];
-        Vec<T>::load(xr + c, e);
+    if (cached) {
 #pragma unroll
-        for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(e[i]));
+        for (int j = 0; j < kQuantVecs; ++j)
+            if (threadIdx.x + j * kTokThreads < per_row) Vec<T>::load(xr + (threadIdx.x + j * kTokThreads) * V, e[j]);
+#pragma unroll
+        for (int j = 0; j < kQuantVecs; ++j) {
+            if (threadIdx.x + j * kTokThreads >= per_row) continue;
+#pragma unroll
+            for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(e[j][i]));
+        }
+    } else {
+        for (int c = threadIdx.x; c < per_row; c += kTokThreads) {
+            Vec<T>::load(xr + c * V, e[0]);
+#pragma unroll
+            for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(e[0][i]));
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    __shared__ float red[kTokThreads / 32];
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kTokThreads / 32; ++w) amax = fmaxf(amax, red[w]);
     const float s = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
-    for (int c = lane * V; c < k; c += 32 * V) {
-        float e[V];
-        Vec<T>::load(xr + c, e);
+    int8_t* dst = xq + (int64_t)row * k;
+    auto put = [&](const float (&v)[V], int c) {
         uint32_t packed[V / 4];
 #pragma unroll
         for (int w = 0; w < V / 4; ++w) {
             uint32_t word = 0;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                float t = rintf(__fdiv_rn(e[4 * w + i], s));
+                float t = rintf(__fdiv_rn(v[4 * w + i], s));
                 t = fminf(fmaxf(t, -127.0f), 127.0f);
                 word |= ((uint32_t)(int32_t)t & 0xFFu) << (8 * i);
             }
             packed[w] = word;
         }
-        int8_t* dst = xq + (int64_t)row * k + c;
         if (V == 4) {
-            *reinterpret_cast<uint32_t*>(dst) = packed[0];
+            *reinterpret_cast<uint32_t*>(dst + c * V) = packed[0];
         } else {
-            *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[V / 4 - 1]);
+            *reinterpret_cast<uint2*>(dst + c * V) = make_uint2(packed[0], packed[V / 4 - 1]);
+        }
+    };
+    if (cached) {
+#pragma unroll
+        for (int j = 0; j < kQuantVecs; ++j)
+            if (threadIdx.x + j * kTokThreads < per_row) put(e[j], threadIdx.x + j * kTokThreads);
+    } else {
+        for (int c = threadIdx.x; c < per_row; c += kTokThreads) {
+            Vec<T>::load(xr + c * V, e[0]);
+            put(e[0], c);
         }
     }
-    if (lane == 0) s_tok[row] = s;
+    if (threadIdx.x == 0) s_tok[row] = s;
 }
 
 // ============================================================================ int8 GEMM ======
@@ -250,6 +324,7 @@ struct GemmI8Params {
     float* y;
     int64_t ldy;
     int32_t* acc_out;       // optional int32 accumulators (zero-point corrected), row stride n
+    int tma_y;              // y is written by TMA stores through tmap_y (no acc_out, aligned rows)
 };
 
 constexpr int kI8BM = 128;         // rows of xq per CTA (MMA M)
@@ -269,8 +344,10 @@ struct I8Smem {
 template <int BN, bool A_SIGNED>
 __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                           const __grid_constant__ CUtensorMap tmap_b,
+                                                          const __grid_constant__ CUtensorMap tmap_y,
                                                           const GemmI8Params p) {
     using S = I8Smem<BN>;
+    static_assert(4 * (BN / 32) * 4096 <= kI8Stages * S::kStage, "epilogue staging exceeds the pipeline buffers");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kI8Stages * S::kStage);
@@ -295,6 +372,7 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
         tc::fence_mbar_init();
         tc::prefetch_tmap(&tmap_a);
         tc::prefetch_tmap(&tmap_b);
+        if (p.tma_y) tc::prefetch_tmap(&tmap_y);
     }
     if (warp == 2) {
         tc::tmem_alloc(tmem_slot, BN < 32 ? 32 : BN);
@@ -312,8 +390,19 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0 && lane == 0) {
-        // ---- producer
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        // ---- producer.  The weight tiles do not depend on the previous kernel (the activation
+        // quantisation, when launched from sbq_linear_dyn as its programmatic dependent): those of
+        // the first stages are requested before griddepcontrol.wait, the activation tiles after it.
+        const int pre = p.num_kb < kI8Stages ? p.num_kb : kI8Stages;
+        for (int kb = 0; kb < pre; ++kb) {
+            uint8_t* b_s = smem + kb * S::kStage + S::kA;
+            tc::mbar_arrive_expect_tx(&full[kb], S::kStage);
+            tc::tma_load_4d(b_s, &tmap_b, &full[kb], 0, 0, 2 * kb, n0 / 16);
+            tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[kb], 0, 0, 2 * kb + 1, n0 / 16);
+        }
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (int kb = 0; kb < pre; ++kb) tc::tma_load_2d(smem + kb * S::kStage, &tmap_a, &full[kb], kb * kI8BK, m0);
+        for (int kb = pre; kb < p.num_kb; ++kb) {
             const int s = kb % kI8Stages;
             const uint32_t phase = (kb / kI8Stages) & 1;
             if (!tc::mbar_wait(&empty[s], phase ^ 1)) { *abort_flag = 1; break; }
@@ -347,13 +436,17 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
     }
     __syncwarp();
 
-    // ---- epilogue: wait for the accumulator, then TMEM -> registers -> global
+    // ---- epilogue: wait for the accumulator, then TMEM -> registers -> global.  With tma_y each
+    // warp stages its 32 x 32 fp32 blocks in the pipeline buffers (free once the last MMA has
+    // completed) in the 128-byte swizzled layout and writes each with one TMA store, so the rows
+    // leave the SM as whole lines instead of 32 scattered 16-byte pieces per instruction.
     // one lane per warp polls (with back-off) so idle threads do not compete with the producer and
     // MMA threads for the barrier; the decision is warp-uniform (tcgen05.ld is warp-collective)
     int waited = 1;
     if (lane == 0) waited = tc::mbar_wait_backoff(done, 0) && !*(volatile int*)abort_flag;
     const bool ok = __shfl_sync(0xffffffffu, waited, 0) != 0;
     tc::fence_after_sync();
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // s_x and zp come from the previous kernel
     if (ok) {
         const int row = m0 + warp * 32 + lane;
         const float sx = p.s_x[p.s_stride ? (row < p.m ? row : 0) : 0];
@@ -363,8 +456,32 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
             uint32_t r[32];
             tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
             tc::tmem_wait_ld();
-            if (row >= p.m) continue;
             const int nb = n0 + c * 32;
+            if (p.tma_y) {
+                // block (warp, c): 32 rows of 128 bytes; 16-byte unit j of row r sits at j ^ (r % 8)
+                uint8_t* blk = smem + (warp * (BN / 32) + c) * 4096;
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int i = c * 32 + j;
+                    const int32_t a = (int32_t)r[j] - zp * s_rowsum[i];
+                    const float f = __fmul_rn(sx, s_scale[i]);
+                    const float af = __int2float_rn(a);
+                    v[j] = p.bias ? __fmaf_rn(af, f, s_bias[i]) : __fmul_rn(af, f);
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    *reinterpret_cast<float4*>(blk + lane * 128 + ((j ^ (lane & 7)) * 16)) =
+                        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                tc::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && m0 + warp * 32 < p.m && nb < p.n) {
+                    tc::tma_store_2d(&tmap_y, blk, nb, m0 + warp * 32);
+                    tc::bulk_commit_group();
+                }
+                continue;
+            }
+            if (row >= p.m) continue;
             float* yrow = p.y + (int64_t)row * p.ldy;
             int32_t* arow = p.acc_out ? p.acc_out + (int64_t)row * p.n : nullptr;
             float v[32];
@@ -394,6 +511,7 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
             }
         }
     }
+    if (p.tma_y && lane == 0) tc::bulk_wait_all();  // the staged blocks stay in use until read
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 2) {
@@ -420,9 +538,10 @@ static int check_x(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k
     return SBQ_OK;
 }
 
-static int minmax_blocks(int64_t m, int64_t k) {
-    const int64_t vecs = m * k / 4;
-    int64_t b = (vecs + kQuantThreads * 4 - 1) / (kQuantThreads * 4);
+// CTAs of the two per-tensor steps: kQuantVecs vectors per thread, at most kMaxPartials CTAs.
+static int minmax_blocks(int64_t m, int64_t k, int vec) {
+    const int64_t vecs = m * (k / vec);
+    int64_t b = (vecs + kQuantThreads * kQuantVecs - 1) / (kQuantThreads * kQuantVecs);
     if (b > kMaxPartials) b = kMaxPartials;
     return (int)(b < 1 ? 1 : b);
 }
@@ -454,20 +573,39 @@ static DynWorkspace dyn_workspace(void* base, int64_t m, int64_t k) {
     return w;
 }
 
+// Launches `kernel` after the previous work on the stream with programmatic stream serialisation:
+// it may start once every CTA of the previous grid has run griddepcontrol.launch_dependents, and
+// must run griddepcontrol.wait before it reads anything that grid writes.
+template <typename... Params, typename... Args>
+static void launch_dependent(void (*kernel)(Params...), dim3 grid, int threads, int smem, cudaStream_t st,
+                             Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3((unsigned)threads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
+// Step 1 is an ordinary launch (x may be the previous kernel's output); step 3 depends on it
+// programmatically.
 template <typename T>
 static void launch_quant_tensor(const void* x, int64_t ldx, int m, int k, float2* partials, uint8_t* xq, float* s,
                                 int32_t* zp, cudaStream_t st) {
-    const int nb = minmax_blocks(m, k);
+    const int nb = minmax_blocks(m, k, Vec<T>::kN);
     minmax_partial_kernel<T><<<nb, kQuantThreads, 0, st>>>(static_cast<const T*>(x), ldx, m, k, partials);
-    quantize_per_tensor_kernel<T><<<nb, kQuantThreads, 0, st>>>(static_cast<const T*>(x), ldx, m, k, partials, nb, xq,
-                                                                s, zp);
+    launch_dependent(quantize_per_tensor_kernel<T>, dim3(nb), kQuantThreads, 0, st, static_cast<const T*>(x), ldx, m,
+                     k, static_cast<const float2*>(partials), nb, xq, s, zp);
 }
 
 template <typename T>
 static void launch_quant_token(const void* x, int64_t ldx, int m, int k, int8_t* xq, float* s, cudaStream_t st) {
-    const int rows_per_block = kQuantThreads / 32;
-    quantize_per_token_kernel<T><<<(m + rows_per_block - 1) / rows_per_block, kQuantThreads, 0, st>>>(
-        static_cast<const T*>(x), ldx, m, k, xq, s);
+    quantize_per_token_kernel<T><<<m, kTokThreads, 0, st>>>(static_cast<const T*>(x), ldx, m, k, xq, s);
 }
 
 static int quant_tensor(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, float2* partials, uint8_t* xq,
@@ -516,19 +654,34 @@ static int make_gemm_maps(CUtensorMap* ma, CUtensorMap* mb, const void* xq, int6
 
 constexpr int kI8BN = 128;
 
-static int launch_gemm_i8(const void* xq, bool a_signed, const void* packed, const GemmI8Params& p, cudaStream_t st) {
-    CUtensorMap ma, mb;
+// dependent: launched as a programmatic dependent of the activation quantisation (sbq_linear_dyn),
+// which lets the pipeline set-up and the first weight tiles overlap that kernel.  Direct calls of
+// sbq_gemm_w8a8 launch in plain stream order: there the scale, bias and row sums read in the
+// prologue could be the previous kernel's output.
+static int launch_gemm_i8(const void* xq, bool a_signed, const void* packed, const GemmI8Params& p, bool dependent,
+                          cudaStream_t st) {
+    CUtensorMap ma, mb, my;
     int rc = make_gemm_maps(&ma, &mb, xq, p.m, p.k, packed, p.n, kI8BN);
     if (rc) return rc;
+    std::memset(&my, 0, sizeof(my));
+    GemmI8Params q = p;
+    q.tma_y = !p.acc_out && reinterpret_cast<uintptr_t>(p.y) % 16 == 0 && p.ldy % 4 == 0;
+    if (q.tma_y) {
+        // y [m, n] fp32 as 32 x 32 boxes, 128-byte swizzle (one 128-byte line per box row)
+        const uint64_t dims[2] = {(uint64_t)p.n, (uint64_t)p.m};
+        const uint64_t strides[1] = {(uint64_t)p.ldy * 4};
+        const uint32_t box[2] = {32, 32};
+        rc = encode_tmap(&my, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    }
     const dim3 grid((unsigned)ceil_div(p.n, kI8BN), (unsigned)ceil_div(p.m, kI8BM));
     const int smem = I8Smem<kI8BN>::kBytes;
-    if (a_signed) {
-        cudaFuncSetAttribute(gemm_w8a8_kernel<kI8BN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        gemm_w8a8_kernel<kI8BN, true><<<grid, 128, smem, st>>>(ma, mb, p);
-    } else {
-        cudaFuncSetAttribute(gemm_w8a8_kernel<kI8BN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        gemm_w8a8_kernel<kI8BN, false><<<grid, 128, smem, st>>>(ma, mb, p);
-    }
+    auto kernel = a_signed ? gemm_w8a8_kernel<kI8BN, true> : gemm_w8a8_kernel<kI8BN, false>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (dependent)
+        launch_dependent(kernel, grid, 128, smem, st, ma, mb, my, q);
+    else
+        kernel<<<grid, 128, smem, st>>>(ma, mb, my, q);
     return check_launch("gemm_w8a8");
 }
 
@@ -582,9 +735,9 @@ static int check_gemm(const void* xq, int mode, const void* packed, const int32_
     return SBQ_OK;
 }
 
-extern "C" int sbq_gemm_w8a8(const void* xq, int mode, const void* packed, const int32_t* rowsum, const float* s_x,
-                             const int32_t* zp, const float* scale, const float* bias, int64_t m, int64_t n, int64_t k,
-                             float* y, int64_t ldy, int32_t* acc_out, void* stream) {
+static int gemm_w8a8(const void* xq, int mode, const void* packed, const int32_t* rowsum, const float* s_x,
+                     const int32_t* zp, const float* scale, const float* bias, int64_t m, int64_t n, int64_t k, float* y,
+                     int64_t ldy, int32_t* acc_out, bool dependent, void* stream) {
     int st = check_gemm(xq, mode, packed, rowsum, s_x, zp, scale, m, n, k, y, ldy);
     if (st) return st;
     GemmI8Params p{};
@@ -602,7 +755,13 @@ extern "C" int sbq_gemm_w8a8(const void* xq, int mode, const void* packed, const
     p.y = y;
     p.ldy = ldy;
     p.acc_out = acc_out;
-    return launch_gemm_i8(xq, !per_tensor, packed, p, static_cast<cudaStream_t>(stream));
+    return launch_gemm_i8(xq, !per_tensor, packed, p, dependent, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sbq_gemm_w8a8(const void* xq, int mode, const void* packed, const int32_t* rowsum, const float* s_x,
+                             const int32_t* zp, const float* scale, const float* bias, int64_t m, int64_t n, int64_t k,
+                             float* y, int64_t ldy, int32_t* acc_out, void* stream) {
+    return gemm_w8a8(xq, mode, packed, rowsum, s_x, zp, scale, bias, m, n, k, y, ldy, acc_out, false, stream);
 }
 
 extern "C" int sbq_linear_dyn(const void* x, int x_dtype, int64_t ldx, int mode, const void* packed,
@@ -624,7 +783,7 @@ extern "C" int sbq_linear_dyn(const void* x, int x_dtype, int64_t ldx, int mode,
         return set_error(SBQ_ERR_INVALID_ARGUMENT, "unknown activation mode %d", mode);
     }
     if (st) return st;
-    return sbq_gemm_w8a8(w.xq, mode, packed, rowsum, w.s, w.zp, scale, bias, m, n, k, y, ldy, nullptr, stream);
+    return gemm_w8a8(w.xq, mode, packed, rowsum, w.s, w.zp, scale, bias, m, n, k, y, ldy, nullptr, true, stream);
 }
 
 // ============================================================================ no-allocation variant

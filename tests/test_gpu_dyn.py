@@ -109,3 +109,29 @@ def test_dyn_host_input_and_batch_dims(sbq):
     assert y.device.type == "cpu" and tuple(y.shape) == (2, 3, 48)
     q, sc = R.quantize_per_channel(w.numpy())
     assert np.array_equal(_bits(y.numpy().reshape(6, 48)), _bits(R.dyn_linear(x.numpy().reshape(6, 128), q, sc)[0]))
+
+
+@pytest.mark.parametrize("ldy_pad", [4, 1, 36])
+@pytest.mark.parametrize("mode", ["per_tensor", "per_token"])
+def test_dyn_strided_output_rows(sbq, ldy_pad, mode):
+    """y with a row stride above n, 16-byte aligned rows (staged tile stores) or not (direct stores);
+    the padding columns between rows stay untouched."""
+    import ctypes
+
+    m, n, k = 200, 300, 512
+    w = sbq.workloads.float_weight(n, k, seed=60)
+    x = sbq.workloads.activation(m, k, seed=61, dtype=torch.float16).cuda()
+    mod = sbq.DynamicInt8Linear(w, None, mode=mode)
+    want = mod(x)
+    L = sbq._lib
+    ldy = n + ldy_pad
+    y = torch.full((m, ldy), -7.25, device="cuda")
+    code = L.ACT_PER_TENSOR if mode == "per_tensor" else L.ACT_PER_TOKEN
+    wsb = int(L.load().sbq_dyn_workspace_bytes(m, k, code))
+    ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+    p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    L.call("sbq_linear_dyn", p(x), L.F16, k, code, p(mod.packed), p(mod.rowsum), p(mod.scale), None, m, n, k, p(y),
+           ldy, p(ws), wsb, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert torch.equal(y[:, :n], want)
+    assert bool((y[:, n:] == -7.25).all())
+    assert sbq._lib.load().sbq_check_device_error() == 0
