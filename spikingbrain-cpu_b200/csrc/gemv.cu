@@ -10,9 +10,10 @@
 //     and every CTA slot of the GPU (three per SM) runs one CTA; each CTA's producer thread takes
 //     its first unit by block index and claims the next ones from a per-launch counter, largest
 //     units first, and streams them with cp.async.bulk copies into a 48 KiB shared-memory ring
-//     (8 KiB chunks, mbarrier transaction counts; each chunk's unit described beside it);
-//   * eight consumer warps (or four on gate and four on up) take one 1 KiB tile of each chunk:
-//     two conflict-free 16-byte shared loads per lane, int8 -> fp16 (or bf16) in registers
+//     (16 KiB chunks, mbarrier transaction counts; each chunk's unit described beside it);
+//   * eight consumer warps (or four on gate and four on up) take two 1 KiB tiles of each chunk
+//     (one chunk's waits and bookkeeping per two tiles): per tile two conflict-free 16-byte shared
+//     loads per lane, int8 -> fp16 (or bf16) in registers
 //     (exact), m16n8k16 tensor-core MMAs with fp32 accumulation and the activation rows as the n
 //     dimension (8 or 16 tokens per pass); activation fragments are read in place (L1-cached)
 //     before waiting for the chunk, so the load overlaps the wait;
@@ -60,7 +61,7 @@ struct GemvJob {
     int n;
     int k;
     int kt_total;      // ceil(k / 64)
-    int chunk_tiles;   // tiles per chunk and matrix: the largest of 8 (4 for gate/up), 4, 2, 1 dividing kt_total
+    int chunk_tiles;   // tiles per chunk and matrix: the largest of 16 (8 for gate/up), 8, 4, 2, 1 dividing kt_total
     int out_f16;       // 1: fp16 output, 0: fp32
     int n_tiles;       // 16-row tiles of the weight
 };
@@ -250,12 +251,12 @@ __device__ __forceinline__ void tile_mma(float (&acc)[MT][4], const uint4& wa, c
 
 
 constexpr int kGemvThreads = (kGemvWarps + 1) * 32;  // 8 consumer warps + 1 producer warp
-constexpr int kChunkTiles = 8;                         // tiles (KiB) per chunk and matrix, at most
+constexpr int kChunkTiles = 16;                        // tiles (KiB) per chunk and matrix, at most
 #ifndef SBQ_GEMV_STAGES
-#define SBQ_GEMV_STAGES 6
+#define SBQ_GEMV_STAGES 3
 #endif
-constexpr int kMaxStages = SBQ_GEMV_STAGES;            // ring stages of 8 KiB (8 tiles, or 4 gate + 4 up tiles)
-constexpr int kRingBytes = kMaxStages * 8 * 1024;
+constexpr int kMaxStages = SBQ_GEMV_STAGES;            // ring stages of 16 KiB (16 tiles, or 8 gate + 8 up tiles)
+constexpr int kRingBytes = kMaxStages * 16 * 1024;
 template <int MT>
 struct GemvSmemSize {
     static constexpr int kRed = 2 * kGemvWarps * MT * 16 * 9 * 4;  // per-warp partial sums of two tiles
@@ -350,9 +351,11 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, unsigned* cl
     }
 }
 
-// Consumers (8 warps): per unit, its chunks (each warp takes one 1 KiB tile of each chunk: two
-// conflict-free 16-byte shared loads per lane, int8 -> fp16/bf16 in registers, m16n8k16 MMAs with
-// the activation rows as the n dimension), then the fixed-order reduction and the epilogue.  The
+// Consumers (8 warps): per unit, its chunks (each warp takes tiles slot and slot + 8 of each chunk,
+// or slot and slot + 4 of each matrix of a gate/up chunk - the same tiles, in the same order, as one
+// tile per warp of chunks half the size; per tile two conflict-free 16-byte shared loads per lane,
+// int8 -> fp16/bf16 in registers, m16n8k16 MMAs with the activation rows as the n dimension), then
+// the fixed-order reduction and the epilogue.  The
 // job and the warp split are read once per unit from the first chunk's stage.
 // False (warp-uniformly) on a timeout.
 // `ci` / `units`: ring position and units done so far (both continue across calls).
@@ -383,10 +386,13 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
         const int C = jb.chunk_tiles;
         const int mat = two ? warp >> 2 : 0, slot = two ? warp & 3 : warp;
         const bool mine = slot < C;
+        const int W2 = two ? 4 : 8;
+        const bool mine2 = slot + W2 < C;
         const void* xj = jb.x;
         const int64_t ldx = jb.ldx;
         const int xm = jb.m, xk = jb.k;
         const uint32_t toff = (uint32_t)((mat * C + slot) * kTileBytes + lane * 16);
+        const uint32_t toff2 = toff + W2 * kTileBytes;
         float acc[MT][4];
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
@@ -403,11 +409,16 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
                 else if (jb.bias) bz = jb.bias[n];
             }
         }
-        XFrag<XK> xf[MT];
+        XFrag<XK> xf[MT], xf2[MT];
         if (mine) {
             const int64_t k0 = (int64_t)(i0 * C + slot) * kTileCols + 16 * c;
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xj, ldx, 8 * mt + g, xm, k0, xk);
+        }
+        if (mine2) {
+            const int64_t k0 = (int64_t)(i0 * C + slot + W2) * kTileCols + 16 * c;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf2[mt], xj, ldx, 8 * mt + g, xm, k0, xk);
         }
         for (int i = 0;;) {
             if (mine) {
@@ -415,6 +426,12 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
                 const uint4 wa = *reinterpret_cast<const uint4*>(t);
                 const uint4 wb = *reinterpret_cast<const uint4*>(t + 512);
                 tile_mma<XK, MT>(acc, wa, wb, xf);
+            }
+            if (mine2) {
+                const uint8_t* t = ring + s * kStageBytes + toff2;
+                const uint4 wa = *reinterpret_cast<const uint4*>(t);
+                const uint4 wb = *reinterpret_cast<const uint4*>(t + 512);
+                tile_mma<XK, MT>(acc, wa, wb, xf2);
             }
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&empty[s]);
@@ -426,6 +443,11 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
                 const int64_t k0 = (int64_t)((i0 + i) * C + slot) * kTileCols + 16 * c;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], xj, ldx, 8 * mt + g, xm, k0, xk);
+            }
+            if (mine2) {
+                const int64_t k0 = (int64_t)((i0 + i) * C + slot + W2) * kTileCols + 16 * c;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf2[mt], xj, ldx, 8 * mt + g, xm, k0, xk);
             }
             s = ci % S;
             if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], (ci / S) & 1))) return false;
@@ -1066,8 +1088,8 @@ static void fill_job(GemvJob& jb, const void* x, int64_t ldx, const void* w0, co
     jb.n = (int)n;
     jb.k = (int)k;
     jb.kt_total = (int)ceil_div(k, kTileCols);
-    const int cmax = w1 ? 4 : 8;  // a chunk is 8 KiB: 8 tiles of one matrix or 4 of each of two
-    jb.chunk_tiles = jb.kt_total % cmax == 0 ? cmax : jb.kt_total % 4 == 0 ? 4 : jb.kt_total % 2 == 0 ? 2 : 1;
+    const int cmax = w1 ? 8 : 16;  // a chunk is 16 KiB: 16 tiles of one matrix or 8 of each of two
+    jb.chunk_tiles = jb.kt_total % cmax == 0 ? cmax : jb.kt_total % 8 == 0 ? 8 : jb.kt_total % 4 == 0 ? 4 : jb.kt_total % 2 == 0 ? 2 : 1;
     jb.out_f16 = y_dtype == SBQ_F16;
 }
 
