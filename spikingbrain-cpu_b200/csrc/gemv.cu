@@ -295,7 +295,9 @@ __device__ __forceinline__ int consumers_sync_and(int v) {
 // shared memory; x is read in place, so a CTA may take units of different jobs.
 // ---------------------------------------------------------------------------------------------
 constexpr int kClaimSlots = 1024;  // per-launch counters, used round-robin by consecutive launches
-static __device__ unsigned g_claim[kClaimSlots][2];  // [next unit, CTAs finished]; reset by the last CTA
+static __device__ unsigned g_claim[kClaimSlots][2];  // [next unit, unused]; reset by the launch's last claimer
+// (every claiming CTA makes exactly one failing claim, so the values handed out are 0 .. units - 1;
+// the producer that gets units - 1 resets the counter, early and off the CTAs' exit path)
 
 // Split-K scratch: when a launch has too few tiles to keep every CTA busy (a sharded step on several
 // GPUs), tiles are cut into K parts; each part's partial sums go here and the CTA that completes a
@@ -308,8 +310,9 @@ static __device__ float g_split[kSplitRegions][kSplitFloats];
 static __device__ unsigned g_split_count[kSplitRegions][kSplitTiles];
 
 // Producer (one thread).  Claims the next unit while the last ring-full of the current one is
-// still to be issued, so the claim's latency is hidden.  False if a wait timed out.
-// `claim`: the work counter pair; `ci`: ring position (continues across calls, the decode program
+// still to be issued, so the claim's latency is hidden; the producer that makes the launch's last
+// claim resets the counter.  False if a wait timed out (after the CTA's remaining claims, so that
+// the reset still happens).  `claim`: the work counter pair; `ci`: ring position (continues across calls, the decode program
 // streams one group per stage through the same ring).  The end marker takes a ring slot too.
 __device__ __forceinline__ bool produce_units(const GemvGroup& grp, unsigned* claim, uint8_t* ring, uint64_t* full,
                                               uint64_t* empty, int4* meta, uint32_t& ci) {
@@ -336,18 +339,27 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, unsigned* cl
         const int8_t* src0 = jb.w0 + (int64_t)tile * jb.kt_total * kTileBytes;
         const int8_t* src1 = jb.w1 ? jb.w1 + (int64_t)tile * jb.kt_total * kTileBytes : nullptr;
         const int claim_at = i1 - i0 > S ? i1 - S : i0;
-        int next = 0;
+        unsigned v = 0;
         for (int i = i0; i < i1; ++i, ++ci) {
-            if (i == claim_at) next = (int)(gridDim.x + atomicAdd(claim, 1u));
+            if (i == claim_at) v = atomicAdd(claim, 1u);
             const int s = ci % S;
-            if (!tc::mbar_wait(&empty[s], ((ci / S) & 1) ^ 1)) return false;
+            if (!tc::mbar_wait(&empty[s], ((ci / S) & 1) ^ 1)) {
+                // keep the count: claim (and drop) until this CTA's one failing claim
+                if (i < claim_at) v = atomicAdd(claim, 1u);
+                while ((int)(gridDim.x + v) < grp.total_units) v = atomicAdd(claim, 1u);
+                if (v == (unsigned)grp.total_units - 1u) claim[0] = 0;
+                return false;
+            }
             meta[s] = make_int4(j | (part << 8), tile, i, i1 - i0);
             uint8_t* dst = ring + s * kStageBytes;
             tc::mbar_arrive_expect_tx(&full[s], bytes * nmat);
             tc::bulk_load(dst, src0 + (int64_t)i * bytes, bytes, &full[s]);
             if (nmat == 2) tc::bulk_load(dst + bytes, src1 + (int64_t)i * bytes, bytes, &full[s]);
         }
-        u = next;
+        // every claiming CTA makes exactly one failing claim, so the values handed out are
+        // 0 .. total_units - 1 and the one that gets the last has made the launch's last claim
+        if (v == (unsigned)grp.total_units - 1u) claim[0] = 0;
+        u = (int)(gridDim.x + v);
     }
 }
 
@@ -617,21 +629,7 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? kCtasPerSm : 2)
     int units = 0;
     const bool ok = consume_units<XK, MT, PEER>(grp, ring, red, full, empty, meta, ps, ci, units);
     if (!consumers_sync_and(ok) && threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
-    if (warp == 0) {
-        // count out; the last CTA resets the launch's counter for the next launch that uses it
-        // (every producer has made its last claim before its consumers saw the end marker)
-        unsigned last = 0;
-        if (lane == 0) {
-            __threadfence();
-            last = atomicAdd(grp.claim + 1, 1u) == gridDim.x - 1;
-            if (last) {
-                grp.claim[0] = 0;
-                grp.claim[1] = 0;
-            }
-        }
-        __syncwarp();
-        if (PEER) peer_publish(ps, lane);  // also after a timeout, so that the other ranks do not wait in vain
-    }
+    if (PEER && warp == 0) peer_publish(ps, lane);  // also after a timeout, so that the other ranks do not wait in vain
 }
 
 // Waits (one CTA) for a peer launch's outputs: the end of a sharded decode step, before the host
