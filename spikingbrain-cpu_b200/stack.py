@@ -6,14 +6,18 @@ Each layer holds the projections the hybrid model runs through its int8 linears
 flow between them is real, so every projection depends on the one before it:
 
     qkvd = [q | k | v | delta_in](x)          one GEMV/GEMM over the concatenated weight (fp16 out)
-    od   = [o(v) | delta_out(delta_in)]       two launches writing one fp16 buffer
     h    = silu(gate(x)) * up(x)              fused gate/up kernel (fp16 h)
-    x'   = down(h)                            fp16, the next layer's input
+    od   = [down(h) | delta_out(delta_in)]    the layer's side outputs, one fp16 buffer
+    x'   = o(v)                               fp16, the next layer's input
 
-so a decode step streams every weight of every layer exactly once.  Constant factors are folded
-into the per-row scales of the projections whose outputs are consumed (v, delta_in, down) so
-the activations stay near unit variance over 36 layers; the int8 weights themselves follow the
-reference quantiser on ``N(0, 0.02)`` weights.
+so a decode step streams every weight of every layer exactly once, and each layer's launches wait
+for the previous layer.  Constant factors are folded into the per-row scales (qkvd, o, delta_out,
+down) so every output has about unit variance; the int8 weights themselves follow the reference
+quantiser on ``N(0, 0.02)`` weights.  The chain from layer to layer runs through the linear
+attention path: h is quadratic in x, so a chain through down(h) is unstable under any constant
+scale (a layer input slightly below unit scale shrinks quadratically from layer to layer and
+reaches zero in fp16 within about twelve layers).  The model's residual stream and norms are not
+part of the quantised-linear path.
 
 Sharding (``world > 1``): rank r owns rows [r n / world, (r+1) n / world) of every projection and
 produces that slice of each output; x is replicated.  Two ways assemble the full activation before
@@ -213,12 +217,13 @@ class PeerExchange:
                              None if i == 0 else self.cnt[i - 1][1], self.state[i][0])
             L.call("sbq_gemv_w8_group_peer", (L.GemvJob * 2)(*jobs), 2, code, m, ctypes.byref(pg), stream)
             s = hd // w
-            jobs = [layer.mlp.down_proj.gemv_job(h, xn[:, r * s:(r + 1) * s]),
-                    layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], od[:, r * s:(r + 1) * s]),
+            jobs = [layer.mlp.down_proj.gemv_job(h, od[:, r * s:(r + 1) * s]),
+                    layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], xn[:, r * s:(r + 1) * s]),
                     layer.dout.gemv_job(qkvd[:, 3 * hd:], od[:, hd + r * s:hd + (r + 1) * s])]
-            pg = self._group([(x_off, r * s), (od_off, r * s), (od_off, hd + r * s)], self.cnt[i][1],
+            pg = self._group([(od_off, r * s), (x_off, r * s), (od_off, hd + r * s)], self.cnt[i][1],
                              self.done[i][1], self.cnt[i][0], self.state[i][1])
             L.call("sbq_gemv_w8_group_peer", (L.GemvJob * 3)(*jobs), 3, code, m, ctypes.byref(pg), stream)
+            st.side = od
             cur = xn
         L.call("sbq_peer_wait", ctypes.c_void_p(self.base + self.cnt[-1][1]),
                ctypes.c_void_p(self.base + self.final_state), w, 0, stream)
@@ -261,6 +266,7 @@ class ProjectionStack(nn.Module):
                                     for i in range(layers))
         self.exchange = exchange if self.world > 1 else "none"
         self.peer = PeerExchange(self) if self.exchange == "peer" else None
+        self.side = None  # the last forward's last-layer side outputs [down(h) | delta_out] (full width)
 
     def weight_bytes(self) -> int:
         """int8 weight bytes this rank streams per decode step."""
@@ -283,7 +289,8 @@ class ProjectionStack(nn.Module):
         """fp16 [m, hidden] on the device -> fp16 [m, hidden] (the last layer's down projection).
 
         Decode sizes (m <= 16) run each layer as two grouped launches: [gate/up, q|k|v|delta_in]
-        (both read x) and [down, o, delta_out] (after their inputs are gathered).
+        (both read x) and [down, o, delta_out] (after their inputs are gathered); o's output is the
+        next layer's input.
         """
         if x.shape[0] <= 16:
             if self.peer is not None:
@@ -293,12 +300,12 @@ class ProjectionStack(nn.Module):
         m = x.shape[0]
         for layer in self.layers:
             qkvd = self._gather(layer.qkvd.forward_into(x, x.new_empty(m, 4 * hd // w)))
-            od = x.new_empty(m, 2 * hd // w)
-            layer.o.forward_into(qkvd[:, 2 * hd:3 * hd], od[:, :hd // w])
-            layer.dout.forward_into(qkvd[:, 3 * hd:], od[:, hd // w:])
-            self._gather(od)
             h = self._gather(layer.mlp.gateup_into(x, x.new_empty(m, self.inter // w)))
-            x = self._gather(layer.mlp.down_proj.forward_into(h, x.new_empty(m, hd // w)))
+            od = x.new_empty(m, 2 * hd // w)
+            layer.mlp.down_proj.forward_into(h, od[:, :hd // w])
+            layer.dout.forward_into(qkvd[:, 3 * hd:], od[:, hd // w:])
+            self.side = self._gather(od)
+            x = self._gather(layer.o.forward_into(qkvd[:, 2 * hd:3 * hd], x.new_empty(m, hd // w)))
         return x
 
     def _forward_grouped(self, x: torch.Tensor) -> torch.Tensor:
@@ -313,9 +320,9 @@ class ProjectionStack(nn.Module):
             qkvd, h = self._gather(qkvd), self._gather(h)
             od = x.new_empty(m, 2 * hd // w)
             xn = x.new_empty(m, hd // w)
-            gemv_group([layer.mlp.down_proj.gemv_job(h, xn), layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], od[:, :hd // w]),
+            gemv_group([layer.mlp.down_proj.gemv_job(h, od[:, :hd // w]), layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], xn),
                         layer.dout.gemv_job(qkvd[:, 3 * hd:], od[:, hd // w:])], x.dtype, m, x.device)
-            self._gather(od)
+            self.side = self._gather(od)
             x = self._gather(xn)
         return x
 
@@ -341,7 +348,7 @@ class DecodeProgram:
     pauses.  On one GPU every layer gets its own activation buffers (written once per step); a
     sharded stack uses its peer arena (outputs stored to every rank, barriers spanning the ranks).
     ``run()`` reads the fixed input buffer ``x`` and returns the fixed output buffer (the last
-    layer's down output, full width).
+    layer's o output, full width).
     """
 
     def __init__(self, stack: ProjectionStack, x: torch.Tensor):
@@ -376,10 +383,10 @@ class DecodeProgram:
                      layer.qkvd.gemv_job(cur, sl(qkvd, r * qs, (r + 1) * qs))]
             dests += [(h_off, r * hs), (q_off, r * qs)]
             stage += [2 * i, 2 * i]
-            jobs += [layer.mlp.down_proj.gemv_job(h, sl(nxt, r * s, (r + 1) * s)),
-                     layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], sl(od, r * s, (r + 1) * s)),
+            jobs += [layer.mlp.down_proj.gemv_job(h, sl(od, r * s, (r + 1) * s)),
+                     layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], sl(nxt, r * s, (r + 1) * s)),
                      layer.dout.gemv_job(qkvd[:, 3 * hd:], sl(od, hd + r * s, hd + (r + 1) * s))]
-            dests += [(x_off, r * s), (od_off, r * s), (od_off, hd + r * s)]
+            dests += [(od_off, r * s), (x_off, r * s), (od_off, hd + r * s)]
             stage += [2 * i + 1] * 3
             cur = nxt
         self.y = cur

@@ -51,8 +51,10 @@ def main() -> int:
         for m in (1, 3, 16):
             x = sbq.workloads.activation(m, shape["hidden"], seed=20 + m, device=dev)
             check("%s eager m=%d" % (exchange, m), st(x).clone(), ref(x))
+            check("%s eager side outputs m=%d" % (exchange, m), st.side.clone(), ref.side)
         x = sbq.workloads.activation(80, shape["hidden"], seed=3, device=dev)
         check_close("%s prefill m=80" % exchange, st(x).clone(), ref(x))
+        check_close("%s prefill side outputs m=80" % exchange, st.side.clone(), ref.side)
         run = sbq.stack.CapturedStack(st, m=1)
         # back-to-back replays with a new input each: a stale slice from an earlier step would show
         xs = [sbq.workloads.activation(1, shape["hidden"], seed=100 + i, device=dev) for i in range(24)]
