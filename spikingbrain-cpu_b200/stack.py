@@ -223,7 +223,7 @@ class PeerExchange:
             pg = self._group([(od_off, r * s), (x_off, r * s), (od_off, hd + r * s)], self.cnt[i][1],
                              self.done[i][1], self.cnt[i][0], self.state[i][1])
             L.call("sbq_gemv_w8_group_peer", (L.GemvJob * 3)(*jobs), 3, code, m, ctypes.byref(pg), stream)
-            st.side = od
+            st._side = (od, False)  # stored in place at full width
             cur = xn
         L.call("sbq_peer_wait", ctypes.c_void_p(self.base + self.cnt[-1][1]),
                ctypes.c_void_p(self.base + self.final_state), w, 0, stream)
@@ -242,6 +242,15 @@ class PeerExchange:
         self.arena = None
         self.L.call("sbq_peer_free", ctypes.c_void_p(self.base))
         self.base = None
+
+
+def side_layout(gathered: torch.Tensor | None, world: int, hidden: int) -> torch.Tensor | None:
+    """[m, world * 2 * hidden / world] all-gathered [down slice | delta_out slice] blocks of every rank
+    -> [m, 2 * hidden] = [down(h) | delta_out(delta_in)] in channel order."""
+    if gathered is None or world == 1:
+        return gathered
+    m = gathered.shape[0]
+    return gathered.reshape(m, world, 2, hidden // world).transpose(1, 2).reshape(m, 2 * hidden)
 
 
 class ProjectionStack(nn.Module):
@@ -266,7 +275,13 @@ class ProjectionStack(nn.Module):
                                     for i in range(layers))
         self.exchange = exchange if self.world > 1 else "none"
         self.peer = PeerExchange(self) if self.exchange == "peer" else None
-        self.side = None  # the last forward's last-layer side outputs [down(h) | delta_out] (full width)
+        self._side = (None, False)  # the last forward's last-layer side outputs, reordered on access?
+
+    @property
+    def side(self) -> torch.Tensor | None:
+        """The last forward's last-layer side outputs [down(h) | delta_out(delta_in)], full width."""
+        t, gathered = self._side
+        return side_layout(t, self.world, self.hidden) if gathered else t
 
     def weight_bytes(self) -> int:
         """int8 weight bytes this rank streams per decode step."""
@@ -304,7 +319,7 @@ class ProjectionStack(nn.Module):
             od = x.new_empty(m, 2 * hd // w)
             layer.mlp.down_proj.forward_into(h, od[:, :hd // w])
             layer.dout.forward_into(qkvd[:, 3 * hd:], od[:, hd // w:])
-            self.side = self._gather(od)
+            self._side = (self._gather(od), True)
             x = self._gather(layer.o.forward_into(qkvd[:, 2 * hd:3 * hd], x.new_empty(m, hd // w)))
         return x
 
@@ -322,7 +337,7 @@ class ProjectionStack(nn.Module):
             xn = x.new_empty(m, hd // w)
             gemv_group([layer.mlp.down_proj.gemv_job(h, od[:, :hd // w]), layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], xn),
                         layer.dout.gemv_job(qkvd[:, 3 * hd:], od[:, hd // w:])], x.dtype, m, x.device)
-            self.side = self._gather(od)
+            self._side = (self._gather(od), True)
             x = self._gather(xn)
         return x
 

@@ -44,6 +44,14 @@ def _worker(rank, world, port, results):
             part = full[:, rank * 64 // world:(rank + 1) * 64 // world]
             got = stack_mod.ProjectionStack._gather(stub, part)
             out[m] = bool(torch.equal(got, full))
+            # the side outputs: each rank holds [down slice | delta_out slice] in one buffer; the
+            # gathered blocks reorder to [down | delta_out] in channel order
+            hd = 32
+            down, dout = full[:, :hd], full[:, hd:] + 1000.0
+            s = hd // world
+            od = torch.cat([down[:, rank * s:(rank + 1) * s], dout[:, rank * s:(rank + 1) * s]], 1)
+            side = stack_mod.side_layout(stack_mod.ProjectionStack._gather(stub, od), world, hd)
+            out["side%d" % m] = bool(torch.equal(side, torch.cat([down, dout], 1)))
         results[rank] = out
     finally:
         dist.destroy_process_group()
@@ -62,4 +70,4 @@ def test_gather_reassembles_sharded_output(world):
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs)
     for r in range(world):
-        assert results[r] == {1: True, 5: True}
+        assert results[r] == {1: True, 5: True, "side1": True, "side5": True}
