@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
                 tc::tmem_wait_ld();
                 if (n >= p.n) continue;
                 const int tb = t0 + c * 32;
-                if (GATED) {
+                if constexpr (GATED) {
                     // all 32 gate values are loaded before any is used (independent loads)
                     float gv[32];
 #pragma unroll
@@ -216,15 +216,15 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
                         if (has_bias) v = __fadd_rn(v, bi);
                         put_y<OUT_F16>(p, tb + j, n, gv[j] / (1.0f + expf(-gv[j])) * v);
                     }
-                    continue;
-                }
+                } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int t = tb + j;
-                    if (t >= p.m) break;
-                    float v = __fmul_rn(__uint_as_float(r[j]), sc);
-                    if (has_bias) v = __fadd_rn(v, bi);
-                    put_y<OUT_F16>(p, t, n, v);
+                    for (int j = 0; j < 32; ++j) {
+                        const int t = tb + j;
+                        if (t >= p.m) break;
+                        float v = __fmul_rn(__uint_as_float(r[j]), sc);
+                        if (has_bias) v = __fadd_rn(v, bi);
+                        put_y<OUT_F16>(p, t, n, v);
+                    }
                 }
             }
         }

@@ -964,8 +964,8 @@ static void choose_parts(const PartsKey& key, int* parts_out) {
 // or one CTA per unit if there are fewer), 0 if the device buffers are unavailable.
 static int plan_units(GemvGroup& grp, PeerSync& ps, int slots, int m) {
     const int nj = grp.njobs;
-    int parts[kMaxJobs], tiles[kMaxJobs];
-    int64_t tile_bytes[kMaxJobs];
+    int parts[kMaxJobs] = {}, tiles[kMaxJobs] = {};
+    int64_t tile_bytes[kMaxJobs] = {};
     PartsKey key{};
     key.slots = slots;
     key.m = m;
