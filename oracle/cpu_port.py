@@ -68,12 +68,12 @@ class StackSample:
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         hd = self.hidden
-        for L in self.layers:
+        for L in self.layers:  # the device stack's data flow: o(v) is the next layer's input
             qkvd = int8_forward(x, *L["qkvd"]).half()
-            int8_forward(qkvd[:, 2 * hd:3 * hd], *L["o"])
-            int8_forward(qkvd[:, 3 * hd:], *L["dout"])
             h = (F.silu(int8_forward(x, *L["gate"])) * int8_forward(x, *L["up"])).half()
-            x = int8_forward(h, *L["down"]).half()
+            int8_forward(h, *L["down"])
+            int8_forward(qkvd[:, 3 * hd:], *L["dout"])
+            x = int8_forward(qkvd[:, 2 * hd:3 * hd], *L["o"]).half()
         return x
 
 
