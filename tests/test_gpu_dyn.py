@@ -85,15 +85,20 @@ def test_dyn_shapes_bit_exact(sbq, m, n, k, xdtype):
     assert np.array_equal(_bits(y), _bits(ry)), "mismatch fraction %.4f" % float((y != ry).mean())
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 64, 128), (5, 130, 320), (128, 256, 512), (300, 200, 1024)])
-def test_per_token_mode_bit_exact(sbq, m, n, k):
+@pytest.mark.parametrize("m,n,k,xdtype", [(1, 64, 128, torch.float32), (5, 130, 320, torch.float32),
+                                          (128, 256, 512, torch.float32), (300, 200, 1024, torch.float32),
+                                          # rows longer than the per-thread register cache (512 vectors):
+                                          # the two-pass path that reads each row twice
+                                          (3, 96, 2560, torch.float32), (4, 64, 4160, torch.float16)])
+def test_per_token_mode_bit_exact(sbq, m, n, k, xdtype):
     w = sbq.workloads.float_weight(n, k, seed=n)
     x = sbq.workloads.activation(m, k, seed=m, dtype=torch.float32)
     x[0] = 0.0  # an all-zero token takes the 1e-8 floor
+    x = x.to(xdtype)
     q, sc = R.quantize_per_channel(w.numpy())
     mod = sbq.DynamicInt8Linear(w, None, mode="per_token")
     y, xq, s, _, acc = mod.forward_stages(x.cuda())
-    ry, rxq, rs, racc = R.tok_linear(x.numpy(), q, sc)
+    ry, rxq, rs, racc = R.tok_linear(x.float().numpy(), q, sc)
     assert np.array_equal(_bits(s.cpu().numpy()), _bits(rs))
     assert np.array_equal(xq.cpu().numpy(), rxq)
     assert np.array_equal(acc.cpu().numpy(), racc)

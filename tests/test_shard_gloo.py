@@ -57,7 +57,7 @@ def _worker(rank, world, port, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4])
 def test_gather_reassembles_sharded_output(world):
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
