@@ -45,11 +45,15 @@ SPEC_I8_TOPS = 4500.0       # dense int8 tensor, nominal
 
 
 def peaks() -> dict:
+    """Roofline denominators: HBM copy GB/s, and bf16 TFLOPS as a burst (a kernel timed alone) and
+    sustained under the power cap (a kernel timed inside a long step)."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
-    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": 1590.0, "source": "fallback"}
+        burst = float(d["bf16_tflops"])
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": burst,
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", burst)), "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 class ClockSampler:
@@ -354,8 +358,11 @@ def stack_cases(sbq, stack, dev, stream, warmup: int) -> dict:
     end.synchronize()
     ms = start.elapsed_time(end) / reps
     fl = 2.0 * m * total
+    pk = peaks()
     out["prefill_8192"] = {"ms": round(ms, 2), "tflops": round(fl / ms / 1e9, 1),
-                           "frac_bf16_peak": round(fl / ms / 1e9 / peaks()["bf16_tflops"], 4),
+                           # a step of ~0.16 s runs under the power cap: the sustained figure applies
+                           "frac_bf16_sustained": round(fl / ms / 1e9 / pk["bf16_tflops_sustained"], 4),
+                           "frac_bf16_peak": round(fl / ms / 1e9 / pk["bf16_tflops"], 4),
                            "frac_f16_spec": round(fl / ms / 1e9 / SPEC_F16_TFLOPS, 4),
                            "note": "per-projection GEMMs; gate GEMM then up GEMM with the SiLU*mul epilogue"}
     return out
