@@ -250,14 +250,18 @@ SBQ_API int sbq_quant_act_per_token(const void* x, int x_dtype, int64_t ldx, int
 
 /* acc[m, n] = sum_k (xq - zp) * q (per-tensor; xq uint8) or sum_k xq * q (per-token; xq int8),
  * y = float(acc) * (s * scale[n]) (or fma with bias[n]).  rowsum is required for the per-tensor
- * mode (zero-point correction).  acc_out (may be NULL) receives the int32 accumulators. */
+ * mode (zero-point correction).  acc_out (may be NULL) receives the int32 accumulators.  Launched in
+ * plain stream order (every input may be the previous kernel's output). */
 SBQ_API int sbq_gemm_w8a8(const void* xq, int mode, const void* packed, const int32_t* rowsum, const float* s_x,
                   const int32_t* zp, const float* scale, const float* bias, int64_t m, int64_t n, int64_t k,
                   float* y, int64_t ldy, int32_t* acc_out, void* stream);
 
-/* DynamicInt8Linear.forward (quant.py:63-66): quantise + GEMM + epilogue.  xq_out / s_out / zp_out
- * may be NULL; when given they receive the quantised activation and its parameters.  workspace
- * must hold sbq_dyn_workspace_bytes(m, k, mode) bytes. */
+/* DynamicInt8Linear.forward (quant.py:63-66): quantise + GEMM + epilogue.  The quantised activation
+ * and its parameters live in the workspace (sbq_dyn_workspace_bytes(m, k, mode) bytes, 256-byte
+ * aligned).  The quantisation and the GEMM are chained by programmatic dependent launch (the GEMM's
+ * set-up and first weight tiles overlap the quantisation); work the caller queues afterwards on the
+ * stream runs after the GEMM as usual.  mode: SBQ_ACT_PER_TENSOR (the reference) or
+ * SBQ_ACT_PER_TOKEN. */
 SBQ_API int sbq_linear_dyn(const void* x, int x_dtype, int64_t ldx, int mode, const void* packed,
                    const int32_t* rowsum, const float* scale, const float* bias, int64_t m, int64_t n,
                    int64_t k, float* y, int64_t ldy, void* workspace, size_t workspace_bytes,
