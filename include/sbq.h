@@ -11,6 +11,16 @@
  * (output channels x input features), activations [m, k], outputs [m, n] - the shapes of the
  * reference's nn.Linear replacements.
  *
+ * Streams and host threads: the entry points may be called from several host threads and launch on
+ * any streams.  The decode GEMV (sbq_linear_w8 up to 32 rows, sbq_gemv_w8, sbq_mlp_gateup_w8,
+ * sbq_gemv_w8_group[_peer]) takes a work counter and, for launches whose tiles are cut into K parts,
+ * a split-K scratch region from device arrays of the library.  These are divided into 8 lanes per
+ * device and each stream is given one lane on first use, so launches on up to 8 distinct streams of
+ * a device may run concurrently; a ninth stream shares a lane with an earlier one and must not run
+ * GEMV launches at the same time as it.  A CUDA graph keeps the lane of the stream it was captured
+ * on: graphs captured on one stream must not be replayed concurrently with each other.  Decode
+ * programs (sbq_gemv_program_*) share one further lane: run them on one stream at a time.
+ *
  * Packed weights: an int8 [n, k] matrix stored as 16 x 64 tiles of 1 KiB, tile (nt, kt) at byte
  * (nt * ceil(k/64) + kt) * 1024, rows row-major inside the tile, padding zero-filled.  Its size is
  * sbq_packed_bytes(n, k); it must be 256-byte aligned.
@@ -250,8 +260,11 @@ SBQ_API int sbq_quant_act_per_token(const void* x, int x_dtype, int64_t ldx, int
 
 /* acc[m, n] = sum_k (xq - zp) * q (per-tensor; xq uint8) or sum_k xq * q (per-token; xq int8),
  * y = float(acc) * (s * scale[n]) (or fma with bias[n]).  rowsum is required for the per-tensor
- * mode (zero-point correction).  acc_out (may be NULL) receives the int32 accumulators.  Launched in
- * plain stream order (every input may be the previous kernel's output). */
+ * mode (zero-point correction).  acc_out (may be NULL) receives the int32 accumulators (row stride n).
+ * y and acc_out need only their element alignment (4 bytes): rows whose base pointer is 16-byte
+ * aligned, with ldy and n multiples of 4, are written with vector (or TMA) stores, any other layout
+ * element by element.  Launched in plain stream order (every input may be the previous kernel's
+ * output). */
 SBQ_API int sbq_gemm_w8a8(const void* xq, int mode, const void* packed, const int32_t* rowsum, const float* s_x,
                   const int32_t* zp, const float* scale, const float* bias, int64_t m, int64_t n, int64_t k,
                   float* y, int64_t ldy, int32_t* acc_out, void* stream);
@@ -261,7 +274,8 @@ SBQ_API int sbq_gemm_w8a8(const void* xq, int mode, const void* packed, const in
  * aligned).  The quantisation and the GEMM are chained by programmatic dependent launch (the GEMM's
  * set-up and first weight tiles overlap the quantisation); work the caller queues afterwards on the
  * stream runs after the GEMM as usual.  mode: SBQ_ACT_PER_TENSOR (the reference) or
- * SBQ_ACT_PER_TOKEN. */
+ * SBQ_ACT_PER_TOKEN.  Every argument (those of the GEMM included) is checked before the first
+ * launch: a call that returns an error has launched nothing.  y: as for sbq_gemm_w8a8. */
 SBQ_API int sbq_linear_dyn(const void* x, int x_dtype, int64_t ldx, int mode, const void* packed,
                    const int32_t* rowsum, const float* scale, const float* bias, int64_t m, int64_t n,
                    int64_t k, float* y, int64_t ldy, void* workspace, size_t workspace_bytes,

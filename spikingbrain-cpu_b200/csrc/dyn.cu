@@ -325,6 +325,8 @@ struct GemmI8Params {
     int64_t ldy;
     int32_t* acc_out;       // optional int32 accumulators (zero-point corrected), row stride n
     int tma_y;              // y is written by TMA stores through tmap_y (no acc_out, aligned rows)
+    int vec_y;              // y (and acc_out) rows take 16-byte vector stores: both base pointers 16-byte
+                            // aligned, ldy and n multiples of 4; otherwise the epilogue stores element-wise
 };
 
 constexpr int kI8BM = 128;         // rows of xq per CTA (MMA M)
@@ -494,7 +496,7 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
                 const float af = __int2float_rn(a[j]);
                 v[j] = p.bias ? __fmaf_rn(af, f, s_bias[i]) : __fmul_rn(af, f);
             }
-            if (nb + 32 <= p.n && (p.ldy % 4) == 0 && (p.n % 4) == 0) {
+            if (nb + 32 <= p.n && p.vec_y) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
                     *reinterpret_cast<float4*>(yrow + nb + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -666,6 +668,8 @@ static int launch_gemm_i8(const void* xq, bool a_signed, const void* packed, con
     std::memset(&my, 0, sizeof(my));
     GemmI8Params q = p;
     q.tma_y = !p.acc_out && reinterpret_cast<uintptr_t>(p.y) % 16 == 0 && p.ldy % 4 == 0;
+    q.vec_y = reinterpret_cast<uintptr_t>(p.y) % 16 == 0 && p.ldy % 4 == 0 && p.n % 4 == 0 &&
+              (!p.acc_out || reinterpret_cast<uintptr_t>(p.acc_out) % 16 == 0);
     if (q.tma_y) {
         // y [m, n] fp32 as 32 x 32 boxes, 128-byte swizzle (one 128-byte line per box row)
         const uint64_t dims[2] = {(uint64_t)p.n, (uint64_t)p.m};
@@ -774,6 +778,10 @@ extern "C" int sbq_linear_dyn(const void* x, int x_dtype, int64_t ldx, int mode,
     if (reinterpret_cast<uintptr_t>(workspace) % 256) return set_error(SBQ_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
     DynWorkspace w = dyn_workspace(workspace, m, k);
     if (workspace_bytes < w.bytes) return set_error(SBQ_ERR_WORKSPACE, "workspace needs %zu bytes", w.bytes);
+    // every GEMM argument is checked before the quantisation is launched: a call that fails launches
+    // nothing (and leaves the workspace untouched)
+    st = check_gemm(w.xq, mode, packed, rowsum, w.s, w.zp, scale, m, n, k, y, ldy);
+    if (st) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (mode == SBQ_ACT_PER_TENSOR) {
         st = quant_tensor(x, x_dtype, ldx, m, k, w.partials, w.xq, w.s, w.zp, s);

@@ -16,6 +16,8 @@
 //     tokens each), apply the fp32 per-row scale (and bias) and store fp16 or fp32 output,
 //     consecutive channels per warp store.
 // The scale stays in the fp32 epilogue, as in the reference: int8 values are exact in fp16.
+#include <atomic>
+
 #include "tc.cuh"
 
 namespace sbq {
@@ -502,16 +504,18 @@ using namespace sbq;
 
 constexpr int64_t kSmallMaxRows = 128;  // up to this many activation rows: the 64-token kernel
 
+// SMs of the current device, cached per device (atomics: first calls may come from several threads)
 static int sm_count_w16() {
-    static int count[64] = {};
+    static std::atomic<int> count[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (!count[dev]) {
-        int c = 0;
+    int c = count[dev].load(std::memory_order_relaxed);
+    if (c == 0) {
         cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
-        count[dev] = c > 0 ? c : 148;
+        c = c > 0 ? c : 148;
+        count[dev].store(c, std::memory_order_relaxed);
     }
-    return count[dev];
+    return c;
 }
 
 static int gemm_small(const void* x, int64_t ldx, const void* packed, const float* scale, const float* bias, int64_t m,

@@ -294,20 +294,32 @@ __device__ __forceinline__ int consumers_sync_and(int v) {
 // one unit of its ideal time.  Each ring stage carries its unit's (job, tile, chunk, chunks) in
 // shared memory; x is read in place, so a CTA may take units of different jobs.
 // ---------------------------------------------------------------------------------------------
-constexpr int kClaimSlots = 1024;  // per-launch counters, used round-robin by consecutive launches
-static __device__ unsigned g_claim[kClaimSlots][2];  // [next unit, unused]; reset by the launch's last claimer
+//
+// Work counters and split-K scratch are device arrays of this library, divided into lanes so that
+// launches on different streams never share them: each stream (per device) is given one of kLanes
+// lanes the first time it launches a grouped GEMV, and launches take their counter and scratch from
+// their stream's lane only (decode programs have a lane of their own).  Up to kLanes streams per
+// device can therefore run grouped GEMVs concurrently; a CUDA graph keeps the lane of the stream it
+// was captured on.
+constexpr int kLanes = 8;                  // stream lanes for grouped launches
+constexpr int kProgramLane = kLanes;       // the decode programs' lane
+constexpr int kLaneCount = kLanes + 1;
+constexpr int kClaimSlots = 128;           // per lane: per-launch counters, used round-robin
+static __device__ unsigned g_claim[kLaneCount][kClaimSlots][2];  // [next unit, unused]; reset by the launch's last claimer
 // (every claiming CTA makes exactly one failing claim, so the values handed out are 0 .. units - 1;
 // the producer that gets units - 1 resets the counter, early and off the CTAs' exit path)
 
 // Split-K scratch: when a launch has too few tiles to keep every CTA busy (a sharded step on several
 // GPUs), tiles are cut into K parts; each part's partial sums go here and the CTA that completes a
-// tile's last part adds them in part order (deterministic).  Two regions, used alternately by
-// consecutive launches.
+// tile's last part adds them in part order (deterministic).  Two regions per lane, used alternately
+// by consecutive launches of the lane: with programmatic dependent launch a launch may overlap the
+// one before it on its stream, but its consumers start only after that one has completed, which
+// itself waited for the one before, so a region is never used by two launches at once.
 constexpr int kSplitRegions = 2;
 constexpr int kSplitFloats = 512 * 1024;  // per region (2 MiB)
 constexpr int kSplitTiles = 8192;         // split tiles per region
-static __device__ float g_split[kSplitRegions][kSplitFloats];
-static __device__ unsigned g_split_count[kSplitRegions][kSplitTiles];
+static __device__ float g_split[kLaneCount][kSplitRegions][kSplitFloats];
+static __device__ unsigned g_split_count[kLaneCount][kSplitRegions][kSplitTiles];
 
 // Producer (one thread).  Claims the next unit while the last ring-full of the current one is
 // still to be issued, so the claim's latency is hidden; the producer that makes the launch's last
@@ -808,23 +820,25 @@ static void launch_group(const GemvGroup& grp, const PeerSync& ps, int total_cta
     cudaLaunchKernelEx(&cfg, gemv_w8_kernel<XK, MT, PEER>, grp, ps);
 }
 
+// SMs of the current device, cached per device (atomics: first calls may come from several threads)
 static int sm_count() {
-    static int count[64] = {};
+    static std::atomic<int> count[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (!count[dev]) {
-        int c = 0;
+    int c = count[dev].load(std::memory_order_relaxed);
+    if (c == 0) {
         cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
-        count[dev] = c > 0 ? c : 148;
+        c = c > 0 ? c : 148;
+        count[dev].store(c, std::memory_order_relaxed);
     }
-    return count[dev];
+    return c;
 }
 
 // Device addresses of this device's claim counters and split scratch (cached per device).
 struct UnitBuffers {
-    unsigned* claim = nullptr;
-    float* split = nullptr;
-    unsigned* split_count = nullptr;
+    unsigned* claim = nullptr;        // [kLaneCount][kClaimSlots][2]
+    float* split = nullptr;           // [kLaneCount][kSplitRegions][kSplitFloats]
+    unsigned* split_count = nullptr;  // [kLaneCount][kSplitRegions][kSplitTiles]
 };
 
 static const UnitBuffers* unit_buffers() {
@@ -846,7 +860,37 @@ static const UnitBuffers* unit_buffers() {
     return &b;
 }
 
-static std::atomic<unsigned> g_claim_next{0};
+// The lane of a stream on the current device (assigned round-robin on first use) and the lane's
+// launch count.  The per-thread default stream is one stream per host thread, so it is keyed by
+// thread too.  The table is bounded: past 4096 entries it starts afresh.
+struct LaneKey {
+    int dev;
+    const void* stream;
+    size_t thread;
+    bool operator==(const LaneKey& o) const { return dev == o.dev && stream == o.stream && thread == o.thread; }
+};
+struct LaneKeyHash {
+    size_t operator()(const LaneKey& k) const {
+        return std::hash<const void*>()(k.stream) ^ ((size_t)k.dev * 0x9E3779B97F4A7C15ull) ^ (k.thread * 1099511628211ull);
+    }
+};
+static std::atomic<unsigned> g_lane_launches[64][kLaneCount];
+
+static int stream_lane(cudaStream_t s, int dev) {
+    static std::mutex mu;
+    static std::unordered_map<LaneKey, int, LaneKeyHash> lanes;
+    static unsigned next[64] = {};
+    static thread_local char thread_tag;
+    LaneKey key{dev, static_cast<const void*>(s),
+                s == cudaStreamPerThread ? reinterpret_cast<size_t>(&thread_tag) : size_t(0)};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = lanes.find(key);
+    if (it != lanes.end()) return it->second;
+    if (lanes.size() >= 4096) lanes.clear();
+    const int lane = (int)(next[dev]++ % kLanes);
+    lanes.emplace(key, lane);
+    return lane;
+}
 
 // Launch time of units claimed greedily by `slots` equally fast CTAs, in bytes per CTA: the units
 // are taken in order, each by the CTA that is free first.
@@ -962,7 +1006,7 @@ static void choose_parts(const PartsKey& key, int* parts_out) {
 // first, so that the last units claimed are the small ones; the peer destinations are permuted
 // alike), unit numbering, this launch's counter and scratch.  Returns the grid size (every CTA slot,
 // or one CTA per unit if there are fewer), 0 if the device buffers are unavailable.
-static int plan_units(GemvGroup& grp, PeerSync& ps, int slots, int m) {
+static int plan_units(GemvGroup& grp, PeerSync& ps, int slots, int m, int lane) {
     const int nj = grp.njobs;
     int parts[kMaxJobs] = {}, tiles[kMaxJobs] = {};
     int64_t tile_bytes[kMaxJobs] = {};
@@ -1006,10 +1050,13 @@ static int plan_units(GemvGroup& grp, PeerSync& ps, int slots, int m) {
     sorted.split_stride = stride;
     const UnitBuffers* ub = unit_buffers();
     if (!ub) return 0;
-    const unsigned slot = g_claim_next.fetch_add(1);
-    sorted.claim = ub->claim + 2 * (slot % kClaimSlots);
-    sorted.split_scratch = ub->split + (size_t)(slot % kSplitRegions) * kSplitFloats;
-    sorted.split_count = ub->split_count + (size_t)(slot % kSplitRegions) * kSplitTiles;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned slot = g_lane_launches[dev & 63][lane].fetch_add(1);
+    const size_t region = (size_t)lane * kSplitRegions + slot % kSplitRegions;
+    sorted.claim = ub->claim + 2 * ((size_t)lane * kClaimSlots + slot % kClaimSlots);
+    sorted.split_scratch = ub->split + region * kSplitFloats;
+    sorted.split_count = ub->split_count + region * kSplitTiles;
     grp = sorted;
     ps = pss;
     return units < slots ? units : slots;
@@ -1017,7 +1064,9 @@ static int plan_units(GemvGroup& grp, PeerSync& ps, int slots, int m) {
 
 template <bool PEER>
 static int dispatch_group_t(GemvGroup& grp, PeerSync ps, int xk, int mt, cudaStream_t s) {
-    const int ctas = plan_units(grp, ps, (mt == 2 ? 2 : kCtasPerSm) * sm_count(), grp.job[0].m);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return check_launch("cudaGetDevice");
+    const int ctas = plan_units(grp, ps, (mt == 2 ? 2 : kCtasPerSm) * sm_count(), grp.job[0].m, stream_lane(s, dev));
     if (ctas <= 0) return set_error(SBQ_ERR_CUDA, "grouped GEMV: no work counter on this device");
     switch (xk) {
         case kXF16:
@@ -1344,10 +1393,11 @@ static int program_build(const sbq_gemv_job* jobs, const int* job_stage, int njo
     for (int st = 0; st < nstages; ++st) {
         ProgStage& ps = stages[st];
         if (ps.grp.njobs == 0) continue;
-        if (plan_units(ps.grp, ps.peer, nctas, (int)m) <= 0) return set_error(SBQ_ERR_CUDA, "decode program plan");
+        if (plan_units(ps.grp, ps.peer, nctas, (int)m, kProgramLane) <= 0) return set_error(SBQ_ERR_CUDA, "decode program plan");
         ps.grp.claim = nullptr;  // the stage's claim pair lives in the run's sync region
-        ps.grp.split_scratch = ub->split + (size_t)(st % kSplitRegions) * kSplitFloats;
-        ps.grp.split_count = ub->split_count + (size_t)(st % kSplitRegions) * kSplitTiles;
+        const size_t region = (size_t)kProgramLane * kSplitRegions + st % kSplitRegions;
+        ps.grp.split_scratch = ub->split + region * kSplitFloats;
+        ps.grp.split_count = ub->split_count + region * kSplitTiles;
     }
     std::memcpy(host.data() + 256, stages.data(), (size_t)nstages * sizeof(ProgStage));
     hdr->nstages = nstages;

@@ -44,6 +44,30 @@ def golden(name: str) -> dict:
     return out
 
 
+def golden_cfg3() -> dict:
+    """Configuration 3's reference digests (golden_cfg3.json) and sampled output rows (golden_cfg3.npz)."""
+    info = json.loads((GOLDEN / "golden_cfg3.json").read_text())
+    info["y_rows"] = np.load(GOLDEN / "golden_cfg3.npz")["y_rows"]
+    return info
+
+
+def cfg3_inputs():
+    """Configuration 3's seeded inputs, made by the package's workload generators (CPU tensors):
+    weight fp32 [4096, 4096], activation fp16 [512, 4096]."""
+    info = json.loads((GOLDEN / "golden_cfg3.json").read_text())
+    wl = importlib.import_module("spikingbrain-cpu_b200.workloads")
+    cfg = wl.CONFIGS[3]
+    w = wl.float_weight(cfg["n"], cfg["k"], seed=info["seeds"]["w"])
+    x = wl.activation(cfg["m"], cfg["k"], seed=info["seeds"]["x"])
+    return w, x
+
+
+def sha256(a) -> str:
+    import hashlib
+
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
 @pytest.fixture(scope="session")
 def sbq():
     return load_package()

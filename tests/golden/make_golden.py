@@ -1,16 +1,23 @@
 """Generate the golden fixtures for the int8 / int8-dyn path from the reference itself.
 
-Run in a container where the reference project is importable (its path is the
-first argument, default ``/root/reference``):
+Run in a container where the reference project is importable; its root
+directory (the one holding ``spikingbrain_cpu/``) is the required argument:
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_golden.py REFERENCE_ROOT [--only small|cfg3]
 
 It imports ``spikingbrain_cpu.quant`` from the reference, builds each case with
 seeded inputs, runs the reference's own ``quantize_per_channel``,
 ``Int8Linear`` and ``DynamicInt8Linear`` (quantized engine ``x86``, i.e.
-fbgemm), and writes ``golden.npz`` plus ``golden_meta.json`` beside this
-script.  The tests read only those two files; the reference is not needed at
-test time.
+fbgemm), and writes beside this script:
+
+* ``golden.npz`` + ``golden_meta.json``: 26 small cases, every array in full;
+* ``golden_cfg3.npz`` + ``golden_cfg3.json``: benchmark configuration 3
+  (int8-dyn, m=512, k=n=4096, the package's seeded workload generators) as
+  SHA-256 digests of the full reference outputs (quantised activation, weight,
+  fp32 output) plus the activation scale / zero point and 16 sampled output
+  rows in full.
+
+The tests read only these files; the reference is not needed at test time.
 """
 
 from __future__ import annotations
@@ -47,11 +54,58 @@ def _tie_weight(n: int, k: int, gen: torch.Generator) -> torch.Tensor:
     return w
 
 
-def main(ref_root: str) -> None:
+CFG3_SEEDS = {"w": 30, "x": 31}  # workloads.float_weight(4096, 4096, 30), workloads.activation(512, 4096, 31)
+CFG3_ROWS = [0, 1, 77, 127, 128, 200, 255, 256, 300, 383, 384, 450, 509, 510, 511, 63]
+
+
+def sha256(a) -> str:
+    import hashlib
+
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def cfg3_inputs():
+    """Configuration 3's seeded weight (fp32 [4096, 4096]) and activation (fp16 [512, 4096])."""
+    import importlib
+
+    sys.path.insert(0, str(HERE.parents[1]))
+    wl = importlib.import_module("spikingbrain-cpu_b200.workloads")
+    cfg = wl.CONFIGS[3]
+    w = wl.float_weight(cfg["n"], cfg["k"], seed=CFG3_SEEDS["w"])
+    x = wl.activation(cfg["m"], cfg["k"], seed=CFG3_SEEDS["x"])
+    return w, x
+
+
+def make_cfg3(quant) -> None:
+    w, x = cfg3_inputs()
+    xf = x.float()  # the reference takes fp32 activations (quant.py:47); fp16 -> fp32 is exact
+    q, scale = quant.quantize_per_channel(w)
+    y = quant.DynamicInt8Linear(w, None)(xf).detach().numpy()
+    # the activation quantisation linear_dynamic applies (fbgemm per-tensor uint8, no range reduction)
+    xq_t = torch.quantize_per_tensor_dynamic(xf, torch.quint8, False)
+    rows = np.array(CFG3_ROWS)
+    info = {"generated_by": "tests/golden/make_golden.py", "torch": torch.__version__,
+            "quantized_engine": torch.backends.quantized.engine, "seeds": CFG3_SEEDS,
+            "shape": {"m": int(x.shape[0]), "n": int(w.shape[0]), "k": int(w.shape[1])},
+            "w_sha256": sha256(w.numpy()), "x_sha256": sha256(x.numpy()),
+            "q_sha256": sha256(q.numpy()), "scale_sha256": sha256(scale.numpy()),
+            "xq_sha256": sha256(xq_t.int_repr().numpy()),
+            "s_x_bits": int(np.float32(xq_t.q_scale()).view(np.uint32)), "zp": int(xq_t.q_zero_point()),
+            "y_sha256": sha256(y), "rows": CFG3_ROWS}
+    np.savez_compressed(HERE / "golden_cfg3.npz", y_rows=y[rows])
+    (HERE / "golden_cfg3.json").write_text(json.dumps(info, indent=1, sort_keys=True) + "\n")
+    print("wrote configuration 3: y", y.shape, "digest", info["y_sha256"][:16])
+
+
+def main(ref_root: str, only: str | None = None) -> None:
     sys.path.insert(0, ref_root)
     from spikingbrain_cpu import quant  # the reference, imported read-only
 
     torch.backends.quantized.engine = "x86"
+    if only in (None, "cfg3"):
+        make_cfg3(quant)
+    if only == "cfg3":
+        return
     arrays: dict[str, np.ndarray] = {}
     meta: dict[str, dict] = {}
 
@@ -119,4 +173,10 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    import argparse
+
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("reference_root", help="directory holding the reference's spikingbrain_cpu package")
+    ap.add_argument("--only", choices=("small", "cfg3"), help="regenerate one fixture set")
+    a = ap.parse_args()
+    main(a.reference_root, a.only)

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import golden, golden_cases
+from conftest import cfg3_inputs, golden, golden_cases, golden_cfg3, sha256
 from oracle import quant_ref as R
 
 pytestmark = pytest.mark.gpu
@@ -70,6 +70,29 @@ def test_config3_full_size(sbq):
     # forward() (fused workspace path) gives the same output as the staged path
     assert torch.equal(mod(x.cuda()), y)
     assert sbq._lib.load().sbq_check_device_error() == 0
+
+
+@pytest.mark.parametrize("path", ["forward", "stages"])
+def test_config3_matches_reference_digests(sbq, path):
+    # configuration 3 at full size against the reference's own outputs (digests of the whole
+    # quantised activation and of the whole fp32 output, made by running the reference's
+    # DynamicInt8Linear): bit-exact on every element, the oracle not involved
+    ref = golden_cfg3()
+    w, x = cfg3_inputs()
+    assert sha256(w.numpy()) == ref["w_sha256"] and sha256(x.numpy()) == ref["x_sha256"], \
+        "the seeded inputs differ on this machine (torch generator), so the digests cannot be compared"
+    mod = sbq.DynamicInt8Linear(w, None)
+    assert sha256(mod.qweight.cpu().numpy()) == ref["q_sha256"]
+    assert sha256(mod.scale.cpu().numpy()) == ref["scale_sha256"]
+    if path == "forward":
+        y = mod(x.cuda()).cpu().numpy()
+    else:
+        yt, xq, s, zp, _ = mod.forward_stages(x.cuda())
+        y = yt.cpu().numpy()
+        assert sha256(xq.cpu().numpy()) == ref["xq_sha256"]
+        assert int(s.cpu().numpy().view(np.uint32)[0]) == ref["s_x_bits"] and int(zp.item()) == ref["zp"]
+    assert np.array_equal(y[ref["rows"]].view(np.uint32), ref["y_rows"].view(np.uint32))
+    assert sha256(y) == ref["y_sha256"]
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 4, 64), (3, 40, 192), (127, 130, 320), (129, 300, 256), (200, 64, 2560),

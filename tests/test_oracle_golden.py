@@ -6,10 +6,13 @@ weight-only forward (quant.py:41-53) must agree with the reference's blocked
 fp32 result to fp32 rounding.
 """
 
+import os
+import sys
+
 import numpy as np
 import pytest
 
-from conftest import golden, golden_cases
+from conftest import cfg3_inputs, golden, golden_cases, golden_cfg3, sha256
 from oracle import quant_ref as R
 
 
@@ -75,3 +78,43 @@ def test_per_token_mode_restatement():
     assert np.array_equal(ref, xq.astype(np.int64) @ q.astype(np.int64).T)
     # the per-token result approximates the float product
     assert R.rel_l2(y, R.int8_linear(x, q, scale)) < 2e-2
+
+
+def test_config3_oracle_matches_reference_digests():
+    # benchmark configuration 3 (int8-dyn, m=512, k=n=4096): the oracle reproduces every output of
+    # the reference's DynamicInt8Linear bit for bit (digests made by make_golden.py from the reference)
+    ref = golden_cfg3()
+    w, x = cfg3_inputs()
+    assert sha256(w.numpy()) == ref["w_sha256"] and sha256(x.numpy()) == ref["x_sha256"], \
+        "the seeded inputs differ on this machine (torch generator), so the digests cannot be compared"
+    q, scale = R.quantize_per_channel(w.numpy())
+    assert sha256(q) == ref["q_sha256"] and sha256(scale) == ref["scale_sha256"]
+    y, xq, s, zp, acc = R.dyn_linear(x.float().numpy(), q, scale)
+    assert int(np.float32(s).view(np.uint32)) == ref["s_x_bits"] and zp == ref["zp"]
+    assert sha256(xq) == ref["xq_sha256"]
+    assert np.array_equal(y[ref["rows"]].view(np.uint32), ref["y_rows"].view(np.uint32))
+    assert sha256(y) == ref["y_sha256"]
+
+
+@pytest.mark.skipif(not os.environ.get("SBQ_REFERENCE_ROOT"),
+                    reason="set SBQ_REFERENCE_ROOT to the reference's root directory to re-run it here")
+@pytest.mark.parametrize("m,n,k,seed", [(512, 4096, 4096, 5), (77, 300, 2560, 6), (1, 64, 128, 7)])
+def test_oracle_matches_live_reference(m, n, k, seed):
+    # the reference itself (its quant.py, fbgemm engine x86) on fresh seeded inputs, against the
+    # oracle: weight quantisation and the int8-dyn output bit for bit, the int8 output to fp32 rounding
+    import torch
+
+    sys.path.insert(0, os.environ["SBQ_REFERENCE_ROOT"])
+    from spikingbrain_cpu import quant
+
+    torch.backends.quantized.engine = "x86"
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(n, k, generator=g) * 0.02
+    x = torch.randn(m, k, generator=g) * 1.5 + 0.1
+    q, s = R.quantize_per_channel(w.numpy())
+    rq, rs = quant.quantize_per_channel(w)
+    assert np.array_equal(q, rq.numpy()) and np.array_equal(s.view(np.uint32), rs.numpy().view(np.uint32))
+    y = R.dyn_linear(x.numpy(), q, s)[0]
+    ry = quant.DynamicInt8Linear(w, None)(x).numpy()
+    assert np.array_equal(y.view(np.uint32), ry.view(np.uint32))
+    assert R.rel_l2(R.int8_linear(x.numpy(), q, s), quant.Int8Linear(w, None)(x).numpy()) < 1e-5

@@ -19,6 +19,8 @@ from oracle import quant_ref as R
 
 pytestmark = pytest.mark.gpu
 
+_DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}  # SBQ_F32, SBQ_F16, SBQ_BF16
+
 
 def _p(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
@@ -27,13 +29,14 @@ def _p(t):
 def _noalloc(lib, mod, x, y, mode_code):
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     m, k = x.shape
-    return lib.sbq_linear_dyn_noalloc(_p(x), 0 if x.dtype == torch.float32 else 1, x.stride(0), mode_code,
+    return lib.sbq_linear_dyn_noalloc(_p(x), _DTYPE_CODE[x.dtype], x.stride(0), mode_code,
                                       _p(mod.packed), _p(mod.rowsum), _p(mod.scale), _p(mod.bias), m,
                                       mod.out_features, k, _p(y), y.stride(0), stream)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("mode", ["per_tensor", "per_token"])
-def test_noalloc_matches_workspace_entry_point_twice(sbq, mode):
+def test_noalloc_matches_workspace_entry_point_twice(sbq, mode, dtype):
     lib = sbq._lib.load()
     m, n, k = 96, 384, 1024
     w = sbq.workloads.float_weight(n, k, seed=71)
@@ -41,7 +44,7 @@ def test_noalloc_matches_workspace_entry_point_twice(sbq, mode):
     mod = sbq.DynamicInt8Linear(w, bias, mode=mode)
     code = sbq._lib.ACT_PER_TENSOR if mode == "per_tensor" else sbq._lib.ACT_PER_TOKEN
     for call, scale in enumerate((1.0, 7.5)):
-        x = (sbq.workloads.activation(m, k, seed=72 + call, dtype=torch.float32) * scale).cuda()
+        x = (sbq.workloads.activation(m, k, seed=72 + call, dtype=torch.float32) * scale).to(dtype).cuda()
         want = mod(x)  # sbq_linear_dyn with a caller-provided workspace
         y = torch.full((m, n), float("nan"), device="cuda")
         assert _noalloc(lib, mod, x, y, code) == 0, lib.sbq_last_error().decode()
