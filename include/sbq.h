@@ -28,7 +28,8 @@
  * Reference interfaces replaced (paths inside the reference project, spikingbrain_cpu/):
  *   quant.py:25-29   quantize_per_channel             -> sbq_quantize_pack
  *   quant.py:35-37   Int8Linear qweight/scale buffers  -> sbq_pack_int8 / sbq_unpack_int8
- *   quant.py:41-53   Int8Linear.forward               -> sbq_linear_w8 (sbq_gemv_w8 / sbq_gemm_w8a16)
+ *   quant.py:41-53   Int8Linear.forward               -> sbq_linear_w8 / sbq_linear_w8_ws
+ *                    (sbq_gemv_w8 / sbq_gemm_w8a16 / sbq_split_f32_bf16x2 + sbq_gemm_w8a16_x2)
  *   model.py:239-240 GatedMLP.forward (gate, up, SiLU) -> sbq_mlp_gateup_w8
  *   quant.py:57-61   DynamicInt8Linear packing         -> sbq_quantize_pack (+ row sums)
  *   quant.py:63-66   DynamicInt8Linear.forward        -> sbq_linear_dyn
@@ -105,35 +106,69 @@ SBQ_API int sbq_unpack_int8(const void* packed, int64_t n, int64_t k, int8_t* q,
 /* ---- int8 weight-only linear (format "int8") --------------------------------------------- */
 
 /* Int8Linear.forward (quant.py:41-53): y[m, n] = (x[m, :] . q[n, :]) * scale[n] (+ bias[n]).
- * x dtype SBQ_F16, SBQ_BF16 or SBQ_F32 (fp32 is split into two bf16 terms, ~16 mantissa bits);
+ * x dtype SBQ_F16, SBQ_BF16 or SBQ_F32 (fp32 is split into two bf16 terms, ~17 significant bits);
  * y dtype SBQ_F32 (the reference's output type) or SBQ_F16.  bias may be NULL.  Chooses the
- * decode GEMV up to 32 rows (and for bf16/fp32 x) and the tensor-memory GEMM above. */
+ * decode GEMV up to 32 rows and the tensor-memory GEMM above for fp16 / bf16 x; fp32 x always
+ * takes the GEMV here (its GEMM path needs a workspace: sbq_linear_w8_ws). */
 SBQ_API int sbq_linear_w8(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                   const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
                   void* stream);
+
+/* Bytes of workspace sbq_linear_w8_ws / sbq_mlp_gateup_w8_ws need for x [m, k] of x_dtype: nonzero
+ * only for fp32 x above 32 rows (the bf16 high / low parts of x, 4 * m * k bytes rounded up). */
+SBQ_API size_t sbq_linear_w8_workspace_bytes(int64_t m, int64_t k, int x_dtype);
+
+/* sbq_linear_w8 with a caller workspace (sbq_linear_w8_workspace_bytes bytes, 256-byte aligned; NULL
+ * when that is 0), which puts fp32 activations above 32 rows - the reference's own prefill, fp32
+ * x in chunks of up to 512 tokens (model.py:439-441, quant.py:47) - on the tensor-memory GEMM:
+ * sbq_split_f32_bf16x2 into the workspace, then sbq_gemm_w8a16_x2.  Other calls behave exactly as
+ * sbq_linear_w8. */
+SBQ_API int sbq_linear_w8_ws(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
+                             const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
+                             void* workspace, size_t workspace_bytes, void* stream);
 
 /* The decode GEMV alone (any m >= 1; streams the weight once per 16 rows of x). */
 SBQ_API int sbq_gemv_w8(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                 const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
                 void* stream);
 
-/* The tensor-memory GEMM alone: TMA-fed, int8 rows dequantised to fp16 straight into tensor memory
- * (the MMA's A operand), tcgen05 MMA with fp32 accumulators in tensor memory, scale epilogue.
+/* The tensor-memory GEMM alone: TMA-fed, int8 rows converted to x's 16-bit type straight into tensor
+ * memory (the MMA's A operand), tcgen05 MMA with fp32 accumulators in tensor memory, scale epilogue.
  * Up to 128 rows of x: 64-token tiles, with the K range split over a thread-block cluster when the
  * tiles are too few for the GPU (partials added through distributed shared memory in part order);
- * more rows: 256-token tiles.  x must be SBQ_F16. */
+ * more rows: 256-token tiles.  x must be SBQ_F16 or SBQ_BF16. */
 SBQ_API int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                    const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
                    void* stream);
 
+/* fp32 x [m, k] (row stride ldx) -> bf16 hi = round(x), lo = round(x - hi), [m, k] each with row
+ * stride ldo (x - hi is exact, so hi + lo carries ~17 significant bits and fp32's range).  k a
+ * multiple of 8; rows 16-byte aligned. */
+SBQ_API int sbq_split_f32_bf16x2(const float* x, int64_t ldx, int64_t m, int64_t k, void* hi, void* lo,
+                                 int64_t ldo, void* stream);
+
+/* sbq_gemm_w8a16 on an fp32 activation given as its bf16 high and low parts (same row stride ldx):
+ * each k-step runs one MMA per part into the same fp32 accumulators against the same converted
+ * weight operand - twice the tensor work of a 16-bit x, the GEMV's fp32 accuracy. */
+SBQ_API int sbq_gemm_w8a16_x2(const void* x_hi, const void* x_lo, int64_t ldx, const void* packed, const float* scale,
+                              const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
+                              void* stream);
+
 /* GatedMLP.forward's first half (model.py:239-240): h = silu(x q_gate^T * s_gate) * (x q_up^T * s_up)
- * with h written as h_dtype (SBQ_F16 or SBQ_F32).  Up to 32 rows (or bf16/fp32 x): one pass over
- * both weights ([n, k] each) in the decode GEMV.  More fp16 rows: the gate projection goes into h
+ * with h written as h_dtype (SBQ_F16 or SBQ_F32).  Up to 32 rows (or fp32 x): one pass over
+ * both weights ([n, k] each) in the decode GEMV.  More fp16 / bf16 rows: the gate projection goes into h
  * (rounded to h_dtype) and the up projection's GEMM epilogue replaces it by silu(gate) * up.  The
  * down projection is a separate sbq_linear_w8 call on h. */
 SBQ_API int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const void* packed_gate,
                       const float* scale_gate, const void* packed_up, const float* scale_up, int64_t m,
                       int64_t n, int64_t k, void* h, int h_dtype, int64_t ldh, void* stream);
+
+/* sbq_mlp_gateup_w8 with a caller workspace (sbq_linear_w8_workspace_bytes(m, k, x_dtype) bytes):
+ * fp32 x above 32 rows is split once and both GEMMs read the split (see sbq_linear_w8_ws). */
+SBQ_API int sbq_mlp_gateup_w8_ws(const void* x, int x_dtype, int64_t ldx, const void* packed_gate,
+                                 const float* scale_gate, const void* packed_up, const float* scale_up, int64_t m,
+                                 int64_t n, int64_t k, void* h, int h_dtype, int64_t ldh, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 
 /* One projection of a grouped decode launch (sbq_gemv_w8_group).  A job with packed_up set is a fused
  * gate/up job: y = silu(x q^T * scale) * (x q_up^T * scale_up), no bias. */

@@ -53,10 +53,17 @@ SIGNATURES = {
     "sbq_pack_int8": (_c_int, [_vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp]),
     "sbq_unpack_int8": (_c_int, [_vp, _c_i64, _c_i64, _vp, _c_i64, _vp]),
     "sbq_linear_w8": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_int, _c_i64, _vp]),
+    "sbq_linear_w8_workspace_bytes": (_sz, [_c_i64, _c_i64, _c_int]),
+    "sbq_linear_w8_ws": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_int, _c_i64, _vp,
+                                  _sz, _vp]),
     "sbq_gemv_w8": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_int, _c_i64, _vp]),
     "sbq_gemm_w8a16": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_int, _c_i64, _vp]),
+    "sbq_split_f32_bf16x2": (_c_int, [_vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _c_i64, _vp]),
+    "sbq_gemm_w8a16_x2": (_c_int, [_vp, _vp, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_int, _c_i64, _vp]),
     "sbq_mlp_gateup_w8": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_int,
                                    _c_i64, _vp]),
+    "sbq_mlp_gateup_w8_ws": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_int,
+                                      _c_i64, _vp, _sz, _vp]),
     "sbq_gemv_w8_group": (_c_int, [ctypes.POINTER(GemvJob), _c_int, _c_int, _c_i64, _vp]),
     "sbq_gemv_plan_parts": (_c_int, [ctypes.POINTER(_c_i64), _c_int, _c_int, _c_i64, ctypes.POINTER(_c_int)]),
     "sbq_gemv_program_bytes": (_sz, [_c_int]),

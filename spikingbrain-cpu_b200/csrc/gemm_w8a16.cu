@@ -16,6 +16,12 @@
 //     tokens each), apply the fp32 per-row scale (and bias) and store fp16 or fp32 output,
 //     consecutive channels per warp store.
 // The scale stays in the fp32 epilogue, as in the reference: int8 values are exact in fp16.
+//
+// Activation kinds: fp16 (int8 -> fp16 weights, kind::f16 with f16 operands), bf16 (int8 -> bf16
+// weights, bf16 operands) and fp32 split into a bf16 high and low part (x = hi + lo to ~2^-17
+// relative; both parts are tiles of the same stage and each k-step issues one MMA per part into the
+// same accumulator, so the weight operand is converted once).  int8 x bf16 products are exact in
+// fp32, so the fp32 path loses only the split's rounding and the fp32 accumulation.
 #include <atomic>
 
 #include "tc.cuh"
@@ -61,29 +67,58 @@ __device__ __forceinline__ void store_y(const P& p, int t, int n, float v) {
         static_cast<float*>(p.y)[idx] = v;
 }
 
+// Activation kinds of the tensor-memory GEMMs.
+enum AKind { kAF16 = 0, kABF16 = 1, kABF16x2 = 2 };
+
+// int8 weight row (64 bytes at w8, 64-byte swizzle of row `row`) -> 32 words of 16-bit pairs in
+// the activation's type (exact: |q| <= 127).
+template <int AK>
+__device__ __forceinline__ void convert_row(const uint8_t* w8, int row, uint32_t (&h)[32]) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint4 v = *reinterpret_cast<const uint4*>(w8 + ((c ^ ((row >> 1) & 3)) << 4));
+        if (AK == kAF16) {
+            i8x4_to_half2x2(v.x, h[8 * c + 0], h[8 * c + 1]);
+            i8x4_to_half2x2(v.y, h[8 * c + 2], h[8 * c + 3]);
+            i8x4_to_half2x2(v.z, h[8 * c + 4], h[8 * c + 5]);
+            i8x4_to_half2x2(v.w, h[8 * c + 6], h[8 * c + 7]);
+        } else {
+            i8x4_to_bf162x2(v.x, h[8 * c + 0], h[8 * c + 1]);
+            i8x4_to_bf162x2(v.y, h[8 * c + 2], h[8 * c + 3]);
+            i8x4_to_bf162x2(v.z, h[8 * c + 4], h[8 * c + 5]);
+            i8x4_to_bf162x2(v.w, h[8 * c + 6], h[8 * c + 7]);
+        }
+    }
+}
+
 constexpr int kWCh = 128;      // output channels per CTA (MMA M, one per TMEM lane)
 constexpr int kWTok = 256;     // activation rows per CTA (MMA N)
-constexpr int kWBK = 64;       // k per stage (one 128-byte fp16 row, one packed tile column)
-constexpr int kWStages = 5;    // TMA stages
+constexpr int kWBK = 64;       // k per stage (one 128-byte 16-bit row, one packed tile column)
 constexpr int kWABufs = 4;     // weight operand buffers in TMEM (32 columns each)
 constexpr int kWThreads = 384; // 12 warps: producer, MMA, TMEM, idle, then two converter warpgroups
 constexpr uint32_t kWTmemCols = 512;
 constexpr uint32_t kWAccCol = 0;    // accumulator: columns [0, 256)
 constexpr uint32_t kWACol = 256;    // weight buffers: 32 columns each from 256
 
+template <int AK>
 struct W16Smem {
-    static constexpr int kX = kWTok * kWBK * 2;  // 32 KiB fp16 activation tile
-    static constexpr int kW8 = kWCh * kWBK;      // 8 KiB int8 weight tile
-    static constexpr int kStage = kX + kW8;
-    static constexpr int kBarOff = kWStages * kStage;
+    static constexpr int kX = kWTok * kWBK * 2;            // 32 KiB 16-bit activation tile
+    static constexpr int kXTiles = AK == kABF16x2 ? 2 : 1;  // high and low part of a split fp32 x
+    static constexpr int kW8 = kWCh * kWBK;                // 8 KiB int8 weight tile
+    static constexpr int kStage = kXTiles * kX + kW8;
+    static constexpr int kStages = AK == kABF16x2 ? 3 : 5;  // TMA stages
+    static constexpr int kBarOff = kStages * kStage;
     static constexpr int kBytes = kBarOff + 256 + kWCh * 8 + 1024;
+    static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
 };
 
-template <bool OUT_F16, bool GATED>
+template <bool OUT_F16, bool GATED, int AK>
 __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                                  const __grid_constant__ CUtensorMap tmap_x2,
                                                                   const __grid_constant__ CUtensorMap tmap_w,
                                                                   const GemmW16Params p) {
-    using S = W16Smem;
+    using S = W16Smem<AK>;
+    constexpr int kWStages = S::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
@@ -110,6 +145,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
         tc::mbar_init(done, 1);
         tc::fence_mbar_init();
         tc::prefetch_tmap(&tmap_x);
+        if (AK == kABF16x2) tc::prefetch_tmap(&tmap_x2);
         tc::prefetch_tmap(&tmap_w);
     }
     if (warp == 2) {
@@ -135,12 +171,13 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
                 uint8_t* xs = smem + s * S::kStage;
                 tc::mbar_arrive_expect_tx(&full[s], S::kStage);
                 tc::tma_load_2d(xs, &tmap_x, &full[s], kb * kWBK, t0);
-                tc::tma_load_4d(xs + S::kX, &tmap_w, &full[s], 0, 0, kb, n0 / 16);
+                if (AK == kABF16x2) tc::tma_load_2d(xs + S::kX, &tmap_x2, &full[s], kb * kWBK, t0);
+                tc::tma_load_4d(xs + S::kXTiles * S::kX, &tmap_w, &full[s], 0, 0, kb, n0 / 16);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_f16(kWCh, kWTok);
+            constexpr uint32_t idesc = tc::idesc_f16(kWCh, kWTok, AK != kAF16);
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 const int s = kb % kWStages, d = kb % kWABufs;
                 const uint32_t ph = (kb / kWStages) & 1, phd = (kb / kWABufs) & 1;
@@ -153,6 +190,10 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
                 for (int j = 0; j < kWBK / 16; ++j) {
                     const uint64_t bd = tc::smem_desc(xs + j * 32, tc::kSwizzle128B, 1024);
                     tc::mma_f16_ts(tmem + kWAccCol, a_col + j * 8, bd, idesc, (kb | j) != 0);
+                    if (AK == kABF16x2) {
+                        const uint64_t bl = tc::smem_desc(xs + S::kX + j * 32, tc::kSwizzle128B, 1024);
+                        tc::mma_f16_ts(tmem + kWAccCol, a_col + j * 8, bl, idesc, 1u);
+                    }
                 }
                 tc::mma_commit(&empty[s]);
                 tc::mma_commit(&a_empty[d]);
@@ -173,16 +214,8 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
             if (!__all_sync(0xffffffffu, tc::mbar_wait(&a_empty[d], phd ^ 1))) { ok = false; break; }
             tc::fence_after_sync();
             // the int8 row: 64 bytes, 16-byte chunk c at (c ^ ((row >> 1) & 3)) (64-byte swizzle)
-            const uint8_t* w8 = smem + s * S::kStage + S::kX + row * 64;
             uint32_t h[32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint4 v = *reinterpret_cast<const uint4*>(w8 + ((c ^ ((row >> 1) & 3)) << 4));
-                i8x4_to_half2x2(v.x, h[8 * c + 0], h[8 * c + 1]);
-                i8x4_to_half2x2(v.y, h[8 * c + 2], h[8 * c + 3]);
-                i8x4_to_half2x2(v.z, h[8 * c + 4], h[8 * c + 5]);
-                i8x4_to_half2x2(v.w, h[8 * c + 6], h[8 * c + 7]);
-            }
+            convert_row<AK>(smem + s * S::kStage + S::kXTiles * S::kX + row * 64, row, h);
             tc::tmem_st_32x32b_x32(tmem + lane_addr + kWACol + d * (kWBK / 2), h);
             tc::tmem_wait_st();
             tc::fence_before_sync();
@@ -247,19 +280,22 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
 // shared memory in part order (deterministic), then scales and stores.  Roles as above.
 // ---------------------------------------------------------------------------------------------
 constexpr int kSTok = 64;      // activation rows per CTA (MMA N)
-constexpr int kSStages = 6;
 constexpr uint32_t kSTmemCols = 256;  // accumulator [0, 64), six weight buffers of 32 columns from 64
 constexpr uint32_t kSACol = 64;
 constexpr int kSABufs = 6;
 constexpr int kSPad = 68;      // floats per row of the partial tile in shared memory (16-byte rows)
 
+template <int AK>
 struct SmallSmem {
-    static constexpr int kX = kSTok * kWBK * 2;  // 8 KiB fp16 activation tile
-    static constexpr int kW8 = kWCh * kWBK;      // 8 KiB int8 weight tile
-    static constexpr int kStage = kX + kW8;
-    static constexpr int kBarOff = kSStages * kStage;
+    static constexpr int kX = kSTok * kWBK * 2;            // 8 KiB 16-bit activation tile
+    static constexpr int kXTiles = AK == kABF16x2 ? 2 : 1;  // high and low part of a split fp32 x
+    static constexpr int kW8 = kWCh * kWBK;                // 8 KiB int8 weight tile
+    static constexpr int kStage = kXTiles * kX + kW8;
+    static constexpr int kStages = AK == kABF16x2 ? 4 : 6;  // two CTAs per SM either way
+    static constexpr int kBarOff = kStages * kStage;
     static constexpr int kBytes = kBarOff + 256 + kWCh * 8 + 1024;
-    static_assert(kWCh * kSPad * 4 <= kSStages * kStage, "partial tile fits in the ring");
+    static_assert(kWCh * kSPad * 4 <= kStages * kStage, "partial tile fits in the ring");
+    static_assert(2 * kBytes <= 228 * 1024, "two CTAs per SM");
 };
 
 struct GemmSmallParams {
@@ -297,11 +333,13 @@ __device__ __forceinline__ float4 ld_dsmem4(uint32_t cluster_addr) {
     return v;
 }
 
-template <bool OUT_F16>
+template <bool OUT_F16, int AK>
 __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                                        const __grid_constant__ CUtensorMap tmap_x2,
                                                                         const __grid_constant__ CUtensorMap tmap_w,
                                                                         const GemmSmallParams p) {
-    using S = SmallSmem;
+    using S = SmallSmem<AK>;
+    constexpr int kSStages = S::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
@@ -331,6 +369,7 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
         tc::mbar_init(done, 1);
         tc::fence_mbar_init();
         tc::prefetch_tmap(&tmap_x);
+        if (AK == kABF16x2) tc::prefetch_tmap(&tmap_x2);
         tc::prefetch_tmap(&tmap_w);
     }
     if (warp == 2) {
@@ -357,12 +396,13 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
                 uint8_t* xs = smem + s * S::kStage;
                 tc::mbar_arrive_expect_tx(&full[s], S::kStage);
                 tc::tma_load_2d(xs, &tmap_x, &full[s], (kb0 + i) * kWBK, t0);
-                tc::tma_load_4d(xs + S::kX, &tmap_w, &full[s], 0, 0, kb0 + i, n0 / 16);
+                if (AK == kABF16x2) tc::tma_load_2d(xs + S::kX, &tmap_x2, &full[s], (kb0 + i) * kWBK, t0);
+                tc::tma_load_4d(xs + S::kXTiles * S::kX, &tmap_w, &full[s], 0, 0, kb0 + i, n0 / 16);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_f16(kWCh, kSTok);
+            constexpr uint32_t idesc = tc::idesc_f16(kWCh, kSTok, AK != kAF16);
             for (int i = 0; i < nkb; ++i) {
                 const int s = i % kSStages, d = i % kSABufs;
                 const uint32_t ph = (i / kSStages) & 1, phd = (i / kSABufs) & 1;
@@ -375,6 +415,10 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
                 for (int j = 0; j < kWBK / 16; ++j) {
                     const uint64_t bd = tc::smem_desc(xs + j * 32, tc::kSwizzle128B, 1024);
                     tc::mma_f16_ts(tmem, a_col + j * 8, bd, idesc, (i | j) != 0);
+                    if (AK == kABF16x2) {
+                        const uint64_t bl = tc::smem_desc(xs + S::kX + j * 32, tc::kSwizzle128B, 1024);
+                        tc::mma_f16_ts(tmem, a_col + j * 8, bl, idesc, 1u);
+                    }
                 }
                 tc::mma_commit(&empty[s]);
                 tc::mma_commit(&a_empty[d]);
@@ -401,15 +445,7 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
                 if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], ph))) { ok = false; break; }
                 if (!__all_sync(0xffffffffu, tc::mbar_wait(&a_empty[d], phd ^ 1))) { ok = false; break; }
                 tc::fence_after_sync();
-                const uint8_t* w8 = smem + s * S::kStage + S::kX + row * 64;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(w8 + ((c ^ ((row >> 1) & 3)) << 4));
-                    i8x4_to_half2x2(v.x, h[u][8 * c + 0], h[u][8 * c + 1]);
-                    i8x4_to_half2x2(v.y, h[u][8 * c + 2], h[u][8 * c + 3]);
-                    i8x4_to_half2x2(v.z, h[u][8 * c + 4], h[u][8 * c + 5]);
-                    i8x4_to_half2x2(v.w, h[u][8 * c + 6], h[u][8 * c + 7]);
-                }
+                convert_row<AK>(smem + s * S::kStage + S::kXTiles * S::kX + row * 64, row, h[u]);
                 tc::tmem_st_32x32b_x32(tmem + lane_addr + kSACol + d * (kWBK / 2), h[u]);
             }
             if (!ok) break;
@@ -518,25 +554,36 @@ static int sm_count_w16() {
     return c;
 }
 
-static int gemm_small(const void* x, int64_t ldx, const void* packed, const float* scale, const float* bias, int64_t m,
-                      int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream, int gated) {
-    CUtensorMap mx, mw;
-    int st;
-    {
-        const uint64_t dims[2] = {(uint64_t)k, (uint64_t)m};
-        const uint64_t strides[1] = {(uint64_t)ldx * 2};
-        const uint32_t box[2] = {kWBK, kSTok};
-        st = encode_tmap(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-        if (st) return st;
-    }
-    {
-        const uint64_t kt = (uint64_t)ceil_div(k, kTileCols), nt = (uint64_t)ceil_div(n, kTileRows);
-        const uint64_t dims[4] = {64, 16, kt, nt};
-        const uint64_t strides[3] = {64, 1024, kt * 1024};
-        const uint32_t box[4] = {64, 16, 1, kWCh / 16};
-        st = encode_tmap(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, packed, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
-        if (st) return st;
-    }
+// 16-bit activation [m, k] (row stride ldx elements) as box_rows x 64 boxes, 128-byte swizzle.
+static int make_x_map(CUtensorMap* map, int ak, const void* x, int64_t ldx, int64_t m, int64_t k, int box_rows) {
+    const uint64_t dims[2] = {(uint64_t)k, (uint64_t)m};
+    const uint64_t strides[1] = {(uint64_t)ldx * 2};
+    const uint32_t box[2] = {kWBK, (uint32_t)box_rows};
+    return encode_tmap(map, ak == kAF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dims,
+                       strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// The packed weight viewed as {64 bytes, 16 rows, KT tiles, NT tile-rows}, one 128-row tile column per box.
+static int make_w_map(CUtensorMap* map, const void* packed, int64_t n, int64_t k) {
+    const uint64_t kt = (uint64_t)ceil_div(k, kTileCols), nt = (uint64_t)ceil_div(n, kTileRows);
+    const uint64_t dims[4] = {64, 16, kt, nt};
+    const uint64_t strides[3] = {64, 1024, kt * 1024};
+    const uint32_t box[4] = {64, 16, 1, kWCh / 16};
+    return encode_tmap(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, packed, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+template <bool OUT_F16, int AK>
+static cudaError_t launch_small(const cudaLaunchConfig_t& cfg, const CUtensorMap& mx, const CUtensorMap& mx2,
+                                const CUtensorMap& mw, const GemmSmallParams& p) {
+    cudaFuncSetAttribute(gemm_w8a16_small_kernel<OUT_F16, AK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)cfg.dynamicSmemBytes);
+    return cudaLaunchKernelEx(&cfg, gemm_w8a16_small_kernel<OUT_F16, AK>, mx, mx2, mw, p);
+}
+
+template <int AK>
+static int gemm_small(const CUtensorMap& mx, const CUtensorMap& mx2, const CUtensorMap& mw, const float* scale,
+                      const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
+                      int gated) {
     GemmSmallParams p{};
     p.gated = gated;
     p.m = (int)m;
@@ -557,7 +604,7 @@ static int gemm_small(const void* x, int64_t ldx, const void* packed, const floa
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)ceil_div(n, kWCh), (unsigned)ceil_div(m, kSTok), (unsigned)parts);
     cfg.blockDim = dim3(kWThreads);
-    cfg.dynamicSmemBytes = SmallSmem::kBytes;
+    cfg.dynamicSmemBytes = SmallSmem<AK>::kBytes;
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -566,23 +613,130 @@ static int gemm_small(const void* x, int64_t ldx, const void* packed, const floa
     attr[0].val.clusterDim.z = (unsigned)parts;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e;
-    if (y_dtype == SBQ_F16) {
-        cudaFuncSetAttribute(gemm_w8a16_small_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SmallSmem::kBytes);
-        e = cudaLaunchKernelEx(&cfg, gemm_w8a16_small_kernel<true>, mx, mw, p);
-    } else {
-        cudaFuncSetAttribute(gemm_w8a16_small_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SmallSmem::kBytes);
-        e = cudaLaunchKernelEx(&cfg, gemm_w8a16_small_kernel<false>, mx, mw, p);
-    }
+    const cudaError_t e = y_dtype == SBQ_F16 ? launch_small<true, AK>(cfg, mx, mx2, mw, p)
+                                             : launch_small<false, AK>(cfg, mx, mx2, mw, p);
     if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "gemm_w8a16 (small batch) launch: %s", cudaGetErrorString(e));
     return check_launch("gemm_w8a16_small");
 }
 
+template <bool OUT_F16, bool GATED, int AK>
+static void launch_large(dim3 grid, cudaStream_t s, const CUtensorMap& mx, const CUtensorMap& mx2,
+                         const CUtensorMap& mw, const GemmW16Params& p) {
+    constexpr int smem = W16Smem<AK>::kBytes;
+    cudaFuncSetAttribute(gemm_w8a16_kernel<OUT_F16, GATED, AK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    gemm_w8a16_kernel<OUT_F16, GATED, AK><<<grid, kWThreads, smem, s>>>(mx, mx2, mw, p);
+}
+
+template <int AK>
+static int gemm_large(const CUtensorMap& mx, const CUtensorMap& mx2, const CUtensorMap& mw, const float* scale,
+                      const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
+                      int gated) {
+    GemmW16Params p{};
+    p.gated = gated;
+    p.m = (int)m;
+    p.n = (int)n;
+    p.k = (int)k;
+    p.num_kb = (int)ceil_div(k, kWBK);
+    p.scale = scale;
+    p.bias = bias;
+    p.y = y;
+    p.ldy = ldy;
+    const dim3 grid((unsigned)ceil_div(n, kWCh), (unsigned)ceil_div(m, kWTok));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (y_dtype == SBQ_F16) {
+        gated ? launch_large<true, true, AK>(grid, s, mx, mx2, mw, p) : launch_large<true, false, AK>(grid, s, mx, mx2, mw, p);
+    } else {
+        gated ? launch_large<false, true, AK>(grid, s, mx, mx2, mw, p) : launch_large<false, false, AK>(grid, s, mx, mx2, mw, p);
+    }
+    return check_launch("gemm_w8a16");
+}
+
+// Both tile sizes for one activation kind; x2: the low part of a split fp32 activation (kABF16x2).
+template <int AK>
+static int gemm_run_ak(const void* x, const void* x2, int64_t ldx, const void* packed, const float* scale,
+                       const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
+                       int gated) {
+    const int rows = m <= kSmallMaxRows ? kSTok : kWTok;
+    CUtensorMap mx, mx2, mw;
+    int st = make_x_map(&mx, AK, x, ldx, m, k, rows);
+    if (st) return st;
+    if (AK == kABF16x2) {
+        st = make_x_map(&mx2, AK, x2, ldx, m, k, rows);
+        if (st) return st;
+    } else {
+        mx2 = mx;
+    }
+    st = make_w_map(&mw, packed, n, k);
+    if (st) return st;
+    if (m <= kSmallMaxRows) return gemm_small<AK>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
+    return gemm_large<AK>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
+}
+
+// ---- fp32 activation split: x = hi + lo, both bf16 -------------------------------------------------
+// hi = bf16(x) (round to nearest even), lo = bf16(x - hi); x - hi is exact in fp32, so hi + lo keeps
+// about 17 significant bits of x and its full exponent range.  Eight elements per thread.
+__global__ void __launch_bounds__(256) split_bf16x2_kernel(const float* __restrict__ x, int64_t ldx, int64_t m,
+                                                           int64_t k, __nv_bfloat16* __restrict__ hi,
+                                                           __nv_bfloat16* __restrict__ lo, int64_t ldo) {
+    const int64_t per_row = k / 8, total = m * per_row;
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = v / per_row, c = (v - row * per_row) * 8;
+        const float4* src = reinterpret_cast<const float4*>(x + row * ldx + c);
+        const float4 a = __ldg(src), b = __ldg(src + 1);
+        const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat162 hh = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+            const float2 hf = __bfloat1622float2(hh);
+            const __nv_bfloat162 ll = __floats2bfloat162_rn(f[2 * i] - hf.x, f[2 * i + 1] - hf.y);
+            h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+            l[i] = *reinterpret_cast<const uint32_t*>(&ll);
+        }
+        *reinterpret_cast<uint4*>(hi + row * ldo + c) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(lo + row * ldo + c) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+}
+
+static int launch_split(const float* x, int64_t ldx, int64_t m, int64_t k, void* hi, void* lo, int64_t ldo,
+                        cudaStream_t s) {
+    const int64_t vecs = m * (k / 8);
+    int64_t blocks = (vecs + 255) / 256;
+    const int64_t cap = (int64_t)sm_count_w16() * 8;
+    if (blocks > cap) blocks = cap;
+    split_bf16x2_kernel<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, s>>>(
+        x, ldx, m, k, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo), ldo);
+    return check_launch("split_bf16x2");
+}
+
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
 namespace sbq {
-// The tensor-memory GEMM of both tile sizes; `gated`: see GemmW16Params (sbq_mlp_gateup_w8 runs the
-// gate projection into h, then the up projection with gated = 1).
+// The tensor-memory GEMM of both tile sizes for fp16 or bf16 x; `gated`: see GemmW16Params
+// (sbq_mlp_gateup_w8 runs the gate projection into h, then the up projection with gated = 1).
 int gemm_w8a16_run(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale, const float* bias,
                    int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream, int gated);
+// The same for an fp32 x already split into bf16 hi / lo (row stride ldx each).
+int gemm_w8a16_run_x2(const void* hi, const void* lo, int64_t ldx, const void* packed, const float* scale,
+                      const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
+                      int gated);
+// Workspace of the fp32 path: hi then lo, [m, k] bf16 each.
+size_t split_workspace_bytes(int64_t m, int64_t k);
+int split_into_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, void* workspace, size_t workspace_bytes,
+                         void** hi, void** lo, void* stream);
+}  // namespace sbq
+
+size_t sbq::split_workspace_bytes(int64_t m, int64_t k) { return 2 * align256((size_t)(m * k * 2)); }
+
+int sbq::split_into_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, void* workspace, size_t workspace_bytes,
+                              void** hi, void** lo, void* stream) {
+    if (!workspace) return set_error(SBQ_ERR_INVALID_ARGUMENT, "fp32 activations need a workspace");
+    if (reinterpret_cast<uintptr_t>(workspace) % 256) return set_error(SBQ_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+    const size_t need = split_workspace_bytes(m, k);
+    if (workspace_bytes < need) return set_error(SBQ_ERR_WORKSPACE, "workspace needs %zu bytes", need);
+    *hi = workspace;
+    *lo = static_cast<uint8_t*>(workspace) + need / 2;
+    return launch_split(static_cast<const float*>(x), ldx, m, k, *hi, *lo, k, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int sbq_gemm_w8a16(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
@@ -596,53 +750,38 @@ int sbq::gemm_w8a16_run(const void* x, int x_dtype, int64_t ldx, const void* pac
                         void* stream, int gated) {
     int st = check_linear_args(x, x_dtype, ldx, packed, scale, m, n, k, y, y_dtype, ldy);
     if (st) return st;
-    if (x_dtype != SBQ_F16) return set_error(SBQ_ERR_UNSUPPORTED, "sbq_gemm_w8a16 takes fp16 activations");
-    CUtensorMap mx, mw;
-    {
-        const uint64_t dims[2] = {(uint64_t)k, (uint64_t)m};
-        const uint64_t strides[1] = {(uint64_t)ldx * 2};
-        const uint32_t box[2] = {kWBK, kWTok};
-        st = encode_tmap(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-        if (st) return st;
-    }
-    {
-        const uint64_t kt = (uint64_t)ceil_div(k, kTileCols), nt = (uint64_t)ceil_div(n, kTileRows);
-        const uint64_t dims[4] = {64, 16, kt, nt};
-        const uint64_t strides[3] = {64, 1024, kt * 1024};
-        const uint32_t box[4] = {64, 16, 1, kWCh / 16};
-        st = encode_tmap(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, packed, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
-        if (st) return st;
-    }
-    if (m <= kSmallMaxRows) return gemm_small(x, ldx, packed, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
-    GemmW16Params p{};
-    p.gated = gated;
-    p.m = (int)m;
-    p.n = (int)n;
-    p.k = (int)k;
-    p.num_kb = (int)ceil_div(k, kWBK);
-    p.scale = scale;
-    p.bias = bias;
-    p.y = y;
-    p.ldy = ldy;
-    const dim3 grid((unsigned)ceil_div(n, kWCh), (unsigned)ceil_div(m, kWTok));
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int smem = W16Smem::kBytes;
-    if (y_dtype == SBQ_F16) {
-        if (gated) {
-            cudaFuncSetAttribute(gemm_w8a16_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            gemm_w8a16_kernel<true, true><<<grid, kWThreads, smem, s>>>(mx, mw, p);
-        } else {
-            cudaFuncSetAttribute(gemm_w8a16_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            gemm_w8a16_kernel<true, false><<<grid, kWThreads, smem, s>>>(mx, mw, p);
-        }
-    } else {
-        if (gated) {
-            cudaFuncSetAttribute(gemm_w8a16_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            gemm_w8a16_kernel<false, true><<<grid, kWThreads, smem, s>>>(mx, mw, p);
-        } else {
-            cudaFuncSetAttribute(gemm_w8a16_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            gemm_w8a16_kernel<false, false><<<grid, kWThreads, smem, s>>>(mx, mw, p);
-        }
-    }
-    return check_launch("gemm_w8a16");
+    if (x_dtype == SBQ_F16)
+        return gemm_run_ak<kAF16>(x, nullptr, ldx, packed, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
+    if (x_dtype == SBQ_BF16)
+        return gemm_run_ak<kABF16>(x, nullptr, ldx, packed, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
+    return set_error(SBQ_ERR_UNSUPPORTED,
+                     "sbq_gemm_w8a16 takes fp16 or bf16 activations (fp32: sbq_gemm_w8a16_x2 or sbq_linear_w8_ws)");
+}
+
+int sbq::gemm_w8a16_run_x2(const void* hi, const void* lo, int64_t ldx, const void* packed, const float* scale,
+                           const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
+                           void* stream, int gated) {
+    int st = check_linear_args(hi, SBQ_BF16, ldx, packed, scale, m, n, k, y, y_dtype, ldy);
+    if (st) return st;
+    if (!lo) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null low part");
+    if (reinterpret_cast<uintptr_t>(lo) % 16) return set_error(SBQ_ERR_ALIGNMENT, "activation rows must be 16-byte aligned");
+    return gemm_run_ak<kABF16x2>(hi, lo, ldx, packed, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
+}
+
+extern "C" int sbq_split_f32_bf16x2(const float* x, int64_t ldx, int64_t m, int64_t k, void* hi, void* lo,
+                                    int64_t ldo, void* stream) {
+    if (!x || !hi || !lo) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null pointer");
+    if (m <= 0 || k <= 0) return set_error(SBQ_ERR_INVALID_ARGUMENT, "m and k must be positive");
+    if (k % 8) return set_error(SBQ_ERR_UNSUPPORTED, "k must be a multiple of 8 (k=%lld)", (long long)k);
+    if (ldx < k || ldo < k) return set_error(SBQ_ERR_INVALID_ARGUMENT, "row stride smaller than the row");
+    if (reinterpret_cast<uintptr_t>(x) % 16 || (ldx * 4) % 16 || reinterpret_cast<uintptr_t>(hi) % 16 ||
+        reinterpret_cast<uintptr_t>(lo) % 16 || (ldo * 2) % 16)
+        return set_error(SBQ_ERR_ALIGNMENT, "rows must be 16-byte aligned");
+    return launch_split(x, ldx, m, k, hi, lo, ldo, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sbq_gemm_w8a16_x2(const void* x_hi, const void* x_lo, int64_t ldx, const void* packed, const float* scale,
+                                 const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
+                                 void* stream) {
+    return gemm_w8a16_run_x2(x_hi, x_lo, ldx, packed, scale, bias, m, n, k, y, y_dtype, ldy, stream, 0);
 }

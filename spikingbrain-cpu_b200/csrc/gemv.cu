@@ -1197,6 +1197,11 @@ extern "C" int sbq_gemv_w8(const void* x, int x_dtype, int64_t ldx, const void* 
 namespace sbq {
 int gemm_w8a16_run(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale, const float* bias,
                    int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream, int gated);
+int gemm_w8a16_run_x2(const void* hi, const void* lo, int64_t ldx, const void* packed, const float* scale,
+                      const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
+                      int gated);
+int split_into_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, void* workspace, size_t workspace_bytes,
+                         void** hi, void** lo, void* stream);
 }
 
 // Rows of x above which the gate/up pair runs as two tensor-memory GEMMs (the gate projection into
@@ -1210,7 +1215,7 @@ extern "C" int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const 
     if (st) return st;
     if (!packed_up || !scale_up) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null up-projection pointer");
     if (reinterpret_cast<uintptr_t>(packed_up) % 256) return set_error(SBQ_ERR_ALIGNMENT, "packed weight must be 256-byte aligned");
-    if (m > kGateUpGemmMinRows && x_dtype == SBQ_F16) {
+    if (m > kGateUpGemmMinRows && (x_dtype == SBQ_F16 || x_dtype == SBQ_BF16)) {
         st = gemm_w8a16_run(x, x_dtype, ldx, packed_gate, scale_gate, nullptr, m, n, k, h, h_dtype, ldh, stream, 0);
         if (st) return st;
         return gemm_w8a16_run(x, x_dtype, ldx, packed_up, scale_up, nullptr, m, n, k, h, h_dtype, ldh, stream, 1);
@@ -1218,6 +1223,26 @@ extern "C" int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const 
     GemvJob jb;
     fill_job(jb, x, ldx, packed_gate, scale_gate, packed_up, scale_up, nullptr, n, k, h, h_dtype, ldh);
     return run_single(jb, m, x_dtype, h_dtype, static_cast<cudaStream_t>(stream), "mlp_gateup_w8");
+}
+
+extern "C" int sbq_mlp_gateup_w8_ws(const void* x, int x_dtype, int64_t ldx, const void* packed_gate,
+                                    const float* scale_gate, const void* packed_up, const float* scale_up, int64_t m,
+                                    int64_t n, int64_t k, void* h, int h_dtype, int64_t ldh, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+    if (m > kGateUpGemmMinRows && x_dtype == SBQ_F32) {
+        int st = check_linear_args(x, x_dtype, ldx, packed_gate, scale_gate, m, n, k, h, h_dtype, ldh);
+        if (st) return st;
+        if (!packed_up || !scale_up) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null up-projection pointer");
+        if (reinterpret_cast<uintptr_t>(packed_up) % 256) return set_error(SBQ_ERR_ALIGNMENT, "packed weight must be 256-byte aligned");
+        void *hi = nullptr, *lo = nullptr;
+        st = split_into_workspace(x, ldx, m, k, workspace, workspace_bytes, &hi, &lo, stream);
+        if (st) return st;
+        st = gemm_w8a16_run_x2(hi, lo, k, packed_gate, scale_gate, nullptr, m, n, k, h, h_dtype, ldh, stream, 0);
+        if (st) return st;
+        return gemm_w8a16_run_x2(hi, lo, k, packed_up, scale_up, nullptr, m, n, k, h, h_dtype, ldh, stream, 1);
+    }
+    return sbq_mlp_gateup_w8(x, x_dtype, ldx, packed_gate, scale_gate, packed_up, scale_up, m, n, k, h, h_dtype, ldh,
+                             stream);
 }
 
 extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m, void* stream) {

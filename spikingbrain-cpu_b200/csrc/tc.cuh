@@ -257,9 +257,11 @@ __host__ __device__ constexpr uint32_t idesc_i8(bool a_signed, int m, int n) {
            (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-// Instruction descriptor, kind::f16: D fp32, A and B fp16, both K-major, M x N.
-__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
-    return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+// Instruction descriptor, kind::f16: D fp32, A and B both fp16 (bf16 = false) or both bf16
+// (bf16 = true; the two operands of one MMA always have the same type), both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool bf16 = false) {
+    return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 }  // namespace tc

@@ -13,7 +13,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib as L
-from .quant import _DTYPE_CODE, Int8Linear, _prepare_x, _ptr, _stream
+from .quant import _DTYPE_CODE, Int8Linear, _prepare_x, _ptr, _stream, _workspace
 
 
 class FusedGatedMLP(nn.Module):
@@ -58,15 +58,17 @@ class FusedGatedMLP(nn.Module):
         """Low-level device call: silu(gate(x2)) * up(x2) into ``h`` [m, n] (fp16/fp32, unit column stride).
 
         x2 is [m, k'] with 16-byte aligned rows (k' = in_features rounded up to 16).  The library
-        picks the kernel: the fused gate/up GEMV up to 32 rows (or for bf16/fp32 x); above, the gate
-        GEMM into ``h`` and the up GEMM whose epilogue replaces it by silu(gate) * up.
+        picks the kernel: the fused gate/up GEMV up to 32 rows; above, the gate GEMM into ``h`` and the
+        up GEMM whose epilogue replaces it by silu(gate) * up (fp32 x split once into bf16 high / low
+        parts in a workspace that both GEMMs read).
         """
         m, n = x2.shape[0], self.gate_proj.out_features
         if m > 0:
-            L.call("sbq_mlp_gateup_w8", _ptr(x2), _DTYPE_CODE[x2.dtype], x2.stride(0), _ptr(self.gate_proj.packed),
-                   _ptr(self.gate_proj.scale), _ptr(self.up_proj.packed), _ptr(self.up_proj.scale), m, n,
-                   x2.shape[1], _ptr(h), L.F16 if h.dtype == torch.float16 else L.F32, h.stride(0),
-                   _stream(h.device))
+            ws, ws_bytes = _workspace(m, x2.shape[1], x2.dtype, h.device)
+            L.call("sbq_mlp_gateup_w8_ws", _ptr(x2), _DTYPE_CODE[x2.dtype], x2.stride(0),
+                   _ptr(self.gate_proj.packed), _ptr(self.gate_proj.scale), _ptr(self.up_proj.packed),
+                   _ptr(self.up_proj.scale), m, n, x2.shape[1], _ptr(h), L.F16 if h.dtype == torch.float16 else L.F32,
+                   h.stride(0), _ptr(ws), ws_bytes, _stream(h.device))
         return h
 
 

@@ -97,6 +97,15 @@ def quantize_per_channel(weight: torch.Tensor, device=None) -> tuple[torch.Tenso
     return unpack_int8(packed, *weight.shape), scale
 
 
+def _workspace(m: int, k: int, x_dtype: torch.dtype, device: torch.device):
+    """(workspace tensor or None, bytes) for the int8 format's fp32 prefill path (sbq_linear_w8_ws):
+    the bf16 high / low parts of x, taken from torch's caching allocator (no device sync)."""
+    nbytes = int(L.load().sbq_linear_w8_workspace_bytes(m, k, _DTYPE_CODE[x_dtype]))
+    if nbytes == 0:
+        return None, 0
+    return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
+
+
 def _prepare_x(x: torch.Tensor, k: int, device: torch.device):
     """Flatten x to [m, k'] on the device with 16-byte aligned rows; k' is k rounded up to 16."""
     if x.shape[-1] != k:
@@ -184,9 +193,11 @@ class Int8Linear(_PackedLinear):
         if out.shape != (m, n) or out.stride(1) != 1 or out.dtype not in (torch.float32, torch.float16):
             raise ValueError("output must be an fp32/fp16 [%d, %d] view with unit column stride" % (m, n))
         if m > 0:
-            L.call("sbq_linear_w8", _ptr(x2), _DTYPE_CODE[x2.dtype], x2.stride(0), _ptr(self.packed),
+            ws, ws_bytes = _workspace(m, x2.shape[1], x2.dtype, out.device)
+            L.call("sbq_linear_w8_ws", _ptr(x2), _DTYPE_CODE[x2.dtype], x2.stride(0), _ptr(self.packed),
                    _ptr(self.scale), _ptr(self.bias), m, n, x2.shape[1], _ptr(out),
-                   L.F32 if out.dtype == torch.float32 else L.F16, out.stride(0), _stream(out.device))
+                   L.F32 if out.dtype == torch.float32 else L.F16, out.stride(0), _ptr(ws), ws_bytes,
+                   _stream(out.device))
         return out
 
     def gemv_job(self, x2: torch.Tensor, out: torch.Tensor) -> L.GemvJob:
