@@ -57,14 +57,17 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+    """nvidia-smi clocks and throttle reasons sampled while the timed region runs.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Every GPU of the host is queried (with its UUID) and only the samples of the GPUs this job
+    runs on are kept."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpus: list[str]):
-        self.gpus = gpus
+        self.gpus = {g.strip().lower() for g in gpus}
         self.proc = None
 
     def __enter__(self):
@@ -72,8 +75,8 @@ class ClockSampler:
             return self
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", ",".join(map(str, self.gpus))], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
         return self
@@ -94,7 +97,7 @@ class ClockSampler:
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for ln in getattr(self, "lines", []):
             f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
+            if len(f) < 9 or f[0].lower() not in self.gpus:
                 continue
             try:
                 sm.append(float(f[1]))
@@ -368,6 +371,63 @@ def stack_cases(sbq, stack, dev, stream, warmup: int) -> dict:
     return out
 
 
+def module_api_cases(sbq, stack, dev, steps: int, warmup: int) -> dict:
+    """The decode step (batch 1) through the drop-in's public module calls, eager (no CUDA graph):
+    with host tensors (every projection copies its input in and its output back and waits, the
+    path the reference's CPU model loop gets by swapping in the modules) and with device tensors.
+    CUDA events on the launching stream around the whole step sequence (host gaps included)."""
+    import torch
+
+    total = stack.weight_bytes()
+    x_dev = sbq.workloads.activation(1, stack.hidden, seed=5, device=dev)
+    out = {}
+    for name, x in (("host_tensors", x_dev.cpu()), ("device_tensors", x_dev)):
+        for _ in range(warmup):
+            stack.forward_modules(x)
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream(dev)
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record(st)
+        for _ in range(steps):
+            y = stack.forward_modules(x)
+        e_ev.record(st)
+        e_ev.synchronize()
+        ms = s_ev.elapsed_time(e_ev) / steps
+        out[name] = {"ms_per_step": round(ms, 3), "gbs": round(total / ms / 1e6, 1),
+                     "module_calls_per_step": 4 * len(stack.layers), "launches_per_step": 5 * len(stack.layers)}
+        if name == "host_tensors":
+            out[name]["h2d_d2h_pairs_per_step"] = 4 * len(stack.layers)
+            assert y.device.type == "cpu"
+    return out
+
+
+def load_pack_case(sbq, dev) -> dict:
+    """The checkpoint's int8 load on the GPU: every linear weight of SpikingBrain2.0's shapes (539
+    weights, 5.17 G parameters, bf16 on the host as the loader reads them) through the streaming
+    packer (host -> pinned staging -> device -> quantise + pack), against the reference's 33.2 s
+    int8 load (which also reads the shards from storage; the storage read is not included here)."""
+    import torch
+
+    shapes = sbq.workloads.checkpoint_linears()
+    biggest = max(n * k for _, n, k in shapes)
+    g = torch.Generator().manual_seed(7)
+    host = (torch.randn(biggest, generator=g) * 0.02).to(torch.bfloat16)  # values do not change the timing
+    packer = sbq.loader.StreamingPacker(device=dev)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    mods = [packer.make_linear("int8", host[:n * k].view(n, k)) for _, n, k in shapes]
+    packer.finish()
+    torch.cuda.synchronize()
+    secs = time.perf_counter() - t0
+    params = sum(n * k for _, n, k in shapes)
+    res = {"seconds": round(secs, 3), "weights": len(mods), "params": params, "h2d_bytes": 2 * params,
+           "h2d_gbs": round(2 * params / secs / 1e9, 1), "packed_bytes": sum(int(m.packed.numel()) for m in mods),
+           "reference_int8_load_s": 33.2, "note": "host bf16 -> device quantise + pack; storage read not included"}
+    del mods, packer
+    torch.cuda.empty_cache()
+    return res
+
+
 def kernel_mode(args) -> None:
     """--kernel NAME: one configuration's kernel alone (also the command the ncu captures use)."""
     import torch
@@ -494,9 +554,12 @@ def main() -> None:
     del g2
 
     extra = None
+    module_api = None
     if world == 1 and not args.no_extra:
         extra = kernel_cases(sbq, dev, stream, args.steps, args.warmup)
         extra["cfg4_stack"] = stack_cases(sbq, stack, dev, stream, args.warmup)
+        module_api = module_api_cases(sbq, stack, dev, steps=max(5, min(20, args.steps)), warmup=2)
+        extra["load_pack"] = load_pack_case(sbq, dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -541,7 +604,9 @@ def main() -> None:
                                                "bytes_per_launch": gu_bytes, "us_per_launch": round(gu_ms * 1e3, 3)}},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 2 * hidden,
-                    "d2h_bytes_per_step": 2 * hidden, "ms_per_step": round(e2e_ms, 4)},
+                    "d2h_bytes_per_step": 2 * hidden, "ms_per_step": round(e2e_ms, 4),
+                    "path": "CapturedStack.__call__ on pinned host tensors (one CUDA graph per step)",
+                    "module_api": module_api},
             "gpu_launches": launches * args.steps,
             "clocks": clocks.summary(),
             "configs_0_3": extra,

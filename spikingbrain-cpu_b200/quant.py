@@ -138,6 +138,28 @@ class _PackedLinear(nn.Module):
             self.rowsum = None
         self.bias = None if bias is None else nn.Parameter(bias.detach().float().to(dev), requires_grad=False)
 
+    @classmethod
+    def from_packed(cls, packed: torch.Tensor, scale: torch.Tensor, rowsum: torch.Tensor | None, out_features: int,
+                    in_features: int, bias: torch.Tensor | None = None, **attrs):
+        """A module around weights already quantised and packed on the device (e.g. by
+        ``loader.StreamingPacker``); the buffers are adopted, not copied."""
+        if packed.numel() != L.packed_bytes(out_features, in_features) or scale.numel() != out_features:
+            raise ValueError("packed buffers do not match a [%d, %d] weight" % (out_features, in_features))
+        mod = cls.__new__(cls)
+        nn.Module.__init__(mod)
+        mod.out_features, mod.in_features = int(out_features), int(in_features)
+        mod.register_buffer("packed", packed, persistent=False)
+        mod.register_buffer("scale", scale)
+        if rowsum is not None:
+            mod.register_buffer("rowsum", rowsum, persistent=False)
+        else:
+            mod.rowsum = None
+        dev = scale.device
+        mod.bias = None if bias is None else nn.Parameter(bias.detach().float().to(dev), requires_grad=False)
+        for k_, v in attrs.items():
+            setattr(mod, k_, v)
+        return mod
+
     @property
     def qweight(self) -> torch.Tensor:
         """Row-major int8 [out, in] view of the packed weight (the reference's ``qweight`` buffer)."""

@@ -323,6 +323,23 @@ class ProjectionStack(nn.Module):
             x = self._gather(layer.o.forward_into(qkvd[:, 2 * hd:3 * hd], x.new_empty(m, hd // w)))
         return x
 
+    def forward_modules(self, x: torch.Tensor) -> torch.Tensor:
+        """The same data flow through the drop-in's public module calls only (Int8Linear.__call__,
+        FusedGatedMLP.__call__ = down(silu(gate(x)) * up(x))), as the reference's model would make
+        them: x may be a host tensor (each call then copies its input in and its output back, the
+        path a reference model loop on the CPU gets) or a device tensor (stream-ordered, no sync).
+        One GPU only."""
+        if self.world != 1:
+            raise RuntimeError("forward_modules runs an unsharded stack")
+        hd = self.hidden
+        for layer in self.layers:
+            qkvd = layer.qkvd(x)
+            side = layer.mlp(x)
+            dout = layer.dout(qkvd[:, 3 * hd:])
+            x = layer.o(qkvd[:, 2 * hd:3 * hd])
+        self._side = (torch.cat([side, dout], 1), False)
+        return x
+
     def _forward_grouped(self, x: torch.Tensor) -> torch.Tensor:
         from .quant import gemv_group
 

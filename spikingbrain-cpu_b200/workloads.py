@@ -59,3 +59,38 @@ def stack_bytes(layers: int = LAYERS) -> int:
 
 def stack_flops(m: int, layers: int = LAYERS) -> int:
     return 2 * m * stack_bytes(layers)
+
+
+# ---- the checkpoint's linear layers (for load-time measurement) ---------------------------------
+# SpikingBrain2.0's projections as the reference's model declares them (spikingbrain_cpu/model.py:
+# GatedMLP :232-240, SoftmaxAttention :243-258, HybridSSEAttention :271-301) with the checkpoint's
+# sizes (config.py defaults: hidden 2560, 32 heads of 128, 8 key/value heads, MLP 9728, vocabulary
+# 151936, 4 sparse partitions, 36 blocks of which 10 are softmax attention) and the tied int8 head
+# (loader.py:94).  Which block indices are attention does not change the list of shapes.
+CKPT = {"hidden": 2560, "heads": 32, "head_dim": 128, "kv_heads": 8, "inter": 9728, "vocab": 151936,
+        "partitions": 4, "layers": 36, "attn_layers": 10}
+
+
+def checkpoint_linears() -> list[tuple[str, int, int]]:
+    """(name, out_features, in_features) of every linear weight the loader hands to make_linear."""
+    c = CKPT
+    hid, hd, kvd = c["hidden"], c["heads"] * c["head_dim"], c["kv_heads"] * c["head_dim"]
+    out = []
+    for i in range(c["layers"]):
+        p = "model.layers.%d." % i
+        if i < c["attn_layers"]:
+            a = p + "attn."
+            out += [(a + "q_proj", hd, hid), (a + "k_proj", kvd, hid), (a + "v_proj", kvd, hid), (a + "o_proj", hid, hd)]
+        else:
+            a = p + "attn."
+            out += [(a + "sse_q_proj", hd, hid), (a + "sse_k_proj", hd, hid), (a + "sse_v_proj", hd, hid),
+                    (a + "lora_q_proj.0", c["head_dim"], hid), (a + "lora_q_proj.1", hd, c["head_dim"]),
+                    (a + "lora_k_proj.0", c["head_dim"], hid), (a + "lora_k_proj.1", hd, c["head_dim"]),
+                    (a + "sse_a_proj", 2 * c["heads"], hid), (a + "sse_b_proj", 2 * c["heads"], hid),
+                    (a + "sse_e_proj", c["partitions"], hid), (a + "sse_o_proj", hid, hd),
+                    (a + "swa_q_proj", hd, hid), (a + "swa_k_proj", kvd, hid), (a + "swa_v_proj", kvd, hid),
+                    (a + "swa_o_proj", hid, hd)]
+        m = p + "mlp."
+        out += [(m + "gate_proj", c["inter"], hid), (m + "up_proj", c["inter"], hid), (m + "down_proj", hid, c["inter"])]
+    out.append(("lm_head", c["vocab"], hid))
+    return out

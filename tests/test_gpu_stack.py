@@ -88,3 +88,18 @@ def test_decode_program_matches_grouped_launches(sbq, layers, hidden, inter):
     assert runner.program is not None
     assert torch.equal(runner(x.cpu()).cuda(), want)
     runner.release()
+
+
+@pytest.mark.parametrize("m", [1, 40])
+def test_module_api_path_host_and_device(sbq, m):
+    # the same data flow through the drop-in's public module calls only (the reference model's way of
+    # calling its projections): host tensors in and out, or device tensors with no host sync
+    stack = sbq.stack.ProjectionStack(layers=2, hidden=256, inter=768, seed=11)
+    x = sbq.workloads.activation(m, 256, seed=12)
+    y_host = stack.forward_modules(x)
+    assert y_host.device.type == "cpu" and y_host.dtype == torch.float16
+    y_dev = stack.forward_modules(x.cuda())
+    assert y_dev.device.type == "cuda"
+    assert torch.equal(y_host, y_dev.cpu())
+    want, _ = _oracle_stack(stack, x)
+    assert R.rel_l2(y_host.float().numpy(), want.astype(np.float32)) < 1e-3
