@@ -330,8 +330,25 @@ def kernel_cases(sbq, dev, stream, steps: int, warmup: int,
 
         ms = _graph_time(f, stream, max(20, steps // 10), warmup)
         ops = 2 * m * n * k
+        byt = 2 * m * k + n * k + 4 * n + 4 * m * n  # x fp16, W, scales, y fp32
+        t_roof = max(byt / (pk["hbm_gbs"] * 1e9), ops / (SPEC_I8_TOPS * 1e12))
         out["cfg3_dyn"] = {"us": round(ms * 1e3, 2), "tops": round(ops / ms / 1e9, 1),
-                           "frac_int8_spec_4500": round(ops / ms / 1e9 / SPEC_I8_TOPS, 4)}
+                           "frac_int8_spec_4500": round(ops / ms / 1e9 / SPEC_I8_TOPS, 4),
+                           "roofline_us": round(t_roof * 1e6, 2), "frac_roofline": round(t_roof * 1e3 / ms, 4)}
+        # the GEMM alone on an already quantised activation (the same launch sbq_linear_dyn chains)
+        xq = torch.empty(m, k, dtype=torch.uint8, device=dev)
+        sx = torch.empty(1, device=dev)
+        zp = torch.empty(1, dtype=torch.int32, device=dev)
+        L.call("sbq_quant_act_per_tensor", vp(x.data_ptr()), L.F16, k, m, k, vp(xq.data_ptr()), vp(sx.data_ptr()),
+               vp(zp.data_ptr()), vp(ws.data_ptr()), wsb, st)
+
+        def g():
+            L.call("sbq_gemm_w8a8", vp(xq.data_ptr()), 0, vp(p_.data_ptr()), vp(rs.data_ptr()), vp(sx.data_ptr()),
+                   vp(zp.data_ptr()), vp(s_.data_ptr()), None, m, n, k, vp(y.data_ptr()), n, None, st)
+
+        ms_g = _graph_time(g, stream, max(20, steps // 10), warmup)
+        out["cfg3_dyn"]["gemm_only_us"] = round(ms_g * 1e3, 2)
+        out["cfg3_dyn"]["quantise_us"] = round((ms - ms_g) * 1e3, 2)
     return out
 
 

@@ -331,7 +331,19 @@ struct GemmI8Params {
 
 constexpr int kI8BM = 128;         // rows of xq per CTA (MMA M)
 constexpr int kI8BK = 128;         // k per pipeline stage (bytes of an int8 row = one 128-byte swizzle row)
-constexpr int kI8Stages = 4;
+#ifndef SBQ_I8_STAGES
+#define SBQ_I8_STAGES 4
+#endif
+constexpr int kI8Stages = SBQ_I8_STAGES;
+#ifndef SBQ_I8_NACC
+#define SBQ_I8_NACC 1
+#endif
+// Independent int32 accumulators per tile in tensor memory: k-step j of every k-block adds into
+// accumulator j % kI8Acc, so consecutive MMAs do not depend on one another; the epilogue adds them.
+constexpr int kI8Acc = SBQ_I8_NACC;
+__host__ __device__ constexpr uint32_t tmem_cols_for(int c) {
+    return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512;
+}
 
 template <int BN>
 struct I8Smem {
@@ -377,7 +389,7 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
         if (p.tma_y) tc::prefetch_tmap(&tmap_y);
     }
     if (warp == 2) {
-        tc::tmem_alloc(tmem_slot, BN < 32 ? 32 : BN);
+        tc::tmem_alloc(tmem_slot, tmem_cols_for(kI8Acc * BN));
         tc::tmem_relinquish();
     }
     for (int i = threadIdx.x; i < BN; i += blockDim.x) {
@@ -430,7 +442,7 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
             for (int j = 0; j < kI8BK / 32; ++j) {
                 const uint64_t ad = tc::smem_desc(a_s + j * 32, tc::kSwizzle128B, 1024);
                 const uint64_t bd = tc::smem_desc(b_s + (j >> 1) * (BN * 64) + (j & 1) * 32, tc::kSwizzle64B, 512);
-                tc::mma_i8(tmem, ad, bd, idesc, (kb | j) != 0);
+                tc::mma_i8(tmem + (j % kI8Acc) * BN, ad, bd, idesc, kb != 0 || j >= kI8Acc);
             }
             tc::mma_commit(&empty[s]);
         }
@@ -458,6 +470,14 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
             uint32_t r[32];
             tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
             tc::tmem_wait_ld();
+#pragma unroll
+            for (int a_ = 1; a_ < kI8Acc; ++a_) {
+                uint32_t r2[32];
+                tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + a_ * BN + c * 32, r2);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 32; ++q) r[q] += r2[q];  // int32, exact
+            }
             const int nb = n0 + c * 32;
             if (p.tma_y) {
                 // block (warp, c): 32 rows of 128 bytes; 16-byte unit j of row r sits at j ^ (r % 8)
@@ -518,7 +538,7 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
     __syncthreads();
     if (warp == 2) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, BN < 32 ? 32 : BN);
+        tc::tmem_dealloc(tmem, tmem_cols_for(kI8Acc * BN));
     }
 }
 
@@ -654,7 +674,10 @@ static int make_gemm_maps(CUtensorMap* ma, CUtensorMap* mb, const void* xq, int6
     return SBQ_OK;
 }
 
-constexpr int kI8BN = 128;
+#ifndef SBQ_I8_BN
+#define SBQ_I8_BN 128
+#endif
+constexpr int kI8BN = SBQ_I8_BN;  // output channels per CTA (MMA N)
 
 // dependent: launched as a programmatic dependent of the activation quantisation (sbq_linear_dyn),
 // which lets the pipeline set-up and the first weight tiles overlap that kernel.  Direct calls of
