@@ -31,6 +31,7 @@
  *   quant.py:41-53   Int8Linear.forward               -> sbq_linear_w8 / sbq_linear_w8_ws
  *                    (sbq_gemv_w8 / sbq_gemm_w8a16 / sbq_split_f32_bf16x2 + sbq_gemm_w8a16_x2)
  *   model.py:239-240 GatedMLP.forward (gate, up, SiLU) -> sbq_mlp_gateup_w8
+ *   model.py:287-288 lora_q_proj / lora_k_proj pairs   -> sbq_lora_pair_w8
  *   quant.py:57-61   DynamicInt8Linear packing         -> sbq_quantize_pack (+ row sums)
  *   quant.py:63-66   DynamicInt8Linear.forward        -> sbq_linear_dyn
  *                    (= sbq_quant_act_per_tensor + sbq_gemm_w8a8)
@@ -169,6 +170,17 @@ SBQ_API int sbq_mlp_gateup_w8_ws(const void* x, int x_dtype, int64_t ldx, const 
                                  const float* scale_gate, const void* packed_up, const float* scale_up, int64_t m,
                                  int64_t n, int64_t k, void* h, int h_dtype, int64_t ldh, void* workspace,
                                  size_t workspace_bytes, void* stream);
+
+/* The rank-r projection pair of the hybrid block's LoRA branches (model.py:287-288: lora_q_proj /
+ * lora_k_proj = Linear(k -> r) then Linear(r -> n), each an Int8Linear in the int8 format) at decode
+ * sizes in one launch: y = ((x q_a^T) * scale_a) q_b^T * scale_b.  The intermediate t [m, r] stays
+ * on the SMs (computed once per 8-CTA cluster, gathered through distributed shared memory) in fp32,
+ * and the second stage reads it as an fp32 activation (bf16 high + low parts).  1 <= m <= 16;
+ * r a multiple of 16, at most 128; packed_a is [r, k], packed_b is [n, r]; y [m, n] fp32 or fp16
+ * (row stride ldy).  x dtype SBQ_F16 / SBQ_BF16 / SBQ_F32. */
+SBQ_API int sbq_lora_pair_w8(const void* x, int x_dtype, int64_t ldx, const void* packed_a, const float* scale_a,
+                             const void* packed_b, const float* scale_b, int64_t m, int64_t r, int64_t n, int64_t k,
+                             void* y, int y_dtype, int64_t ldy, void* stream);
 
 /* One projection of a grouped decode launch (sbq_gemv_w8_group).  A job with packed_up set is a fused
  * gate/up job: y = silu(x q^T * scale) * (x q_up^T * scale_up), no bias. */

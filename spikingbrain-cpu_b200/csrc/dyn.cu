@@ -11,6 +11,7 @@
 // accumulators in tensor memory) and applies the zero-point correction acc - zp * rowsum[n] in the
 // epilogue, which is exact integer arithmetic.  The per-token mode (symmetric int8, one scale per
 // row, no reference counterpart) shares the GEMM with a signed A operand.
+#include <atomic>
 #include <cstring>
 
 #include "tc.cuh"
@@ -312,9 +313,24 @@ __global__ void __launch_bounds__(kTokThreads) quantize_per_token_kernel(const T
 }
 
 // ============================================================================ int8 GEMM ======
+//
+// One CTA computes a 128 (xq rows) x 256 (weight rows) output tile: 4-stage TMA ring (xq 128 x 128 B
+// with 128-byte swizzle, weight two 256 x 64 B halves with 64-byte swizzle), one thread issues
+// tcgen05.mma.cta_group::1.kind::i8 (M = 128, N = 256, K = 32) into int32 accumulators in tensor
+// memory.  The N = 256 shape matters: a per-k-block trace showed the issuing thread held about as
+// long per MMA at N = 128 as at N = 256, so the wide instruction does twice the work per issue
+// (~80 % of the int8 tensor peak in the loop).  When those tiles are too few for the GPU, the K range
+// of a tile is split over a cluster of 2 or 4 CTAs (one K part each).  After the main loop each CTA
+// owns 256/S of the tile's columns: it writes its partial sums of the other columns to shared
+// memory, bulk-copies them (the copy engine, cp.async.bulk shared::cta -> shared::cluster) into the
+// owning CTA, and adds the partials it receives to its own columns - int32, so the sum is exact and
+// independent of order.  Epilogue (8 warps; warps w and w + 4 share tensor-memory lanes and split
+// the column blocks): acc - zp * rowsum[n], float(acc) * (s * scale[n]) (fma with a bias), staged in
+// the freed ring and written with TMA stores.
 
 struct GemmI8Params {
     int m, n, k, num_kb;
+    int splits;             // K parts of a tile (CTAs of one cluster): 1, 2 or 4
     const int32_t* rowsum;  // per-tensor zero-point correction (may be null in per-token mode)
     const float* s_x;       // one scale (per-tensor) or one per row (per-token)
     int s_stride;           // 0 or 1
@@ -329,52 +345,66 @@ struct GemmI8Params {
                             // aligned, ldy and n multiples of 4; otherwise the epilogue stores element-wise
 };
 
-constexpr int kI8BM = 128;         // rows of xq per CTA (MMA M)
+constexpr int kI8BM = 128;         // rows of xq per tile (MMA M)
+constexpr int kI8BN = 256;         // weight rows (output channels) per tile (MMA N)
 constexpr int kI8BK = 128;         // k per pipeline stage (bytes of an int8 row = one 128-byte swizzle row)
 #ifndef SBQ_I8_STAGES
 #define SBQ_I8_STAGES 4
 #endif
 constexpr int kI8Stages = SBQ_I8_STAGES;
-#ifndef SBQ_I8_NACC
-#define SBQ_I8_NACC 1
-#endif
-// Independent int32 accumulators per tile in tensor memory: k-step j of every k-block adds into
-// accumulator j % kI8Acc, so consecutive MMAs do not depend on one another; the epilogue adds them.
-constexpr int kI8Acc = SBQ_I8_NACC;
-__host__ __device__ constexpr uint32_t tmem_cols_for(int c) {
-    return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512;
-}
+constexpr int kI8Threads = 256;                // 8 warps
+constexpr int kI8MaxSplits = 4;
+constexpr int kI8Blocks = kI8BN / 32;          // 32-column blocks of a tile
+constexpr int kI8SlotBytes = kI8BM * 32 * 4;   // one block: 128 rows x 32 int32 = 16 KiB
 
-template <int BN>
 struct I8Smem {
     static constexpr int kA = kI8BM * kI8BK;  // 16 KiB
-    static constexpr int kB = BN * kI8BK;     // two 64-wide halves of BN rows
+    static constexpr int kB = kI8BN * kI8BK;  // 32 KiB: two 64-wide halves of 256 rows
     static constexpr int kStage = kA + kB;
-    static constexpr int kBytes = kI8Stages * kStage + 1024 /* alignment */ + 256 /* barriers */ + BN * 12;
+    static constexpr int kRing = kI8Stages * kStage;
+    // after the main loop the ring holds 16 KiB slots: the outgoing partials (blocks other CTAs own),
+    // the incoming ones (blocks this CTA owns, one slot per sender) and the TMA-store staging
+    static constexpr int kSlots = kRing / kI8SlotBytes;
+    static constexpr int kTail = 256 /* barriers */ + kI8BN * 5 * 4;  // scale, bias, rowsum, s*scale, zp*rowsum
+    static constexpr int kBytes = kRing + 1024 /* alignment */ + kTail;
+    static_assert(kSlots >= kI8Blocks, "every split uses at most 8 slots (S = 1, 2) or 12 (S = 4)");
+    static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
 };
 
-// One 128 x BN output tile per CTA.  Warp 0: TMA producer.  Warp 1: MMA issuer.  Warp 2: TMEM
-// allocation.  All four warps: epilogue (warp w owns accumulator lanes 32 w .. 32 w + 31).
-template <int BN, bool A_SIGNED>
-__global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                                                          const __grid_constant__ CUtensorMap tmap_b,
-                                                          const __grid_constant__ CUtensorMap tmap_y,
-                                                          const GemmI8Params p) {
-    using S = I8Smem<BN>;
-    static_assert(4 * (BN / 32) * 4096 <= kI8Stages * S::kStage, "epilogue staging exceeds the pipeline buffers");
+// 16-byte unit j (of 8) of row `lane` of a 32-row block in a slot region: [j][lane], so that a warp's
+// accesses to one unit are 512 contiguous bytes.
+__device__ __forceinline__ uint32_t slot_unit(int j, int lane) { return (uint32_t)((j * 32 + lane) * 16); }
+
+// Warp 0: TMA producer.  Warp 1: MMA issuer.  Warp 2: TMEM allocation.  Warps 2, 3: per-channel
+// epilogue factors.  All eight warps: epilogue (warp w reads accumulator lanes 32 (w % 4) ..).
+template <bool A_SIGNED>
+__global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                                 const __grid_constant__ CUtensorMap tmap_b,
+                                                                 const __grid_constant__ CUtensorMap tmap_y,
+                                                                 const GemmI8Params p) {
+    using S = I8Smem;
+    constexpr int BN = kI8BN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kI8Stages * S::kStage);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kRing);
     uint64_t* empty = full + kI8Stages;
     uint64_t* done = empty + kI8Stages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* recv = done + 1;  // incoming partials of the other K parts
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv + 1);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
-    float* s_scale = reinterpret_cast<float*>(smem + kI8Stages * S::kStage + 256);
+    float* s_scale = reinterpret_cast<float*>(smem + S::kRing + 256);
     float* s_bias = s_scale + BN;
     int32_t* s_rowsum = reinterpret_cast<int32_t*>(s_bias + BN);
+    float* s_f = reinterpret_cast<float*>(s_rowsum + BN);   // s_x * scale[n] (per-tensor mode)
+    int32_t* s_zr = reinterpret_cast<int32_t*>(s_f + BN);   // zp * rowsum[n]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * kI8BM, n0 = blockIdx.x * BN;
+    const int splits = p.splits;
+    const int part = splits > 1 ? (int)tc::cluster_ctarank() : 0;
+    const int kb0 = part * p.num_kb / splits, nkb = (part + 1) * p.num_kb / splits - kb0;  // >= 1 (host)
+    const int nown = kI8Blocks / splits, own0 = part * nown;  // this CTA's column blocks
+    const int nout = kI8Blocks - nown;                        // blocks it sends to their owners
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kI8Stages; ++s) {
@@ -382,123 +412,179 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
             tc::mbar_init(&empty[s], 1);
         }
         tc::mbar_init(done, 1);
+        tc::mbar_init(recv, 1);
         *abort_flag = 0;
         tc::fence_mbar_init();
+        // armed before any other CTA can send (they send after the cluster barrier that follows
+        // every CTA's main loop)
+        if (splits > 1) tc::mbar_arrive_expect_tx(recv, (uint32_t)((splits - 1) * nown * kI8SlotBytes));
         tc::prefetch_tmap(&tmap_a);
         tc::prefetch_tmap(&tmap_b);
         if (p.tma_y) tc::prefetch_tmap(&tmap_y);
     }
     if (warp == 2) {
-        tc::tmem_alloc(tmem_slot, tmem_cols_for(kI8Acc * BN));
+        tc::tmem_alloc(tmem_slot, BN);
         tc::tmem_relinquish();
-    }
-    for (int i = threadIdx.x; i < BN; i += blockDim.x) {
-        const int n = n0 + i;
-        s_scale[i] = n < p.n ? p.scale[n] : 0.0f;
-        s_bias[i] = (p.bias && n < p.n) ? p.bias[n] : 0.0f;
-        s_rowsum[i] = (p.rowsum && n < p.n) ? p.rowsum[n] : 0;
     }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0 && lane == 0) {
-        // ---- producer.  The weight tiles do not depend on the previous kernel (the activation
-        // quantisation, when launched from sbq_linear_dyn as its programmatic dependent): those of
-        // the first stages are requested before griddepcontrol.wait, the activation tiles after it.
-        const int pre = p.num_kb < kI8Stages ? p.num_kb : kI8Stages;
-        for (int kb = 0; kb < pre; ++kb) {
-            uint8_t* b_s = smem + kb * S::kStage + S::kA;
-            tc::mbar_arrive_expect_tx(&full[kb], S::kStage);
-            tc::tma_load_4d(b_s, &tmap_b, &full[kb], 0, 0, 2 * kb, n0 / 16);
-            tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[kb], 0, 0, 2 * kb + 1, n0 / 16);
-        }
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        for (int kb = 0; kb < pre; ++kb) tc::tma_load_2d(smem + kb * S::kStage, &tmap_a, &full[kb], kb * kI8BK, m0);
-        for (int kb = pre; kb < p.num_kb; ++kb) {
-            const int s = kb % kI8Stages;
-            const uint32_t phase = (kb / kI8Stages) & 1;
-            if (!tc::mbar_wait(&empty[s], phase ^ 1)) { *abort_flag = 1; break; }
-            if (*(volatile int*)abort_flag) break;
-            uint8_t* a_s = smem + s * S::kStage;
-            uint8_t* b_s = a_s + S::kA;
-            tc::mbar_arrive_expect_tx(&full[s], S::kStage);
-            tc::tma_load_2d(a_s, &tmap_a, &full[s], kb * kI8BK, m0);
-            tc::tma_load_4d(b_s, &tmap_b, &full[s], 0, 0, 2 * kb, n0 / 16);
-            tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[s], 0, 0, 2 * kb + 1, n0 / 16);
-        }
-    } else if (warp == 1 && lane == 0) {
-        // ---- MMA issuer
-        constexpr uint32_t idesc = tc::idesc_i8(A_SIGNED, kI8BM, BN);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-            const int s = kb % kI8Stages;
-            const uint32_t phase = (kb / kI8Stages) & 1;
-            if (!tc::mbar_wait(&full[s], phase)) { *abort_flag = 1; break; }
-            tc::fence_after_sync();
-            const uint8_t* a_s = smem + s * S::kStage;
-            const uint8_t* b_s = a_s + S::kA;
-#pragma unroll
-            for (int j = 0; j < kI8BK / 32; ++j) {
-                const uint64_t ad = tc::smem_desc(a_s + j * 32, tc::kSwizzle128B, 1024);
-                const uint64_t bd = tc::smem_desc(b_s + (j >> 1) * (BN * 64) + (j & 1) * 32, tc::kSwizzle64B, 512);
-                tc::mma_i8(tmem + (j % kI8Acc) * BN, ad, bd, idesc, kb != 0 || j >= kI8Acc);
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- producer.  The weight tiles do not depend on the previous kernel (the activation
+            // quantisation, when launched from sbq_linear_dyn as its programmatic dependent): those of
+            // the first stages are requested before griddepcontrol.wait, the activation tiles after it.
+            const int pre = nkb < kI8Stages ? nkb : kI8Stages;
+            for (int i = 0; i < pre; ++i) {
+                uint8_t* b_s = smem + i * S::kStage + S::kA;
+                tc::mbar_arrive_expect_tx(&full[i], S::kStage);
+                tc::tma_load_4d(b_s, &tmap_b, &full[i], 0, 0, 2 * (kb0 + i), n0 / 16);
+                tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[i], 0, 0, 2 * (kb0 + i) + 1, n0 / 16);
             }
-            tc::mma_commit(&empty[s]);
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            for (int i = 0; i < pre; ++i)
+                tc::tma_load_2d(smem + i * S::kStage, &tmap_a, &full[i], (kb0 + i) * kI8BK, m0);
+            for (int i = pre; i < nkb; ++i) {
+                const int s = i % kI8Stages;
+                const uint32_t phase = (i / kI8Stages) & 1;
+                if (!tc::mbar_wait(&empty[s], phase ^ 1)) { *abort_flag = 1; break; }
+                if (*(volatile int*)abort_flag) break;
+                uint8_t* a_s = smem + s * S::kStage;
+                uint8_t* b_s = a_s + S::kA;
+                tc::mbar_arrive_expect_tx(&full[s], S::kStage);
+                tc::tma_load_2d(a_s, &tmap_a, &full[s], (kb0 + i) * kI8BK, m0);
+                tc::tma_load_4d(b_s, &tmap_b, &full[s], 0, 0, 2 * (kb0 + i), n0 / 16);
+                tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[s], 0, 0, 2 * (kb0 + i) + 1, n0 / 16);
+            }
         }
-        tc::mma_commit(done);
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer
+            constexpr uint32_t idesc = tc::idesc_i8(A_SIGNED, kI8BM, BN);
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % kI8Stages;
+                const uint32_t phase = (i / kI8Stages) & 1;
+                if (!tc::mbar_wait(&full[s], phase)) { *abort_flag = 1; break; }
+                tc::fence_after_sync();
+                const uint8_t* a_s = smem + s * S::kStage;
+                const uint8_t* b_s = a_s + S::kA;
+#pragma unroll
+                for (int j = 0; j < kI8BK / 32; ++j) {
+                    const uint64_t ad = tc::smem_desc(a_s + j * 32, tc::kSwizzle128B, 1024);
+                    const uint64_t bd = tc::smem_desc(b_s + (j >> 1) * (BN * 64) + (j & 1) * 32, tc::kSwizzle64B, 512);
+                    tc::mma_i8(tmem, ad, bd, idesc, (i | j) != 0);
+                }
+                tc::mma_commit(&empty[s]);
+            }
+            tc::mma_commit(done);
+        }
+    } else if (warp == 2 || warp == 3) {
+        // per-channel factors, off the producer's critical path (read in the epilogue only)
+        for (int i = threadIdx.x - 64; i < BN; i += 64) {
+            const int n = n0 + i;
+            s_scale[i] = n < p.n ? p.scale[n] : 0.0f;
+            s_bias[i] = (p.bias && n < p.n) ? p.bias[n] : 0.0f;
+            s_rowsum[i] = (p.rowsum && n < p.n) ? p.rowsum[n] : 0;
+        }
     }
     __syncwarp();
 
-    // ---- epilogue: wait for the accumulator, then TMEM -> registers -> global.  With tma_y each
-    // warp stages its 32 x 32 fp32 blocks in the pipeline buffers (free once the last MMA has
-    // completed) in the 128-byte swizzled layout and writes each with one TMA store, so the rows
-    // leave the SM as whole lines instead of 32 scattered 16-byte pieces per instruction.
-    // one lane per warp polls (with back-off) so idle threads do not compete with the producer and
-    // MMA threads for the barrier; the decision is warp-uniform (tcgen05.ld is warp-collective)
+    // ---- epilogue.  One lane per warp polls (with back-off) so idle threads do not compete with the
+    // producer and MMA threads; the decision is warp-uniform (tcgen05.ld is warp-collective).
     int waited = 1;
     if (lane == 0) waited = tc::mbar_wait_backoff(done, 0) && !*(volatile int*)abort_flag;
     const bool ok = __shfl_sync(0xffffffffu, waited, 0) != 0;
     tc::fence_after_sync();
     asm volatile("griddepcontrol.wait;" ::: "memory");  // s_x and zp come from the previous kernel
-    if (ok) {
-        const int row = m0 + warp * 32 + lane;
-        const float sx = p.s_x[p.s_stride ? (row < p.m ? row : 0) : 0];
-        const int32_t zp = p.zp ? *p.zp : 0;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+    const bool per_tensor = p.s_stride == 0;
+    const float sx0 = p.s_x[0];
+    const int32_t zp = p.zp ? *p.zp : 0;
+    __syncthreads();  // the factors of warps 2, 3 are in shared memory
+    if (per_tensor) {
+        s_f[threadIdx.x] = __fmul_rn(sx0, s_scale[threadIdx.x]);
+        s_zr[threadIdx.x] = zp * s_rowsum[threadIdx.x];
+    }
+    const int g = warp & 3, h = warp >> 2;         // lane group, column-block half
+    const uint32_t lane_base = tmem + ((uint32_t)(g * 32) << 16);
+    const int trow = g * 32 + lane;                // row of the tile
+    const int row = m0 + trow;
+    if (splits > 1) {
+        // partial sums of the blocks other CTAs own: out slot o (o-th such block), this lane group's
+        // 4 KiB; then one thread copies each slot into its owner's incoming slot for this CTA
+        for (int o = h; o < nout; o += 2) {
+            const int b = o < own0 ? o : o + nown;
             uint32_t r[32];
-            tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + c * 32, r);
+            tc::tmem_ld_32x32b_x32(lane_base + b * 32, r);
             tc::tmem_wait_ld();
+            uint8_t* reg = smem + o * kI8SlotBytes + g * 4096;
 #pragma unroll
-            for (int a_ = 1; a_ < kI8Acc; ++a_) {
-                uint32_t r2[32];
-                tc::tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + a_ * BN + c * 32, r2);
-                tc::tmem_wait_ld();
-#pragma unroll
-                for (int q = 0; q < 32; ++q) r[q] += r2[q];  // int32, exact
+            for (int j = 0; j < 8; ++j)
+                *reinterpret_cast<uint4*>(reg + slot_unit(j, lane)) =
+                    ok ? make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]) : make_uint4(0, 0, 0, 0);
+        }
+        tc::fence_proxy_async_smem();  // generic writes -> the bulk copies' reads
+        tc::cluster_sync();            // every CTA is past its main loop and has written its partials
+        if (threadIdx.x == 0) {
+            for (int o = 0; o < nout; ++o) {
+                const int b = o < own0 ? o : o + nown;
+                const int owner = b / nown, ob = b - owner * nown;
+                const int qi = part < owner ? part : part - 1;  // this CTA's index among the owner's senders
+                uint8_t* dst = smem + (nout + qi * nown + ob) * kI8SlotBytes;  // same offset in the owner
+                tc::bulk_copy_to_peer(tc::cluster_addr(dst, (uint32_t)owner), smem + o * kI8SlotBytes, kI8SlotBytes,
+                                      tc::cluster_addr(recv, (uint32_t)owner));
             }
-            const int nb = n0 + c * 32;
-            if (p.tma_y) {
-                // block (warp, c): 32 rows of 128 bytes; 16-byte unit j of row r sits at j ^ (r % 8)
-                uint8_t* blk = smem + (warp * (BN / 32) + c) * 4096;
-                float v[32];
+        }
+        int got = 1;
+        if (lane == 0) got = tc::mbar_wait_backoff(recv, 0);
+        if (!__shfl_sync(0xffffffffu, got, 0)) waited = 0;
+    } else {
+        __syncthreads();  // s_f / s_zr
+    }
+    const bool ok2 = __shfl_sync(0xffffffffu, waited, 0) != 0 && ok;
+    if (splits > 1) __syncthreads();  // s_f / s_zr (the cluster barrier came before they were written)
+    if (ok2) {
+        const float sx = per_tensor ? sx0 : p.s_x[row < p.m ? row : 0];
+#pragma unroll 1
+        for (int ob = h; ob < nown; ob += 2) {
+            const int b = own0 + ob;
+            uint32_t r[32];
+            tc::tmem_ld_32x32b_x32(lane_base + b * 32, r);
+            tc::tmem_wait_ld();
+            // staging region of this block: its first incoming slot (S > 1), else slot b
+            uint8_t* reg = smem + (splits > 1 ? nout + ob : b) * kI8SlotBytes + g * 4096;
+            for (int qi = 0; qi < splits - 1; ++qi) {  // the other K parts (exact: int32)
+                const uint8_t* in = smem + (nout + qi * nown + ob) * kI8SlotBytes + g * 4096;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int i = c * 32 + j;
-                    const int32_t a = (int32_t)r[j] - zp * s_rowsum[i];
-                    const float f = __fmul_rn(sx, s_scale[i]);
-                    const float af = __int2float_rn(a);
-                    v[j] = p.bias ? __fmaf_rn(af, f, s_bias[i]) : __fmul_rn(af, f);
+                for (int j = 0; j < 8; ++j) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(in + slot_unit(j, lane));
+                    r[4 * j] += v.x; r[4 * j + 1] += v.y; r[4 * j + 2] += v.z; r[4 * j + 3] += v.w;
                 }
+            }
+            float v[32];
+            int32_t a[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int i = b * 32 + j;
+                a[j] = (int32_t)r[j] - (per_tensor ? s_zr[i] : 0);
+                const float f = per_tensor ? s_f[i] : __fmul_rn(sx, s_scale[i]);
+                const float af = __int2float_rn(a[j]);
+                v[j] = p.bias ? __fmaf_rn(af, f, s_bias[i]) : __fmul_rn(af, f);
+            }
+            const int nb = n0 + b * 32;
+            if (p.tma_y) {
+                // the lane group's 32 x 32 fp32 block: 32 rows of 128 bytes, 16-byte unit j of row r at
+                // j ^ (r % 8) (128-byte swizzle); written over this warp's own incoming data, already read
+                __syncwarp();
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
-                    *reinterpret_cast<float4*>(blk + lane * 128 + ((j ^ (lane & 7)) * 16)) =
+                    *reinterpret_cast<float4*>(reg + lane * 128 + ((j ^ (lane & 7)) * 16)) =
                         make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
                 tc::fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0 && m0 + warp * 32 < p.m && nb < p.n) {
-                    tc::tma_store_2d(&tmap_y, blk, nb, m0 + warp * 32);
+                if (lane == 0 && m0 + g * 32 < p.m && nb < p.n) {
+                    tc::tma_store_2d(&tmap_y, reg, nb, m0 + g * 32);
                     tc::bulk_commit_group();
                 }
                 continue;
@@ -506,16 +592,6 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
             if (row >= p.m) continue;
             float* yrow = p.y + (int64_t)row * p.ldy;
             int32_t* arow = p.acc_out ? p.acc_out + (int64_t)row * p.n : nullptr;
-            float v[32];
-            int32_t a[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int i = c * 32 + j;
-                a[j] = (int32_t)r[j] - zp * s_rowsum[i];
-                const float f = __fmul_rn(sx, s_scale[i]);
-                const float af = __int2float_rn(a[j]);
-                v[j] = p.bias ? __fmaf_rn(af, f, s_bias[i]) : __fmul_rn(af, f);
-            }
             if (nb + 32 <= p.n && p.vec_y) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
@@ -534,11 +610,12 @@ __global__ void __launch_bounds__(128, 1) gemm_w8a8_kernel(const __grid_constant
         }
     }
     if (p.tma_y && lane == 0) tc::bulk_wait_all();  // the staged blocks stay in use until read
+    if (splits > 1) tc::cluster_sync();               // every copy out of this CTA has landed
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 2) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, tmem_cols_for(kI8Acc * BN));
+        tc::tmem_dealloc(tmem, BN);
     }
 }
 
@@ -674,10 +751,29 @@ static int make_gemm_maps(CUtensorMap* ma, CUtensorMap* mb, const void* xq, int6
     return SBQ_OK;
 }
 
-#ifndef SBQ_I8_BN
-#define SBQ_I8_BN 128
-#endif
-constexpr int kI8BN = SBQ_I8_BN;  // output channels per CTA (MMA N)
+// SMs of the current device, cached per device (atomics: first calls may come from several threads)
+static int sm_count_dyn() {
+    static std::atomic<int> count[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    int c = count[dev].load(std::memory_order_relaxed);
+    if (c == 0) {
+        cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+        c = c > 0 ? c : 148;
+        count[dev].store(c, std::memory_order_relaxed);
+    }
+    return c;
+}
+
+// K parts per tile: as many (1, 2 or 4) as still fit the tiles on the GPU's SMs once, each part at
+// least one k-block.
+static int i8_splits(int64_t m, int64_t n, int num_kb) {
+    const int64_t tiles = ceil_div(m, kI8BM) * ceil_div(n, kI8BN);
+    const int sms = sm_count_dyn();
+    int s = 1;
+    while (s < kI8MaxSplits && tiles * (2 * s) <= sms && num_kb >= 2 * s) s *= 2;
+    return s;
+}
 
 // dependent: launched as a programmatic dependent of the activation quantisation (sbq_linear_dyn),
 // which lets the pipeline set-up and the first weight tiles overlap that kernel.  Direct calls of
@@ -701,14 +797,25 @@ static int launch_gemm_i8(const void* xq, bool a_signed, const void* packed, con
         rc = encode_tmap(&my, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
-    const dim3 grid((unsigned)ceil_div(p.n, kI8BN), (unsigned)ceil_div(p.m, kI8BM));
-    const int smem = I8Smem<kI8BN>::kBytes;
-    auto kernel = a_signed ? gemm_w8a8_kernel<kI8BN, true> : gemm_w8a8_kernel<kI8BN, false>;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (dependent)
-        launch_dependent(kernel, grid, 128, smem, st, ma, mb, my, q);
-    else
-        kernel<<<grid, 128, smem, st>>>(ma, mb, my, q);
+    q.splits = i8_splits(p.m, p.n, p.num_kb);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)ceil_div(p.n, kI8BN), (unsigned)ceil_div(p.m, kI8BM), (unsigned)q.splits);
+    cfg.blockDim = dim3(kI8Threads);
+    cfg.dynamicSmemBytes = (size_t)I8Smem::kBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;  // the K parts of a tile form one cluster
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = (unsigned)q.splits;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent ? 2 : 1;
+    auto kernel = a_signed ? gemm_w8a8_kernel<true> : gemm_w8a8_kernel<false>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, I8Smem::kBytes);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, my, q);
+    if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "gemm_w8a8 launch: %s", cudaGetErrorString(e));
     return check_launch("gemm_w8a8");
 }
 

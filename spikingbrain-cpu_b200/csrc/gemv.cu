@@ -1089,6 +1089,119 @@ static int dispatch_group(GemvGroup& grp, int xk, int mt, cudaStream_t s) {
 
 SBQ_DEFINE_ERROR_POLL(poll_error_gemv)
 
+// ---------------------------------------------------------------------------------------------
+// Fused rank-r pair of projections y = B(A(x)) (the LoRA pairs lora_q_proj / lora_k_proj of the
+// hybrid block, model.py:287-288: Linear(hidden -> 128) then Linear(128 -> heads * head_dim)), at
+// decode sizes in one launch.  A cluster of 8 CTAs computes t = A(x) once: CTA c owns rows
+// 16 c .. 16 c + 15 of A (its eight warps split the K range; partial sums added in warp order, the
+// fp32 per-row scale applied after the dot product as in Int8Linear), and every CTA then gathers all
+// of t [m, r] from the cluster's shared memory (distributed shared memory) - t never leaves the SMs.
+// Each cluster then streams its share of B's 16-row tiles, one tile per warp, with t as an fp32
+// activation (split into bf16 high + low parts, as the GEMV does for fp32 x).  Several clusters
+// cover B; each recomputes t (A is small: r x hidden bytes, from L2).
+constexpr int kLoraCluster = 8;
+constexpr int kLoraMaxR = 16 * kLoraCluster;  // 128
+constexpr int kLoraThreads = 256;
+constexpr int kLoraTPad = kLoraMaxR + 4;      // row stride of the gathered t (floats; 16-byte rows)
+
+struct LoraParams {
+    const void* x;
+    int64_t ldx;
+    int m, k, kt;          // kt = ceil(k / 64)
+    const int8_t* wa;      // packed [r, k]
+    const float* sa;
+    int r, kt_b;           // kt_b = ceil(r / 64)
+    const int8_t* wb;      // packed [n, r]
+    const float* sb;
+    int n, n_tiles, tiles_per_cta;
+    void* y;
+    int64_t ldy;
+    int out_f16;
+};
+
+template <int XK, int MT>
+__global__ void __launch_bounds__(kLoraThreads, 1) lora_pair_kernel(const LoraParams p) {
+    __shared__ float red[kGemvWarps][MT * 8][17];                       // per-warp partials [token][row]
+    __shared__ __align__(16) float t_loc[MT * 8][16];                   // this CTA's 16 columns of t
+    __shared__ __align__(16) float t_full[MT * 8][kLoraTPad];           // t [token][0, r)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    const int rank = (int)tc::cluster_ctarank();
+
+    // ---- stage 1: rows 16 rank .. of A, the K tiles split over the warps
+    float acc[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[mt][e] = 0.0f;
+    if (16 * rank < p.r) {
+        for (int kt = warp; kt < p.kt; kt += kGemvWarps) {
+            const int8_t* t = p.wa + ((int64_t)rank * p.kt + kt) * kTileBytes + lane * 16;
+            const uint4 wa = ld_stream(t), wb = ld_stream(t + 512);
+            XFrag<XK> xf[MT];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) load_x<XK>(xf[mt], p.x, p.ldx, 8 * mt + g, p.m, (int64_t)kt * kTileCols + 16 * c, p.k);
+            tile_mma<XK, MT>(acc, wa, wb, xf);
+        }
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+        red[warp][8 * mt + 2 * c][g] = acc[mt][0];
+        red[warp][8 * mt + 2 * c + 1][g] = acc[mt][1];
+        red[warp][8 * mt + 2 * c][g + 8] = acc[mt][2];
+        red[warp][8 * mt + 2 * c + 1][g + 8] = acc[mt][3];
+    }
+    __syncthreads();
+    if (threadIdx.x < MT * 8 * 16) {
+        const int rr = threadIdx.x & 15, tok = threadIdx.x >> 4, ch = 16 * rank + rr;
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; ++w) v += red[w][tok][rr];
+        t_loc[tok][rr] = ch < p.r ? __fmul_rn(v, p.sa[ch]) : 0.0f;
+    }
+    tc::cluster_sync();  // every CTA's 16 columns of t are written
+    for (int e = threadIdx.x; e < MT * 8 * (kLoraMaxR / 4); e += kLoraThreads) {
+        const int tok = e / (kLoraMaxR / 4), q = e % (kLoraMaxR / 4);  // q: 4-column group
+        const int src = q / 4, col = (q % 4) * 4;
+        const uint4 v = tc::ld_cluster_v4(tc::cluster_addr(&t_loc[tok][col], (uint32_t)src));
+        *reinterpret_cast<uint4*>(&t_full[tok][src * 16 + col]) = v;
+    }
+    tc::cluster_sync();  // t gathered everywhere (and no CTA leaves while another reads its t_loc)
+
+    // ---- stage 2: this CTA's 16-row tiles of B, one per warp, t as an fp32 activation
+    for (int ti = warp; ti < p.tiles_per_cta; ti += kGemvWarps) {
+        const int tile = blockIdx.x * p.tiles_per_cta + ti;
+        if (tile >= p.n_tiles) break;
+        float acc2[MT][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc2[mt][e] = 0.0f;
+        for (int kt = 0; kt < p.kt_b; ++kt) {
+            const int8_t* t = p.wb + ((int64_t)tile * p.kt_b + kt) * kTileBytes + lane * 16;
+            const uint4 wa = ld_stream(t), wb = ld_stream(t + 512);
+            XFrag<kXF32> xf[MT];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+                load_x<kXF32>(xf[mt], &t_full[0][0], kLoraTPad, 8 * mt + g, p.m, (int64_t)kt * kTileCols + 16 * c, p.r);
+            tile_mma<kXF32, MT>(acc2, wa, wb, xf);
+        }
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int rrow = g + (e >> 1) * 8, tok = 8 * mt + 2 * c + (e & 1);
+                const int nn = tile * 16 + rrow;
+                if (nn >= p.n || tok >= p.m) continue;
+                const float v = __fmul_rn(acc2[mt][e], p.sb[nn]);
+                if (p.out_f16)
+                    static_cast<__half*>(p.y)[(int64_t)tok * p.ldy + nn] = __float2half_rn(v);
+                else
+                    static_cast<float*>(p.y)[(int64_t)tok * p.ldy + nn] = v;
+            }
+    }
+}
+
 static int x_kind(int dtype) {
     switch (dtype) {
         case SBQ_F16: return kXF16;
@@ -1243,6 +1356,66 @@ extern "C" int sbq_mlp_gateup_w8_ws(const void* x, int x_dtype, int64_t ldx, con
     }
     return sbq_mlp_gateup_w8(x, x_dtype, ldx, packed_gate, scale_gate, packed_up, scale_up, m, n, k, h, h_dtype, ldh,
                              stream);
+}
+
+template <int XK, int MT>
+static cudaError_t launch_lora(const LoraParams& lp, int clusters, cudaStream_t s) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)(kLoraCluster * clusters));
+    cfg.blockDim = dim3(kLoraThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kLoraCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, lora_pair_kernel<XK, MT>, lp);
+}
+
+extern "C" int sbq_lora_pair_w8(const void* x, int x_dtype, int64_t ldx, const void* packed_a, const float* scale_a,
+                                const void* packed_b, const float* scale_b, int64_t m, int64_t r, int64_t n, int64_t k,
+                                void* y, int y_dtype, int64_t ldy, void* stream) {
+    int st = check_linear_args(x, x_dtype, ldx, packed_a, scale_a, m, r, k, y, y_dtype, ldy);
+    if (st) return st;
+    if (!packed_b || !scale_b) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null second-stage pointer");
+    if (reinterpret_cast<uintptr_t>(packed_b) % 256) return set_error(SBQ_ERR_ALIGNMENT, "packed weight must be 256-byte aligned");
+    if (m > 16) return set_error(SBQ_ERR_UNSUPPORTED, "the fused pair takes 1..16 rows of x (m=%lld)", (long long)m);
+    if (r % 16 || r > kLoraMaxR)
+        return set_error(SBQ_ERR_UNSUPPORTED, "the pair's inner size must be a multiple of 16 up to %d (r=%lld)", kLoraMaxR,
+                         (long long)r);
+    if (n <= 0 || n >= (int64_t(1) << 31) || ldy < n) return set_error(SBQ_ERR_INVALID_ARGUMENT, "bad output size or stride");
+    LoraParams lp{};
+    lp.x = x;
+    lp.ldx = ldx;
+    lp.m = (int)m;
+    lp.k = (int)k;
+    lp.kt = (int)ceil_div(k, kTileCols);
+    lp.wa = static_cast<const int8_t*>(packed_a);
+    lp.sa = scale_a;
+    lp.r = (int)r;
+    lp.kt_b = (int)ceil_div(r, kTileCols);
+    lp.wb = static_cast<const int8_t*>(packed_b);
+    lp.sb = scale_b;
+    lp.n = (int)n;
+    lp.n_tiles = (int)ceil_div(n, 16);
+    // one B tile per warp: 64 tiles per cluster of 8 CTAs
+    const int clusters = (int)ceil_div(lp.n_tiles, kLoraCluster * kGemvWarps);
+    lp.tiles_per_cta = (int)ceil_div(lp.n_tiles, kLoraCluster * clusters);
+    lp.y = y;
+    lp.ldy = ldy;
+    lp.out_f16 = y_dtype == SBQ_F16;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool two = m > 8;
+    cudaError_t e;
+    switch (x_kind(x_dtype)) {
+        case kXF16: e = two ? launch_lora<kXF16, 2>(lp, clusters, s) : launch_lora<kXF16, 1>(lp, clusters, s); break;
+        case kXBF16: e = two ? launch_lora<kXBF16, 2>(lp, clusters, s) : launch_lora<kXBF16, 1>(lp, clusters, s); break;
+        default: e = two ? launch_lora<kXF32, 2>(lp, clusters, s) : launch_lora<kXF32, 1>(lp, clusters, s); break;
+    }
+    if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "lora pair launch: %s", cudaGetErrorString(e));
+    return check_launch("lora_pair_w8");
 }
 
 extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m, void* stream) {

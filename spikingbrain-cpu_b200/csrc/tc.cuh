@@ -235,6 +235,45 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// ---- thread-block clusters ----------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Shared-memory address of this CTA's `p` as seen in cluster CTA `rank` (a shared::cluster address).
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+
+// Every thread of every CTA of the cluster; orders shared-memory writes before the other CTAs' reads.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 16 bytes from another CTA's shared memory (distributed shared memory).
+__device__ __forceinline__ uint4 ld_cluster_v4(uint32_t cluster_address) {
+    uint4 v;
+    asm volatile("ld.shared::cluster.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(cluster_address)
+                 : "memory");
+    return v;
+}
+
+// Bulk copy of `bytes` from this CTA's shared memory to another cluster CTA's (shared::cluster
+// address dst), completing on that CTA's mbarrier (shared::cluster address bar).  16-byte aligned
+// addresses, size a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst),
+                 "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 // ---- descriptors ------------------------------------------------------------------------------
 enum SmemLayout : uint32_t { kSwizzleNone = 0, kSwizzle128B = 2, kSwizzle64B = 4, kSwizzle32B = 6 };
 

@@ -91,3 +91,70 @@ def fuse_gated_mlp(model: nn.Module, h_dtype: torch.dtype = torch.float16) -> in
             setattr(parent, child, fused)
             count += 1
     return count
+
+
+class FusedLoRAPair(nn.Module):
+    """The hybrid block's rank-128 pair (model.py:287-288): ``nn.Sequential(Linear(hidden, 128),
+    Linear(128, heads * head_dim))`` with both stages in the int8 format, as one module.
+
+    Up to 16 rows of x run as one launch (sbq_lora_pair_w8: the rank-r intermediate stays on the SMs
+    in fp32); more rows run the two projections one after the other (the intermediate in fp32, as
+    the reference's Sequential passes it).  Returns fp32 like the reference (``out_dtype`` may be set
+    to float16).
+    """
+
+    MAX_FUSED_ROWS = 16
+    MAX_RANK = 128
+
+    def __init__(self, first: Int8Linear, second: Int8Linear):
+        super().__init__()
+        if not isinstance(first, Int8Linear) or not isinstance(second, Int8Linear):
+            raise ValueError("FusedLoRAPair needs two int8 projections")
+        if second.in_features != first.out_features:
+            raise ValueError("the second projection must read the first one's output")
+        if first.bias is not None or second.bias is not None:
+            raise ValueError("the fused pair has no bias terms")
+        if first.out_features % 16 or first.out_features > self.MAX_RANK:
+            raise ValueError("the pair's inner size must be a multiple of 16 up to %d" % self.MAX_RANK)
+        self.first, self.second = first, second
+        self.in_features, self.out_features = first.in_features, second.out_features
+        self.out_dtype = torch.float32
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        dev = self.first.scale.device
+        x2, k16, on_host = _prepare_x(x, self.in_features, dev)
+        m = x2.shape[0]
+        if m > self.MAX_FUSED_ROWS:
+            t = self.first.forward_into(x2, torch.empty(m, self.first.out_features, device=dev))
+            y = self.second.forward_into(t, torch.empty(m, self.out_features, dtype=self.out_dtype, device=dev))
+        else:
+            y = torch.empty(m, self.out_features, dtype=self.out_dtype, device=dev)
+            if m > 0:
+                L.call("sbq_lora_pair_w8", _ptr(x2), _DTYPE_CODE[x2.dtype], x2.stride(0), _ptr(self.first.packed),
+                       _ptr(self.first.scale), _ptr(self.second.packed), _ptr(self.second.scale), m,
+                       self.first.out_features, self.out_features, x2.shape[1], _ptr(y),
+                       L.F32 if y.dtype == torch.float32 else L.F16, y.stride(0), _stream(dev))
+        y = y.reshape(*shape[:-1], self.out_features)
+        return y.to("cpu") if on_host else y
+
+
+def fuse_lora_pairs(model: nn.Module) -> int:
+    """Replace every ``nn.Sequential`` of two int8 projections whose inner size fits the fused kernel
+    (the LoRA pairs) by a FusedLoRAPair; returns how many were replaced."""
+    count = 0
+    for name, mod in list(model.named_modules()):
+        if not (isinstance(mod, nn.Sequential) and len(mod) == 2):
+            continue
+        a, b = mod[0], mod[1]
+        if not (isinstance(a, Int8Linear) and isinstance(b, Int8Linear)) or a.bias is not None or b.bias is not None:
+            continue
+        if b.in_features != a.out_features or a.out_features % 16 or a.out_features > FusedLoRAPair.MAX_RANK:
+            continue
+        parent_name, _, child = name.rpartition(".")
+        if not name:
+            raise ValueError("cannot replace the root module in place")
+        parent = model.get_submodule(parent_name) if parent_name else model
+        setattr(parent, child, FusedLoRAPair(a, b))
+        count += 1
+    return count
