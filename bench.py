@@ -4,18 +4,22 @@
 Workload: the synthetic 36-layer projection stack, hidden 4096,
 intermediate 12288, int8 weight-only, seeded N(0, 0.02) weights quantised by the reference's
 per-channel recipe.  One step = one decode step at batch 1 through all 36 layers (every weight of
-the stack streamed once, 9.06 GB).  With N GPUs the projections are output-channel sharded and
-NCCL all-gathers assemble each activation (strong scaling: the total work is fixed).
+the stack streamed once, 9.06 GB).  With N GPUs the projections are output-channel sharded; by
+default each grouped GEMV stores its output slice into every rank's buffer over NVLink and signals
+per-launch arrival counters (peer exchange), --exchange nccl uses NCCL all-gathers instead
+(strong scaling: the total work is fixed).
 
 value      weight GB/s of the whole job (stack bytes / max-over-ranks step time), inputs resident,
            one CUDA graph replay per step, CUDA events on the launching stream.
 e2e        the same metric through the public API with host buffers: pinned input copied in, the
-           captured stack run, the output copied back, every step.
-roofline   the fused gate/up GEMV (the largest kernel of a step), timed alone over the 36 layers'
-           distinct weights, against the measured HBM copy bandwidth.
+           captured stack run, the output copied back, every step; beside it (module_api) the same
+           step through the drop-in's module calls on host and on device tensors.
+roofline   the grouped decode GEMV, which is every launch of the timed step: bytes per launch over
+           the average launch time, against the measured HBM copy bandwidth; the fused gate/up
+           launch timed alone is reported beside it.
 cpu_baseline / --impl reference
            the reference's CPU algorithm (oracle/cpu_port.py) on a bounded sample of the same
-           workload on this host's cores.
+           workload on this host's cores (and at the reference's own 4-thread setting).
 
 Flags: --gpus N --steps K --warmup W [--impl reference] [--layers L] [--extra].
 """
@@ -583,9 +587,14 @@ def main() -> None:
         from oracle import cpu_port
 
         r = cpu_port.time_stack_decode(layers=2, warmup=1, max_steps=400, min_seconds=8.0, max_seconds=30.0)
+        r4 = cpu_port.time_stack_decode(layers=2, warmup=1, max_steps=200, min_seconds=4.0, max_seconds=10.0,
+                                        threads=cpu_port.REFERENCE_THREADS)
         cpu = {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": r["cores"], "kind": "port",
                "sample": "reference int8 algorithm (blocked fp32 dequant + sgemm) on 2 of 36 stack layers, "
-                         "batch 1, %d steps" % r["steps"]}
+                         "batch 1, %d steps" % r["steps"],
+               "reference_threads_setting": {"value": round(r4["gbs"], 3), "unit": "GB/s", "cores": r4["cores"],
+                                             "note": "SB_THREADS=4, the reference's default thread count",
+                                             "steps": r4["steps"]}}
 
     launches = stack.launches_per_step(1, program=runner.program is not None)
     per_gpu = value / world  # each rank streams 1/world of the weights per step

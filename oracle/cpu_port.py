@@ -27,6 +27,10 @@ def use_all_cores() -> int:
     return torch.get_num_threads()
 
 
+# The reference's own thread setting (SB_THREADS, default 4: spikingbrain_cpu/bench.py:231).
+REFERENCE_THREADS = 4
+
+
 def int8_forward(x: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, block: int = 128) -> torch.Tensor:
     """fp32 x [m, k] times int8 q [n, k] dequantised block by block, then scaled (quant.py:46-53)."""
     x2 = x.reshape(-1, q.shape[1]).float()
@@ -78,13 +82,19 @@ class StackSample:
 
 
 def time_stack_decode(layers: int = 2, m: int = 1, warmup: int = 1, max_steps: int = 1000,
-                      min_seconds: float = 0.0, max_seconds: float = 120.0) -> dict:
+                      min_seconds: float = 0.0, max_seconds: float = 120.0, threads: int | None = None) -> dict:
     """Weight GB/s of the reference algorithm on ``layers`` stack layers.
 
     Runs ``warmup`` untimed steps, then timed steps until ``max_steps`` are done or ``max_seconds``
-    have passed (and at least ``min_seconds``, if ``max_steps`` allows).
+    have passed (and at least ``min_seconds``, if ``max_steps`` allows).  ``threads``: torch's
+    intra-op threads (default: every core of the host).
     """
-    cores = use_all_cores()
+    before = torch.get_num_threads()
+    if threads is None:
+        cores = use_all_cores()
+    else:
+        torch.set_num_threads(threads)
+        cores = torch.get_num_threads()
     sample = StackSample(layers)
     x = torch.randn(m, sample.hidden).half()
     for _ in range(max(0, warmup)):
@@ -97,5 +107,6 @@ def time_stack_decode(layers: int = 2, m: int = 1, warmup: int = 1, max_steps: i
         if el >= max_seconds or (min_seconds and el >= min_seconds):
             break
     dt = (time.perf_counter() - t0) / steps
+    torch.set_num_threads(before)
     return {"gbs": sample.weight_bytes() / dt / 1e9, "s_per_step": dt, "steps": steps, "cores": cores,
             "layers": layers, "m": m, "bytes": sample.weight_bytes()}

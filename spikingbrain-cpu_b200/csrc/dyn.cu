@@ -320,17 +320,18 @@ __global__ void __launch_bounds__(kTokThreads) quantize_per_token_kernel(const T
 // memory.  The N = 256 shape matters: a per-k-block trace showed the issuing thread held about as
 // long per MMA at N = 128 as at N = 256, so the wide instruction does twice the work per issue
 // (~80 % of the int8 tensor peak in the loop).  When those tiles are too few for the GPU, the K range
-// of a tile is split over a cluster of 2 or 4 CTAs (one K part each).  After the main loop each CTA
-// owns 256/S of the tile's columns: it writes its partial sums of the other columns to shared
-// memory, bulk-copies them (the copy engine, cp.async.bulk shared::cta -> shared::cluster) into the
-// owning CTA, and adds the partials it receives to its own columns - int32, so the sum is exact and
-// independent of order.  Epilogue (8 warps; warps w and w + 4 share tensor-memory lanes and split
-// the column blocks): acc - zp * rowsum[n], float(acc) * (s * scale[n]) (fma with a bias), staged in
-// the freed ring and written with TMA stores.
+// of a tile is split over a cluster of 2 CTAs (one K half each).  After the main loop each CTA owns
+// half of the tile's columns: it stores its int32 partial sums of the other half into y itself (the
+// cells the owner then overwrites with the finished values - no workspace), one cluster barrier
+// orders those stores before the owner's loads, and the owner adds them to its own accumulators -
+// int32, so the sum is exact and independent of order.  (Moving the partials through distributed
+// shared memory measured about 30 GB/s per SM here, slower than L2.)  Epilogue (8 warps; warps w and
+// w + 4 share tensor-memory lanes and split the column blocks): acc - zp * rowsum[n],
+// float(acc) * (s * scale[n]) (fma with a bias), staged in the freed ring and written with TMA stores.
 
 struct GemmI8Params {
     int m, n, k, num_kb;
-    int splits;             // K parts of a tile (CTAs of one cluster): 1, 2 or 4
+    int splits;             // K parts of a tile (CTAs of one cluster): 1 or 2
     const int32_t* rowsum;  // per-tensor zero-point correction (may be null in per-token mode)
     const float* s_x;       // one scale (per-tensor) or one per row (per-token)
     int s_stride;           // 0 or 1
@@ -353,7 +354,7 @@ constexpr int kI8BK = 128;         // k per pipeline stage (bytes of an int8 row
 #endif
 constexpr int kI8Stages = SBQ_I8_STAGES;
 constexpr int kI8Threads = 256;                // 8 warps
-constexpr int kI8MaxSplits = 4;
+constexpr int kI8MaxSplits = 2;
 constexpr int kI8Blocks = kI8BN / 32;          // 32-column blocks of a tile
 constexpr int kI8SlotBytes = kI8BM * 32 * 4;   // one block: 128 rows x 32 int32 = 16 KiB
 
@@ -362,18 +363,12 @@ struct I8Smem {
     static constexpr int kB = kI8BN * kI8BK;  // 32 KiB: two 64-wide halves of 256 rows
     static constexpr int kStage = kA + kB;
     static constexpr int kRing = kI8Stages * kStage;
-    // after the main loop the ring holds 16 KiB slots: the outgoing partials (blocks other CTAs own),
-    // the incoming ones (blocks this CTA owns, one slot per sender) and the TMA-store staging
-    static constexpr int kSlots = kRing / kI8SlotBytes;
+    // after the main loop the ring holds the TMA-store staging, one 16 KiB slot per column block
     static constexpr int kTail = 256 /* barriers */ + kI8BN * 5 * 4;  // scale, bias, rowsum, s*scale, zp*rowsum
     static constexpr int kBytes = kRing + 1024 /* alignment */ + kTail;
-    static_assert(kSlots >= kI8Blocks, "every split uses at most 8 slots (S = 1, 2) or 12 (S = 4)");
+    static_assert(kI8Blocks * kI8SlotBytes <= kRing, "staging slots fit in the ring");
     static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
 };
-
-// 16-byte unit j (of 8) of row `lane` of a 32-row block in a slot region: [j][lane], so that a warp's
-// accesses to one unit are 512 contiguous bytes.
-__device__ __forceinline__ uint32_t slot_unit(int j, int lane) { return (uint32_t)((j * 32 + lane) * 16); }
 
 // Warp 0: TMA producer.  Warp 1: MMA issuer.  Warp 2: TMEM allocation.  Warps 2, 3: per-channel
 // epilogue factors.  All eight warps: epilogue (warp w reads accumulator lanes 32 (w % 4) ..).
@@ -389,8 +384,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kRing);
     uint64_t* empty = full + kI8Stages;
     uint64_t* done = empty + kI8Stages;
-    uint64_t* recv = done + 1;  // incoming partials of the other K parts
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv + 1);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     float* s_scale = reinterpret_cast<float*>(smem + S::kRing + 256);
     float* s_bias = s_scale + BN;
@@ -404,7 +398,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
     const int part = splits > 1 ? (int)tc::cluster_ctarank() : 0;
     const int kb0 = part * p.num_kb / splits, nkb = (part + 1) * p.num_kb / splits - kb0;  // >= 1 (host)
     const int nown = kI8Blocks / splits, own0 = part * nown;  // this CTA's column blocks
-    const int nout = kI8Blocks - nown;                        // blocks it sends to their owners
+    const int nout = kI8Blocks - nown;                        // blocks whose partials go to the other CTA
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kI8Stages; ++s) {
@@ -412,12 +406,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
             tc::mbar_init(&empty[s], 1);
         }
         tc::mbar_init(done, 1);
-        tc::mbar_init(recv, 1);
         *abort_flag = 0;
         tc::fence_mbar_init();
-        // armed before any other CTA can send (they send after the cluster barrier that follows
-        // every CTA's main loop)
-        if (splits > 1) tc::mbar_arrive_expect_tx(recv, (uint32_t)((splits - 1) * nown * kI8SlotBytes));
         tc::prefetch_tmap(&tmap_a);
         tc::prefetch_tmap(&tmap_b);
         if (p.tma_y) tc::prefetch_tmap(&tmap_y);
@@ -511,72 +501,84 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
     const int trow = g * 32 + lane;                // row of the tile
     const int row = m0 + trow;
     if (splits > 1) {
-        // partial sums of the blocks other CTAs own: out slot o (o-th such block), this lane group's
-        // 4 KiB; then one thread copies each slot into its owner's incoming slot for this CTA
+        // the other CTA's K part of the blocks it owns goes into y itself (the cells the owner
+        // overwrites with the finished values), as int32; then one cluster barrier
         for (int o = h; o < nout; o += 2) {
             const int b = o < own0 ? o : o + nown;
             uint32_t r[32];
             tc::tmem_ld_32x32b_x32(lane_base + b * 32, r);
             tc::tmem_wait_ld();
-            uint8_t* reg = smem + o * kI8SlotBytes + g * 4096;
+            const int nb = n0 + b * 32;
+            if (!ok || row >= p.m) continue;
+            int32_t* dst = reinterpret_cast<int32_t*>(p.y + (int64_t)row * p.ldy + nb);
+            if (nb + 32 <= p.n && p.vec_y) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                *reinterpret_cast<uint4*>(reg + slot_unit(j, lane)) =
-                    ok ? make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]) : make_uint4(0, 0, 0, 0);
-        }
-        tc::fence_proxy_async_smem();  // generic writes -> the bulk copies' reads
-        tc::cluster_sync();            // every CTA is past its main loop and has written its partials
-        if (threadIdx.x == 0) {
-            for (int o = 0; o < nout; ++o) {
-                const int b = o < own0 ? o : o + nown;
-                const int owner = b / nown, ob = b - owner * nown;
-                const int qi = part < owner ? part : part - 1;  // this CTA's index among the owner's senders
-                uint8_t* dst = smem + (nout + qi * nown + ob) * kI8SlotBytes;  // same offset in the owner
-                tc::bulk_copy_to_peer(tc::cluster_addr(dst, (uint32_t)owner), smem + o * kI8SlotBytes, kI8SlotBytes,
-                                      tc::cluster_addr(recv, (uint32_t)owner));
+                for (int j = 0; j < 8; ++j)
+                    __stcg(reinterpret_cast<int4*>(dst) + j, make_int4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (nb + j < p.n) __stcg(dst + j, (int32_t)r[j]);
             }
         }
-        int got = 1;
-        if (lane == 0) got = tc::mbar_wait_backoff(recv, 0);
-        if (!__shfl_sync(0xffffffffu, got, 0)) waited = 0;
+        tc::cluster_sync();  // release / acquire at cluster scope: the partials are visible to the owners
     } else {
         __syncthreads();  // s_f / s_zr
     }
-    const bool ok2 = __shfl_sync(0xffffffffu, waited, 0) != 0 && ok;
-    if (splits > 1) __syncthreads();  // s_f / s_zr (the cluster barrier came before they were written)
-    if (ok2) {
+    if (splits > 1) __syncthreads();  // s_f / s_zr
+    if (ok) {
         const float sx = per_tensor ? sx0 : p.s_x[row < p.m ? row : 0];
+        // the finished values replace the partials in y through TMA stores (async proxy) after this
+        // thread's ordinary loads and the other CTA's ordinary stores of the same cells
+        if (splits > 1) asm volatile("fence.proxy.async.global;" ::: "memory");
 #pragma unroll 1
         for (int ob = h; ob < nown; ob += 2) {
             const int b = own0 + ob;
+            const int nb = n0 + b * 32;
             uint32_t r[32];
             tc::tmem_ld_32x32b_x32(lane_base + b * 32, r);
             tc::tmem_wait_ld();
-            // staging region of this block: its first incoming slot (S > 1), else slot b
-            uint8_t* reg = smem + (splits > 1 ? nout + ob : b) * kI8SlotBytes + g * 4096;
-            for (int qi = 0; qi < splits - 1; ++qi) {  // the other K parts (exact: int32)
-                const uint8_t* in = smem + (nout + qi * nown + ob) * kI8SlotBytes + g * 4096;
+            if (splits > 1 && row < p.m) {  // the other K part (exact: int32)
+                const int32_t* src = reinterpret_cast<const int32_t*>(p.y + (int64_t)row * p.ldy + nb);
+                if (nb + 32 <= p.n && p.vec_y) {
+                    int4 q[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(in + slot_unit(j, lane));
-                    r[4 * j] += v.x; r[4 * j + 1] += v.y; r[4 * j + 2] += v.z; r[4 * j + 3] += v.w;
+                    for (int j = 0; j < 8; ++j) q[j] = __ldcg(reinterpret_cast<const int4*>(src) + j);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        r[4 * j] += q[j].x; r[4 * j + 1] += q[j].y; r[4 * j + 2] += q[j].z; r[4 * j + 3] += q[j].w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (nb + j < p.n) r[j] += (uint32_t)__ldcg(src + j);
                 }
+                if (p.tma_y) asm volatile("fence.proxy.async.global;" ::: "memory");
             }
             float v[32];
             int32_t a[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int i = b * 32 + j;
-                a[j] = (int32_t)r[j] - (per_tensor ? s_zr[i] : 0);
-                const float f = per_tensor ? s_f[i] : __fmul_rn(sx, s_scale[i]);
-                const float af = __int2float_rn(a[j]);
-                v[j] = p.bias ? __fmaf_rn(af, f, s_bias[i]) : __fmul_rn(af, f);
+            for (int j4 = 0; j4 < 8; ++j4) {
+                const int i = b * 32 + 4 * j4;
+                const float4 f4 = per_tensor ? *reinterpret_cast<const float4*>(s_f + i)
+                                             : make_float4(__fmul_rn(sx, s_scale[i]), __fmul_rn(sx, s_scale[i + 1]),
+                                                           __fmul_rn(sx, s_scale[i + 2]), __fmul_rn(sx, s_scale[i + 3]));
+                const int4 z4 = per_tensor ? *reinterpret_cast<const int4*>(s_zr + i) : make_int4(0, 0, 0, 0);
+                const float4 b4 = *reinterpret_cast<const float4*>(s_bias + i);
+                const float fs[4] = {f4.x, f4.y, f4.z, f4.w}, bs[4] = {b4.x, b4.y, b4.z, b4.w};
+                const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int jj = 4 * j4 + e;
+                    a[jj] = (int32_t)r[jj] - zs[e];
+                    const float af = __int2float_rn(a[jj]);
+                    v[jj] = p.bias ? __fmaf_rn(af, fs[e], bs[e]) : __fmul_rn(af, fs[e]);
+                }
             }
-            const int nb = n0 + b * 32;
             if (p.tma_y) {
                 // the lane group's 32 x 32 fp32 block: 32 rows of 128 bytes, 16-byte unit j of row r at
-                // j ^ (r % 8) (128-byte swizzle); written over this warp's own incoming data, already read
-                __syncwarp();
+                // j ^ (r % 8) (128-byte swizzle), staged in slot b of the freed ring
+                uint8_t* reg = smem + b * kI8SlotBytes + g * 4096;
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
                     *reinterpret_cast<float4*>(reg + lane * 128 + ((j ^ (lane & 7)) * 16)) =
@@ -610,7 +612,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
         }
     }
     if (p.tma_y && lane == 0) tc::bulk_wait_all();  // the staged blocks stay in use until read
-    if (splits > 1) tc::cluster_sync();               // every copy out of this CTA has landed
+    if (splits > 1) tc::cluster_sync();               // no CTA leaves while the other may read its cells
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 2) {
@@ -765,8 +767,8 @@ static int sm_count_dyn() {
     return c;
 }
 
-// K parts per tile: as many (1, 2 or 4) as still fit the tiles on the GPU's SMs once, each part at
-// least one k-block.
+// K parts per tile: 2 when twice the tiles still fit on the GPU's SMs once (each part at least one
+// k-block), else 1.
 static int i8_splits(int64_t m, int64_t n, int num_kb) {
     const int64_t tiles = ceil_div(m, kI8BM) * ceil_div(n, kI8BN);
     const int sms = sm_count_dyn();

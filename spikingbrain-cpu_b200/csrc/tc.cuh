@@ -264,16 +264,6 @@ __device__ __forceinline__ uint4 ld_cluster_v4(uint32_t cluster_address) {
     return v;
 }
 
-// Bulk copy of `bytes` from this CTA's shared memory to another cluster CTA's (shared::cluster
-// address dst), completing on that CTA's mbarrier (shared::cluster address bar).  16-byte aligned
-// addresses, size a multiple of 16.  No multicast.
-__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     dst),
-                 "r"(smem_u32(src)), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-
 // ---- descriptors ------------------------------------------------------------------------------
 enum SmemLayout : uint32_t { kSwizzleNone = 0, kSwizzle128B = 2, kSwizzle64B = 4, kSwizzle32B = 6 };
 
