@@ -392,6 +392,40 @@ def stack_cases(sbq, stack, dev, stream, warmup: int) -> dict:
     return out
 
 
+def sharded_prefill_case(sbq, stack, dev, stream, world: int) -> dict:
+    """Configuration 4's prefill (8192 tokens, 36 layers) on the output-channel sharded stack: every
+    rank runs its shard of each projection's GEMM and NCCL all-gathers assemble the activations.
+    CUDA events on the launching stream, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    m = 8192
+    x = sbq.workloads.activation(m, stack.hidden, seed=m, device=dev)
+    with torch.cuda.stream(stream):
+        stack(x)  # warm-up (allocator, communicators)
+    stream.synchronize()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 2
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(reps):
+            stack(x)
+        end.record(stream)
+    end.synchronize()
+    t = torch.tensor([start.elapsed_time(end) / reps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    fl = 2.0 * m * sbq.workloads.stack_bytes(len(stack.layers))
+    pk = peaks()
+    gathered = 2 * m * (4 * stack.hidden + stack.inter + 2 * stack.hidden + stack.hidden) * len(stack.layers)
+    return {"ms": round(ms, 2), "tflops": round(fl / ms / 1e9, 1),
+            "frac_bf16_sustained_per_gpu": round(fl / ms / 1e9 / world / pk["bf16_tflops_sustained"], 4),
+            "allgather_bytes_per_step": gathered,
+            "note": "per-projection GEMMs on each rank's output-channel shard; NCCL all_gather_into_tensor "
+                    "after each sharded projection (4 per layer)"}
+
+
 def module_api_cases(sbq, stack, dev, steps: int, warmup: int) -> dict:
     """The decode step (batch 1) through the drop-in's public module calls, eager (no CUDA graph):
     with host tensors (every projection copies its input in and its output back and waits, the
@@ -581,6 +615,8 @@ def main() -> None:
         extra["cfg4_stack"] = stack_cases(sbq, stack, dev, stream, args.warmup)
         module_api = module_api_cases(sbq, stack, dev, steps=max(5, min(20, args.steps)), warmup=2)
         extra["load_pack"] = load_pack_case(sbq, dev)
+    elif world > 1 and not args.no_extra:
+        extra = {"cfg4_prefill_8192_sharded": sharded_prefill_case(sbq, stack, dev, stream, world)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -314,24 +314,22 @@ __global__ void __launch_bounds__(kTokThreads) quantize_per_token_kernel(const T
 
 // ============================================================================ int8 GEMM ======
 //
-// One CTA computes a 128 (xq rows) x 256 (weight rows) output tile: 4-stage TMA ring (xq 128 x 128 B
-// with 128-byte swizzle, weight two 256 x 64 B halves with 64-byte swizzle), one thread issues
-// tcgen05.mma.cta_group::1.kind::i8 (M = 128, N = 256, K = 32) into int32 accumulators in tensor
-// memory.  The N = 256 shape matters: a per-k-block trace showed the issuing thread held about as
-// long per MMA at N = 128 as at N = 256, so the wide instruction does twice the work per issue
-// (~80 % of the int8 tensor peak in the loop).  When those tiles are too few for the GPU, the K range
-// of a tile is split over a cluster of 2 CTAs (one K half each).  After the main loop each CTA owns
-// half of the tile's columns: it stores its int32 partial sums of the other half into y itself (the
-// cells the owner then overwrites with the finished values - no workspace), one cluster barrier
-// orders those stores before the owner's loads, and the owner adds them to its own accumulators -
-// int32, so the sum is exact and independent of order.  (Moving the partials through distributed
-// shared memory measured about 30 GB/s per SM here, slower than L2.)  Epilogue (8 warps; warps w and
-// w + 4 share tensor-memory lanes and split the column blocks): acc - zp * rowsum[n],
-// float(acc) * (s * scale[n]) (fma with a bias), staged in the freed ring and written with TMA stores.
+// One CTA computes a 128 (xq rows) x BN (weight rows) output tile, BN = 256 or 128: 4-stage TMA ring
+// (xq 128 x 128 B with 128-byte swizzle, weight two BN x 64 B halves with 64-byte swizzle), one
+// thread issues tcgen05.mma.cta_group::1.kind::i8 (M = 128, N = BN, K = 32) into int32 accumulators
+// in tensor memory.  A per-k-block trace showed the issuing thread held about as long per MMA at
+// N = 128 as at N = 256 (~150 cycles), so the 256-wide tile does twice the work per k-block; it is
+// used when its tiles still cover the GPU.  When they would leave SMs idle (configuration 3: 64 such
+// tiles for 148 SMs) the 128-wide tile, at twice the tile count, is as fast in total; splitting the
+// K range of 256-wide tiles over a CTA pair and exchanging int32 partials (through distributed shared
+// memory, or through L2) measured slower than either, the exchange being latency-bound.
+// The per-channel factors are loaded by otherwise idle warps while the first tiles stream in;
+// epilogue (8 warps; warps w and w + 4 share tensor-memory lanes and split the column blocks):
+// acc - zp * rowsum[n], float(acc) * (s * scale[n]) (fma with a bias), staged in the freed ring and
+// written with TMA stores.
 
 struct GemmI8Params {
     int m, n, k, num_kb;
-    int splits;             // K parts of a tile (CTAs of one cluster): 1 or 2
     const int32_t* rowsum;  // per-tensor zero-point correction (may be null in per-token mode)
     const float* s_x;       // one scale (per-tensor) or one per row (per-token)
     int s_stride;           // 0 or 1
@@ -347,38 +345,35 @@ struct GemmI8Params {
 };
 
 constexpr int kI8BM = 128;         // rows of xq per tile (MMA M)
-constexpr int kI8BN = 256;         // weight rows (output channels) per tile (MMA N)
 constexpr int kI8BK = 128;         // k per pipeline stage (bytes of an int8 row = one 128-byte swizzle row)
 #ifndef SBQ_I8_STAGES
 #define SBQ_I8_STAGES 4
 #endif
 constexpr int kI8Stages = SBQ_I8_STAGES;
 constexpr int kI8Threads = 256;                // 8 warps
-constexpr int kI8MaxSplits = 2;
-constexpr int kI8Blocks = kI8BN / 32;          // 32-column blocks of a tile
-constexpr int kI8SlotBytes = kI8BM * 32 * 4;   // one block: 128 rows x 32 int32 = 16 KiB
+constexpr int kI8SlotBytes = kI8BM * 32 * 4;   // staging of one 32-column block: 128 rows x 128 B
 
+template <int BN>
 struct I8Smem {
     static constexpr int kA = kI8BM * kI8BK;  // 16 KiB
-    static constexpr int kB = kI8BN * kI8BK;  // 32 KiB: two 64-wide halves of 256 rows
+    static constexpr int kB = BN * kI8BK;     // two 64-wide halves of BN rows
     static constexpr int kStage = kA + kB;
     static constexpr int kRing = kI8Stages * kStage;
-    // after the main loop the ring holds the TMA-store staging, one 16 KiB slot per column block
-    static constexpr int kTail = 256 /* barriers */ + kI8BN * 5 * 4;  // scale, bias, rowsum, s*scale, zp*rowsum
+    static constexpr int kTail = 256 /* barriers */ + BN * 5 * 4;  // scale, bias, rowsum, s*scale, zp*rowsum
     static constexpr int kBytes = kRing + 1024 /* alignment */ + kTail;
-    static_assert(kI8Blocks * kI8SlotBytes <= kRing, "staging slots fit in the ring");
+    static_assert((BN / 32) * kI8SlotBytes <= kRing, "epilogue staging fits in the ring");
     static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
 };
 
 // Warp 0: TMA producer.  Warp 1: MMA issuer.  Warp 2: TMEM allocation.  Warps 2, 3: per-channel
 // epilogue factors.  All eight warps: epilogue (warp w reads accumulator lanes 32 (w % 4) ..).
-template <bool A_SIGNED>
+template <int BN, bool A_SIGNED>
 __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                                  const __grid_constant__ CUtensorMap tmap_b,
                                                                  const __grid_constant__ CUtensorMap tmap_y,
                                                                  const GemmI8Params p) {
-    using S = I8Smem;
-    constexpr int BN = kI8BN;
+    using S = I8Smem<BN>;
+    constexpr int kBlocks = BN / 32;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kRing);
@@ -394,11 +389,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * kI8BM, n0 = blockIdx.x * BN;
-    const int splits = p.splits;
-    const int part = splits > 1 ? (int)tc::cluster_ctarank() : 0;
-    const int kb0 = part * p.num_kb / splits, nkb = (part + 1) * p.num_kb / splits - kb0;  // >= 1 (host)
-    const int nown = kI8Blocks / splits, own0 = part * nown;  // this CTA's column blocks
-    const int nout = kI8Blocks - nown;                        // blocks whose partials go to the other CTA
+    const int nkb = p.num_kb;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kI8Stages; ++s) {
@@ -430,12 +421,11 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
             for (int i = 0; i < pre; ++i) {
                 uint8_t* b_s = smem + i * S::kStage + S::kA;
                 tc::mbar_arrive_expect_tx(&full[i], S::kStage);
-                tc::tma_load_4d(b_s, &tmap_b, &full[i], 0, 0, 2 * (kb0 + i), n0 / 16);
-                tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[i], 0, 0, 2 * (kb0 + i) + 1, n0 / 16);
+                tc::tma_load_4d(b_s, &tmap_b, &full[i], 0, 0, 2 * i, n0 / 16);
+                tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[i], 0, 0, 2 * i + 1, n0 / 16);
             }
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            for (int i = 0; i < pre; ++i)
-                tc::tma_load_2d(smem + i * S::kStage, &tmap_a, &full[i], (kb0 + i) * kI8BK, m0);
+            for (int i = 0; i < pre; ++i) tc::tma_load_2d(smem + i * S::kStage, &tmap_a, &full[i], i * kI8BK, m0);
             for (int i = pre; i < nkb; ++i) {
                 const int s = i % kI8Stages;
                 const uint32_t phase = (i / kI8Stages) & 1;
@@ -444,9 +434,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
                 uint8_t* a_s = smem + s * S::kStage;
                 uint8_t* b_s = a_s + S::kA;
                 tc::mbar_arrive_expect_tx(&full[s], S::kStage);
-                tc::tma_load_2d(a_s, &tmap_a, &full[s], (kb0 + i) * kI8BK, m0);
-                tc::tma_load_4d(b_s, &tmap_b, &full[s], 0, 0, 2 * (kb0 + i), n0 / 16);
-                tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[s], 0, 0, 2 * (kb0 + i) + 1, n0 / 16);
+                tc::tma_load_2d(a_s, &tmap_a, &full[s], i * kI8BK, m0);
+                tc::tma_load_4d(b_s, &tmap_b, &full[s], 0, 0, 2 * i, n0 / 16);
+                tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[s], 0, 0, 2 * i + 1, n0 / 16);
             }
         }
     } else if (warp == 1) {
@@ -492,69 +482,22 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
     const float sx0 = p.s_x[0];
     const int32_t zp = p.zp ? *p.zp : 0;
     __syncthreads();  // the factors of warps 2, 3 are in shared memory
-    if (per_tensor) {
+    if (per_tensor && threadIdx.x < BN) {
         s_f[threadIdx.x] = __fmul_rn(sx0, s_scale[threadIdx.x]);
         s_zr[threadIdx.x] = zp * s_rowsum[threadIdx.x];
     }
-    const int g = warp & 3, h = warp >> 2;         // lane group, column-block half
+    __syncthreads();
+    const int g = warp & 3, h = warp >> 2;  // lane group, column-block half
     const uint32_t lane_base = tmem + ((uint32_t)(g * 32) << 16);
-    const int trow = g * 32 + lane;                // row of the tile
-    const int row = m0 + trow;
-    if (splits > 1) {
-        // the other CTA's K part of the blocks it owns goes into y itself (the cells the owner
-        // overwrites with the finished values), as int32; then one cluster barrier
-        for (int o = h; o < nout; o += 2) {
-            const int b = o < own0 ? o : o + nown;
-            uint32_t r[32];
-            tc::tmem_ld_32x32b_x32(lane_base + b * 32, r);
-            tc::tmem_wait_ld();
-            const int nb = n0 + b * 32;
-            if (!ok || row >= p.m) continue;
-            int32_t* dst = reinterpret_cast<int32_t*>(p.y + (int64_t)row * p.ldy + nb);
-            if (nb + 32 <= p.n && p.vec_y) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    __stcg(reinterpret_cast<int4*>(dst) + j, make_int4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]));
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (nb + j < p.n) __stcg(dst + j, (int32_t)r[j]);
-            }
-        }
-        tc::cluster_sync();  // release / acquire at cluster scope: the partials are visible to the owners
-    } else {
-        __syncthreads();  // s_f / s_zr
-    }
-    if (splits > 1) __syncthreads();  // s_f / s_zr
+    const int row = m0 + g * 32 + lane;
     if (ok) {
         const float sx = per_tensor ? sx0 : p.s_x[row < p.m ? row : 0];
-        // the finished values replace the partials in y through TMA stores (async proxy) after this
-        // thread's ordinary loads and the other CTA's ordinary stores of the same cells
-        if (splits > 1) asm volatile("fence.proxy.async.global;" ::: "memory");
 #pragma unroll 1
-        for (int ob = h; ob < nown; ob += 2) {
-            const int b = own0 + ob;
+        for (int b = h; b < kBlocks; b += 2) {
             const int nb = n0 + b * 32;
             uint32_t r[32];
             tc::tmem_ld_32x32b_x32(lane_base + b * 32, r);
             tc::tmem_wait_ld();
-            if (splits > 1 && row < p.m) {  // the other K part (exact: int32)
-                const int32_t* src = reinterpret_cast<const int32_t*>(p.y + (int64_t)row * p.ldy + nb);
-                if (nb + 32 <= p.n && p.vec_y) {
-                    int4 q[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) q[j] = __ldcg(reinterpret_cast<const int4*>(src) + j);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        r[4 * j] += q[j].x; r[4 * j + 1] += q[j].y; r[4 * j + 2] += q[j].z; r[4 * j + 3] += q[j].w;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (nb + j < p.n) r[j] += (uint32_t)__ldcg(src + j);
-                }
-                if (p.tma_y) asm volatile("fence.proxy.async.global;" ::: "memory");
-            }
             float v[32];
             int32_t a[32];
 #pragma unroll
@@ -612,7 +555,6 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
         }
     }
     if (p.tma_y && lane == 0) tc::bulk_wait_all();  // the staged blocks stay in use until read
-    if (splits > 1) tc::cluster_sync();               // no CTA leaves while the other may read its cells
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 2) {
@@ -767,14 +709,31 @@ static int sm_count_dyn() {
     return c;
 }
 
-// K parts per tile: 2 when twice the tiles still fit on the GPU's SMs once (each part at least one
-// k-block), else 1.
-static int i8_splits(int64_t m, int64_t n, int num_kb) {
-    const int64_t tiles = ceil_div(m, kI8BM) * ceil_div(n, kI8BN);
-    const int sms = sm_count_dyn();
-    int s = 1;
-    while (s < kI8MaxSplits && tiles * (2 * s) <= sms && num_kb >= 2 * s) s *= 2;
-    return s;
+// Tile width: 256 weight rows when those tiles still give every SM one (the wider MMA does twice the
+// work per issue), else 128 (twice the tiles, as fast in total where 256-wide tiles leave SMs idle).
+static int i8_tile_n(int64_t m, int64_t n) {
+    const int64_t tiles256 = ceil_div(m, kI8BM) * ceil_div(n, 256);
+    return tiles256 * 10 >= (int64_t)sm_count_dyn() * 9 ? 256 : 128;
+}
+
+template <int BN>
+static int launch_gemm_bn(bool a_signed, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
+                          const GemmI8Params& q, bool dependent, cudaStream_t st) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)ceil_div(q.n, BN), (unsigned)ceil_div(q.m, kI8BM));
+    cfg.blockDim = dim3(kI8Threads);
+    cfg.dynamicSmemBytes = (size_t)I8Smem<BN>::kBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent ? 1 : 0;
+    auto kernel = a_signed ? gemm_w8a8_kernel<BN, true> : gemm_w8a8_kernel<BN, false>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, I8Smem<BN>::kBytes);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, my, q);
+    if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "gemm_w8a8 launch: %s", cudaGetErrorString(e));
+    return check_launch("gemm_w8a8");
 }
 
 // dependent: launched as a programmatic dependent of the activation quantisation (sbq_linear_dyn),
@@ -783,8 +742,9 @@ static int i8_splits(int64_t m, int64_t n, int num_kb) {
 // prologue could be the previous kernel's output.
 static int launch_gemm_i8(const void* xq, bool a_signed, const void* packed, const GemmI8Params& p, bool dependent,
                           cudaStream_t st) {
+    const int bn = i8_tile_n(p.m, p.n);
     CUtensorMap ma, mb, my;
-    int rc = make_gemm_maps(&ma, &mb, xq, p.m, p.k, packed, p.n, kI8BN);
+    int rc = make_gemm_maps(&ma, &mb, xq, p.m, p.k, packed, p.n, bn);
     if (rc) return rc;
     std::memset(&my, 0, sizeof(my));
     GemmI8Params q = p;
@@ -799,26 +759,8 @@ static int launch_gemm_i8(const void* xq, bool a_signed, const void* packed, con
         rc = encode_tmap(&my, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
-    q.splits = i8_splits(p.m, p.n, p.num_kb);
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)ceil_div(p.n, kI8BN), (unsigned)ceil_div(p.m, kI8BM), (unsigned)q.splits);
-    cfg.blockDim = dim3(kI8Threads);
-    cfg.dynamicSmemBytes = (size_t)I8Smem::kBytes;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;  // the K parts of a tile form one cluster
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = (unsigned)q.splits;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = dependent ? 2 : 1;
-    auto kernel = a_signed ? gemm_w8a8_kernel<true> : gemm_w8a8_kernel<false>;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, I8Smem::kBytes);
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, my, q);
-    if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "gemm_w8a8 launch: %s", cudaGetErrorString(e));
-    return check_launch("gemm_w8a8");
+    return bn == 256 ? launch_gemm_bn<256>(a_signed, ma, mb, my, q, dependent, st)
+                     : launch_gemm_bn<128>(a_signed, ma, mb, my, q, dependent, st);
 }
 
 }  // namespace sbq
