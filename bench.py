@@ -79,8 +79,11 @@ class ClockSampler:
             return self
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits", "-lms", "10"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            # the timed region starts once nvidia-smi is producing samples (it takes a moment to
+            # start; a short timed region would otherwise end before the first sample)
+            self.first = self.proc.stdout.readline()
         except OSError:
             self.proc = None
         return self
