@@ -220,7 +220,7 @@ def _graph_time(fn, stream, reps: int, warmup: int) -> float:
 
 
 def kernel_cases(sbq, dev, stream, steps: int, warmup: int,
-                 which=("gemv", "mlp", "gemm", "gemm_small", "dyn")) -> dict:
+                 which=("gemv", "mlp", "gemm", "gemm_f32", "gemm_small", "dyn", "lora", "groups")) -> dict:
     """Configurations 0-3 at their own shapes, each kernel timed alone (CUDA graph, CUDA events).
 
     HBM-bound cases rotate over enough distinct weight copies that every launch reads its weight
@@ -322,6 +322,78 @@ def kernel_cases(sbq, dev, stream, steps: int, warmup: int,
                          "frac_hbm": round(b / ms / 1e6 / pk["hbm_gbs"], 4)}
             del ws
         out["cfg4_b64_gemm_small"] = res
+
+    if "gemm_f32" in which:  # configuration 2's shape with the reference's fp32 activations
+        m, k, n = 2048, W.HIDDEN, W.INTER
+        (p_, s_, _), = int8_weights(n, k, 1)
+        x = W.activation(m, k, seed=2, dtype=torch.float32, device=dev)
+        y = torch.empty(m, n, device=dev)
+        wsb = int(L.load().sbq_linear_w8_workspace_bytes(m, k, L.F32))
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+
+        def f():
+            L.call("sbq_linear_w8_ws", vp(x.data_ptr()), L.F32, k, vp(p_.data_ptr()), vp(s_.data_ptr()), None, m, n,
+                   k, vp(y.data_ptr()), L.F32, n, vp(ws.data_ptr()), wsb, st)
+
+        ms = _graph_time(f, stream, max(20, steps // 10), warmup)
+        fl = 2 * m * n * k
+        out["cfg2_prefill_gemm_f32x"] = {"us": round(ms * 1e3, 2), "tflops": round(fl / ms / 1e9, 1),
+                                         "frac_bf16_peak": round(fl / ms / 1e9 / pk["bf16_tflops"], 4),
+                                         "note": "fp32 x split into bf16 high/low parts (one extra kernel), two "
+                                                 "MMAs per k-step; useful FLOPs 2mnk; fp32 out"}
+
+    if "lora" in which:  # the hybrid block's rank-128 LoRA pair (2560 -> 128 -> 4096) at decode
+        res = {}
+        a = sbq.Int8Linear(W.float_weight(128, 2560, seed=1, device=dev), None, device=dev)
+        b = sbq.Int8Linear(W.float_weight(4096, 128, seed=2, device=dev), None, device=dev)
+        for m in (1, 16):
+            x = W.activation(m, 2560, seed=m, dtype=torch.float32, device=dev)
+            y = torch.empty(m, 4096, device=dev)
+            t = torch.empty(m, 128, device=dev)
+
+            def fused():
+                L.call("sbq_lora_pair_w8", vp(x.data_ptr()), L.F32, 2560, vp(a.packed.data_ptr()),
+                       vp(a.scale.data_ptr()), vp(b.packed.data_ptr()), vp(b.scale.data_ptr()), m, 128, 4096, 2560,
+                       vp(y.data_ptr()), L.F32, 4096, st)
+
+            def separate():
+                L.call("sbq_linear_w8", vp(x.data_ptr()), L.F32, 2560, vp(a.packed.data_ptr()), vp(a.scale.data_ptr()),
+                       None, m, 128, 2560, vp(t.data_ptr()), L.F32, 128, st)
+                L.call("sbq_linear_w8", vp(t.data_ptr()), L.F32, 128, vp(b.packed.data_ptr()), vp(b.scale.data_ptr()),
+                       None, m, 4096, 128, vp(y.data_ptr()), L.F32, 4096, st)
+
+            res[str(m)] = {"fused_us": round(_graph_time(fused, stream, max(20, steps // 10), warmup) * 1e3, 2),
+                           "two_launches_us": round(_graph_time(separate, stream, max(20, steps // 10), warmup) * 1e3, 2)}
+        out["lora_pair"] = res
+
+    if "groups" in which:  # a hybrid block's shared-input projections: one launch vs eleven
+        from torch import nn
+        res = {}
+        names = [("sse_q_proj", 4096), ("sse_k_proj", 4096), ("sse_v_proj", 4096), ("lora_q_proj", 128),
+                 ("lora_k_proj", 128), ("sse_a_proj", 64), ("sse_b_proj", 64), ("sse_e_proj", 4), ("swa_q_proj", 4096),
+                 ("swa_k_proj", 1024), ("swa_v_proj", 1024)]
+        blk = nn.Module()
+        for i, (nm, n) in enumerate(names):
+            setattr(blk, nm, sbq.Int8Linear(W.float_weight(n, 2560, seed=30 + i, device=dev), None, device=dev))
+        mods = [getattr(blk, nm) for nm, _ in names]
+        group = sbq.groups.SharedInputGroup(mods)
+        for m in (1, 512):
+            x = W.activation(m, 2560, seed=m, dtype=torch.float32, device=dev)
+            outs = [torch.empty(m, mod.out_features, device=dev) for mod in mods]
+
+            def separate():
+                with torch.cuda.stream(stream):
+                    for mod, o in zip(mods, outs):
+                        mod.forward_into(x, o)
+
+            def grouped():
+                with torch.cuda.stream(stream):
+                    group.forward_all(x)
+
+            res["m%d" % m] = {"grouped_us": round(_graph_time(grouped, stream, max(20, steps // 10), warmup) * 1e3, 2),
+                              "separate_us": round(_graph_time(separate, stream, max(20, steps // 10), warmup) * 1e3, 2),
+                              "weight_bytes": sum(n * 2560 for _, n in names)}
+        out["hybrid_shared_input_group"] = res
 
     if "dyn" in which:  # configuration 3: int8-dyn, m=512, k=n=4096
         m, k, n = 512, W.HIDDEN, W.HIDDEN
@@ -507,7 +579,7 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline measurement")
     ap.add_argument("--no-extra", action="store_true", help="skip the per-configuration kernel timings")
-    ap.add_argument("--kernel", choices=("gemv", "mlp", "gemm", "gemm_small", "dyn"),
+    ap.add_argument("--kernel", choices=("gemv", "mlp", "gemm", "gemm_f32", "gemm_small", "dyn", "lora", "groups"),
                     help="time one configuration's kernel alone")
     ap.add_argument("--program", action="store_true",
                     help="run the decode step as one persistent decode-program launch instead of grouped launches")
