@@ -94,7 +94,11 @@ __device__ __forceinline__ void convert_row(const uint8_t* w8, int row, uint32_t
 constexpr int kWCh = 128;      // output channels per CTA (MMA M, one per TMEM lane)
 constexpr int kWTok = 256;     // activation rows per CTA (MMA N)
 constexpr int kWBK = 64;       // k per stage (one 128-byte 16-bit row, one packed tile column)
-constexpr int kWABufs = 4;     // weight operand buffers in TMEM (32 columns each)
+#ifndef SBQ_W16_ABUFS
+#define SBQ_W16_ABUFS 4
+#endif
+constexpr int kWABufs = SBQ_W16_ABUFS;  // weight operand buffers in TMEM (32 columns each; 256 + 32 * 8 = 512 at most)
+static_assert(kWABufs >= 2 && kWABufs <= 8, "tensor-memory columns");
 constexpr int kWThreads = 384; // 12 warps: producer, MMA, TMEM, idle, then two converter warpgroups
 constexpr uint32_t kWTmemCols = 512;
 constexpr uint32_t kWAccCol = 0;    // accumulator: columns [0, 256)

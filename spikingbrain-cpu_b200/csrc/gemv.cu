@@ -914,7 +914,10 @@ static double greedy_makespan(const std::vector<double>& unit_bytes, int slots) 
 // added in part order) only while that lowers the modelled time by more than 2 %: a sharded step
 // on several GPUs, whose launches have few tiles, cuts its large tiles; a one-GPU launch does not.
 // Cached per shape: eager callers plan each shape once.
-constexpr double kCtaShare = 200.0;
+#ifndef SBQ_GEMV_CTA_SHARE
+#define SBQ_GEMV_CTA_SHARE 200.0
+#endif
+constexpr double kCtaShare = SBQ_GEMV_CTA_SHARE;
 struct PartsKey {
     int slots, m, nj;
     int64_t shape[kMaxJobs][3];  // tiles, tile bytes, chunks per tile
