@@ -624,9 +624,12 @@ def main() -> None:
         allu = [None] * world
         dist.all_gather_object(allu, uuids[0])
         uuids = allu
-        dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(uuids if rank == 0 else []) as clocks:
+        # every rank enters the timed region together, after rank 0's sampler is running
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         ms = timed_graph(graph, args.steps, stream)
         torch.cuda.synchronize()
         if world > 1:
