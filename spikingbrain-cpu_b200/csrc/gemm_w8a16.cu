@@ -277,6 +277,240 @@ __global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_c
 }
 
 // ---------------------------------------------------------------------------------------------
+// CTA-pair variant of the prefill GEMM (more than 128 activation rows): a 2-CTA cluster computes a
+// 256-channel x 256-token tile with tcgen05.mma.cta_group::2 (M = 256 over both CTAs' tensor memory,
+// N = 256 over both CTAs' shared memory).  Each CTA converts its own 128 weight rows into its own
+// tensor memory and loads half of the activation tile (128 tokens), so a k-block moves 24 KiB into
+// each SM instead of 40 KiB: a per-k-block trace of the single-CTA kernel showed its converters
+// waiting ~0.6 us per k-block for the TMA data while the MMAs ran near their peak, i.e. the loop was
+// bound by the L2 -> shared-memory traffic of the activation tile each CTA re-reads.  Both CTAs'
+// activation loads complete on the leader's (rank 0's) barrier, both CTAs' converters arrive on
+// the leader's operand barrier, and the leader's MMA commits release each CTA's stage and operand
+// buffer (one commit per barrier, no multicast).  The epilogue is the single-CTA kernel's, per CTA.
+constexpr int kPTokHalf = kWTok / 2;  // activation rows each CTA of the pair loads
+#ifndef SBQ_W16_PAIR_KH
+#define SBQ_W16_PAIR_KH 2
+#endif
+#ifndef SBQ_W16_PAIR_STAGES
+#define SBQ_W16_PAIR_STAGES 4
+#endif
+#ifndef SBQ_W16_PAIR_STAGES_X2
+#define SBQ_W16_PAIR_STAGES_X2 5
+#endif
+constexpr int kPThreads = kWThreads;
+
+template <int AK>
+struct PairSmem {
+    // k per stage: kKH sub-blocks of 64 (128 for 16-bit x, so that the MMA thread's two waits and two
+    // commits per stage cover 8 MMAs; 64 for a split fp32 x, whose stage is twice as large)
+    static constexpr int kKH = AK == kABF16x2 ? 1 : SBQ_W16_PAIR_KH;
+    static constexpr int kXSub = kPTokHalf * kWBK * 2;     // 16 KiB: 128 tokens x 64 k of this CTA's half
+    static constexpr int kXTiles = AK == kABF16x2 ? 2 : 1;  // high and low part of a split fp32 x
+    static constexpr int kXStage = kKH * kXTiles * kXSub;
+    static constexpr int kW8Sub = kWCh * kWBK;             // 8 KiB: this CTA's 128 weight rows x 64 k
+    static constexpr int kStage = kXStage + kKH * kW8Sub;
+    static constexpr int kStages = AK == kABF16x2 ? SBQ_W16_PAIR_STAGES_X2 : SBQ_W16_PAIR_STAGES;
+    static constexpr int kBarOff = kStages * kStage;
+    static constexpr int kBytes = kBarOff + 512 + kWCh * 8 + 1024;
+    static_assert(kKH >= 1 && kKH <= 4, "64 to 256 k per stage");
+    static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
+    // operand buffers in tensor memory (kACols columns each, after the 256 accumulator columns):
+    // buffer d is released by the commit of the k-block that last read it, which must still be
+    // tracked by a stage barrier
+    static constexpr int kACols = kKH * (kWBK / 2);
+    static constexpr int kABufMax = (int)(kWTmemCols - kWAccCol - kWTok) / kACols;
+    static constexpr int kABufs0 = kWABufs < kStages ? kWABufs : kStages;
+    static constexpr int kABufs = kABufs0 < kABufMax ? kABufs0 : kABufMax;
+    static_assert(kABufs >= 2, "operand buffers");
+    static_assert(4 * kStages + kABufs + 1 <= 60, "barriers fit in 512 bytes with the TMEM slot");
+};
+
+template <bool OUT_F16, bool GATED, int AK>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
+    gemm_w8a16_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_x2,
+                           const __grid_constant__ CUtensorMap tmap_w, const GemmW16Params p) {
+    using S = PairSmem<AK>;
+    constexpr int kStages = S::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + S::kBarOff);  // this CTA's weight tile landed
+    uint64_t* xfull = wfull + kStages;      // both activation halves landed (the leader's is used)
+    uint64_t* conv_done = xfull + kStages;  // this CTA's 4 converter warps have read the weight tile
+    uint64_t* mma_done = conv_done + kStages;  // the pair's MMAs of the stage's k-block completed
+    uint64_t* a_full = mma_done + kStages;  // operand buffer written by both CTAs' converters (leader's used)
+    uint64_t* done = a_full + S::kABufs;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    float* s_scale = reinterpret_cast<float*>(smem + S::kBarOff + 512);
+    float* s_bias = s_scale + kWCh;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = tc::cluster_ctarank();
+    const bool leader = rank == 0;
+    const int n0 = (blockIdx.x >> 1) * (2 * kWCh) + (int)rank * kWCh;  // this CTA's 128 channels
+    const int t0 = blockIdx.y * kWTok;                                  // the pair's 256 tokens
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            tc::mbar_init(&wfull[s], 1);
+            tc::mbar_init(&xfull[s], 1);
+            tc::mbar_init(&conv_done[s], 4);
+            tc::mbar_init(&mma_done[s], 1);
+        }
+        for (int d = 0; d < S::kABufs; ++d) tc::mbar_init(&a_full[d], 8);  // 4 converter warps of each CTA
+        tc::mbar_init(done, 1);
+        tc::fence_mbar_init();
+        tc::prefetch_tmap(&tmap_x);
+        if (AK == kABF16x2) tc::prefetch_tmap(&tmap_x2);
+        tc::prefetch_tmap(&tmap_w);
+    }
+    if (warp == 2) {
+        tc::tmem_alloc_pair(tmem_slot, kWTmemCols);
+        tc::tmem_relinquish_pair();
+    }
+    for (int i = threadIdx.x; i < kWCh; i += blockDim.x) {
+        const int n = n0 + i;
+        s_scale[i] = n < p.n ? p.scale[n] : 0.0f;
+        s_bias[i] = (p.bias && n < p.n) ? p.bias[n] : 0.0f;
+    }
+    tc::fence_before_sync();
+    tc::cluster_sync();  // both CTAs' barriers exist before either CTA's loads or arrivals reach them
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                const int s = kb % kStages;
+                const uint32_t ph = (kb / kStages) & 1;
+                if (!tc::mbar_wait(&conv_done[s], ph ^ 1)) break;
+                if (!tc::mbar_wait(&mma_done[s], ph ^ 1)) break;
+                uint8_t* xs = smem + s * S::kStage;
+                uint8_t* ws = xs + S::kXStage;
+                tc::mbar_arrive_expect_tx(&wfull[s], S::kKH * S::kW8Sub);
+                const uint32_t xb = tc::cluster_addr(&xfull[s], 0);
+                if (leader) tc::mbar_arrive_expect_tx(&xfull[s], 2 * S::kXStage);
+                const int tr = t0 + (int)rank * kPTokHalf;
+#pragma unroll
+                for (int h = 0; h < S::kKH; ++h) {
+                    const int kc = kb * S::kKH + h;  // 64-wide k column
+                    tc::tma_load_4d(ws + h * S::kW8Sub, &tmap_w, &wfull[s], 0, 0, kc, n0 / 16);
+                    tc::tma_load_2d_pair(xs + h * S::kXTiles * S::kXSub, &tmap_x, xb, kc * kWBK, tr);
+                    if (AK == kABF16x2)
+                        tc::tma_load_2d_pair(xs + (h * S::kXTiles + 1) * S::kXSub, &tmap_x2, xb, kc * kWBK, tr);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = tc::idesc_f16(2 * kWCh, kWTok, AK != kAF16);
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                const int s = kb % kStages, d = kb % S::kABufs;
+                const uint32_t ph = (kb / kStages) & 1, phd = (kb / S::kABufs) & 1;
+                if (!tc::mbar_wait(&xfull[s], ph)) break;
+                if (!tc::mbar_wait_cluster(&a_full[d], phd)) break;
+                tc::fence_after_sync();
+                const uint8_t* xs = smem + s * S::kStage;
+                const uint32_t a_col = tmem + kWACol + d * S::kACols;
+#pragma unroll
+                for (int h = 0; h < S::kKH; ++h) {
+                    const uint8_t* xh = xs + h * S::kXTiles * S::kXSub;
+#pragma unroll
+                    for (int j = 0; j < kWBK / 16; ++j) {
+                        const uint64_t bd = tc::smem_desc(xh + j * 32, tc::kSwizzle128B, 1024);
+                        tc::mma_f16_ts_pair(tmem + kWAccCol, a_col + h * (kWBK / 2) + j * 8, bd, idesc, (kb | h | j) != 0);
+                        if (AK == kABF16x2) {
+                            const uint64_t bl = tc::smem_desc(xh + S::kXSub + j * 32, tc::kSwizzle128B, 1024);
+                            tc::mma_f16_ts_pair(tmem + kWAccCol, a_col + h * (kWBK / 2) + j * 8, bl, idesc, 1u);
+                        }
+                    }
+                }
+                // one barrier per CTA: frees the stage's activation half and operand buffer d
+                tc::mma_commit_pair(tc::cluster_addr(&mma_done[s], 0));
+                tc::mma_commit_pair(tc::cluster_addr(&mma_done[s], 1));
+            }
+            tc::mma_commit_pair(tc::cluster_addr(done, 0));
+            tc::mma_commit_pair(tc::cluster_addr(done, 1));
+        }
+    } else if (warp >= 4) {
+        const int grp = (warp - 4) >> 2;          // converter warpgroup: even (0) or odd (1) k-blocks
+        const int wq = (warp - 4) & 3;            // lanes 32 wq .. 32 wq + 31 of tensor memory
+        const int row = wq * 32 + lane;           // weight row (output channel) of this thread
+        const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
+        bool ok = true;
+        for (int kb = grp; kb < p.num_kb; kb += 2) {
+            const int s = kb % kStages, d = kb % S::kABufs;
+            const uint32_t ph = (kb / kStages) & 1;
+            // warp-uniform waits: tcgen05.st below is warp-collective.  Operand buffer d was last
+            // read by the MMAs of k-block kb - S::kABufs.
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&wfull[s], ph))) { ok = false; break; }
+            if (kb >= S::kABufs) {
+                const int kp = kb - S::kABufs;
+                if (!__all_sync(0xffffffffu, tc::mbar_wait(&mma_done[kp % kStages], (kp / kStages) & 1))) { ok = false; break; }
+            }
+            tc::fence_after_sync();
+#pragma unroll
+            for (int hh = 0; hh < S::kKH; ++hh) {
+                uint32_t h[32];
+                convert_row<AK>(smem + s * S::kStage + S::kXStage + hh * S::kW8Sub + row * 64, row, h);
+                tc::tmem_st_32x32b_x32(tmem + lane_addr + kWACol + d * S::kACols + hh * (kWBK / 2), h);
+            }
+            tc::tmem_wait_st();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) {
+                tc::mbar_arrive_cluster(tc::cluster_addr(&a_full[d], 0));
+                tc::mbar_arrive(&conv_done[s]);
+            }
+        }
+        // ---- epilogue: this thread's channel, 256 tokens of accumulators (as gemm_w8a16_kernel)
+        ok = __all_sync(0xffffffffu, ok && tc::mbar_wait(done, 0));
+        tc::fence_after_sync();
+        if (ok) {
+            const int n = n0 + row;
+            const float sc = s_scale[row], bi = s_bias[row];
+            const bool has_bias = p.bias != nullptr;
+#pragma unroll 1
+            for (int c = grp * (kWTok / 64); c < (grp + 1) * (kWTok / 64); ++c) {  // this group's token half
+                uint32_t r[32];
+                tc::tmem_ld_32x32b_x32(tmem + lane_addr + kWAccCol + c * 32, r);
+                tc::tmem_wait_ld();
+                if (n >= p.n) continue;
+                const int tb = t0 + c * 32;
+                if constexpr (GATED) {
+                    float gv[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) gv[j] = tb + j < p.m ? load_y<OUT_F16>(p, tb + j, n) : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (tb + j >= p.m) break;
+                        float v = __fmul_rn(__uint_as_float(r[j]), sc);
+                        if (has_bias) v = __fadd_rn(v, bi);
+                        put_y<OUT_F16>(p, tb + j, n, gv[j] / (1.0f + expf(-gv[j])) * v);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int t = tb + j;
+                        if (t >= p.m) break;
+                        float v = __fmul_rn(__uint_as_float(r[j]), sc);
+                        if (has_bias) v = __fadd_rn(v, bi);
+                        put_y<OUT_F16>(p, t, n, v);
+                    }
+                }
+            }
+        }
+    }
+    tc::fence_before_sync();
+    // neither CTA frees its tensor memory or leaves while the pair's MMAs or commits may still use
+    // its shared or tensor memory
+    tc::cluster_sync();
+    if (warp == 2) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc_pair(tmem, kWTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // Small-batch variant (17..128 activation rows, e.g. batched decode): 128-channel x 64-token tiles,
 // 6-stage TMA ring (2 CTAs per SM), and split-K over a thread-block cluster when the tiles alone
 // cannot fill the GPU: the S CTAs of a cluster (one K part each) keep their fp32 partial tile in
@@ -543,6 +777,10 @@ int check_linear_args(const void* x, int x_dtype, int64_t ldx, const void* packe
 using namespace sbq;
 
 constexpr int64_t kSmallMaxRows = 128;  // up to this many activation rows: the 64-token kernel
+#ifndef SBQ_W16_PAIR
+#define SBQ_W16_PAIR 1
+#endif
+constexpr bool kW16Pair = SBQ_W16_PAIR != 0;  // more rows: the CTA-pair kernel (else the single-CTA one)
 
 // SMs of the current device, cached per device (atomics: first calls may come from several threads)
 static int sm_count_w16() {
@@ -631,6 +869,39 @@ static void launch_large(dim3 grid, cudaStream_t s, const CUtensorMap& mx, const
     gemm_w8a16_kernel<OUT_F16, GATED, AK><<<grid, kWThreads, smem, s>>>(mx, mx2, mw, p);
 }
 
+template <bool OUT_F16, bool GATED, int AK>
+static void launch_pair(dim3 grid, cudaStream_t s, const CUtensorMap& mx, const CUtensorMap& mx2,
+                        const CUtensorMap& mw, const GemmW16Params& p) {
+    constexpr int smem = PairSmem<AK>::kBytes;
+    cudaFuncSetAttribute(gemm_w8a16_pair_kernel<OUT_F16, GATED, AK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    gemm_w8a16_pair_kernel<OUT_F16, GATED, AK><<<grid, kPThreads, smem, s>>>(mx, mx2, mw, p);
+}
+
+// The CTA-pair kernel over 256-channel x 256-token tiles (clusters of two CTAs along x).
+template <int AK>
+static int gemm_pair(const CUtensorMap& mx, const CUtensorMap& mx2, const CUtensorMap& mw, const float* scale,
+                     const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
+                     int gated) {
+    GemmW16Params p{};
+    p.gated = gated;
+    p.m = (int)m;
+    p.n = (int)n;
+    p.k = (int)k;
+    p.num_kb = (int)ceil_div(k, kWBK * PairSmem<AK>::kKH);  // k columns past k read zeros (TMA fill)
+    p.scale = scale;
+    p.bias = bias;
+    p.y = y;
+    p.ldy = ldy;
+    const dim3 grid((unsigned)(2 * ceil_div(n, 2 * kWCh)), (unsigned)ceil_div(m, kWTok));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (y_dtype == SBQ_F16) {
+        gated ? launch_pair<true, true, AK>(grid, s, mx, mx2, mw, p) : launch_pair<true, false, AK>(grid, s, mx, mx2, mw, p);
+    } else {
+        gated ? launch_pair<false, true, AK>(grid, s, mx, mx2, mw, p) : launch_pair<false, false, AK>(grid, s, mx, mx2, mw, p);
+    }
+    return check_launch("gemm_w8a16 (CTA pairs)");
+}
+
 template <int AK>
 static int gemm_large(const CUtensorMap& mx, const CUtensorMap& mx2, const CUtensorMap& mw, const float* scale,
                       const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
@@ -660,7 +931,7 @@ template <int AK>
 static int gemm_run_ak(const void* x, const void* x2, int64_t ldx, const void* packed, const float* scale,
                        const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
                        int gated) {
-    const int rows = m <= kSmallMaxRows ? kSTok : kWTok;
+    const int rows = m <= kSmallMaxRows ? kSTok : (kW16Pair ? kPTokHalf : kWTok);
     CUtensorMap mx, mx2, mw;
     int st = make_x_map(&mx, AK, x, ldx, m, k, rows);
     if (st) return st;
@@ -673,6 +944,7 @@ static int gemm_run_ak(const void* x, const void* x2, int64_t ldx, const void* p
     st = make_w_map(&mw, packed, n, k);
     if (st) return st;
     if (m <= kSmallMaxRows) return gemm_small<AK>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
+    if (kW16Pair) return gemm_pair<AK>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
     return gemm_large<AK>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
 }
 

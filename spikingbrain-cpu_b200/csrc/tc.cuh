@@ -264,6 +264,88 @@ __device__ __forceinline__ uint4 ld_cluster_v4(uint32_t cluster_address) {
     return v;
 }
 
+// ---- CTA pairs (cta_group::2) ---------------------------------------------------------------------
+// A 2-CTA cluster runs one M = 256 MMA: rows 0-127 of A (and of the accumulator) in cluster rank 0's
+// tensor memory, rows 128-255 in rank 1's; the N columns of B are split in halves, N/2 rows of B in
+// each CTA's shared memory at the same offset.  Rank 0 issues the MMAs; both CTAs allocate tensor
+// memory together (the same warp, the same destination offset).
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[tmem of both] x B[smem of both]^T, kind::f16, issued by rank 0.
+__device__ __forceinline__ void mma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives on the mbarrier at shared::cluster address `bar` (this CTA's or the peer's) once every
+// pair MMA this thread issued before has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// TMA tile load into this CTA's shared memory whose transaction bytes complete on the mbarrier at
+// shared::cluster address `bar` (the pair leader's).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// Arrive on the mbarrier at shared::cluster address `bar` (possibly the peer CTA's), with the
+// instruction's default semantics.  An explicit .release.cluster form held each arriving warp for
+// about 0.8 us on B200; the waiting side acquires at cluster scope (mbar_wait_cluster), and tensor
+// memory written before the arrive is ordered by tcgen05.wait::st + tcgen05.fence::before_thread_sync.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait for a barrier that other CTAs of the cluster arrive on (acquire at cluster scope).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    uint64_t t0 = 0;
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((i & 255) == 0) {
+            if (t0 == 0) {
+                t0 = now_ns();
+            } else if (now_ns() - t0 > kWaitLimitNs) {
+                raise_error(SBQ_ERR_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+
 // ---- descriptors ------------------------------------------------------------------------------
 enum SmemLayout : uint32_t { kSwizzleNone = 0, kSwizzle128B = 2, kSwizzle64B = 4, kSwizzle32B = 6 };
 

@@ -43,7 +43,8 @@ def test_config2_prefill_gemm(sbq):
 
 
 @pytest.mark.parametrize("m,n,k", [(65, 130, 320), (128, 256, 64), (129, 300, 4096), (300, 1000, 128),
-                                   (257, 4, 256), (200, 4096, 2560), (512, 12288, 4096), (1000, 512, 12288)])
+                                   (257, 4, 256), (200, 4096, 2560), (512, 12288, 4096), (1000, 512, 12288),
+                                   (300, 640, 320), (260, 136, 336)])
 @pytest.mark.parametrize("out", [torch.float32, torch.float16])
 def test_gemm_shapes(sbq, m, n, k, out):
     w = sbq.workloads.float_weight(n, k, seed=m + k)
