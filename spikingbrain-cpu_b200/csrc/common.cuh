@@ -29,6 +29,12 @@ constexpr int kTileBytes = kTileRows * kTileCols;
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Stream lanes (host): each (device, stream) pair is given one of kStreamLanes lanes, round robin on
+// first use, so that launches on up to kStreamLanes distinct streams of a device use disjoint
+// library-internal counters and scratch.  A CUDA graph keeps the lane of the stream it was captured on.
+constexpr int kStreamLanes = 8;
+int stream_lane(cudaStream_t s, int dev);
+
 // ---------------------------------------------------------------------------------------------
 // Loads.
 // ---------------------------------------------------------------------------------------------

@@ -29,12 +29,15 @@ struct Vec<float> {
         float4 t = __ldg(reinterpret_cast<const float4*>(p));
         v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
     }
+    __device__ static void cvt(const uint4& t, float (&v)[4]) {
+        v[0] = __uint_as_float(t.x); v[1] = __uint_as_float(t.y); v[2] = __uint_as_float(t.z); v[3] = __uint_as_float(t.w);
+    }
 };
 template <>
 struct Vec<__half> {
     static constexpr int kN = 8;
-    __device__ static void load(const __half* p, float (&v)[8]) {
-        uint4 t = __ldg(reinterpret_cast<const uint4*>(p));
+    __device__ static void load(const __half* p, float (&v)[8]) { cvt(__ldg(reinterpret_cast<const uint4*>(p)), v); }
+    __device__ static void cvt(const uint4& t, float (&v)[8]) {
         const __half2* h = reinterpret_cast<const __half2*>(&t);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -46,8 +49,8 @@ struct Vec<__half> {
 template <>
 struct Vec<__nv_bfloat16> {
     static constexpr int kN = 8;
-    __device__ static void load(const __nv_bfloat16* p, float (&v)[8]) {
-        uint4 t = __ldg(reinterpret_cast<const uint4*>(p));
+    __device__ static void load(const __nv_bfloat16* p, float (&v)[8]) { cvt(__ldg(reinterpret_cast<const uint4*>(p)), v); }
+    __device__ static void cvt(const uint4& t, float (&v)[8]) {
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&t);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -68,7 +71,7 @@ __device__ __forceinline__ int64_t vec_offset(int64_t v, int64_t per_row, int V,
     return row * ldx + (v - row * per_row) * V;
 }
 
-// Step 1: per-CTA (min, max) of x [m, k] (row stride ldx; k a multiple of the vector width).  Each
+// Two-kernel per-tensor quantisation (x up to kFusedMinBytes), step 1: per-CTA (min, max) of x [m, k] (row stride ldx; k a multiple of the vector width).  Each
 // thread requests kQuantVecs vectors before folding any, so one memory latency covers them.
 template <typename T>
 __global__ void __launch_bounds__(kQuantThreads) minmax_partial_kernel(const T* __restrict__ x, int64_t ldx, int m,
@@ -112,6 +115,7 @@ __global__ void __launch_bounds__(kQuantThreads) minmax_partial_kernel(const T* 
     }
 }
 
+
 // Step 2: torch ChooseQuantizationParams (quint8, reduce_range = false, preserve_sparsity = false).
 __device__ void choose_qparams(float mn, float mx, float* scale_out, int* zp_out) {
     const int qmin = 0, qmax = 255;
@@ -146,20 +150,23 @@ __device__ void choose_qparams(float mn, float mx, float* scale_out, int* zp_out
     *zp_out = zp;
 }
 
-// Quantise V elements to V/4 packed bytes: clamp(rint(fma(x, inv, zp)), 0, 255).
+// Quantise V elements to V/4 packed bytes: clamp(rint(fma(x, inv, zp)), 0, 255), computed as
+// rint(clamp(y, 0, 255)) - the same value, since rounding is monotonic and both bounds are integers
+// (NaN: fmaxf gives 0 either way) - with the rounding done by adding 1.5 * 2^23: every float in
+// [2^23, 2^24) is an integer, so the sum is y rounded to nearest even and its low mantissa byte is
+// that integer (0..255).  No float -> int conversion instructions.
 template <int V>
 __device__ __forceinline__ void quant_u8(const float (&e)[V], float inv, float fzp, uint8_t* dst) {
     uint32_t packed[V / 4];
 #pragma unroll
     for (int w = 0; w < V / 4; ++w) {
-        uint32_t word = 0;
+        uint32_t u[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            float t = rintf(__fmaf_rn(e[4 * w + i], inv, fzp));
-            t = fminf(fmaxf(t, 0.0f), 255.0f);
-            word |= (uint32_t)t << (8 * i);
+            const float t = fminf(fmaxf(__fmaf_rn(e[4 * w + i], inv, fzp), 0.0f), 255.0f);
+            u[i] = __float_as_uint(__fadd_rn(t, 12582912.0f));
         }
-        packed[w] = word;
+        packed[w] = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410);
     }
     if (V == 4) {
         *reinterpret_cast<uint32_t*>(dst) = packed[0];
@@ -168,7 +175,7 @@ __device__ __forceinline__ void quant_u8(const float (&e)[V], float inv, float f
     }
 }
 
-// Step 3, launched as a programmatic dependent of step 1.  Every CTA loads its first vectors of x
+// Step 3 of the two-kernel path, launched as a programmatic dependent of step 1.  Every CTA loads its first vectors of x
 // while step 1 still runs, then waits for it, folds the partials and derives the parameters itself
 // (identical result, no grid-wide synchronisation or counters); CTA 0 publishes them.
 template <typename T>
@@ -234,6 +241,190 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_per_tensor_kernel(cons
             if (v >= total) continue;
             const int64_t row = v / per_row;
             quant_u8<V>(e[j], inv, fzp, xq + row * (int64_t)k + (v - row * per_row) * V);
+        }
+    }
+}
+
+// Grid barrier of the per-tensor quantiser (one per stream lane).  Every CTA reads the generation
+// before it arrives; arrivals count modulo the grid size (atomicInc wraps the count to zero on the
+// last one), and the last CTA to arrive bumps the generation while the others wait (bounded) for the
+// bump.  The counters start at zero with the library and are left at zero for the next launch, so no
+// memset precedes a launch and CUDA graphs replay it as captured.  The grid is a cooperative launch:
+// all of its CTAs are resident together.
+__device__ unsigned g_qbar_count[kStreamLanes];
+__device__ unsigned g_qbar_gen[kStreamLanes];
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// atomicInc with acquire-release semantics at GPU scope
+__device__ __forceinline__ unsigned atom_inc_acq_rel_gpu(unsigned* p, unsigned limit) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(limit) : "memory");
+    return old;
+}
+
+// Returns false (error word set) if the other CTAs did not arrive within the wait limit.  `gen` is
+// the generation thread 0 read (acquire) before this CTA's arrival, e.g. at the start of the kernel.
+// Arrivals are acquire-release atomics (each publishes its CTA's partial and the last one acquires
+// all of them); the last CTA's release store of the new generation publishes them to the waiters.
+__device__ bool quant_grid_barrier(int lane, unsigned gen, int* s_flag) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned old = atom_inc_acq_rel_gpu(&g_qbar_count[lane], gridDim.x - 1);
+        int ok = 1;
+        if (old >= gridDim.x - 1) {
+            st_release_gpu(&g_qbar_gen[lane], gen + 1);
+        } else {
+            const uint64_t t0 = tc::now_ns();
+            for (uint32_t i = 1; ld_acquire_gpu(&g_qbar_gen[lane]) == gen; ++i) {
+                if (i > 64) __nanosleep(32);
+                if ((i & 255) == 0 && tc::now_ns() - t0 > tc::kWaitLimitNs) {
+                    tc::raise_error(SBQ_ERR_TIMEOUT);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        *s_flag = ok;
+    }
+    __syncthreads();
+    return *s_flag != 0;
+}
+
+// Per-tensor quantisation of larger x (at least kFusedMinBytes; fbgemm / torch quint8, the
+// reference's DynamicInt8Linear step) in one cooperative launch, which reads x from memory once: (1) each thread loads up to kFusedVecs vectors of x into registers (128 bytes)
+// and the CTA folds their (min, max) into partials[blockIdx.x]; (2) grid barrier; (3) every CTA folds
+// all partials, derives the parameters itself (ChooseQuantizationParams: identical in every CTA) and
+// quantises the vectors it holds; CTA 0 publishes s and zp.  When x is larger than the registers
+// of the grid hold, step 1 walks all of its vectors and step 3 reads them again.
+constexpr int kFusedThreads = 512;
+// x of at least this many bytes takes the one-launch quantiser.  Measured on B200 (CUDA graphs, m x
+// 4096 fp32): the grid barrier costs more than the two-kernel path's programmatic launch boundary,
+// so small x (1-3 MB) ran ~2 us slower in one launch, 8 MB (m = 512) the same, and 64 MB 12 us
+// faster (x read once instead of twice).
+constexpr int64_t kFusedMinBytes = int64_t(8) << 20;
+#ifndef SBQ_QUANT_COOP
+#define SBQ_QUANT_COOP 1
+#endif
+template <typename T>
+struct FusedVecs {
+    static constexpr int kN = 8;  // 16-byte vectors per thread: 128 bytes of x held in registers
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+    quantize_per_tensor_fused_kernel(const T* __restrict__ x, int64_t ldx, int m, int k,
+                                     float2* __restrict__ partials, uint8_t* __restrict__ xq,
+                                     float* __restrict__ s_out, int32_t* __restrict__ zp_out, int lane) {
+    // the GEMM launched next prepares its pipeline and streams its first weight tiles meanwhile; it
+    // waits for this grid before reading xq and the parameters
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // the barrier generation before this launch's arrivals (read now: its latency overlaps the loads)
+    const unsigned gen = threadIdx.x == 0 ? ld_acquire_gpu(&g_qbar_gen[lane]) : 0u;
+    constexpr int V = Vec<T>::kN, NV = FusedVecs<T>::kN;
+    const int64_t per_row = k / V, total = (int64_t)m * per_row;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool cached = total <= stride * NV;
+    const bool dense = ldx == k;  // rows back to back: vector v of x and of xq at v * V
+
+    uint4 raw[NV];  // 16 bytes of x per vector, as loaded (converted to fp32 where used)
+    float mn = INFINITY, mx = -INFINITY;
+    for (int64_t v0 = first; v0 < total; v0 += NV * stride) {
+#pragma unroll
+        for (int j = 0; j < NV; ++j)
+            if (v0 + j * stride < total)
+                raw[j] = __ldg(reinterpret_cast<const uint4*>(
+                    x + (dense ? (v0 + j * stride) * V : vec_offset(v0 + j * stride, per_row, V, ldx))));
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            if (v0 + j * stride >= total) continue;
+            float e[V];
+            Vec<T>::cvt(raw[j], e);
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                mn = fminf(mn, e[i]);
+                mx = fmaxf(mx, e[i]);
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    __shared__ float2 red[kFusedThreads / 32];
+    __shared__ float s_inv, s_zp;
+    __shared__ int s_flag;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(mn, mx);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kFusedThreads / 32; ++w) {
+            mn = fminf(mn, red[w].x);
+            mx = fmaxf(mx, red[w].y);
+        }
+        partials[blockIdx.x] = make_float2(mn, mx);
+    }
+    if (!quant_grid_barrier(lane, gen, &s_flag)) return;
+
+    mn = INFINITY;
+    mx = -INFINITY;
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
+        const float2 q = __ldcg(partials + i);  // written by other SMs in this launch: read through L2
+        mn = fminf(mn, q.x);
+        mx = fmaxf(mx, q.y);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    __syncthreads();  // red[] is reused
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(mn, mx);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kFusedThreads / 32; ++w) {
+            mn = fminf(mn, red[w].x);
+            mx = fmaxf(mx, red[w].y);
+        }
+        float s;
+        int zp;
+        choose_qparams(mn, mx, &s, &zp);
+        s_inv = __fdiv_rn(1.0f, s);
+        s_zp = (float)zp;
+        if (blockIdx.x == 0) {
+            *s_out = s;
+            *zp_out = zp;
+        }
+    }
+    __syncthreads();
+    const float inv = s_inv, fzp = s_zp;
+    for (int64_t v0 = first; v0 < total; v0 += NV * stride) {
+        if (!cached) {
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+                if (v0 + j * stride < total)
+                    raw[j] = __ldg(reinterpret_cast<const uint4*>(
+                        x + (dense ? (v0 + j * stride) * V : vec_offset(v0 + j * stride, per_row, V, ldx))));
+        }
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int64_t v = v0 + j * stride;
+            if (v >= total) continue;
+            int64_t off = v * V;
+            if (!dense) {
+                const int64_t row = v / per_row;
+                off = row * (int64_t)k + (v - row * per_row) * V;
+            }
+            float e[V];
+            Vec<T>::cvt(raw[j], e);
+            quant_u8<V>(e, inv, fzp, xq + off);
         }
     }
 }
@@ -365,6 +556,121 @@ struct I8Smem {
     static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
 };
 
+// Per-channel epilogue factors of the tile's BN weight rows from n0, loaded by warps 2 and 3 while the
+// main loop runs: scale, bias, row sums and, per tensor, s_x * scale[n] and zp * rowsum[n] (s_x and
+// zp are the previous kernel's output: read after griddepcontrol.wait, which these otherwise idle
+// warps can afford to block on).  Each thread computes the products of the entries it loaded.
+template <int BN>
+__device__ __forceinline__ void i8_load_factors(const GemmI8Params& p, int n0, float* s_scale, float* s_bias,
+                                                int32_t* s_rowsum, float* s_f, int32_t* s_zr) {
+    for (int i = threadIdx.x - 64; i < BN; i += 64) {
+        const int n = n0 + i;
+        s_scale[i] = n < p.n ? p.scale[n] : 0.0f;
+        s_bias[i] = (p.bias && n < p.n) ? p.bias[n] : 0.0f;
+        s_rowsum[i] = (p.rowsum && n < p.n) ? p.rowsum[n] : 0;
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (p.s_stride == 0) {
+        const float sx0 = p.s_x[0];
+        const int32_t zp = p.zp ? *p.zp : 0;
+        for (int i = threadIdx.x - 64; i < BN; i += 64) {
+            s_f[i] = __fmul_rn(sx0, s_scale[i]);
+            s_zr[i] = zp * s_rowsum[i];
+        }
+    }
+}
+
+// Epilogue of the int8 GEMMs, run by all 8 warps of a CTA after its accumulators (128 xq rows x BN
+// weight rows from row m0 / column n0, int32 in tensor memory from column 0) are complete: one lane
+// per warp polls `done` (with back-off) so idle threads do not compete with the producer and MMA
+// threads; the decision is warp-uniform (tcgen05.ld is warp-collective).  Warps w and w + 4 share
+// lane quarter w % 4 and split the 32-column blocks.
+template <int BN>
+__device__ __forceinline__ void i8_epilogue(const GemmI8Params& p, const CUtensorMap* tmap_y, uint8_t* smem,
+                                            uint64_t* done, int* abort_flag, const float* s_scale,
+                                            const float* s_bias, const int32_t* s_rowsum, float* s_f, int32_t* s_zr,
+                                            uint32_t tmem, int m0, int n0) {
+    constexpr int kBlocks = BN / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool per_tensor = p.s_stride == 0;
+    const int g = warp & 3, h = warp >> 2;  // lane group, column-block half
+    const uint32_t lane_base = tmem + ((uint32_t)(g * 32) << 16);
+    const int row = m0 + g * 32 + lane;
+    // the per-token scale of this thread's row comes from the previous kernel; it is read before the
+    // accumulators are complete (the producer's griddepcontrol.wait has long returned by then)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const float sx = per_tensor ? 0.0f : p.s_x[row < p.m ? row : 0];
+    int waited = 1;
+    if (lane == 0) waited = tc::mbar_wait_backoff(done, 0) && !*(volatile int*)abort_flag;
+    const bool ok = __shfl_sync(0xffffffffu, waited, 0) != 0;
+    tc::fence_after_sync();
+    __syncthreads();  // the factors of warps 2, 3 (i8_load_factors) are in shared memory
+    if (ok) {
+#pragma unroll 1
+        for (int b = h; b < kBlocks; b += 2) {
+            const int nb = n0 + b * 32;
+            uint32_t r[32];
+            tc::tmem_ld_32x32b_x32(lane_base + b * 32, r);
+            tc::tmem_wait_ld();
+            float v[32];
+            int32_t a[32];
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+                const int i = b * 32 + 4 * j4;
+                const float4 f4 = per_tensor ? *reinterpret_cast<const float4*>(s_f + i)
+                                             : make_float4(__fmul_rn(sx, s_scale[i]), __fmul_rn(sx, s_scale[i + 1]),
+                                                           __fmul_rn(sx, s_scale[i + 2]), __fmul_rn(sx, s_scale[i + 3]));
+                const int4 z4 = per_tensor ? *reinterpret_cast<const int4*>(s_zr + i) : make_int4(0, 0, 0, 0);
+                const float4 b4 = *reinterpret_cast<const float4*>(s_bias + i);
+                const float fs[4] = {f4.x, f4.y, f4.z, f4.w}, bs[4] = {b4.x, b4.y, b4.z, b4.w};
+                const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int jj = 4 * j4 + e;
+                    a[jj] = (int32_t)r[jj] - zs[e];
+                    const float af = __int2float_rn(a[jj]);
+                    v[jj] = p.bias ? __fmaf_rn(af, fs[e], bs[e]) : __fmul_rn(af, fs[e]);
+                }
+            }
+            if (p.tma_y) {
+                // the lane group's 32 x 32 fp32 block: 32 rows of 128 bytes, 16-byte unit j of row r at
+                // j ^ (r % 8) (128-byte swizzle), staged in slot b of the freed ring
+                uint8_t* reg = smem + b * kI8SlotBytes + g * 4096;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    *reinterpret_cast<float4*>(reg + lane * 128 + ((j ^ (lane & 7)) * 16)) =
+                        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                tc::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && m0 + g * 32 < p.m && nb < p.n) {
+                    tc::tma_store_2d(tmap_y, reg, nb, m0 + g * 32);
+                    tc::bulk_commit_group();
+                }
+                continue;
+            }
+            if (row >= p.m) continue;
+            float* yrow = p.y + (int64_t)row * p.ldy;
+            int32_t* arow = p.acc_out ? p.acc_out + (int64_t)row * p.n : nullptr;
+            if (nb + 32 <= p.n && p.vec_y) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    *reinterpret_cast<float4*>(yrow + nb + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    if (arow) *reinterpret_cast<int4*>(arow + nb + j) = make_int4(a[j], a[j + 1], a[j + 2], a[j + 3]);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (nb + j < p.n) {
+                        yrow[nb + j] = v[j];
+                        if (arow) arow[nb + j] = a[j];
+                    }
+                }
+            }
+        }
+    }
+    if (p.tma_y && lane == 0) tc::bulk_wait_all_read();  // the staged blocks stay in use until read
+}
+
 // Warp 0: TMA producer.  Warp 1: MMA issuer.  Warp 2: TMEM allocation.  Warps 2, 3: per-channel
 // epilogue factors.  All eight warps: epilogue (warp w reads accumulator lanes 32 (w % 4) ..).
 template <int BN, bool A_SIGNED>
@@ -373,7 +679,6 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
                                                                  const __grid_constant__ CUtensorMap tmap_y,
                                                                  const GemmI8Params p) {
     using S = I8Smem<BN>;
-    constexpr int kBlocks = BN / 32;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kRing);
@@ -461,105 +766,174 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
             tc::mma_commit(done);
         }
     } else if (warp == 2 || warp == 3) {
-        // per-channel factors, off the producer's critical path (read in the epilogue only)
-        for (int i = threadIdx.x - 64; i < BN; i += 64) {
-            const int n = n0 + i;
-            s_scale[i] = n < p.n ? p.scale[n] : 0.0f;
-            s_bias[i] = (p.bias && n < p.n) ? p.bias[n] : 0.0f;
-            s_rowsum[i] = (p.rowsum && n < p.n) ? p.rowsum[n] : 0;
-        }
+        i8_load_factors<BN>(p, n0, s_scale, s_bias, s_rowsum, s_f, s_zr);  // off the producer's critical path
     }
     __syncwarp();
-
-    // ---- epilogue.  One lane per warp polls (with back-off) so idle threads do not compete with the
-    // producer and MMA threads; the decision is warp-uniform (tcgen05.ld is warp-collective).
-    int waited = 1;
-    if (lane == 0) waited = tc::mbar_wait_backoff(done, 0) && !*(volatile int*)abort_flag;
-    const bool ok = __shfl_sync(0xffffffffu, waited, 0) != 0;
-    tc::fence_after_sync();
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // s_x and zp come from the previous kernel
-    const bool per_tensor = p.s_stride == 0;
-    const float sx0 = p.s_x[0];
-    const int32_t zp = p.zp ? *p.zp : 0;
-    __syncthreads();  // the factors of warps 2, 3 are in shared memory
-    if (per_tensor && threadIdx.x < BN) {
-        s_f[threadIdx.x] = __fmul_rn(sx0, s_scale[threadIdx.x]);
-        s_zr[threadIdx.x] = zp * s_rowsum[threadIdx.x];
-    }
-    __syncthreads();
-    const int g = warp & 3, h = warp >> 2;  // lane group, column-block half
-    const uint32_t lane_base = tmem + ((uint32_t)(g * 32) << 16);
-    const int row = m0 + g * 32 + lane;
-    if (ok) {
-        const float sx = per_tensor ? sx0 : p.s_x[row < p.m ? row : 0];
-#pragma unroll 1
-        for (int b = h; b < kBlocks; b += 2) {
-            const int nb = n0 + b * 32;
-            uint32_t r[32];
-            tc::tmem_ld_32x32b_x32(lane_base + b * 32, r);
-            tc::tmem_wait_ld();
-            float v[32];
-            int32_t a[32];
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-                const int i = b * 32 + 4 * j4;
-                const float4 f4 = per_tensor ? *reinterpret_cast<const float4*>(s_f + i)
-                                             : make_float4(__fmul_rn(sx, s_scale[i]), __fmul_rn(sx, s_scale[i + 1]),
-                                                           __fmul_rn(sx, s_scale[i + 2]), __fmul_rn(sx, s_scale[i + 3]));
-                const int4 z4 = per_tensor ? *reinterpret_cast<const int4*>(s_zr + i) : make_int4(0, 0, 0, 0);
-                const float4 b4 = *reinterpret_cast<const float4*>(s_bias + i);
-                const float fs[4] = {f4.x, f4.y, f4.z, f4.w}, bs[4] = {b4.x, b4.y, b4.z, b4.w};
-                const int zs[4] = {z4.x, z4.y, z4.z, z4.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int jj = 4 * j4 + e;
-                    a[jj] = (int32_t)r[jj] - zs[e];
-                    const float af = __int2float_rn(a[jj]);
-                    v[jj] = p.bias ? __fmaf_rn(af, fs[e], bs[e]) : __fmul_rn(af, fs[e]);
-                }
-            }
-            if (p.tma_y) {
-                // the lane group's 32 x 32 fp32 block: 32 rows of 128 bytes, 16-byte unit j of row r at
-                // j ^ (r % 8) (128-byte swizzle), staged in slot b of the freed ring
-                uint8_t* reg = smem + b * kI8SlotBytes + g * 4096;
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    *reinterpret_cast<float4*>(reg + lane * 128 + ((j ^ (lane & 7)) * 16)) =
-                        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                tc::fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0 && m0 + g * 32 < p.m && nb < p.n) {
-                    tc::tma_store_2d(&tmap_y, reg, nb, m0 + g * 32);
-                    tc::bulk_commit_group();
-                }
-                continue;
-            }
-            if (row >= p.m) continue;
-            float* yrow = p.y + (int64_t)row * p.ldy;
-            int32_t* arow = p.acc_out ? p.acc_out + (int64_t)row * p.n : nullptr;
-            if (nb + 32 <= p.n && p.vec_y) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                    *reinterpret_cast<float4*>(yrow + nb + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    if (arow) *reinterpret_cast<int4*>(arow + nb + j) = make_int4(a[j], a[j + 1], a[j + 2], a[j + 3]);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    if (nb + j < p.n) {
-                        yrow[nb + j] = v[j];
-                        if (arow) arow[nb + j] = a[j];
-                    }
-                }
-            }
-        }
-    }
-    if (p.tma_y && lane == 0) tc::bulk_wait_all();  // the staged blocks stay in use until read
+    i8_epilogue<BN>(p, &tmap_y, smem, done, abort_flag, s_scale, s_bias, s_rowsum, s_f, s_zr, tmem, m0, n0);
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 2) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, BN);
+    }
+}
+
+// ---- CTA-pair variant (more than 128 xq rows) ---------------------------------------------------
+// A 2-CTA cluster computes a 256 (xq rows) x BN (weight rows) tile with
+// tcgen05.mma.cta_group::2.kind::i8 (M = 256 over both CTAs' tensor memory): each CTA loads its own
+// 128 xq rows and half of the BN weight rows, so a 128-deep k-block moves 16 + BN/2 * 128 / 1024 KiB
+// into each SM instead of 16 + BN * 128 / 1024 KiB.  Timed without MMAs, the single-CTA loop ran at
+// the SM's L2 -> shared-memory rate (32 KiB per k-block in ~0.25 us), above the MMA time.  Each
+// stage holds kKH k-blocks so the MMA thread's wait and commit cover 4 kKH MMAs.  All loads of a
+// stage complete on the leader's (rank 0's) barrier; the leader's commits release each CTA's stage.
+#ifndef SBQ_I8P_KH
+#define SBQ_I8P_KH 2
+#endif
+
+template <int BN>
+struct I8PairSmem {
+    static constexpr int kKH = SBQ_I8P_KH;              // 128-deep k-blocks per stage
+    static constexpr int kASub = kI8BM * kI8BK;         // 16 KiB: this CTA's 128 xq rows
+    static constexpr int kBHalf = (BN / 2) * 64;        // one 64-byte column of this CTA's BN/2 weight rows
+    static constexpr int kBSub = 2 * kBHalf;
+    static constexpr int kStage = kKH * (kASub + kBSub);
+    static constexpr int kStages = (200 * 1024) / kStage < 8 ? (200 * 1024) / kStage : 8;
+    static constexpr int kRing = kStages * kStage;
+    static constexpr int kTail = 256 /* barriers */ + BN * 5 * 4;
+    static constexpr int kBytes = kRing + 1024 /* alignment */ + kTail;
+    static_assert(kStages >= 2, "pipeline depth");
+    static_assert((BN / 32) * kI8SlotBytes <= kRing, "epilogue staging fits in the ring");
+    static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
+};
+
+template <int BN, bool A_SIGNED>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kI8Threads, 1)
+    gemm_w8a8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                          const __grid_constant__ CUtensorMap tmap_y, const GemmI8Params p) {
+    using S = I8PairSmem<BN>;
+    constexpr int kStages = S::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kRing);  // the leader's: both CTAs' loads landed
+    uint64_t* empty = full + kStages;                               // this CTA's stage read by the pair's MMAs
+    uint64_t* done = empty + kStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+    float* s_scale = reinterpret_cast<float*>(smem + S::kRing + 256);
+    float* s_bias = s_scale + BN;
+    int32_t* s_rowsum = reinterpret_cast<int32_t*>(s_bias + BN);
+    float* s_f = reinterpret_cast<float*>(s_rowsum + BN);
+    int32_t* s_zr = reinterpret_cast<int32_t*>(s_f + BN);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = tc::cluster_ctarank();
+    const bool leader = rank == 0;
+    const int m0 = blockIdx.x * kI8BM;          // this CTA's 128 xq rows (the pair's 256 are adjacent)
+    const int n0 = blockIdx.y * BN;             // the pair's BN weight rows (output columns)
+    const int nb0 = n0 + (int)rank * (BN / 2);  // the half this CTA loads
+    const int nkb = p.num_kb;                   // stages (kKH k-blocks each)
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        tc::mbar_init(done, 1);
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+        tc::prefetch_tmap(&tmap_a);
+        tc::prefetch_tmap(&tmap_b);
+        if (p.tma_y) tc::prefetch_tmap(&tmap_y);
+    }
+    if (warp == 2) {
+        tc::tmem_alloc_pair(tmem_slot, BN);
+        tc::tmem_relinquish_pair();
+    }
+    tc::fence_before_sync();
+    tc::cluster_sync();  // both CTAs' barriers exist before either CTA's loads or commits reach them
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- producer (both CTAs).  Weight tiles of the first stages before griddepcontrol.wait
+            // (they do not depend on the activation quantisation), activation tiles after it.
+            const int pre = nkb < kStages ? nkb : kStages;
+            for (int i = 0; i < pre; ++i) {
+                uint8_t* b_s = smem + i * S::kStage + S::kKH * S::kASub;
+                const uint32_t fb = tc::cluster_addr(&full[i], 0);
+                if (leader) tc::mbar_arrive_expect_tx(&full[i], 2 * S::kStage);
+#pragma unroll
+                for (int h = 0; h < S::kKH; ++h) {
+                    const int kc = 2 * (i * S::kKH + h);  // 64-byte weight tile column
+                    tc::tma_load_4d_pair(b_s + h * S::kBSub, &tmap_b, fb, 0, 0, kc, nb0 / 16);
+                    tc::tma_load_4d_pair(b_s + h * S::kBSub + S::kBHalf, &tmap_b, fb, 0, 0, kc + 1, nb0 / 16);
+                }
+            }
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            for (int i = 0; i < pre; ++i) {
+                const uint32_t fb = tc::cluster_addr(&full[i], 0);
+#pragma unroll
+                for (int h = 0; h < S::kKH; ++h)
+                    tc::tma_load_2d_pair(smem + i * S::kStage + h * S::kASub, &tmap_a, fb, (i * S::kKH + h) * kI8BK, m0);
+            }
+            for (int i = pre; i < nkb; ++i) {
+                const int s = i % kStages;
+                const uint32_t phase = (i / kStages) & 1;
+                if (!tc::mbar_wait(&empty[s], phase ^ 1)) { *abort_flag = 1; break; }
+                if (*(volatile int*)abort_flag) break;
+                uint8_t* a_s = smem + s * S::kStage;
+                uint8_t* b_s = a_s + S::kKH * S::kASub;
+                const uint32_t fb = tc::cluster_addr(&full[s], 0);
+                if (leader) tc::mbar_arrive_expect_tx(&full[s], 2 * S::kStage);
+#pragma unroll
+                for (int h = 0; h < S::kKH; ++h) {
+                    const int kc = 2 * (i * S::kKH + h);
+                    tc::tma_load_2d_pair(a_s + h * S::kASub, &tmap_a, fb, (i * S::kKH + h) * kI8BK, m0);
+                    tc::tma_load_4d_pair(b_s + h * S::kBSub, &tmap_b, fb, 0, 0, kc, nb0 / 16);
+                    tc::tma_load_4d_pair(b_s + h * S::kBSub + S::kBHalf, &tmap_b, fb, 0, 0, kc + 1, nb0 / 16);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ---- MMA issuer (the leader only)
+            constexpr uint32_t idesc = tc::idesc_i8(A_SIGNED, 2 * kI8BM, BN);
+            for (int i = 0; i < nkb; ++i) {
+                const int s = i % kStages;
+                const uint32_t phase = (i / kStages) & 1;
+                if (!tc::mbar_wait(&full[s], phase)) { *abort_flag = 1; break; }
+                tc::fence_after_sync();
+                const uint8_t* a_s = smem + s * S::kStage;
+                const uint8_t* b_s = a_s + S::kKH * S::kASub;
+#pragma unroll
+                for (int h = 0; h < S::kKH; ++h) {
+#pragma unroll
+                    for (int j = 0; j < kI8BK / 32; ++j) {
+                        const uint64_t ad = tc::smem_desc(a_s + h * S::kASub + j * 32, tc::kSwizzle128B, 1024);
+                        const uint64_t bd = tc::smem_desc(b_s + h * S::kBSub + (j >> 1) * S::kBHalf + (j & 1) * 32,
+                                                          tc::kSwizzle64B, 512);
+                        tc::mma_i8_pair(tmem, ad, bd, idesc, (i | h | j) != 0);
+                    }
+                }
+                tc::mma_commit_pair(tc::cluster_addr(&empty[s], 0));
+                tc::mma_commit_pair(tc::cluster_addr(&empty[s], 1));
+            }
+            tc::mma_commit_pair(tc::cluster_addr(done, 0));
+            tc::mma_commit_pair(tc::cluster_addr(done, 1));
+        }
+    } else if (warp == 2 || warp == 3) {
+        i8_load_factors<BN>(p, n0, s_scale, s_bias, s_rowsum, s_f, s_zr);
+    }
+    __syncwarp();
+    i8_epilogue<BN>(p, &tmap_y, smem, done, abort_flag, s_scale, s_bias, s_rowsum, s_f, s_zr, tmem, m0, n0);
+    tc::fence_before_sync();
+    // neither CTA frees its tensor memory or exits while the pair's MMAs, loads or commits may still
+    // reach its shared or tensor memory
+    tc::cluster_sync();
+    if (warp == 2) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc_pair(tmem, BN);
     }
 }
 
@@ -579,14 +953,6 @@ static int check_x(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k
         return set_error(SBQ_ERR_ALIGNMENT, "activation rows must be 16-byte aligned");
     if (m >= (int64_t(1) << 31) || k >= (int64_t(1) << 30)) return set_error(SBQ_ERR_UNSUPPORTED, "shape too large");
     return SBQ_OK;
-}
-
-// CTAs of the two per-tensor steps: kQuantVecs vectors per thread, at most kMaxPartials CTAs.
-static int minmax_blocks(int64_t m, int64_t k, int vec) {
-    const int64_t vecs = m * (k / vec);
-    int64_t b = (vecs + kQuantThreads * kQuantVecs - 1) / (kQuantThreads * kQuantVecs);
-    if (b > kMaxPartials) b = kMaxPartials;
-    return (int)(b < 1 ? 1 : b);
 }
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -637,13 +1003,65 @@ static void launch_dependent(void (*kernel)(Params...), dim3 grid, int threads, 
 
 // Step 1 is an ordinary launch (x may be the previous kernel's output); step 3 depends on it
 // programmatically.
+// SMs of the current device, cached per device (atomics: first calls may come from several threads)
+static int sm_count_dyn() {
+    static std::atomic<int> count[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    int c = count[dev].load(std::memory_order_relaxed);
+    if (c == 0) {
+        cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+        c = c > 0 ? c : 148;
+        count[dev].store(c, std::memory_order_relaxed);
+    }
+    return c;
+}
+
+// CTAs of the two per-tensor steps: kQuantVecs vectors per thread, at most kMaxPartials CTAs.
+static int minmax_blocks(int64_t m, int64_t k, int vec) {
+    const int64_t vecs = m * (k / vec);
+    int64_t b = (vecs + kQuantThreads * kQuantVecs - 1) / (kQuantThreads * kQuantVecs);
+    if (b > kMaxPartials) b = kMaxPartials;
+    return (int)(b < 1 ? 1 : b);
+}
+
+
 template <typename T>
-static void launch_quant_tensor(const void* x, int64_t ldx, int m, int k, float2* partials, uint8_t* xq, float* s,
-                                int32_t* zp, cudaStream_t st) {
-    const int nb = minmax_blocks(m, k, Vec<T>::kN);
-    minmax_partial_kernel<T><<<nb, kQuantThreads, 0, st>>>(static_cast<const T*>(x), ldx, m, k, partials);
-    launch_dependent(quantize_per_tensor_kernel<T>, dim3(nb), kQuantThreads, 0, st, static_cast<const T*>(x), ldx, m,
-                     k, static_cast<const float2*>(partials), nb, xq, s, zp);
+static cudaError_t launch_quant_tensor(const void* x, int64_t ldx, int m, int k, float2* partials, uint8_t* xq,
+                                       float* s, int32_t* zp, cudaStream_t st) {
+    if ((int64_t)m * k * (int64_t)sizeof(T) < kFusedMinBytes) {
+        const int nb = minmax_blocks(m, k, Vec<T>::kN);
+        minmax_partial_kernel<T><<<nb, kQuantThreads, 0, st>>>(static_cast<const T*>(x), ldx, m, k, partials);
+        launch_dependent(quantize_per_tensor_kernel<T>, dim3(nb), kQuantThreads, 0, st, static_cast<const T*>(x), ldx,
+                         m, k, static_cast<const float2*>(partials), nb, xq, s, zp);
+        return cudaSuccess;
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    auto kernel = quantize_per_tensor_fused_kernel<T>;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kFusedThreads, 0);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    // as many CTAs as hold x in registers (at most the resident limit, and the partials' capacity)
+    const int64_t vecs = (int64_t)m * (k / Vec<T>::kN);
+    int64_t nb = ceil_div(vecs, (int64_t)kFusedThreads * FusedVecs<T>::kN);
+    const int64_t cap = (int64_t)per_sm * sm_count_dyn();
+    if (nb > cap) nb = cap;
+    if (nb > kMaxPartials) nb = kMaxPartials;
+    if (nb < 1) nb = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)nb);
+    cfg.blockDim = dim3(kFusedThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = SBQ_QUANT_COOP ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<const T*>(x), ldx, m, k, partials, xq, s, zp,
+                              stream_lane(st, dev));
 }
 
 template <typename T>
@@ -653,11 +1071,13 @@ static void launch_quant_token(const void* x, int64_t ldx, int m, int k, int8_t*
 
 static int quant_tensor(const void* x, int x_dtype, int64_t ldx, int64_t m, int64_t k, float2* partials, uint8_t* xq,
                         float* s, int32_t* zp, cudaStream_t st) {
+    cudaError_t e;
     switch (x_dtype) {
-        case SBQ_F32: launch_quant_tensor<float>(x, ldx, (int)m, (int)k, partials, xq, s, zp, st); break;
-        case SBQ_F16: launch_quant_tensor<__half>(x, ldx, (int)m, (int)k, partials, xq, s, zp, st); break;
-        default: launch_quant_tensor<__nv_bfloat16>(x, ldx, (int)m, (int)k, partials, xq, s, zp, st); break;
+        case SBQ_F32: e = launch_quant_tensor<float>(x, ldx, (int)m, (int)k, partials, xq, s, zp, st); break;
+        case SBQ_F16: e = launch_quant_tensor<__half>(x, ldx, (int)m, (int)k, partials, xq, s, zp, st); break;
+        default: e = launch_quant_tensor<__nv_bfloat16>(x, ldx, (int)m, (int)k, partials, xq, s, zp, st); break;
     }
+    if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "quantize activation (per tensor): %s", cudaGetErrorString(e));
     return check_launch("quantize activation (per tensor)");
 }
 
@@ -695,19 +1115,6 @@ static int make_gemm_maps(CUtensorMap* ma, CUtensorMap* mb, const void* xq, int6
     return SBQ_OK;
 }
 
-// SMs of the current device, cached per device (atomics: first calls may come from several threads)
-static int sm_count_dyn() {
-    static std::atomic<int> count[64] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    int c = count[dev].load(std::memory_order_relaxed);
-    if (c == 0) {
-        cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
-        c = c > 0 ? c : 148;
-        count[dev].store(c, std::memory_order_relaxed);
-    }
-    return c;
-}
 
 // Tile width: 256 weight rows when those tiles still give every SM one (the wider MMA does twice the
 // work per issue), else 128 (twice the tiles, as fast in total where 256-wide tiles leave SMs idle).
@@ -736,15 +1143,49 @@ static int launch_gemm_bn(bool a_signed, const CUtensorMap& ma, const CUtensorMa
     return check_launch("gemm_w8a8");
 }
 
+template <int BN>
+static int launch_gemm_pair_bn(bool a_signed, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
+                               const GemmI8Params& q, bool dependent, cudaStream_t st) {
+    using S = I8PairSmem<BN>;
+    GemmI8Params p = q;
+    p.num_kb = (int)ceil_div(q.k, (int64_t)kI8BK * S::kKH);  // k past the end reads zeros (TMA fill)
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)(2 * ceil_div(q.m, 2 * kI8BM)), (unsigned)ceil_div(q.n, BN));
+    cfg.blockDim = dim3(kI8Threads);
+    cfg.dynamicSmemBytes = (size_t)S::kBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent ? 1 : 0;
+    auto kernel = a_signed ? gemm_w8a8_pair_kernel<BN, true> : gemm_w8a8_pair_kernel<BN, false>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, my, p);
+    if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "gemm_w8a8 (CTA pairs) launch: %s", cudaGetErrorString(e));
+    return check_launch("gemm_w8a8 (CTA pairs)");
+}
+
+#ifndef SBQ_I8_PAIR
+#define SBQ_I8_PAIR 1
+#endif
+
+// Tile of the CTA-pair kernel: BN = 256 weight rows when those pairs still give every SM a CTA, else 128.
+static int i8_pair_tile_n(int64_t m, int64_t n) {
+    const int64_t ctas256 = 2 * ceil_div(m, 2 * kI8BM) * ceil_div(n, 256);
+    return ctas256 * 10 >= (int64_t)sm_count_dyn() * 9 ? 256 : 128;
+}
+
 // dependent: launched as a programmatic dependent of the activation quantisation (sbq_linear_dyn),
 // which lets the pipeline set-up and the first weight tiles overlap that kernel.  Direct calls of
 // sbq_gemm_w8a8 launch in plain stream order: there the scale, bias and row sums read in the
 // prologue could be the previous kernel's output.
 static int launch_gemm_i8(const void* xq, bool a_signed, const void* packed, const GemmI8Params& p, bool dependent,
                           cudaStream_t st) {
-    const int bn = i8_tile_n(p.m, p.n);
+    const bool pair = SBQ_I8_PAIR && p.m > kI8BM;  // more than one 128-row tile of xq: CTA pairs
+    const int bn = pair ? i8_pair_tile_n(p.m, p.n) : i8_tile_n(p.m, p.n);
     CUtensorMap ma, mb, my;
-    int rc = make_gemm_maps(&ma, &mb, xq, p.m, p.k, packed, p.n, bn);
+    int rc = make_gemm_maps(&ma, &mb, xq, p.m, p.k, packed, p.n, pair ? bn / 2 : bn);  // a pair CTA loads bn/2 rows
     if (rc) return rc;
     std::memset(&my, 0, sizeof(my));
     GemmI8Params q = p;
@@ -759,6 +1200,9 @@ static int launch_gemm_i8(const void* xq, bool a_signed, const void* packed, con
         rc = encode_tmap(&my, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
+    if (pair)
+        return bn == 256 ? launch_gemm_pair_bn<256>(a_signed, ma, mb, my, q, dependent, st)
+                         : launch_gemm_pair_bn<128>(a_signed, ma, mb, my, q, dependent, st);
     return bn == 256 ? launch_gemm_bn<256>(a_signed, ma, mb, my, q, dependent, st)
                      : launch_gemm_bn<128>(a_signed, ma, mb, my, q, dependent, st);
 }

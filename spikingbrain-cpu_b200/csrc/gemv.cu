@@ -301,7 +301,7 @@ __device__ __forceinline__ int consumers_sync_and(int v) {
 // their stream's lane only (decode programs have a lane of their own).  Up to kLanes streams per
 // device can therefore run grouped GEMVs concurrently; a CUDA graph keeps the lane of the stream it
 // was captured on.
-constexpr int kLanes = 8;                  // stream lanes for grouped launches
+constexpr int kLanes = kStreamLanes;       // stream lanes for grouped launches
 constexpr int kProgramLane = kLanes;       // the decode programs' lane
 constexpr int kLaneCount = kLanes + 1;
 constexpr int kClaimSlots = 128;           // per lane: per-launch counters, used round-robin
@@ -876,7 +876,7 @@ struct LaneKeyHash {
 };
 static std::atomic<unsigned> g_lane_launches[64][kLaneCount];
 
-static int stream_lane(cudaStream_t s, int dev) {
+int stream_lane(cudaStream_t s, int dev) {
     static std::mutex mu;
     static std::unordered_map<LaneKey, int, LaneKeyHash> lanes;
     static unsigned next[64] = {};

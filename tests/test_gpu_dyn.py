@@ -163,3 +163,59 @@ def test_dyn_strided_output_rows(sbq, ldy_pad, mode):
     assert torch.equal(y[:, :n], want)
     assert bool((y[:, n:] == -7.25).all())
     assert sbq._lib.load().sbq_check_device_error() == 0
+
+
+# x of 8 MiB and more takes the one-launch quantiser (grid barrier): with the whole of x held in
+# registers (cached) or, above what the grid's registers hold, read twice; dense and strided rows.
+@pytest.mark.parametrize("m,k,xdtype,ld_pad", [(1024, 2048, torch.float32, 0), (1100, 4096, torch.float16, 0),
+                                               (1200, 4096, torch.float32, 0), (2400, 4096, torch.bfloat16, 0),
+                                               (1100, 2048, torch.float32, 64)])
+def test_one_launch_quantiser_bit_exact(sbq, m, k, xdtype, ld_pad):
+    import ctypes
+
+    n = 64
+    w = sbq.workloads.float_weight(n, k, seed=m)
+    x = (sbq.workloads.activation(m, k, seed=k + m, dtype=torch.float32) * 3.0).to(xdtype)
+    x[7, 5] = 40.0  # an outlier that sets the range
+    q, sc = R.quantize_per_channel(w.numpy())
+    ry, rxq, rs, rzp, racc = R.dyn_linear(x.float().numpy(), q, sc)
+    mod = sbq.DynamicInt8Linear(w, None)
+    if ld_pad == 0:
+        y, xq, s, zp, acc = mod.forward_stages(x.cuda())
+        assert np.array_equal(acc.cpu().numpy(), racc)
+    else:
+        xs = torch.zeros(m, k + ld_pad, dtype=xdtype)
+        xs[:, :k] = x
+        xs = xs.cuda()
+        L = sbq._lib
+        dt = {torch.float32: L.F32, torch.float16: L.F16, torch.bfloat16: L.BF16}[xdtype]
+        wsb = int(L.load().sbq_dyn_workspace_bytes(m, k, L.ACT_PER_TENSOR))
+        ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+        xq = torch.empty(m, k, dtype=torch.uint8, device="cuda")
+        s = torch.empty(1, device="cuda")
+        zp = torch.empty(1, dtype=torch.int32, device="cuda")
+        p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        L.call("sbq_quant_act_per_tensor", p(xs), dt, k + ld_pad, m, k, p(xq), p(s), p(zp), p(ws), wsb,
+               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        y = torch.empty(m, n, device="cuda")
+        L.call("sbq_linear_dyn", p(xs), dt, k + ld_pad, L.ACT_PER_TENSOR, p(mod.packed), p(mod.rowsum), p(mod.scale),
+               None, m, n, k, p(y), n, p(ws), wsb, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert float(s.item()) == float(rs) and int(zp.item()) == rzp
+    assert np.array_equal(xq.cpu().numpy(), rxq)
+    assert np.array_equal(_bits(y.cpu().numpy()), _bits(ry))
+    assert sbq._lib.load().sbq_check_device_error() == 0
+
+
+def test_one_launch_quantiser_repeated_and_alternating(sbq):
+    """The grid barrier's counters are reused launch after launch (and by launches of other sizes in
+    between, which take the other path or another grid size): results stay bit-identical."""
+    w = sbq.workloads.float_weight(64, 4096, seed=3)
+    mod = sbq.DynamicInt8Linear(w, None)
+    big = sbq.workloads.activation(1024, 4096, seed=4, dtype=torch.float32).cuda()  # 16 MiB: re-read path
+    mid = sbq.workloads.activation(600, 4096, seed=5, dtype=torch.float32).cuda()   # 9.4 MiB: cached
+    small = sbq.workloads.activation(40, 4096, seed=6, dtype=torch.float32).cuda()  # two-kernel path
+    want = [mod(t) for t in (big, mid, small)]
+    for _ in range(5):
+        for t, wv in zip((big, mid, small), want):
+            assert torch.equal(mod(t), wv)
+    assert sbq._lib.load().sbq_check_device_error() == 0
