@@ -91,9 +91,9 @@ __device__ __forceinline__ void convert_row(const uint8_t* w8, int row, uint32_t
     }
 }
 
-constexpr int kWCh = 128;      // output channels per CTA (MMA M, one per TMEM lane)
-constexpr int kWTok = 256;     // activation rows per CTA (MMA N)
-constexpr int kWBK = 64;       // k per stage (one 128-byte 16-bit row, one packed tile column)
+constexpr int kWCh = 128;      // output channels per CTA (one per TMEM lane)
+constexpr int kWTok = 256;     // activation rows per prefill tile (MMA N; each CTA of a pair loads half)
+constexpr int kWBK = 64;       // k per k-block (one 128-byte 16-bit row, one packed tile column)
 #ifndef SBQ_W16_ABUFS
 #define SBQ_W16_ABUFS 4
 #endif
@@ -104,189 +104,19 @@ constexpr uint32_t kWTmemCols = 512;
 constexpr uint32_t kWAccCol = 0;    // accumulator: columns [0, 256)
 constexpr uint32_t kWACol = 256;    // weight buffers: 32 columns each from 256
 
-template <int AK>
-struct W16Smem {
-    static constexpr int kX = kWTok * kWBK * 2;            // 32 KiB 16-bit activation tile
-    static constexpr int kXTiles = AK == kABF16x2 ? 2 : 1;  // high and low part of a split fp32 x
-    static constexpr int kW8 = kWCh * kWBK;                // 8 KiB int8 weight tile
-    static constexpr int kStage = kXTiles * kX + kW8;
-    static constexpr int kStages = AK == kABF16x2 ? 3 : 5;  // TMA stages
-    static constexpr int kBarOff = kStages * kStage;
-    static constexpr int kBytes = kBarOff + 256 + kWCh * 8 + 1024;
-    static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
-};
-
-template <bool OUT_F16, bool GATED, int AK>
-__global__ void __launch_bounds__(kWThreads, 1) gemm_w8a16_kernel(const __grid_constant__ CUtensorMap tmap_x,
-                                                                  const __grid_constant__ CUtensorMap tmap_x2,
-                                                                  const __grid_constant__ CUtensorMap tmap_w,
-                                                                  const GemmW16Params p) {
-    using S = W16Smem<AK>;
-    constexpr int kWStages = S::kStages;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
-    uint64_t* empty = full + kWStages;
-    uint64_t* a_full = empty + kWStages;
-    uint64_t* a_empty = a_full + kWABufs;
-    uint64_t* done = a_empty + kWABufs;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-    float* s_scale = reinterpret_cast<float*>(smem + S::kBarOff + 256);
-    float* s_bias = s_scale + kWCh;
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kWCh, t0 = blockIdx.y * kWTok;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kWStages; ++s) {
-            tc::mbar_init(&full[s], 1);
-            tc::mbar_init(&empty[s], 4 + 1);  // 4 converter warps (weight read) + MMA commit (x read)
-        }
-        for (int d = 0; d < kWABufs; ++d) {
-            tc::mbar_init(&a_full[d], 4);
-            tc::mbar_init(&a_empty[d], 1);
-        }
-        tc::mbar_init(done, 1);
-        tc::fence_mbar_init();
-        tc::prefetch_tmap(&tmap_x);
-        if (AK == kABF16x2) tc::prefetch_tmap(&tmap_x2);
-        tc::prefetch_tmap(&tmap_w);
-    }
-    if (warp == 2) {
-        tc::tmem_alloc(tmem_slot, kWTmemCols);
-        tc::tmem_relinquish();
-    }
-    for (int i = threadIdx.x; i < kWCh; i += blockDim.x) {
-        const int n = n0 + i;
-        s_scale[i] = n < p.n ? p.scale[n] : 0.0f;
-        s_bias[i] = (p.bias && n < p.n) ? p.bias[n] : 0.0f;
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    const uint32_t tmem = *tmem_slot;
-
-    if (warp == 0) {
-        if (lane == 0) {
-            for (int kb = 0; kb < p.num_kb; ++kb) {
-                const int s = kb % kWStages;
-                const uint32_t ph = (kb / kWStages) & 1;
-                if (!tc::mbar_wait(&empty[s], ph ^ 1)) break;
-                uint8_t* xs = smem + s * S::kStage;
-                tc::mbar_arrive_expect_tx(&full[s], S::kStage);
-                tc::tma_load_2d(xs, &tmap_x, &full[s], kb * kWBK, t0);
-                if (AK == kABF16x2) tc::tma_load_2d(xs + S::kX, &tmap_x2, &full[s], kb * kWBK, t0);
-                tc::tma_load_4d(xs + S::kXTiles * S::kX, &tmap_w, &full[s], 0, 0, kb, n0 / 16);
-            }
-        }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_f16(kWCh, kWTok, AK != kAF16);
-            for (int kb = 0; kb < p.num_kb; ++kb) {
-                const int s = kb % kWStages, d = kb % kWABufs;
-                const uint32_t ph = (kb / kWStages) & 1, phd = (kb / kWABufs) & 1;
-                if (!tc::mbar_wait(&full[s], ph)) break;
-                if (!tc::mbar_wait(&a_full[d], phd)) break;
-                tc::fence_after_sync();
-                const uint8_t* xs = smem + s * S::kStage;
-                const uint32_t a_col = tmem + kWACol + d * (kWBK / 2);
-#pragma unroll
-                for (int j = 0; j < kWBK / 16; ++j) {
-                    const uint64_t bd = tc::smem_desc(xs + j * 32, tc::kSwizzle128B, 1024);
-                    tc::mma_f16_ts(tmem + kWAccCol, a_col + j * 8, bd, idesc, (kb | j) != 0);
-                    if (AK == kABF16x2) {
-                        const uint64_t bl = tc::smem_desc(xs + S::kX + j * 32, tc::kSwizzle128B, 1024);
-                        tc::mma_f16_ts(tmem + kWAccCol, a_col + j * 8, bl, idesc, 1u);
-                    }
-                }
-                tc::mma_commit(&empty[s]);
-                tc::mma_commit(&a_empty[d]);
-            }
-            tc::mma_commit(done);
-        }
-    } else if (warp >= 4) {
-        const int grp = (warp - 4) >> 2;          // converter warpgroup: even (0) or odd (1) k-blocks
-        const int wq = (warp - 4) & 3;            // lanes 32 wq .. 32 wq + 31 of tensor memory
-        const int row = wq * 32 + lane;           // weight row (output channel) of this thread
-        const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
-        bool ok = true;
-        for (int kb = grp; kb < p.num_kb; kb += 2) {
-            const int s = kb % kWStages, d = kb % kWABufs;
-            const uint32_t ph = (kb / kWStages) & 1, phd = (kb / kWABufs) & 1;
-            // warp-uniform waits: tcgen05.st below is warp-collective
-            if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], ph))) { ok = false; break; }
-            if (!__all_sync(0xffffffffu, tc::mbar_wait(&a_empty[d], phd ^ 1))) { ok = false; break; }
-            tc::fence_after_sync();
-            // the int8 row: 64 bytes, 16-byte chunk c at (c ^ ((row >> 1) & 3)) (64-byte swizzle)
-            uint32_t h[32];
-            convert_row<AK>(smem + s * S::kStage + S::kXTiles * S::kX + row * 64, row, h);
-            tc::tmem_st_32x32b_x32(tmem + lane_addr + kWACol + d * (kWBK / 2), h);
-            tc::tmem_wait_st();
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) {
-                tc::mbar_arrive(&a_full[d]);
-                tc::mbar_arrive(&empty[s]);
-            }
-        }
-        // ---- epilogue: this thread's channel, 256 tokens of accumulators
-        ok = __all_sync(0xffffffffu, ok && tc::mbar_wait(done, 0));
-        tc::fence_after_sync();
-        if (ok) {
-            const int n = n0 + row;
-            const float sc = s_scale[row], bi = s_bias[row];
-            const bool has_bias = p.bias != nullptr;
-#pragma unroll 1
-            for (int c = grp * (kWTok / 64); c < (grp + 1) * (kWTok / 64); ++c) {  // this group's token half
-                uint32_t r[32];
-                tc::tmem_ld_32x32b_x32(tmem + lane_addr + kWAccCol + c * 32, r);
-                tc::tmem_wait_ld();
-                if (n >= p.n) continue;
-                const int tb = t0 + c * 32;
-                if constexpr (GATED) {
-                    // all 32 gate values are loaded before any is used (independent loads)
-                    float gv[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) gv[j] = tb + j < p.m ? load_y<OUT_F16>(p, tb + j, n) : 0.0f;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        if (tb + j >= p.m) break;
-                        float v = __fmul_rn(__uint_as_float(r[j]), sc);
-                        if (has_bias) v = __fadd_rn(v, bi);
-                        put_y<OUT_F16>(p, tb + j, n, gv[j] / (1.0f + expf(-gv[j])) * v);
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int t = tb + j;
-                        if (t >= p.m) break;
-                        float v = __fmul_rn(__uint_as_float(r[j]), sc);
-                        if (has_bias) v = __fadd_rn(v, bi);
-                        put_y<OUT_F16>(p, t, n, v);
-                    }
-                }
-            }
-        }
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    if (warp == 2) {
-        tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, kWTmemCols);
-    }
-}
-
 // ---------------------------------------------------------------------------------------------
-// CTA-pair variant of the prefill GEMM (more than 128 activation rows): a 2-CTA cluster computes a
-// 256-channel x 256-token tile with tcgen05.mma.cta_group::2 (M = 256 over both CTAs' tensor memory,
-// N = 256 over both CTAs' shared memory).  Each CTA converts its own 128 weight rows into its own
-// tensor memory and loads half of the activation tile (128 tokens), so a k-block moves 24 KiB into
-// each SM instead of 40 KiB: a per-k-block trace of the single-CTA kernel showed its converters
-// waiting ~0.6 us per k-block for the TMA data while the MMAs ran near their peak, i.e. the loop was
-// bound by the L2 -> shared-memory traffic of the activation tile each CTA re-reads.  Both CTAs'
-// activation loads complete on the leader's (rank 0's) barrier, both CTAs' converters arrive on
-// the leader's operand barrier, and the leader's MMA commits release each CTA's stage and operand
-// buffer (one commit per barrier, no multicast).  The epilogue is the single-CTA kernel's, per CTA.
+// Prefill GEMM (more than 128 activation rows), CTA pairs: a 2-CTA cluster computes a 256-channel x
+// 256-token tile with tcgen05.mma.cta_group::2 (M = 256 over both CTAs' tensor memory, N = 256 over
+// both CTAs' shared memory).  Each CTA converts its own 128 weight rows (int8 -> 16-bit, exact) into
+// its own tensor memory and loads half of the activation tile (128 tokens), so a 64-deep k-block
+// moves 24 KiB into each SM instead of the 40 KiB of a one-CTA 128 x 256 tile: a per-k-block trace
+// of that one-CTA kernel showed its converters waiting ~0.6 us per k-block for TMA data, the loop
+// bound by the L2 -> shared-memory traffic of the activation tile each CTA re-read.  Both CTAs'
+// activation loads complete on the leader's (rank 0's) barrier, both CTAs' converters arrive on the
+// leader's operand barrier, and the leader's MMA commits release each CTA's stage and operand buffer
+// (one commit per barrier, no multicast).  Roles: warp 0 TMA producer, warp 1 MMA issuer (leader),
+// warp 2 TMEM allocation, warps 4-11 two converter warpgroups (alternate k-blocks), then the
+// epilogue (each thread one channel, each warpgroup one half of the 256 tokens).
 constexpr int kPTokHalf = kWTok / 2;  // activation rows each CTA of the pair loads
 #ifndef SBQ_W16_PAIR_KH
 #define SBQ_W16_PAIR_KH 2
@@ -441,12 +271,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             const int s = kb % kStages, d = kb % S::kABufs;
             const uint32_t ph = (kb / kStages) & 1;
             // warp-uniform waits: tcgen05.st below is warp-collective.  Operand buffer d was last
-            // read by the MMAs of k-block kb - S::kABufs.
-            if (!__all_sync(0xffffffffu, tc::mbar_wait(&wfull[s], ph))) { ok = false; break; }
+            // read by the MMAs of k-block kb - kABufs; waiting for them first also guarantees that
+            // every k-block up to there was converted, so the weight stage's earlier phases are
+            // complete and its parity wait can only pass on this k-block's tile (kABufs <= kStages).
             if (kb >= S::kABufs) {
                 const int kp = kb - S::kABufs;
                 if (!__all_sync(0xffffffffu, tc::mbar_wait(&mma_done[kp % kStages], (kp / kStages) & 1))) { ok = false; break; }
             }
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&wfull[s], ph))) { ok = false; break; }
             tc::fence_after_sync();
 #pragma unroll
             for (int hh = 0; hh < S::kKH; ++hh) {
@@ -462,7 +294,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 tc::mbar_arrive(&conv_done[s]);
             }
         }
-        // ---- epilogue: this thread's channel, 256 tokens of accumulators (as gemm_w8a16_kernel)
+        // ---- epilogue: this thread's channel, 256 tokens of accumulators
         ok = __all_sync(0xffffffffu, ok && tc::mbar_wait(done, 0));
         tc::fence_after_sync();
         if (ok) {
@@ -518,20 +350,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 // shared memory in part order (deterministic), then scales and stores.  Roles as above.
 // ---------------------------------------------------------------------------------------------
 constexpr int kSTok = 64;      // activation rows per CTA (MMA N)
-constexpr uint32_t kSTmemCols = 256;  // accumulator [0, 64), six weight buffers of 32 columns from 64
+constexpr uint32_t kSTmemCols = 256;  // accumulator [0, 64), weight operand buffers from 64
 constexpr uint32_t kSACol = 64;
-constexpr int kSABufs = 6;
 constexpr int kSPad = 68;      // floats per row of the partial tile in shared memory (16-byte rows)
+#ifndef SBQ_W16_SMALL_KH
+#define SBQ_W16_SMALL_KH 2
+#endif
 
+// A pipeline block is kKH 64-deep k-blocks: the MMA thread waits twice and commits twice per block,
+// which at N = 64 (four short MMAs per 64-deep k-block) cost as much as the MMAs themselves.
 template <int AK>
 struct SmallSmem {
-    static constexpr int kX = kSTok * kWBK * 2;            // 8 KiB 16-bit activation tile
+    static constexpr int kKH = AK == kABF16x2 ? 1 : SBQ_W16_SMALL_KH;  // 64-deep k-blocks per stage
+    static constexpr int kX = kSTok * kWBK * 2;            // 8 KiB 16-bit activation tile (64 deep)
     static constexpr int kXTiles = AK == kABF16x2 ? 2 : 1;  // high and low part of a split fp32 x
-    static constexpr int kW8 = kWCh * kWBK;                // 8 KiB int8 weight tile
-    static constexpr int kStage = kXTiles * kX + kW8;
-    static constexpr int kStages = AK == kABF16x2 ? 4 : 6;  // two CTAs per SM either way
+    static constexpr int kW8 = kWCh * kWBK;                // 8 KiB int8 weight tile (64 deep)
+    static constexpr int kXStage = kKH * kXTiles * kX;
+    static constexpr int kStage = kXStage + kKH * kW8;
+    static constexpr int kStages = (96 * 1024) / kStage;   // 96 KiB ring: two CTAs per SM
     static constexpr int kBarOff = kStages * kStage;
     static constexpr int kBytes = kBarOff + 256 + kWCh * 8 + 1024;
+    static constexpr int kACols = kKH * (kWBK / 2);        // tensor-memory columns of one operand buffer
+    // operand buffers: at most the stage count, so that a converter which has seen the operand
+    // buffer of block i released (the MMA of block i - kABufs done) knows that the stage of block i
+    // has completed every earlier phase, and its parity wait on that stage cannot pass early
+    static constexpr int kABufs1 = 6 / kKH < kStages ? 6 / kKH : kStages;
+    static constexpr int kABufs = kABufs1 * kACols <= (int)(kSTmemCols - kSACol) ? kABufs1 : (int)(kSTmemCols - kSACol) / kACols;
+    static_assert(kKH >= 1 && kKH <= 2, "64 or 128 k per stage");
+    static_assert(kStages >= 2 && kABufs >= 2, "pipeline depth");
+    static_assert(2 * kStages + 2 * kABufs + 1 <= 30, "barriers fit in 256 bytes with the TMEM slot");
     static_assert(kWCh * kSPad * 4 <= kStages * kStage, "partial tile fits in the ring");
     static_assert(2 * kBytes <= 228 * 1024, "two CTAs per SM");
 };
@@ -583,8 +430,8 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
     uint64_t* empty = full + kSStages;
     uint64_t* a_full = empty + kSStages;
-    uint64_t* a_empty = a_full + kSABufs;
-    uint64_t* done = a_empty + kSABufs;
+    uint64_t* a_empty = a_full + S::kABufs;
+    uint64_t* done = a_empty + S::kABufs;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     float* s_scale = reinterpret_cast<float*>(smem + S::kBarOff + 256);
     float* s_bias = s_scale + kWCh;
@@ -600,7 +447,7 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
             tc::mbar_init(&full[s], 1);
             tc::mbar_init(&empty[s], 4 + 1);
         }
-        for (int d = 0; d < kSABufs; ++d) {
+        for (int d = 0; d < S::kABufs; ++d) {
             tc::mbar_init(&a_full[d], 4);
             tc::mbar_init(&a_empty[d], 1);
         }
@@ -633,29 +480,38 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
                 if (!tc::mbar_wait(&empty[s], ph ^ 1)) break;
                 uint8_t* xs = smem + s * S::kStage;
                 tc::mbar_arrive_expect_tx(&full[s], S::kStage);
-                tc::tma_load_2d(xs, &tmap_x, &full[s], (kb0 + i) * kWBK, t0);
-                if (AK == kABF16x2) tc::tma_load_2d(xs + S::kX, &tmap_x2, &full[s], (kb0 + i) * kWBK, t0);
-                tc::tma_load_4d(xs + S::kXTiles * S::kX, &tmap_w, &full[s], 0, 0, kb0 + i, n0 / 16);
+#pragma unroll
+                for (int h = 0; h < S::kKH; ++h) {
+                    const int kc = (kb0 + i) * S::kKH + h;  // 64-deep k column
+                    tc::tma_load_2d(xs + h * S::kXTiles * S::kX, &tmap_x, &full[s], kc * kWBK, t0);
+                    if (AK == kABF16x2)
+                        tc::tma_load_2d(xs + (h * S::kXTiles + 1) * S::kX, &tmap_x2, &full[s], kc * kWBK, t0);
+                    tc::tma_load_4d(xs + S::kXStage + h * S::kW8, &tmap_w, &full[s], 0, 0, kc, n0 / 16);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = tc::idesc_f16(kWCh, kSTok, AK != kAF16);
             for (int i = 0; i < nkb; ++i) {
-                const int s = i % kSStages, d = i % kSABufs;
-                const uint32_t ph = (i / kSStages) & 1, phd = (i / kSABufs) & 1;
+                const int s = i % kSStages, d = i % S::kABufs;
+                const uint32_t ph = (i / kSStages) & 1, phd = (i / S::kABufs) & 1;
                 if (!tc::mbar_wait(&full[s], ph)) break;
                 if (!tc::mbar_wait(&a_full[d], phd)) break;
                 tc::fence_after_sync();
                 const uint8_t* xs = smem + s * S::kStage;
-                const uint32_t a_col = tmem + kSACol + d * (kWBK / 2);
+                const uint32_t a_col = tmem + kSACol + d * S::kACols;
 #pragma unroll
-                for (int j = 0; j < kWBK / 16; ++j) {
-                    const uint64_t bd = tc::smem_desc(xs + j * 32, tc::kSwizzle128B, 1024);
-                    tc::mma_f16_ts(tmem, a_col + j * 8, bd, idesc, (i | j) != 0);
-                    if (AK == kABF16x2) {
-                        const uint64_t bl = tc::smem_desc(xs + S::kX + j * 32, tc::kSwizzle128B, 1024);
-                        tc::mma_f16_ts(tmem, a_col + j * 8, bl, idesc, 1u);
+                for (int h = 0; h < S::kKH; ++h) {
+                    const uint8_t* xh = xs + h * S::kXTiles * S::kX;
+#pragma unroll
+                    for (int j = 0; j < kWBK / 16; ++j) {
+                        const uint64_t bd = tc::smem_desc(xh + j * 32, tc::kSwizzle128B, 1024);
+                        tc::mma_f16_ts(tmem, a_col + h * (kWBK / 2) + j * 8, bd, idesc, (i | h | j) != 0);
+                        if (AK == kABF16x2) {
+                            const uint64_t bl = tc::smem_desc(xh + S::kX + j * 32, tc::kSwizzle128B, 1024);
+                            tc::mma_f16_ts(tmem, a_col + h * (kWBK / 2) + j * 8, bl, idesc, 1u);
+                        }
                     }
                 }
                 tc::mma_commit(&empty[s]);
@@ -668,34 +524,32 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
         const int wq = (warp - 4) & 3;
         const int row = wq * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
-        // each group converts two consecutive k-blocks per turn (pairs alternate between the
-        // groups): two tensor-memory stores share one wait, which halves the conversion latency
-        // per k-block (the MMA of a 64-token tile is short, so that latency sets the pace)
+        // the two groups take alternate pipeline blocks; a block's kKH tensor-memory stores share
+        // one wait (the MMA of a 64-token tile is short, so the conversion latency sets the pace)
         bool ok = true;
-        for (int i = 2 * grp; i < nkb; i += 4) {
-            const int cnt = nkb - i >= 2 ? 2 : 1;
-            uint32_t h[2][32];
+        for (int i = grp; i < nkb; i += 2) {
+            const int s = i % kSStages, d = i % S::kABufs;
+            const uint32_t ph = (i / kSStages) & 1, phd = (i / S::kABufs) & 1;
+            // operand buffer first: the MMAs of block i - kABufs are done, so every block up to
+            // there was loaded (the MMA thread waits in order) and the stage's earlier phases are
+            // complete - the parity wait below can only pass on block i's own data.  (The other
+            // group converts block i - 1; this group's previous block, i - 2, says nothing about
+            // when block i - kStages landed.)
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&a_empty[d], phd ^ 1))) { ok = false; break; }
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], ph))) { ok = false; break; }
+            tc::fence_after_sync();
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                if (u >= cnt) break;
-                const int kb = i + u, s = kb % kSStages, d = kb % kSABufs;
-                const uint32_t ph = (kb / kSStages) & 1, phd = (kb / kSABufs) & 1;
-                if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], ph))) { ok = false; break; }
-                if (!__all_sync(0xffffffffu, tc::mbar_wait(&a_empty[d], phd ^ 1))) { ok = false; break; }
-                tc::fence_after_sync();
-                convert_row<AK>(smem + s * S::kStage + S::kXTiles * S::kX + row * 64, row, h[u]);
-                tc::tmem_st_32x32b_x32(tmem + lane_addr + kSACol + d * (kWBK / 2), h[u]);
+            for (int h = 0; h < S::kKH; ++h) {
+                uint32_t hv[32];
+                convert_row<AK>(smem + s * S::kStage + S::kXStage + h * S::kW8 + row * 64, row, hv);
+                tc::tmem_st_32x32b_x32(tmem + lane_addr + kSACol + d * S::kACols + h * (kWBK / 2), hv);
             }
-            if (!ok) break;
             tc::tmem_wait_st();
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) {
-                for (int u = 0; u < cnt; ++u) {
-                    const int kb = i + u;
-                    tc::mbar_arrive(&a_full[kb % kSABufs]);
-                    tc::mbar_arrive(&empty[kb % kSStages]);
-                }
+                tc::mbar_arrive(&a_full[d]);
+                tc::mbar_arrive(&empty[s]);
             }
         }
         // ---- this thread's channel, this group's 32 tokens of accumulators
@@ -777,10 +631,6 @@ int check_linear_args(const void* x, int x_dtype, int64_t ldx, const void* packe
 using namespace sbq;
 
 constexpr int64_t kSmallMaxRows = 128;  // up to this many activation rows: the 64-token kernel
-#ifndef SBQ_W16_PAIR
-#define SBQ_W16_PAIR 1
-#endif
-constexpr bool kW16Pair = SBQ_W16_PAIR != 0;  // more rows: the CTA-pair kernel (else the single-CTA one)
 
 // SMs of the current device, cached per device (atomics: first calls may come from several threads)
 static int sm_count_w16() {
@@ -831,7 +681,7 @@ static int gemm_small(const CUtensorMap& mx, const CUtensorMap& mx2, const CUten
     p.m = (int)m;
     p.n = (int)n;
     p.k = (int)k;
-    p.num_kb = (int)ceil_div(k, kWBK);
+    p.num_kb = (int)ceil_div(k, kWBK * SmallSmem<AK>::kKH);  // pipeline blocks; k past the end reads zeros
     p.scale = scale;
     p.bias = bias;
     p.y = y;
@@ -859,14 +709,6 @@ static int gemm_small(const CUtensorMap& mx, const CUtensorMap& mx2, const CUten
                                              : launch_small<false, AK>(cfg, mx, mx2, mw, p);
     if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "gemm_w8a16 (small batch) launch: %s", cudaGetErrorString(e));
     return check_launch("gemm_w8a16_small");
-}
-
-template <bool OUT_F16, bool GATED, int AK>
-static void launch_large(dim3 grid, cudaStream_t s, const CUtensorMap& mx, const CUtensorMap& mx2,
-                         const CUtensorMap& mw, const GemmW16Params& p) {
-    constexpr int smem = W16Smem<AK>::kBytes;
-    cudaFuncSetAttribute(gemm_w8a16_kernel<OUT_F16, GATED, AK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    gemm_w8a16_kernel<OUT_F16, GATED, AK><<<grid, kWThreads, smem, s>>>(mx, mx2, mw, p);
 }
 
 template <bool OUT_F16, bool GATED, int AK>
@@ -903,35 +745,10 @@ static int gemm_pair(const CUtensorMap& mx, const CUtensorMap& mx2, const CUtens
 }
 
 template <int AK>
-static int gemm_large(const CUtensorMap& mx, const CUtensorMap& mx2, const CUtensorMap& mw, const float* scale,
-                      const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
-                      int gated) {
-    GemmW16Params p{};
-    p.gated = gated;
-    p.m = (int)m;
-    p.n = (int)n;
-    p.k = (int)k;
-    p.num_kb = (int)ceil_div(k, kWBK);
-    p.scale = scale;
-    p.bias = bias;
-    p.y = y;
-    p.ldy = ldy;
-    const dim3 grid((unsigned)ceil_div(n, kWCh), (unsigned)ceil_div(m, kWTok));
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (y_dtype == SBQ_F16) {
-        gated ? launch_large<true, true, AK>(grid, s, mx, mx2, mw, p) : launch_large<true, false, AK>(grid, s, mx, mx2, mw, p);
-    } else {
-        gated ? launch_large<false, true, AK>(grid, s, mx, mx2, mw, p) : launch_large<false, false, AK>(grid, s, mx, mx2, mw, p);
-    }
-    return check_launch("gemm_w8a16");
-}
-
-// Both tile sizes for one activation kind; x2: the low part of a split fp32 activation (kABF16x2).
-template <int AK>
 static int gemm_run_ak(const void* x, const void* x2, int64_t ldx, const void* packed, const float* scale,
                        const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
                        int gated) {
-    const int rows = m <= kSmallMaxRows ? kSTok : (kW16Pair ? kPTokHalf : kWTok);
+    const int rows = m <= kSmallMaxRows ? kSTok : kPTokHalf;
     CUtensorMap mx, mx2, mw;
     int st = make_x_map(&mx, AK, x, ldx, m, k, rows);
     if (st) return st;
@@ -944,8 +761,7 @@ static int gemm_run_ak(const void* x, const void* x2, int64_t ldx, const void* p
     st = make_w_map(&mw, packed, n, k);
     if (st) return st;
     if (m <= kSmallMaxRows) return gemm_small<AK>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
-    if (kW16Pair) return gemm_pair<AK>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
-    return gemm_large<AK>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
+    return gemm_pair<AK>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
 }
 
 // ---- fp32 activation split: x = hi + lo, both bf16 -------------------------------------------------
