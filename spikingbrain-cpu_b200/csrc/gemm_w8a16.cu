@@ -344,15 +344,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 
 // ---------------------------------------------------------------------------------------------
 // Small-batch variant (17..128 activation rows, e.g. batched decode): 128-channel x 64-token tiles,
-// 6-stage TMA ring (2 CTAs per SM), and split-K over a thread-block cluster when the tiles alone
-// cannot fill the GPU: the S CTAs of a cluster (one K part each) keep their fp32 partial tile in
-// shared memory and each reduces 1/S of the channels by reading all S partials through distributed
-// shared memory in part order (deterministic), then scales and stores.  Roles as above.
+// a 96 KiB TMA ring (2 CTAs per SM), and split-K over a thread-block cluster when the tiles alone
+// cannot fill the GPU: the S CTAs of a cluster (one K part each) push their fp32 partial sums into
+// the shared memory of the CTA owning each channel (1/S of the channels per CTA) through distributed
+// shared memory, and each CTA reduces its share in part order (deterministic), then scales and
+// stores.  Roles as in the prefill kernel (one CTA, no pair).
 // ---------------------------------------------------------------------------------------------
 constexpr int kSTok = 64;      // activation rows per CTA (MMA N)
 constexpr uint32_t kSTmemCols = 256;  // accumulator [0, 64), weight operand buffers from 64
 constexpr uint32_t kSACol = 64;
-constexpr int kSPad = 68;      // floats per row of the partial tile in shared memory (16-byte rows)
 #ifndef SBQ_W16_SMALL_KH
 #define SBQ_W16_SMALL_KH 2
 #endif
@@ -379,7 +379,9 @@ struct SmallSmem {
     static_assert(kKH >= 1 && kKH <= 2, "64 or 128 k per stage");
     static_assert(kStages >= 2 && kABufs >= 2, "pipeline depth");
     static_assert(2 * kStages + 2 * kABufs + 1 <= 30, "barriers fit in 256 bytes with the TMEM slot");
-    static_assert(kWCh * kSPad * 4 <= kStages * kStage, "partial tile fits in the ring");
+    // split-K receive buffer: [parts][64 tokens][rs] floats, rs = ceil(128 / parts) rounded up to
+    // 4: at most 6 x 64 x 24 floats (parts = 6) for parts <= 8
+    static_assert(6 * kSTok * 24 * 4 <= kStages * kStage, "receive buffer fits in the ring");
     static_assert(2 * kBytes <= 228 * 1024, "two CTAs per SM");
 };
 
@@ -409,6 +411,16 @@ __device__ __forceinline__ uint32_t dsmem_map(uint32_t a, uint32_t rank) {
     return r;
 }
 
+__device__ __forceinline__ void st_dsmem(uint32_t cluster_addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_dsmem4(uint32_t cluster_addr, float4 v) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(cluster_addr), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w)
+                 : "memory");
+}
+
 __device__ __forceinline__ float4 ld_dsmem4(uint32_t cluster_addr) {
     float4 v;
     asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
@@ -435,7 +447,7 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     float* s_scale = reinterpret_cast<float*>(smem + S::kBarOff + 256);
     float* s_bias = s_scale + kWCh;
-    float* part_tile = reinterpret_cast<float*>(smem);  // [128][kSPad], after the main loop
+    float* recv = reinterpret_cast<float*>(smem);  // split-K receive buffer, after the main loop
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kWCh, t0 = blockIdx.y * kSTok;
@@ -471,6 +483,7 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
     const int nkb = kb1 - kb0;
+    uint32_t r[32];  // a converter thread's accumulators after the main loop (split-K partial sums)
 
     if (warp == 0) {
         if (lane == 0) {
@@ -555,7 +568,6 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
         // ---- this thread's channel, this group's 32 tokens of accumulators
         ok = __all_sync(0xffffffffu, ok && tc::mbar_wait(done, 0));
         tc::fence_after_sync();
-        uint32_t r[32];
         tc::tmem_ld_32x32b_x32(tmem + lane_addr + grp * 32, r);
         tc::tmem_wait_ld();
         if (!ok) {
@@ -575,43 +587,52 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
                     store_y<OUT_F16>(p, t, n, v);
                 }
             }
-        } else {
-            // the ring is idle (every stage consumed): keep the raw partial tile there
-#pragma unroll
-            for (int j = 0; j < 32; ++j) part_tile[row * kSPad + grp * 32 + j] = __uint_as_float(r[j]);
         }
     }
     if (p.parts > 1) {
-        // every part's partial tile is in its CTA's shared memory; this CTA reduces its share of
-        // the channels over all parts, in part order: four tokens per load, all parts' loads issued
-        // before the sum
+        // split K.  (1) Every CTA of the cluster has finished its main loop, so every ring is free.
+        // (2) Each converter thread pushes its 32 partial sums into the shared memory of the CTA
+        // that owns its channel, token-major: recv[part][token][row - r0] (row stride rs), so the 32
+        // lanes of a warp (32 consecutive channels) store 128 contiguous bytes per token - remote
+        // stores of scattered 16-byte pieces ran at ~17 GB/s per SM.  (3) Once all have landed,
+        // each CTA reduces its channel share in part order (a fixed order: deterministic), scales
+        // and stores.  Every thread takes both cluster barriers.
+        cluster_sync_all();
+        const int share = (kWCh + p.parts - 1) / p.parts, rs = (share + 3) & ~3;
+        if (warp >= 4) {
+            const int row = ((warp - 4) & 3) * 32 + lane, grp = (warp - 4) >> 2;
+            int q = 0;
+            while (q + 1 < p.parts && (q + 1) * kWCh / p.parts <= row) ++q;
+            const int qr0 = q * kWCh / p.parts;
+            const uint32_t dst =
+                dsmem_map(tc::smem_u32(recv + ((part * kSTok + grp * 32) * rs + row - qr0)), (uint32_t)q);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) st_dsmem(dst + (uint32_t)(j * rs * 4), __uint_as_float(r[j]));
+        }
         cluster_sync_all();
         const int r0 = part * kWCh / p.parts, r1 = (part + 1) * kWCh / p.parts, nr = r1 - r0;
-        for (int e = threadIdx.x; e < nr * (kSTok / 4); e += blockDim.x) {
-            const int row = r0 + e % nr, tq = (e / nr) * 4;
-            const uint32_t a = tc::smem_u32(part_tile + row * kSPad + tq);
-            float4 v[8];
+        const int nq = (nr + 3) / 4;  // row quads of this CTA's share (the last may be partial)
+        for (int e = threadIdx.x; e < nq * kSTok; e += blockDim.x) {
+            const int rq = (e % nq) * 4, t = e / nq;  // 4 channels x 1 token: y stores along channels
+            if (t0 + t >= p.m) continue;
+            float4 acc = *reinterpret_cast<const float4*>(recv + t * rs + rq);
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-                if (q < p.parts) v[q] = ld_dsmem4(dsmem_map(a, (uint32_t)q));
-            float4 acc = v[0];
-#pragma unroll
-            for (int q = 1; q < 8; ++q)
-                if (q < p.parts) acc.x += v[q].x, acc.y += v[q].y, acc.z += v[q].z, acc.w += v[q].w;
-            const int n = n0 + row;
-            if (n >= p.n) continue;
-            const float sc = s_scale[row], bi = s_bias[row];
-            const float r4[4] = {acc.x, acc.y, acc.z, acc.w};
+            for (int q = 1; q < 8; ++q) {
+                if (q < p.parts) {
+                    const float4 v = *reinterpret_cast<const float4*>(recv + ((q * kSTok + t) * rs + rq));
+                    acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+                }
+            }
+            const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const int t = t0 + tq + j;
-                if (t >= p.m) break;
-                float o = __fmul_rn(r4[j], sc);
-                if (p.bias) o = __fadd_rn(o, bi);
-                store_y<OUT_F16>(p, t, n, o);
+                const int row = r0 + rq + j, n = n0 + row;
+                if (rq + j >= nr || n >= p.n) break;
+                float o = __fmul_rn(a4[j], s_scale[row]);
+                if (p.bias) o = __fadd_rn(o, s_bias[row]);
+                store_y<OUT_F16>(p, t0 + t, n, o);
             }
         }
-        cluster_sync_all();  // no CTA leaves while another may still read its shared memory
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -672,6 +693,39 @@ static cudaError_t launch_small(const cudaLaunchConfig_t& cfg, const CUtensorMap
     return cudaLaunchKernelEx(&cfg, gemm_w8a16_small_kernel<OUT_F16, AK>, mx, mx2, mw, p);
 }
 
+// Clusters of `size` small-batch CTAs the device keeps resident at once (cached per device and kernel
+// variant).  Clusters must fit inside one GPC, so this is well below SMs * 2 / size for the larger
+// sizes: 15 clusters of 8 on a B200 at this kernel's 100 KiB of shared memory (ncu launch
+// statistics), i.e. 120 of the 296 CTA slots.
+template <bool OUT_F16, int AK>
+static int small_max_clusters(int size) {
+    static std::atomic<int> cache[64][9] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || size < 1 || size > 8) return 1;
+    int c = cache[dev][size].load(std::memory_order_relaxed);
+    if (c == 0) {
+        auto kernel = gemm_w8a16_small_kernel<OUT_F16, AK>;
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SmallSmem<AK>::kBytes);
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(1, 1, (unsigned)size);
+        cfg.blockDim = dim3(kWThreads);
+        cfg.dynamicSmemBytes = SmallSmem<AK>::kBytes;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = (unsigned)size;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&c, kernel, &cfg) != cudaSuccess || c < 1) {
+            cudaGetLastError();
+            c = 1;
+        }
+        cache[dev][size].store(c, std::memory_order_relaxed);
+    }
+    return c;
+}
+
 template <int AK>
 static int gemm_small(const CUtensorMap& mx, const CUtensorMap& mx2, const CUtensorMap& mw, const float* scale,
                       const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
@@ -686,12 +740,20 @@ static int gemm_small(const CUtensorMap& mx, const CUtensorMap& mx2, const CUten
     p.bias = bias;
     p.y = y;
     p.ldy = ldy;
-    // K parts per tile: as many as fill the GPU's CTA slots (2 per SM) once, at most 8 (a portable
-    // cluster) and at least 2 k-blocks each
+    // K parts per tile (the cluster size, at most 8, at least 2 pipeline blocks each): the count with
+    // the least estimated time, waves of resident clusters x blocks per part.  Filling every CTA slot
+    // with large clusters does not pay: fewer of them fit at once (see small_max_clusters).
     const int tiles = (int)(ceil_div(n, kWCh) * ceil_div(m, kSTok));
-    int parts = 2 * sm_count_w16() / tiles;
-    parts = parts < 1 ? 1 : (parts > 8 ? 8 : parts);
-    while (parts > 1 && p.num_kb / parts < 2) --parts;
+    const bool f16 = y_dtype == SBQ_F16;
+    int parts = 1;
+    int64_t best = -1;
+    for (int q = 1; q <= 8; ++q) {
+        if (q > 1 && p.num_kb / q < 2) break;
+        const int fit = f16 ? small_max_clusters<true, AK>(q) : small_max_clusters<false, AK>(q);
+        const int64_t waves = ceil_div(tiles, fit);
+        const int64_t cost = waves * ceil_div(p.num_kb, q);
+        if (best < 0 || cost <= best) best = cost, parts = q;  // ties: more CTAs streaming
+    }
     p.parts = parts;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)ceil_div(n, kWCh), (unsigned)ceil_div(m, kSTok), (unsigned)parts);
