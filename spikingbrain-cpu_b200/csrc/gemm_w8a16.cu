@@ -178,6 +178,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const bool leader = rank == 0;
     const int n0 = (blockIdx.x >> 1) * (2 * kWCh) + (int)rank * kWCh;  // this CTA's 128 channels
     const int t0 = blockIdx.y * kWTok;                                  // the pair's 256 tokens
+    // the next launch on the stream may start its prologue (and weight tiles) now; it waits for
+    // this grid before it touches activations or outputs
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -209,25 +212,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            for (int kb = 0; kb < p.num_kb; ++kb) {
+            // weight tiles of the first stages before griddepcontrol.wait (launched as a programmatic
+            // dependent, the previous kernel may still run: it writes activations, never weights),
+            // activation tiles after it
+            const int tr = t0 + (int)rank * kPTokHalf;
+            auto load_w = [&](int kb) {
                 const int s = kb % kStages;
-                const uint32_t ph = (kb / kStages) & 1;
-                if (!tc::mbar_wait(&conv_done[s], ph ^ 1)) break;
-                if (!tc::mbar_wait(&mma_done[s], ph ^ 1)) break;
-                uint8_t* xs = smem + s * S::kStage;
-                uint8_t* ws = xs + S::kXStage;
+                uint8_t* ws = smem + s * S::kStage + S::kXStage;
                 tc::mbar_arrive_expect_tx(&wfull[s], S::kKH * S::kW8Sub);
+#pragma unroll
+                for (int h = 0; h < S::kKH; ++h)
+                    tc::tma_load_4d(ws + h * S::kW8Sub, &tmap_w, &wfull[s], 0, 0, kb * S::kKH + h, n0 / 16);
+            };
+            auto load_x = [&](int kb) {
+                const int s = kb % kStages;
+                uint8_t* xs = smem + s * S::kStage;
                 const uint32_t xb = tc::cluster_addr(&xfull[s], 0);
                 if (leader) tc::mbar_arrive_expect_tx(&xfull[s], 2 * S::kXStage);
-                const int tr = t0 + (int)rank * kPTokHalf;
 #pragma unroll
                 for (int h = 0; h < S::kKH; ++h) {
                     const int kc = kb * S::kKH + h;  // 64-wide k column
-                    tc::tma_load_4d(ws + h * S::kW8Sub, &tmap_w, &wfull[s], 0, 0, kc, n0 / 16);
                     tc::tma_load_2d_pair(xs + h * S::kXTiles * S::kXSub, &tmap_x, xb, kc * kWBK, tr);
                     if (AK == kABF16x2)
                         tc::tma_load_2d_pair(xs + (h * S::kXTiles + 1) * S::kXSub, &tmap_x2, xb, kc * kWBK, tr);
                 }
+            };
+            const int pre = p.num_kb < kStages ? p.num_kb : kStages;
+            for (int kb = 0; kb < pre; ++kb) load_w(kb);
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            for (int kb = 0; kb < pre; ++kb) load_x(kb);
+            for (int kb = pre; kb < p.num_kb; ++kb) {
+                const int s = kb % kStages;
+                const uint32_t ph = (kb / kStages) & 1;
+                if (!tc::mbar_wait(&conv_done[s], ph ^ 1)) break;
+                if (!tc::mbar_wait(&mma_done[s], ph ^ 1)) break;
+                load_w(kb);
+                load_x(kb);
             }
         }
     } else if (warp == 1) {
@@ -297,6 +317,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         // ---- epilogue: this thread's channel, 256 tokens of accumulators
         ok = __all_sync(0xffffffffu, ok && tc::mbar_wait(done, 0));
         tc::fence_after_sync();
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // y may be read (gated) or written from here
         if (ok) {
             const int n = n0 + row;
             const float sc = s_scale[row], bi = s_bias[row];
@@ -453,6 +474,9 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
     const int n0 = blockIdx.x * kWCh, t0 = blockIdx.y * kSTok;
     const int part = p.parts > 1 ? (int)cluster_rank() : 0;
     const int kb0 = part * p.num_kb / p.parts, kb1 = (part + 1) * p.num_kb / p.parts;
+    // the next launch on the stream may start its prologue (and weight tiles) now; it waits for
+    // this grid before it touches activations or outputs
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSStages; ++s) {
@@ -487,20 +511,40 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
 
     if (warp == 0) {
         if (lane == 0) {
-            for (int i = 0; i < nkb; ++i) {
-                const int s = i % kSStages;
-                const uint32_t ph = (i / kSStages) & 1;
-                if (!tc::mbar_wait(&empty[s], ph ^ 1)) break;
-                uint8_t* xs = smem + s * S::kStage;
-                tc::mbar_arrive_expect_tx(&full[s], S::kStage);
+            // weight tiles of the first stages before griddepcontrol.wait (launched as a programmatic
+            // dependent, the previous kernel may still run: it writes activations, never weights),
+            // activation tiles after it
+            auto load_x = [&](int i) {
+                uint8_t* xs = smem + (i % kSStages) * S::kStage;
 #pragma unroll
                 for (int h = 0; h < S::kKH; ++h) {
                     const int kc = (kb0 + i) * S::kKH + h;  // 64-deep k column
-                    tc::tma_load_2d(xs + h * S::kXTiles * S::kX, &tmap_x, &full[s], kc * kWBK, t0);
+                    tc::tma_load_2d(xs + h * S::kXTiles * S::kX, &tmap_x, &full[i % kSStages], kc * kWBK, t0);
                     if (AK == kABF16x2)
-                        tc::tma_load_2d(xs + (h * S::kXTiles + 1) * S::kX, &tmap_x2, &full[s], kc * kWBK, t0);
-                    tc::tma_load_4d(xs + S::kXStage + h * S::kW8, &tmap_w, &full[s], 0, 0, kc, n0 / 16);
+                        tc::tma_load_2d(xs + (h * S::kXTiles + 1) * S::kX, &tmap_x2, &full[i % kSStages], kc * kWBK, t0);
                 }
+            };
+            auto load_w = [&](int i) {
+                uint8_t* xs = smem + (i % kSStages) * S::kStage;
+#pragma unroll
+                for (int h = 0; h < S::kKH; ++h)
+                    tc::tma_load_4d(xs + S::kXStage + h * S::kW8, &tmap_w, &full[i % kSStages], 0, 0,
+                                    (kb0 + i) * S::kKH + h, n0 / 16);
+            };
+            const int pre = nkb < kSStages ? nkb : kSStages;
+            for (int i = 0; i < pre; ++i) {
+                tc::mbar_arrive_expect_tx(&full[i], S::kStage);
+                load_w(i);
+            }
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            for (int i = 0; i < pre; ++i) load_x(i);
+            for (int i = pre; i < nkb; ++i) {
+                const int s = i % kSStages;
+                const uint32_t ph = (i / kSStages) & 1;
+                if (!tc::mbar_wait(&empty[s], ph ^ 1)) break;
+                tc::mbar_arrive_expect_tx(&full[s], S::kStage);
+                load_x(i);
+                load_w(i);
             }
         }
     } else if (warp == 1) {
@@ -568,6 +612,7 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
         // ---- this thread's channel, this group's 32 tokens of accumulators
         ok = __all_sync(0xffffffffu, ok && tc::mbar_wait(done, 0));
         tc::fence_after_sync();
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // y may be read (gated) or written from here
         tc::tmem_ld_32x32b_x32(tmem + lane_addr + grp * 32, r);
         tc::tmem_wait_ld();
         if (!ok) {
@@ -610,6 +655,7 @@ __global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __
             for (int j = 0; j < 32; ++j) st_dsmem(dst + (uint32_t)(j * rs * 4), __uint_as_float(r[j]));
         }
         cluster_sync_all();
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // y is read (gated) or written below
         const int r0 = part * kWCh / p.parts, r1 = (part + 1) * kWCh / p.parts, nr = r1 - r0;
         const int nq = (nr + 3) / 4;  // row quads of this CTA's share (the last may be partial)
         for (int e = threadIdx.x; e < nq * kSTok; e += blockDim.x) {
@@ -760,25 +806,42 @@ static int gemm_small(const CUtensorMap& mx, const CUtensorMap& mx2, const CUten
     cfg.blockDim = dim3(kWThreads);
     cfg.dynamicSmemBytes = SmallSmem<AK>::kBytes;
     cfg.stream = static_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = (unsigned)parts;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // as the prefill kernel (launch_pair)
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     const cudaError_t e = y_dtype == SBQ_F16 ? launch_small<true, AK>(cfg, mx, mx2, mw, p)
                                              : launch_small<false, AK>(cfg, mx, mx2, mw, p);
     if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "gemm_w8a16 (small batch) launch: %s", cudaGetErrorString(e));
     return check_launch("gemm_w8a16_small");
 }
 
+// Both GEMMs launch as programmatic dependents of the previous kernel on the stream: they set up,
+// request their first weight tiles and convert them before griddepcontrol.wait, and touch
+// activations and outputs only after it.  Only kernels that call griddepcontrol.launch_dependents
+// let a dependent start early, and in this library those write activations only (never packed
+// weights, scales or biases); any other predecessor completes first, as in plain stream order.
 template <bool OUT_F16, bool GATED, int AK>
-static void launch_pair(dim3 grid, cudaStream_t s, const CUtensorMap& mx, const CUtensorMap& mx2,
-                        const CUtensorMap& mw, const GemmW16Params& p) {
+static cudaError_t launch_pair(dim3 grid, cudaStream_t s, const CUtensorMap& mx, const CUtensorMap& mx2,
+                               const CUtensorMap& mw, const GemmW16Params& p) {
     constexpr int smem = PairSmem<AK>::kBytes;
     cudaFuncSetAttribute(gemm_w8a16_pair_kernel<OUT_F16, GATED, AK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    gemm_w8a16_pair_kernel<OUT_F16, GATED, AK><<<grid, kPThreads, smem, s>>>(mx, mx2, mw, p);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_w8a16_pair_kernel<OUT_F16, GATED, AK>, mx, mx2, mw, p);
 }
 
 // The CTA-pair kernel over 256-channel x 256-token tiles (clusters of two CTAs along x).
@@ -798,11 +861,13 @@ static int gemm_pair(const CUtensorMap& mx, const CUtensorMap& mx2, const CUtens
     p.ldy = ldy;
     const dim3 grid((unsigned)(2 * ceil_div(n, 2 * kWCh)), (unsigned)ceil_div(m, kWTok));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
     if (y_dtype == SBQ_F16) {
-        gated ? launch_pair<true, true, AK>(grid, s, mx, mx2, mw, p) : launch_pair<true, false, AK>(grid, s, mx, mx2, mw, p);
+        e = gated ? launch_pair<true, true, AK>(grid, s, mx, mx2, mw, p) : launch_pair<true, false, AK>(grid, s, mx, mx2, mw, p);
     } else {
-        gated ? launch_pair<false, true, AK>(grid, s, mx, mx2, mw, p) : launch_pair<false, false, AK>(grid, s, mx, mx2, mw, p);
+        e = gated ? launch_pair<false, true, AK>(grid, s, mx, mx2, mw, p) : launch_pair<false, false, AK>(grid, s, mx, mx2, mw, p);
     }
+    if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "gemm_w8a16 (CTA pairs) launch: %s", cudaGetErrorString(e));
     return check_launch("gemm_w8a16 (CTA pairs)");
 }
 
