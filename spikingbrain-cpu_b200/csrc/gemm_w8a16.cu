@@ -377,6 +377,10 @@ constexpr uint32_t kSACol = 64;
 #ifndef SBQ_W16_SMALL_KH
 #define SBQ_W16_SMALL_KH 2
 #endif
+#ifndef SBQ_W16_SMALL_RING_KB
+#define SBQ_W16_SMALL_RING_KB 96
+#endif
+constexpr int kSmallCtasPerSm = SBQ_W16_SMALL_RING_KB <= 100 ? 2 : 1;
 
 // A pipeline block is kKH 64-deep k-blocks: the MMA thread waits twice and commits twice per block,
 // which at N = 64 (four short MMAs per 64-deep k-block) cost as much as the MMAs themselves.
@@ -388,7 +392,7 @@ struct SmallSmem {
     static constexpr int kW8 = kWCh * kWBK;                // 8 KiB int8 weight tile (64 deep)
     static constexpr int kXStage = kKH * kXTiles * kX;
     static constexpr int kStage = kXStage + kKH * kW8;
-    static constexpr int kStages = (96 * 1024) / kStage;   // 96 KiB ring: two CTAs per SM
+    static constexpr int kStages = (SBQ_W16_SMALL_RING_KB * 1024) / kStage;
     static constexpr int kBarOff = kStages * kStage;
     static constexpr int kBytes = kBarOff + 256 + kWCh * 8 + 1024;
     static constexpr int kACols = kKH * (kWBK / 2);        // tensor-memory columns of one operand buffer
@@ -403,7 +407,7 @@ struct SmallSmem {
     // split-K receive buffer: [parts][64 tokens][rs] floats, rs = ceil(128 / parts) rounded up to
     // 4: at most 6 x 64 x 24 floats (parts = 6) for parts <= 8
     static_assert(6 * kSTok * 24 * 4 <= kStages * kStage, "receive buffer fits in the ring");
-    static_assert(2 * kBytes <= 228 * 1024, "two CTAs per SM");
+    static_assert(kSmallCtasPerSm * kBytes <= 228 * 1024, "CTAs per SM");
 };
 
 struct GemmSmallParams {
@@ -452,7 +456,7 @@ __device__ __forceinline__ float4 ld_dsmem4(uint32_t cluster_addr) {
 }
 
 template <bool OUT_F16, int AK>
-__global__ void __launch_bounds__(kWThreads, 2) gemm_w8a16_small_kernel(const __grid_constant__ CUtensorMap tmap_x,
+__global__ void __launch_bounds__(kWThreads, kSmallCtasPerSm) gemm_w8a16_small_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                                         const __grid_constant__ CUtensorMap tmap_x2,
                                                                         const __grid_constant__ CUtensorMap tmap_w,
                                                                         const GemmSmallParams p) {
