@@ -743,39 +743,6 @@ static cudaError_t launch_small(const cudaLaunchConfig_t& cfg, const CUtensorMap
     return cudaLaunchKernelEx(&cfg, gemm_w8a16_small_kernel<OUT_F16, AK>, mx, mx2, mw, p);
 }
 
-// Clusters of `size` small-batch CTAs the device keeps resident at once (cached per device and kernel
-// variant).  Clusters must fit inside one GPC, so this is well below SMs * 2 / size for the larger
-// sizes: 15 clusters of 8 on a B200 at this kernel's 100 KiB of shared memory (ncu launch
-// statistics), i.e. 120 of the 296 CTA slots.
-template <bool OUT_F16, int AK>
-static int small_max_clusters(int size) {
-    static std::atomic<int> cache[64][9] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || size < 1 || size > 8) return 1;
-    int c = cache[dev][size].load(std::memory_order_relaxed);
-    if (c == 0) {
-        auto kernel = gemm_w8a16_small_kernel<OUT_F16, AK>;
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SmallSmem<AK>::kBytes);
-        cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3(1, 1, (unsigned)size);
-        cfg.blockDim = dim3(kWThreads);
-        cfg.dynamicSmemBytes = SmallSmem<AK>::kBytes;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = (unsigned)size;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&c, kernel, &cfg) != cudaSuccess || c < 1) {
-            cudaGetLastError();
-            c = 1;
-        }
-        cache[dev][size].store(c, std::memory_order_relaxed);
-    }
-    return c;
-}
-
 template <int AK>
 static int gemm_small(const CUtensorMap& mx, const CUtensorMap& mx2, const CUtensorMap& mw, const float* scale,
                       const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
@@ -790,20 +757,22 @@ static int gemm_small(const CUtensorMap& mx, const CUtensorMap& mx2, const CUten
     p.bias = bias;
     p.y = y;
     p.ldy = ldy;
-    // K parts per tile (the cluster size, at most 8, at least 2 pipeline blocks each): the count with
-    // the least estimated time, waves of resident clusters x blocks per part.  Filling every CTA slot
-    // with large clusters does not pay: fewer of them fit at once (see small_max_clusters).
+    // K parts per tile (the cluster size): the largest power of two up to 8 that keeps the grid within
+    // ~7/8 of the CTA slots (two per SM) and gives every part at least 2 pipeline blocks.  Measured on
+    // B200 (20 calls per CUDA graph, us; the chosen count marked):
+    //   m x n x k          tiles  parts=1    2      4      8
+    //   64 x 4096 x 4096     32    20.9   14.2   12.0  *10.8
+    //   64 x 12288 x 4096    96    23.6  *17.8   21.5   31.4
+    //   64 x 4096 x 12288    32    56.8   33.4   22.1  *19.0
+    //   128 x 4096 x 4096    64    22.3   16.9  *12.9   21.0
+    //   100 x 2560 x 2560    40    14.3   12.2  *10.3   15.6
+    // (cluster sizes 3 and 6 were never better).  Larger grids leave clusters waiting for a second
+    // wave: a cluster needs all its CTAs resident in one GPC at once.
     const int tiles = (int)(ceil_div(n, kWCh) * ceil_div(m, kSTok));
-    const bool f16 = y_dtype == SBQ_F16;
+    const int slots = 2 * sm_count_w16();
     int parts = 1;
-    int64_t best = -1;
-    for (int q = 1; q <= 8; ++q) {
-        if (q > 1 && p.num_kb / q < 2) break;
-        const int fit = f16 ? small_max_clusters<true, AK>(q) : small_max_clusters<false, AK>(q);
-        const int64_t waves = ceil_div(tiles, fit);
-        const int64_t cost = waves * ceil_div(p.num_kb, q);
-        if (best < 0 || cost <= best) best = cost, parts = q;  // ties: more CTAs streaming
-    }
+    while (parts < 8 && (int64_t)tiles * (2 * parts) * 8 <= (int64_t)slots * 7 && p.num_kb / (2 * parts) >= 2)
+        parts *= 2;
     p.parts = parts;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)ceil_div(n, kWCh), (unsigned)ceil_div(m, kSTok), (unsigned)parts);
