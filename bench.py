@@ -149,6 +149,8 @@ def dist_setup(args):
     if world > 1:
         import datetime
 
+        # keep stdout to the one JSON line (NCCL prints its version banner there at VERSION level)
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
