@@ -533,6 +533,7 @@ struct GemmI8Params {
     int tma_y;              // y is written by TMA stores through tmap_y (no acc_out, aligned rows)
     int vec_y;              // y (and acc_out) rows take 16-byte vector stores: both base pointers 16-byte
                             // aligned, ldy and n multiples of 4; otherwise the epilogue stores element-wise
+    int parts;              // K parts of the single-CTA kernel (a cluster along z; 1 = no split)
 };
 
 constexpr int kI8BM = 128;         // rows of xq per tile (MMA M)
@@ -553,6 +554,7 @@ struct I8Smem {
     static constexpr int kTail = 256 /* barriers */ + BN * 5 * 4;  // scale, bias, rowsum, s*scale, zp*rowsum
     static constexpr int kBytes = kRing + 1024 /* alignment */ + kTail;
     static_assert((BN / 32) * kI8SlotBytes <= kRing, "epilogue staging fits in the ring");
+    static_assert(BN * kI8BM * 4 <= kRing, "split-K receive buffer fits in the ring");
     static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
 };
 
@@ -671,6 +673,63 @@ __device__ __forceinline__ void i8_epilogue(const GemmI8Params& p, const CUtenso
     if (p.tma_y && lane == 0) tc::bulk_wait_all_read();  // the staged blocks stay in use until read
 }
 
+// Split-K epilogue of the single-CTA kernel (one 128-row xq tile, K cut over a cluster of p.parts
+// CTAs along z).  (1) A cluster barrier: every CTA's main loop is done, so every ring is free.  (2)
+// Each warp whose 32 xq rows include valid ones pushes its int32 partial sums into the shared memory
+// of the CTA owning each channel (BN / parts channels per CTA), column-major recv[part][channel][row]
+// so that a warp (32 consecutive rows) stores 128 contiguous bytes per channel.  (3) A cluster
+// barrier, then each CTA adds the parts of its channels in part order - integer sums, so the result
+// equals the unsplit kernel's bit for bit - and applies the epilogue arithmetic of i8_epilogue.
+template <int BN>
+__device__ __forceinline__ void i8_splitk_epilogue(const GemmI8Params& p, uint8_t* smem, uint64_t* done,
+                                                   int* abort_flag, const float* s_scale, const float* s_bias,
+                                                   const float* s_f, const int32_t* s_zr, uint32_t tmem, int m0,
+                                                   int n0, int part) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = warp & 3, h = warp >> 2;
+    const int share = BN / p.parts;
+    int32_t* recv = reinterpret_cast<int32_t*>(smem);  // [parts][share][kI8BM]
+    int waited = 1;
+    if (lane == 0) waited = tc::mbar_wait_backoff(done, 0) && !*(volatile int*)abort_flag;
+    const bool ok = __shfl_sync(0xffffffffu, waited, 0) != 0;
+    tc::fence_after_sync();
+    tc::cluster_sync();
+    if (m0 + g * 32 < p.m) {
+        const uint32_t lane_base = tmem + ((uint32_t)(g * 32) << 16);
+        const int row = g * 32 + lane;
+#pragma unroll 1
+        for (int b = h; b < BN / 32; b += 2) {
+            uint32_t r[32];
+            tc::tmem_ld_32x32b_x32(lane_base + b * 32, r);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int c = b * 32 + j, q = c / share;
+                const uint32_t a = tc::cluster_addr(recv + ((part * share + (c - q * share)) * kI8BM + row), (uint32_t)q);
+                const int32_t v = ok ? (int32_t)r[j] : 0;
+                asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+            }
+        }
+    }
+    tc::cluster_sync();
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // s_x (per token) and y belong to the previous kernel's era
+    const bool per_tensor = p.s_stride == 0;
+    const int rows = p.m - m0 < kI8BM ? p.m - m0 : kI8BM;
+    for (int e = threadIdx.x; e < rows * share; e += blockDim.x) {
+        const int cl = e % share, row = e / share;  // channels fastest: y stores along a row
+        const int c = part * share + cl, n = n0 + c;
+        if (n >= p.n) continue;
+        int32_t acc = recv[cl * kI8BM + row];
+        for (int q = 1; q < p.parts; ++q) acc += recv[(q * share + cl) * kI8BM + row];
+        const int t = m0 + row;
+        const int32_t a = acc - (per_tensor ? s_zr[c] : 0);
+        const float f = per_tensor ? s_f[c] : __fmul_rn(p.s_x[t], s_scale[c]);
+        const float af = __int2float_rn(a);
+        p.y[(int64_t)t * p.ldy + n] = p.bias ? __fmaf_rn(af, f, s_bias[c]) : __fmul_rn(af, f);
+        if (p.acc_out) p.acc_out[(int64_t)t * p.n + n] = a;
+    }
+}
+
 // Warp 0: TMA producer.  Warp 1: MMA issuer.  Warp 2: TMEM allocation.  Warps 2, 3: per-channel
 // epilogue factors.  All eight warps: epilogue (warp w reads accumulator lanes 32 (w % 4) ..).
 template <int BN, bool A_SIGNED>
@@ -694,7 +753,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * kI8BM, n0 = blockIdx.x * BN;
-    const int nkb = p.num_kb;
+    const int part = p.parts > 1 ? (int)tc::cluster_ctarank() : 0;  // K part (cluster along z)
+    const int kb0 = part * p.num_kb / p.parts;
+    const int nkb = (part + 1) * p.num_kb / p.parts - kb0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kI8Stages; ++s) {
@@ -725,23 +786,24 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
             const int pre = nkb < kI8Stages ? nkb : kI8Stages;
             for (int i = 0; i < pre; ++i) {
                 uint8_t* b_s = smem + i * S::kStage + S::kA;
+                const int kb = kb0 + i;
                 tc::mbar_arrive_expect_tx(&full[i], S::kStage);
-                tc::tma_load_4d(b_s, &tmap_b, &full[i], 0, 0, 2 * i, n0 / 16);
-                tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[i], 0, 0, 2 * i + 1, n0 / 16);
+                tc::tma_load_4d(b_s, &tmap_b, &full[i], 0, 0, 2 * kb, n0 / 16);
+                tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[i], 0, 0, 2 * kb + 1, n0 / 16);
             }
             asm volatile("griddepcontrol.wait;" ::: "memory");
-            for (int i = 0; i < pre; ++i) tc::tma_load_2d(smem + i * S::kStage, &tmap_a, &full[i], i * kI8BK, m0);
+            for (int i = 0; i < pre; ++i) tc::tma_load_2d(smem + i * S::kStage, &tmap_a, &full[i], (kb0 + i) * kI8BK, m0);
             for (int i = pre; i < nkb; ++i) {
-                const int s = i % kI8Stages;
+                const int s = i % kI8Stages, kb = kb0 + i;
                 const uint32_t phase = (i / kI8Stages) & 1;
                 if (!tc::mbar_wait(&empty[s], phase ^ 1)) { *abort_flag = 1; break; }
                 if (*(volatile int*)abort_flag) break;
                 uint8_t* a_s = smem + s * S::kStage;
                 uint8_t* b_s = a_s + S::kA;
                 tc::mbar_arrive_expect_tx(&full[s], S::kStage);
-                tc::tma_load_2d(a_s, &tmap_a, &full[s], i * kI8BK, m0);
-                tc::tma_load_4d(b_s, &tmap_b, &full[s], 0, 0, 2 * i, n0 / 16);
-                tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[s], 0, 0, 2 * i + 1, n0 / 16);
+                tc::tma_load_2d(a_s, &tmap_a, &full[s], kb * kI8BK, m0);
+                tc::tma_load_4d(b_s, &tmap_b, &full[s], 0, 0, 2 * kb, n0 / 16);
+                tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[s], 0, 0, 2 * kb + 1, n0 / 16);
             }
         }
     } else if (warp == 1) {
@@ -769,7 +831,12 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
         i8_load_factors<BN>(p, n0, s_scale, s_bias, s_rowsum, s_f, s_zr);  // off the producer's critical path
     }
     __syncwarp();
-    i8_epilogue<BN>(p, &tmap_y, smem, done, abort_flag, s_scale, s_bias, s_rowsum, s_f, s_zr, tmem, m0, n0);
+    if (p.parts > 1) {
+        __syncthreads();  // the factors of warps 2, 3 are in shared memory
+        i8_splitk_epilogue<BN>(p, smem, done, abort_flag, s_scale, s_bias, s_f, s_zr, tmem, m0, n0, part);
+    } else {
+        i8_epilogue<BN>(p, &tmap_y, smem, done, abort_flag, s_scale, s_bias, s_rowsum, s_f, s_zr, tmem, m0, n0);
+    }
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 2) {
@@ -1127,15 +1194,26 @@ template <int BN>
 static int launch_gemm_bn(bool a_signed, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my,
                           const GemmI8Params& q, bool dependent, cudaStream_t st) {
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)ceil_div(q.n, BN), (unsigned)ceil_div(q.m, kI8BM));
+    cfg.gridDim = dim3((unsigned)ceil_div(q.n, BN), (unsigned)ceil_div(q.m, kI8BM), (unsigned)q.parts);
     cfg.blockDim = dim3(kI8Threads);
     cfg.dynamicSmemBytes = (size_t)I8Smem<BN>::kBytes;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (dependent) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (q.parts > 1) {  // split K: the parts of a tile form a cluster along z
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = (unsigned)q.parts;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = dependent ? 1 : 0;
+    cfg.numAttrs = na;
     auto kernel = a_signed ? gemm_w8a8_kernel<BN, true> : gemm_w8a8_kernel<BN, false>;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, I8Smem<BN>::kBytes);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, my, q);
@@ -1184,11 +1262,22 @@ static int launch_gemm_i8(const void* xq, bool a_signed, const void* packed, con
                           cudaStream_t st) {
     const bool pair = SBQ_I8_PAIR && p.m > kI8BM;  // more than one 128-row tile of xq: CTA pairs
     const int bn = pair ? i8_pair_tile_n(p.m, p.n) : i8_tile_n(p.m, p.n);
+    GemmI8Params q = p;
+    q.parts = 1;
+    if (!pair && p.m <= 32) {
+        // decode sizes (up to 32 rows of xq): the weight stream of ceil(n / bn) CTAs alone is too
+        // narrow, so K is split over a cluster - the largest power of two up to 8 that keeps one CTA
+        // per SM and at least 2 k-blocks per part (int32 partial sums: the result is unchanged).
+        // Measured at n = k = 4096: m = 1 17.5 -> 13.6 us, m = 16 18.2 -> 15.0 us per quantise +
+        // GEMM call; at m = 64 no change and at m = 128 slower (24.9 us: the exchange of 128 rows)
+        const int64_t tiles = ceil_div(p.n, bn);
+        while (q.parts < 8 && tiles * (2 * q.parts) <= (int64_t)sm_count_dyn() && p.num_kb / (2 * q.parts) >= 2)
+            q.parts *= 2;
+    }
     CUtensorMap ma, mb, my;
     int rc = make_gemm_maps(&ma, &mb, xq, p.m, p.k, packed, p.n, pair ? bn / 2 : bn);  // a pair CTA loads bn/2 rows
     if (rc) return rc;
     std::memset(&my, 0, sizeof(my));
-    GemmI8Params q = p;
     q.tma_y = !p.acc_out && reinterpret_cast<uintptr_t>(p.y) % 16 == 0 && p.ldy % 4 == 0;
     q.vec_y = reinterpret_cast<uintptr_t>(p.y) % 16 == 0 && p.ldy % 4 == 0 && p.n % 4 == 0 &&
               (!p.acc_out || reinterpret_cast<uintptr_t>(p.acc_out) % 16 == 0);

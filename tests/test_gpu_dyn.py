@@ -219,3 +219,28 @@ def test_one_launch_quantiser_repeated_and_alternating(sbq):
         for t, wv in zip((big, mid, small), want):
             assert torch.equal(mod(t), wv)
     assert sbq._lib.load().sbq_check_device_error() == 0
+
+
+# decode sizes (up to 32 rows): K split over a cluster of CTAs (int32 partial sums added in the owning
+# CTA); bit-exact like every other int8-dyn path, per tensor and per token, with and without bias;
+# 33 rows takes the unsplit kernel
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (16, 4096, 4096), (5, 1000, 2560), (32, 512, 1024),
+                                   (33, 512, 1024)])
+@pytest.mark.parametrize("mode", ["per_tensor", "per_token"])
+def test_decode_split_k_bit_exact(sbq, m, n, k, mode):
+    w = sbq.workloads.float_weight(n, k, seed=n + m)
+    bias = torch.randn(n) if m % 2 else None
+    x = sbq.workloads.activation(m, k, seed=k + m, dtype=torch.float32) * 2.0
+    q, sc = R.quantize_per_channel(w.numpy())
+    mod = sbq.DynamicInt8Linear(w, bias, mode=mode)
+    y, xq, s, _, acc = mod.forward_stages(x.cuda())
+    b = None if bias is None else bias.numpy()
+    if mode == "per_tensor":
+        ry, rxq, rs, rzp, racc = R.dyn_linear(x.numpy(), q, sc, b)
+    else:
+        ry, rxq, rs, racc = R.tok_linear(x.numpy(), q, sc, b)
+    assert np.array_equal(xq.cpu().numpy(), rxq)
+    assert np.array_equal(acc.cpu().numpy(), racc)
+    assert np.array_equal(_bits(y.cpu().numpy()), _bits(ry))
+    assert torch.equal(mod(x.cuda()), y)
+    assert sbq._lib.load().sbq_check_device_error() == 0
