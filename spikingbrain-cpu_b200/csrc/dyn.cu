@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     // waits for this grid before reading xq and the parameters
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // the barrier generation before this launch's arrivals (read now: its latency overlaps the loads)
-    const unsigned gen = threadIdx.x == 0 ? ld_acquire_gpu(&g_qbar_gen[lane]) : 0u;
+    const unsigned gen = threadIdx.x == 0 && gridDim.x > 1 ? ld_acquire_gpu(&g_qbar_gen[lane]) : 0u;
     constexpr int V = Vec<T>::kN, NV = FusedVecs<T>::kN;
     const int64_t per_row = k / V, total = (int64_t)m * per_row;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -364,30 +364,32 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     __shared__ int s_flag;
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(mn, mx);
     __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < kFusedThreads / 32; ++w) {
-            mn = fminf(mn, red[w].x);
-            mx = fmaxf(mx, red[w].y);
+    if (gridDim.x > 1) {  // (a one-CTA grid, for small x, has the whole reduction in red[] already)
+        if (threadIdx.x == 0) {
+            for (int w = 1; w < kFusedThreads / 32; ++w) {
+                mn = fminf(mn, red[w].x);
+                mx = fmaxf(mx, red[w].y);
+            }
+            partials[blockIdx.x] = make_float2(mn, mx);
         }
-        partials[blockIdx.x] = make_float2(mn, mx);
-    }
-    if (!quant_grid_barrier(lane, gen, &s_flag)) return;
+        if (!quant_grid_barrier(lane, gen, &s_flag)) return;
 
-    mn = INFINITY;
-    mx = -INFINITY;
-    for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
-        const float2 q = __ldcg(partials + i);  // written by other SMs in this launch: read through L2
-        mn = fminf(mn, q.x);
-        mx = fmaxf(mx, q.y);
-    }
+        mn = INFINITY;
+        mx = -INFINITY;
+        for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
+            const float2 q = __ldcg(partials + i);  // written by other SMs in this launch: read through L2
+            mn = fminf(mn, q.x);
+            mx = fmaxf(mx, q.y);
+        }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (int o = 16; o > 0; o >>= 1) {
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        __syncthreads();  // red[] is reused
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(mn, mx);
+        __syncthreads();
     }
-    __syncthreads();  // red[] is reused
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(mn, mx);
-    __syncthreads();
     if (threadIdx.x == 0) {
         for (int w = 1; w < kFusedThreads / 32; ++w) {
             mn = fminf(mn, red[w].x);
@@ -1096,6 +1098,14 @@ static int minmax_blocks(int64_t m, int64_t k, int vec) {
 template <typename T>
 static cudaError_t launch_quant_tensor(const void* x, int64_t ldx, int m, int k, float2* partials, uint8_t* xq,
                                        float* s, int32_t* zp, cudaStream_t st) {
+    const int64_t vecs = (int64_t)m * (k / Vec<T>::kN);
+    if (vecs <= (int64_t)kFusedThreads * FusedVecs<T>::kN) {
+        // small x (up to 64 KiB, e.g. decode rows): the one-launch kernel with a single CTA, which
+        // needs no grid barrier - one launch instead of two
+        quantize_per_tensor_fused_kernel<T><<<1, kFusedThreads, 0, st>>>(static_cast<const T*>(x), ldx, m, k, partials,
+                                                                          xq, s, zp, 0);
+        return cudaGetLastError();
+    }
     if ((int64_t)m * k * (int64_t)sizeof(T) < kFusedMinBytes) {
         const int nb = minmax_blocks(m, k, Vec<T>::kN);
         minmax_partial_kernel<T><<<nb, kQuantThreads, 0, st>>>(static_cast<const T*>(x), ldx, m, k, partials);
@@ -1112,7 +1122,6 @@ static cudaError_t launch_quant_tensor(const void* x, int64_t ldx, int m, int k,
     if (e != cudaSuccess) return e;
     if (per_sm < 1) per_sm = 1;
     // as many CTAs as hold x in registers (at most the resident limit, and the partials' capacity)
-    const int64_t vecs = (int64_t)m * (k / Vec<T>::kN);
     int64_t nb = ceil_div(vecs, (int64_t)kFusedThreads * FusedVecs<T>::kN);
     const int64_t cap = (int64_t)per_sm * sm_count_dyn();
     if (nb > cap) nb = cap;
