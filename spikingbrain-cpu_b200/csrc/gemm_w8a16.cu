@@ -440,20 +440,6 @@ __device__ __forceinline__ void st_dsmem(uint32_t cluster_addr, float v) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
 }
 
-__device__ __forceinline__ void st_dsmem4(uint32_t cluster_addr, float4 v) {
-    asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(cluster_addr), "f"(v.x), "f"(v.y), "f"(v.z),
-                 "f"(v.w)
-                 : "memory");
-}
-
-__device__ __forceinline__ float4 ld_dsmem4(uint32_t cluster_addr) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(cluster_addr)
-                 : "memory");
-    return v;
-}
 
 template <bool OUT_F16, int AK>
 __global__ void __launch_bounds__(kWThreads, kSmallCtasPerSm) gemm_w8a16_small_kernel(const __grid_constant__ CUtensorMap tmap_x,

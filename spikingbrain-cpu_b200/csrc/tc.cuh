@@ -140,8 +140,6 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                  : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// Waits until every bulk copy this thread committed has completed (writes included).
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Waits until every bulk copy this thread committed has finished reading its shared-memory source
 // (the global writes may still be in flight; they are complete when the grid is).
 __device__ __forceinline__ void bulk_wait_all_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
