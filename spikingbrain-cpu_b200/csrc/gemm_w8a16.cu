@@ -92,17 +92,15 @@ __device__ __forceinline__ void convert_row(const uint8_t* w8, int row, uint32_t
 }
 
 constexpr int kWCh = 128;      // output channels per CTA (one per TMEM lane)
-constexpr int kWTok = 256;     // activation rows per prefill tile (MMA N; each CTA of a pair loads half)
 constexpr int kWBK = 64;       // k per k-block (one 128-byte 16-bit row, one packed tile column)
 #ifndef SBQ_W16_ABUFS
 #define SBQ_W16_ABUFS 4
 #endif
-constexpr int kWABufs = SBQ_W16_ABUFS;  // weight operand buffers in TMEM (32 columns each; 256 + 32 * 8 = 512 at most)
+constexpr int kWABufs = SBQ_W16_ABUFS;  // prefill weight operand buffers in TMEM (at most; stages and columns cap it)
 static_assert(kWABufs >= 2 && kWABufs <= 8, "tensor-memory columns");
 constexpr int kWThreads = 384; // 12 warps: producer, MMA, TMEM, idle, then two converter warpgroups
 constexpr uint32_t kWTmemCols = 512;
-constexpr uint32_t kWAccCol = 0;    // accumulator: columns [0, 256)
-constexpr uint32_t kWACol = 256;    // weight buffers: 32 columns each from 256
+constexpr uint32_t kWAccCol = 0;    // accumulator from column 0; weight operand buffers after it
 
 // ---------------------------------------------------------------------------------------------
 // Prefill GEMM (more than 128 activation rows), CTA pairs: a 2-CTA cluster computes a 256-channel x
@@ -117,7 +115,6 @@ constexpr uint32_t kWACol = 256;    // weight buffers: 32 columns each from 256
 // (one commit per barrier, no multicast).  Roles: warp 0 TMA producer, warp 1 MMA issuer (leader),
 // warp 2 TMEM allocation, warps 4-11 two converter warpgroups (alternate k-blocks), then the
 // epilogue (each thread one channel, each warpgroup one half of the 256 tokens).
-constexpr int kPTokHalf = kWTok / 2;  // activation rows each CTA of the pair loads
 #ifndef SBQ_W16_PAIR_KH
 #define SBQ_W16_PAIR_KH 2
 #endif
@@ -129,37 +126,45 @@ constexpr int kPTokHalf = kWTok / 2;  // activation rows each CTA of the pair lo
 #endif
 constexpr int kPThreads = kWThreads;
 
-template <int AK>
+// TOK: the pair's tokens per tile (the MMA's N): 256, or 128 when 256-token tiles leave SMs idle
+// (the reference's 512-token prefill chunks); each CTA loads TOK / 2 of them.
+template <int AK, int TOK>
 struct PairSmem {
+    static_assert(TOK == 128 || TOK == 256, "token tile");
+    static constexpr int kTokHalf = TOK / 2;
     // k per stage: kKH sub-blocks of 64 (128 for 16-bit x, so that the MMA thread's two waits and two
     // commits per stage cover 8 MMAs; 64 for a split fp32 x, whose stage is twice as large)
     static constexpr int kKH = AK == kABF16x2 ? 1 : SBQ_W16_PAIR_KH;
-    static constexpr int kXSub = kPTokHalf * kWBK * 2;     // 16 KiB: 128 tokens x 64 k of this CTA's half
+    static constexpr int kXSub = kTokHalf * kWBK * 2;      // this CTA's tokens x 64 k (16 or 8 KiB)
     static constexpr int kXTiles = AK == kABF16x2 ? 2 : 1;  // high and low part of a split fp32 x
     static constexpr int kXStage = kKH * kXTiles * kXSub;
     static constexpr int kW8Sub = kWCh * kWBK;             // 8 KiB: this CTA's 128 weight rows x 64 k
     static constexpr int kStage = kXStage + kKH * kW8Sub;
-    static constexpr int kStages = AK == kABF16x2 ? SBQ_W16_PAIR_STAGES_X2 : SBQ_W16_PAIR_STAGES;
+    static constexpr int kStages0 = AK == kABF16x2 ? SBQ_W16_PAIR_STAGES_X2 : SBQ_W16_PAIR_STAGES;
+    // 128-token tiles have smaller stages: as many as fit the same ring (at most 8)
+    static constexpr int kStagesFit = (196 * 1024) / kStage < 8 ? (196 * 1024) / kStage : 8;
+    static constexpr int kStages = TOK == 256 ? kStages0 : kStagesFit;
     static constexpr int kBarOff = kStages * kStage;
     static constexpr int kBytes = kBarOff + 512 + kWCh * 8 + 1024;
     static_assert(kKH >= 1 && kKH <= 4, "64 to 256 k per stage");
     static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
-    // operand buffers in tensor memory (kACols columns each, after the 256 accumulator columns):
+    // operand buffers in tensor memory (kACols columns each, after the TOK accumulator columns):
     // buffer d is released by the commit of the k-block that last read it, which must still be
     // tracked by a stage barrier
+    static constexpr uint32_t kACol = TOK;
     static constexpr int kACols = kKH * (kWBK / 2);
-    static constexpr int kABufMax = (int)(kWTmemCols - kWAccCol - kWTok) / kACols;
+    static constexpr int kABufMax = (int)(kWTmemCols - kWAccCol - TOK) / kACols;
     static constexpr int kABufs0 = kWABufs < kStages ? kWABufs : kStages;
     static constexpr int kABufs = kABufs0 < kABufMax ? kABufs0 : kABufMax;
     static_assert(kABufs >= 2, "operand buffers");
     static_assert(4 * kStages + kABufs + 1 <= 60, "barriers fit in 512 bytes with the TMEM slot");
 };
 
-template <bool OUT_F16, bool GATED, int AK>
+template <bool OUT_F16, bool GATED, int AK, int TOK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm_w8a16_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_x2,
                            const __grid_constant__ CUtensorMap tmap_w, const GemmW16Params p) {
-    using S = PairSmem<AK>;
+    using S = PairSmem<AK, TOK>;
     constexpr int kStages = S::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -177,7 +182,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const uint32_t rank = tc::cluster_ctarank();
     const bool leader = rank == 0;
     const int n0 = (blockIdx.x >> 1) * (2 * kWCh) + (int)rank * kWCh;  // this CTA's 128 channels
-    const int t0 = blockIdx.y * kWTok;                                  // the pair's 256 tokens
+    const int t0 = blockIdx.y * TOK;                                    // the pair's TOK tokens
     // the next launch on the stream may start its prologue (and weight tiles) now; it waits for
     // this grid before it touches activations or outputs
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -215,7 +220,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             // weight tiles of the first stages before griddepcontrol.wait (launched as a programmatic
             // dependent, the previous kernel may still run: it writes activations, never weights),
             // activation tiles after it
-            const int tr = t0 + (int)rank * kPTokHalf;
+            const int tr = t0 + (int)rank * S::kTokHalf;
             auto load_w = [&](int kb) {
                 const int s = kb % kStages;
                 uint8_t* ws = smem + s * S::kStage + S::kXStage;
@@ -252,7 +257,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0 && leader) {
-            constexpr uint32_t idesc = tc::idesc_f16(2 * kWCh, kWTok, AK != kAF16);
+            constexpr uint32_t idesc = tc::idesc_f16(2 * kWCh, TOK, AK != kAF16);
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 const int s = kb % kStages, d = kb % S::kABufs;
                 const uint32_t ph = (kb / kStages) & 1, phd = (kb / S::kABufs) & 1;
@@ -260,7 +265,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 if (!tc::mbar_wait_cluster(&a_full[d], phd)) break;
                 tc::fence_after_sync();
                 const uint8_t* xs = smem + s * S::kStage;
-                const uint32_t a_col = tmem + kWACol + d * S::kACols;
+                const uint32_t a_col = tmem + S::kACol + d * S::kACols;
 #pragma unroll
                 for (int h = 0; h < S::kKH; ++h) {
                     const uint8_t* xh = xs + h * S::kXTiles * S::kXSub;
@@ -304,7 +309,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             for (int hh = 0; hh < S::kKH; ++hh) {
                 uint32_t h[32];
                 convert_row<AK>(smem + s * S::kStage + S::kXStage + hh * S::kW8Sub + row * 64, row, h);
-                tc::tmem_st_32x32b_x32(tmem + lane_addr + kWACol + d * S::kACols + hh * (kWBK / 2), h);
+                tc::tmem_st_32x32b_x32(tmem + lane_addr + S::kACol + d * S::kACols + hh * (kWBK / 2), h);
             }
             tc::tmem_wait_st();
             tc::fence_before_sync();
@@ -323,7 +328,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             const float sc = s_scale[row], bi = s_bias[row];
             const bool has_bias = p.bias != nullptr;
 #pragma unroll 1
-            for (int c = grp * (kWTok / 64); c < (grp + 1) * (kWTok / 64); ++c) {  // this group's token half
+            for (int c = grp * (TOK / 64); c < (grp + 1) * (TOK / 64); ++c) {  // this group's token half
                 uint32_t r[32];
                 tc::tmem_ld_32x32b_x32(tmem + lane_addr + kWAccCol + c * 32, r);
                 tc::tmem_wait_ld();
@@ -785,11 +790,12 @@ static int gemm_small(const CUtensorMap& mx, const CUtensorMap& mx2, const CUten
 // activations and outputs only after it.  Only kernels that call griddepcontrol.launch_dependents
 // let a dependent start early, and in this library those write activations only (never packed
 // weights, scales or biases); any other predecessor completes first, as in plain stream order.
-template <bool OUT_F16, bool GATED, int AK>
+template <bool OUT_F16, bool GATED, int AK, int TOK>
 static cudaError_t launch_pair(dim3 grid, cudaStream_t s, const CUtensorMap& mx, const CUtensorMap& mx2,
                                const CUtensorMap& mw, const GemmW16Params& p) {
-    constexpr int smem = PairSmem<AK>::kBytes;
-    cudaFuncSetAttribute(gemm_w8a16_pair_kernel<OUT_F16, GATED, AK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    constexpr int smem = PairSmem<AK, TOK>::kBytes;
+    cudaFuncSetAttribute(gemm_w8a16_pair_kernel<OUT_F16, GATED, AK, TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         smem);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kPThreads);
@@ -800,11 +806,20 @@ static cudaError_t launch_pair(dim3 grid, cudaStream_t s, const CUtensorMap& mx,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_w8a16_pair_kernel<OUT_F16, GATED, AK>, mx, mx2, mw, p);
+    return cudaLaunchKernelEx(&cfg, gemm_w8a16_pair_kernel<OUT_F16, GATED, AK, TOK>, mx, mx2, mw, p);
 }
 
-// The CTA-pair kernel over 256-channel x 256-token tiles (clusters of two CTAs along x).
-template <int AK>
+// Token tile of the CTA-pair kernel: 256 unless the 256-token tiles fill less than ~90 % of one wave
+// of pairs (one pair per two SMs) and 128-token tiles give more pairs - e.g. the reference's
+// 512-token prefill chunks at n = 4096: 32 pairs of 256 tokens, 64 of 128.
+static int pair_tok(int64_t m, int64_t n) {
+    const int64_t cols = ceil_div(n, 2 * kWCh), pairs256 = cols * ceil_div(m, 256), pairs128 = cols * ceil_div(m, 128);
+    const int64_t wave = sm_count_w16() / 2;
+    return (pairs256 * 10 < wave * 9 && pairs128 > pairs256) ? 128 : 256;
+}
+
+// The CTA-pair kernel over 256-channel x TOK-token tiles (clusters of two CTAs along x).
+template <int AK, int TOK>
 static int gemm_pair(const CUtensorMap& mx, const CUtensorMap& mx2, const CUtensorMap& mw, const float* scale,
                      const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
                      int gated) {
@@ -813,18 +828,20 @@ static int gemm_pair(const CUtensorMap& mx, const CUtensorMap& mx2, const CUtens
     p.m = (int)m;
     p.n = (int)n;
     p.k = (int)k;
-    p.num_kb = (int)ceil_div(k, kWBK * PairSmem<AK>::kKH);  // k columns past k read zeros (TMA fill)
+    p.num_kb = (int)ceil_div(k, kWBK * PairSmem<AK, TOK>::kKH);  // k columns past k read zeros (TMA fill)
     p.scale = scale;
     p.bias = bias;
     p.y = y;
     p.ldy = ldy;
-    const dim3 grid((unsigned)(2 * ceil_div(n, 2 * kWCh)), (unsigned)ceil_div(m, kWTok));
+    const dim3 grid((unsigned)(2 * ceil_div(n, 2 * kWCh)), (unsigned)ceil_div(m, TOK));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e;
     if (y_dtype == SBQ_F16) {
-        e = gated ? launch_pair<true, true, AK>(grid, s, mx, mx2, mw, p) : launch_pair<true, false, AK>(grid, s, mx, mx2, mw, p);
+        e = gated ? launch_pair<true, true, AK, TOK>(grid, s, mx, mx2, mw, p)
+                  : launch_pair<true, false, AK, TOK>(grid, s, mx, mx2, mw, p);
     } else {
-        e = gated ? launch_pair<false, true, AK>(grid, s, mx, mx2, mw, p) : launch_pair<false, false, AK>(grid, s, mx, mx2, mw, p);
+        e = gated ? launch_pair<false, true, AK, TOK>(grid, s, mx, mx2, mw, p)
+                  : launch_pair<false, false, AK, TOK>(grid, s, mx, mx2, mw, p);
     }
     if (e != cudaSuccess) return set_error(SBQ_ERR_CUDA, "gemm_w8a16 (CTA pairs) launch: %s", cudaGetErrorString(e));
     return check_launch("gemm_w8a16 (CTA pairs)");
@@ -834,7 +851,8 @@ template <int AK>
 static int gemm_run_ak(const void* x, const void* x2, int64_t ldx, const void* packed, const float* scale,
                        const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy, void* stream,
                        int gated) {
-    const int rows = m <= kSmallMaxRows ? kSTok : kPTokHalf;
+    const int tok = m <= kSmallMaxRows ? 0 : pair_tok(m, n);
+    const int rows = m <= kSmallMaxRows ? kSTok : tok / 2;
     CUtensorMap mx, mx2, mw;
     int st = make_x_map(&mx, AK, x, ldx, m, k, rows);
     if (st) return st;
@@ -847,7 +865,8 @@ static int gemm_run_ak(const void* x, const void* x2, int64_t ldx, const void* p
     st = make_w_map(&mw, packed, n, k);
     if (st) return st;
     if (m <= kSmallMaxRows) return gemm_small<AK>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
-    return gemm_pair<AK>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
+    if (tok == 128) return gemm_pair<AK, 128>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
+    return gemm_pair<AK, 256>(mx, mx2, mw, scale, bias, m, n, k, y, y_dtype, ldy, stream, gated);
 }
 
 // ---- fp32 activation split: x = hi + lo, both bf16 -------------------------------------------------
