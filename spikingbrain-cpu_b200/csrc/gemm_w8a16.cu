@@ -93,11 +93,6 @@ __device__ __forceinline__ void convert_row(const uint8_t* w8, int row, uint32_t
 
 constexpr int kWCh = 128;      // output channels per CTA (one per TMEM lane)
 constexpr int kWBK = 64;       // k per k-block (one 128-byte 16-bit row, one packed tile column)
-#ifndef SBQ_W16_ABUFS
-#define SBQ_W16_ABUFS 4
-#endif
-constexpr int kWABufs = SBQ_W16_ABUFS;  // prefill weight operand buffers in TMEM (at most; stages and columns cap it)
-static_assert(kWABufs >= 2 && kWABufs <= 8, "tensor-memory columns");
 constexpr int kWThreads = 384; // 12 warps: producer, MMA, TMEM, idle, then two converter warpgroups
 constexpr uint32_t kWTmemCols = 512;
 constexpr uint32_t kWAccCol = 0;    // accumulator from column 0; weight operand buffers after it
@@ -148,16 +143,12 @@ struct PairSmem {
     static constexpr int kBytes = kBarOff + 512 + kWCh * 8 + 1024;
     static_assert(kKH >= 1 && kKH <= 4, "64 to 256 k per stage");
     static_assert(kBytes <= 227 * 1024, "shared memory per CTA");
-    // operand buffers in tensor memory (kACols columns each, after the TOK accumulator columns):
-    // buffer d is released by the commit of the k-block that last read it, which must still be
-    // tracked by a stage barrier
+    // one weight operand buffer in tensor memory per stage (kACols columns each, after the TOK
+    // accumulator columns): a stage's activation tiles and converted weights are ready together
     static constexpr uint32_t kACol = TOK;
     static constexpr int kACols = kKH * (kWBK / 2);
-    static constexpr int kABufMax = (int)(kWTmemCols - kWAccCol - TOK) / kACols;
-    static constexpr int kABufs0 = kWABufs < kStages ? kWABufs : kStages;
-    static constexpr int kABufs = kABufs0 < kABufMax ? kABufs0 : kABufMax;
-    static_assert(kABufs >= 2, "operand buffers");
-    static_assert(4 * kStages + kABufs + 1 <= 60, "barriers fit in 512 bytes with the TMEM slot");
+    static_assert(TOK + kStages * kACols <= (int)(kWTmemCols - kWAccCol), "operand buffers fit in tensor memory");
+    static_assert(4 * kStages + 1 <= 60, "barriers fit in 512 bytes with the TMEM slot");
 };
 
 template <bool OUT_F16, bool GATED, int AK, int TOK>
@@ -169,11 +160,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + S::kBarOff);  // this CTA's weight tile landed
-    uint64_t* xfull = wfull + kStages;      // both activation halves landed (the leader's is used)
-    uint64_t* conv_done = xfull + kStages;  // this CTA's 4 converter warps have read the weight tile
+    // the stage is ready for the MMAs: both activation halves landed (transaction bytes) and both
+    // CTAs' 4 converter warps wrote its weight operand buffer (arrivals); the leader's is used
+    uint64_t* ready = wfull + kStages;
+    uint64_t* conv_done = ready + kStages;  // this CTA's 4 converter warps have read the weight tile
     uint64_t* mma_done = conv_done + kStages;  // the pair's MMAs of the stage's k-block completed
-    uint64_t* a_full = mma_done + kStages;  // operand buffer written by both CTAs' converters (leader's used)
-    uint64_t* done = a_full + S::kABufs;
+    uint64_t* done = mma_done + kStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     float* s_scale = reinterpret_cast<float*>(smem + S::kBarOff + 512);
     float* s_bias = s_scale + kWCh;
@@ -190,11 +182,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             tc::mbar_init(&wfull[s], 1);
-            tc::mbar_init(&xfull[s], 1);
+            tc::mbar_init(&ready[s], 1 + 8);  // the leader's producer (with the bytes) + 8 converter warps
             tc::mbar_init(&conv_done[s], 4);
             tc::mbar_init(&mma_done[s], 1);
         }
-        for (int d = 0; d < S::kABufs; ++d) tc::mbar_init(&a_full[d], 8);  // 4 converter warps of each CTA
         tc::mbar_init(done, 1);
         tc::fence_mbar_init();
         tc::prefetch_tmap(&tmap_x);
@@ -232,8 +223,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             auto load_x = [&](int kb) {
                 const int s = kb % kStages;
                 uint8_t* xs = smem + s * S::kStage;
-                const uint32_t xb = tc::cluster_addr(&xfull[s], 0);
-                if (leader) tc::mbar_arrive_expect_tx(&xfull[s], 2 * S::kXStage);
+                const uint32_t xb = tc::cluster_addr(&ready[s], 0);
+                if (leader) tc::mbar_arrive_expect_tx(&ready[s], 2 * S::kXStage);
 #pragma unroll
                 for (int h = 0; h < S::kKH; ++h) {
                     const int kc = kb * S::kKH + h;  // 64-wide k column
@@ -259,13 +250,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         if (lane == 0 && leader) {
             constexpr uint32_t idesc = tc::idesc_f16(2 * kWCh, TOK, AK != kAF16);
             for (int kb = 0; kb < p.num_kb; ++kb) {
-                const int s = kb % kStages, d = kb % S::kABufs;
-                const uint32_t ph = (kb / kStages) & 1, phd = (kb / S::kABufs) & 1;
-                if (!tc::mbar_wait(&xfull[s], ph)) break;
-                if (!tc::mbar_wait_cluster(&a_full[d], phd)) break;
+                const int s = kb % kStages;
+                const uint32_t ph = (kb / kStages) & 1;
+                if (!tc::mbar_wait_cluster(&ready[s], ph)) break;
                 tc::fence_after_sync();
                 const uint8_t* xs = smem + s * S::kStage;
-                const uint32_t a_col = tmem + S::kACol + d * S::kACols;
+                const uint32_t a_col = tmem + S::kACol + s * S::kACols;
 #pragma unroll
                 for (int h = 0; h < S::kKH; ++h) {
                     const uint8_t* xh = xs + h * S::kXTiles * S::kXSub;
@@ -279,7 +269,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                         }
                     }
                 }
-                // one barrier per CTA: frees the stage's activation half and operand buffer d
+                // one barrier per CTA: frees the stage's activation half and operand buffer
                 tc::mma_commit_pair(tc::cluster_addr(&mma_done[s], 0));
                 tc::mma_commit_pair(tc::cluster_addr(&mma_done[s], 1));
             }
@@ -293,15 +283,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
         bool ok = true;
         for (int kb = grp; kb < p.num_kb; kb += 2) {
-            const int s = kb % kStages, d = kb % S::kABufs;
+            const int s = kb % kStages;
             const uint32_t ph = (kb / kStages) & 1;
-            // warp-uniform waits: tcgen05.st below is warp-collective.  Operand buffer d was last
-            // read by the MMAs of k-block kb - kABufs; waiting for them first also guarantees that
-            // every k-block up to there was converted, so the weight stage's earlier phases are
-            // complete and its parity wait can only pass on this k-block's tile (kABufs <= kStages).
-            if (kb >= S::kABufs) {
-                const int kp = kb - S::kABufs;
-                if (!__all_sync(0xffffffffu, tc::mbar_wait(&mma_done[kp % kStages], (kp / kStages) & 1))) { ok = false; break; }
+            // warp-uniform waits: tcgen05.st below is warp-collective.  The stage's operand buffer
+            // was last read by the MMAs of k-block kb - kStages; waiting for them first also
+            // guarantees that every k-block up to there was converted, so the weight stage's earlier
+            // phases are complete and its parity wait can only pass on this k-block's tile.
+            if (kb >= kStages) {
+                if (!__all_sync(0xffffffffu, tc::mbar_wait(&mma_done[s], ph ^ 1))) { ok = false; break; }
             }
             if (!__all_sync(0xffffffffu, tc::mbar_wait(&wfull[s], ph))) { ok = false; break; }
             tc::fence_after_sync();
@@ -309,13 +298,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             for (int hh = 0; hh < S::kKH; ++hh) {
                 uint32_t h[32];
                 convert_row<AK>(smem + s * S::kStage + S::kXStage + hh * S::kW8Sub + row * 64, row, h);
-                tc::tmem_st_32x32b_x32(tmem + lane_addr + S::kACol + d * S::kACols + hh * (kWBK / 2), h);
+                tc::tmem_st_32x32b_x32(tmem + lane_addr + S::kACol + s * S::kACols + hh * (kWBK / 2), h);
             }
             tc::tmem_wait_st();
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) {
-                tc::mbar_arrive_cluster(tc::cluster_addr(&a_full[d], 0));
+                tc::mbar_arrive_cluster(tc::cluster_addr(&ready[s], 0));
                 tc::mbar_arrive(&conv_done[s]);
             }
         }
