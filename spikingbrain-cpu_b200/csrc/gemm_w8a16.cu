@@ -390,14 +390,12 @@ struct SmallSmem {
     static constexpr int kBarOff = kStages * kStage;
     static constexpr int kBytes = kBarOff + 256 + kWCh * 8 + 1024;
     static constexpr int kACols = kKH * (kWBK / 2);        // tensor-memory columns of one operand buffer
-    // operand buffers: at most the stage count, so that a converter which has seen the operand
-    // buffer of block i released (the MMA of block i - kABufs done) knows that the stage of block i
-    // has completed every earlier phase, and its parity wait on that stage cannot pass early
-    static constexpr int kABufs1 = 6 / kKH < kStages ? 6 / kKH : kStages;
-    static constexpr int kABufs = kABufs1 * kACols <= (int)(kSTmemCols - kSACol) ? kABufs1 : (int)(kSTmemCols - kSACol) / kACols;
+    // one weight operand buffer per stage in tensor memory (a converter that has seen the stage's
+    // previous MMAs complete also knows every earlier phase of the stage's barriers is complete)
+    static_assert(kSACol + kStages * kACols <= (int)kSTmemCols, "operand buffers fit in tensor memory");
     static_assert(kKH >= 1 && kKH <= 2, "64 or 128 k per stage");
-    static_assert(kStages >= 2 && kABufs >= 2, "pipeline depth");
-    static_assert(2 * kStages + 2 * kABufs + 1 <= 30, "barriers fit in 256 bytes with the TMEM slot");
+    static_assert(kStages >= 2, "pipeline depth");
+    static_assert(4 * kStages + 1 <= 30, "barriers fit in 256 bytes with the TMEM slot");
     // split-K receive buffer: [parts][64 tokens][rs] floats, rs = ceil(128 / parts) rounded up to
     // 4: at most 6 x 64 x 24 floats (parts = 6) for parts <= 8
     static_assert(6 * kSTok * 24 * 4 <= kStages * kStage, "receive buffer fits in the ring");
@@ -444,11 +442,11 @@ __global__ void __launch_bounds__(kWThreads, kSmallCtasPerSm) gemm_w8a16_small_k
     constexpr int kSStages = S::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
-    uint64_t* empty = full + kSStages;
-    uint64_t* a_full = empty + kSStages;
-    uint64_t* a_empty = a_full + S::kABufs;
-    uint64_t* done = a_empty + S::kABufs;
+    uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + S::kBarOff);  // the stage's weight tiles landed
+    uint64_t* ready = wfull + kSStages;      // activation tiles landed and the 4 converter warps wrote
+    uint64_t* conv_done = ready + kSStages;  // the 4 converter warps have read the weight tiles
+    uint64_t* mma_done = conv_done + kSStages;  // the stage's MMAs completed (activations, operand buffer)
+    uint64_t* done = mma_done + kSStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     float* s_scale = reinterpret_cast<float*>(smem + S::kBarOff + 256);
     float* s_bias = s_scale + kWCh;
@@ -464,12 +462,10 @@ __global__ void __launch_bounds__(kWThreads, kSmallCtasPerSm) gemm_w8a16_small_k
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSStages; ++s) {
-            tc::mbar_init(&full[s], 1);
-            tc::mbar_init(&empty[s], 4 + 1);
-        }
-        for (int d = 0; d < S::kABufs; ++d) {
-            tc::mbar_init(&a_full[d], 4);
-            tc::mbar_init(&a_empty[d], 1);
+            tc::mbar_init(&wfull[s], 1);
+            tc::mbar_init(&ready[s], 1 + 4);  // the producer (with the activation bytes) + 4 converter warps
+            tc::mbar_init(&conv_done[s], 4);
+            tc::mbar_init(&mma_done[s], 1);
         }
         tc::mbar_init(done, 1);
         tc::fence_mbar_init();
@@ -499,49 +495,49 @@ __global__ void __launch_bounds__(kWThreads, kSmallCtasPerSm) gemm_w8a16_small_k
             // dependent, the previous kernel may still run: it writes activations, never weights),
             // activation tiles after it
             auto load_x = [&](int i) {
-                uint8_t* xs = smem + (i % kSStages) * S::kStage;
+                const int s = i % kSStages;
+                uint8_t* xs = smem + s * S::kStage;
+                tc::mbar_arrive_expect_tx(&ready[s], S::kXStage);
 #pragma unroll
                 for (int h = 0; h < S::kKH; ++h) {
                     const int kc = (kb0 + i) * S::kKH + h;  // 64-deep k column
-                    tc::tma_load_2d(xs + h * S::kXTiles * S::kX, &tmap_x, &full[i % kSStages], kc * kWBK, t0);
+                    tc::tma_load_2d(xs + h * S::kXTiles * S::kX, &tmap_x, &ready[s], kc * kWBK, t0);
                     if (AK == kABF16x2)
-                        tc::tma_load_2d(xs + (h * S::kXTiles + 1) * S::kX, &tmap_x2, &full[i % kSStages], kc * kWBK, t0);
+                        tc::tma_load_2d(xs + (h * S::kXTiles + 1) * S::kX, &tmap_x2, &ready[s], kc * kWBK, t0);
                 }
             };
             auto load_w = [&](int i) {
-                uint8_t* xs = smem + (i % kSStages) * S::kStage;
+                const int s = i % kSStages;
+                uint8_t* xs = smem + s * S::kStage;
+                tc::mbar_arrive_expect_tx(&wfull[s], S::kStage - S::kXStage);
 #pragma unroll
                 for (int h = 0; h < S::kKH; ++h)
-                    tc::tma_load_4d(xs + S::kXStage + h * S::kW8, &tmap_w, &full[i % kSStages], 0, 0,
-                                    (kb0 + i) * S::kKH + h, n0 / 16);
+                    tc::tma_load_4d(xs + S::kXStage + h * S::kW8, &tmap_w, &wfull[s], 0, 0, (kb0 + i) * S::kKH + h,
+                                    n0 / 16);
             };
             const int pre = nkb < kSStages ? nkb : kSStages;
-            for (int i = 0; i < pre; ++i) {
-                tc::mbar_arrive_expect_tx(&full[i], S::kStage);
-                load_w(i);
-            }
+            for (int i = 0; i < pre; ++i) load_w(i);
             asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int i = 0; i < pre; ++i) load_x(i);
             for (int i = pre; i < nkb; ++i) {
                 const int s = i % kSStages;
                 const uint32_t ph = (i / kSStages) & 1;
-                if (!tc::mbar_wait(&empty[s], ph ^ 1)) break;
-                tc::mbar_arrive_expect_tx(&full[s], S::kStage);
-                load_x(i);
+                if (!tc::mbar_wait(&conv_done[s], ph ^ 1)) break;
+                if (!tc::mbar_wait(&mma_done[s], ph ^ 1)) break;
                 load_w(i);
+                load_x(i);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = tc::idesc_f16(kWCh, kSTok, AK != kAF16);
             for (int i = 0; i < nkb; ++i) {
-                const int s = i % kSStages, d = i % S::kABufs;
-                const uint32_t ph = (i / kSStages) & 1, phd = (i / S::kABufs) & 1;
-                if (!tc::mbar_wait(&full[s], ph)) break;
-                if (!tc::mbar_wait(&a_full[d], phd)) break;
+                const int s = i % kSStages;
+                const uint32_t ph = (i / kSStages) & 1;
+                if (!tc::mbar_wait(&ready[s], ph)) break;
                 tc::fence_after_sync();
                 const uint8_t* xs = smem + s * S::kStage;
-                const uint32_t a_col = tmem + kSACol + d * S::kACols;
+                const uint32_t a_col = tmem + kSACol + s * S::kACols;
 #pragma unroll
                 for (int h = 0; h < S::kKH; ++h) {
                     const uint8_t* xh = xs + h * S::kXTiles * S::kX;
@@ -555,8 +551,7 @@ __global__ void __launch_bounds__(kWThreads, kSmallCtasPerSm) gemm_w8a16_small_k
                         }
                     }
                 }
-                tc::mma_commit(&empty[s]);
-                tc::mma_commit(&a_empty[d]);
+                tc::mma_commit(&mma_done[s]);
             }
             tc::mma_commit(done);
         }
@@ -569,28 +564,30 @@ __global__ void __launch_bounds__(kWThreads, kSmallCtasPerSm) gemm_w8a16_small_k
         // one wait (the MMA of a 64-token tile is short, so the conversion latency sets the pace)
         bool ok = true;
         for (int i = grp; i < nkb; i += 2) {
-            const int s = i % kSStages, d = i % S::kABufs;
-            const uint32_t ph = (i / kSStages) & 1, phd = (i / S::kABufs) & 1;
-            // operand buffer first: the MMAs of block i - kABufs are done, so every block up to
-            // there was loaded (the MMA thread waits in order) and the stage's earlier phases are
-            // complete - the parity wait below can only pass on block i's own data.  (The other
-            // group converts block i - 1; this group's previous block, i - 2, says nothing about
-            // when block i - kStages landed.)
-            if (!__all_sync(0xffffffffu, tc::mbar_wait(&a_empty[d], phd ^ 1))) { ok = false; break; }
-            if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[s], ph))) { ok = false; break; }
+            const int s = i % kSStages;
+            const uint32_t ph = (i / kSStages) & 1;
+            // operand buffer first: the MMAs of block i - kStages are done, so every block up to
+            // there was loaded and converted (the MMA thread waits in order) and the stage's earlier
+            // phases are complete - the parity wait below can only pass on block i's own data.  (The
+            // other group converts block i - 1; this group's previous block, i - 2, says nothing
+            // about when block i - kStages landed.)
+            if (i >= kSStages) {
+                if (!__all_sync(0xffffffffu, tc::mbar_wait(&mma_done[s], ph ^ 1))) { ok = false; break; }
+            }
+            if (!__all_sync(0xffffffffu, tc::mbar_wait(&wfull[s], ph))) { ok = false; break; }
             tc::fence_after_sync();
 #pragma unroll
             for (int h = 0; h < S::kKH; ++h) {
                 uint32_t hv[32];
                 convert_row<AK>(smem + s * S::kStage + S::kXStage + h * S::kW8 + row * 64, row, hv);
-                tc::tmem_st_32x32b_x32(tmem + lane_addr + kSACol + d * S::kACols + h * (kWBK / 2), hv);
+                tc::tmem_st_32x32b_x32(tmem + lane_addr + kSACol + s * S::kACols + h * (kWBK / 2), hv);
             }
             tc::tmem_wait_st();
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) {
-                tc::mbar_arrive(&a_full[d]);
-                tc::mbar_arrive(&empty[s]);
+                tc::mbar_arrive(&ready[s]);
+                tc::mbar_arrive(&conv_done[s]);
             }
         }
         // ---- this thread's channel, this group's 32 tokens of accumulators
