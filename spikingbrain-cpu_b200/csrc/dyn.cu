@@ -544,6 +544,9 @@ constexpr int kI8BK = 128;         // k per pipeline stage (bytes of an int8 row
 #define SBQ_I8_STAGES 4
 #endif
 constexpr int kI8Stages = SBQ_I8_STAGES;
+#ifndef SBQ_I8_STAGES_128
+#define SBQ_I8_STAGES_128 6
+#endif
 constexpr int kI8Threads = 256;                // 8 warps
 constexpr int kI8SlotBytes = kI8BM * 32 * 4;   // staging of one 32-column block: 128 rows x 128 B
 
@@ -552,7 +555,9 @@ struct I8Smem {
     static constexpr int kA = kI8BM * kI8BK;  // 16 KiB
     static constexpr int kB = BN * kI8BK;     // two 64-wide halves of BN rows
     static constexpr int kStage = kA + kB;
-    static constexpr int kRing = kI8Stages * kStage;
+    // stages: as many as the build sets for the tile width (the 128-wide tile's are smaller)
+    static constexpr int kStages = BN == 128 ? SBQ_I8_STAGES_128 : kI8Stages;
+    static constexpr int kRing = kStages * kStage;
     static constexpr int kTail = 256 /* barriers */ + BN * 5 * 4;  // scale, bias, rowsum, s*scale, zp*rowsum
     static constexpr int kBytes = kRing + 1024 /* alignment */ + kTail;
     static_assert((BN / 32) * kI8SlotBytes <= kRing, "epilogue staging fits in the ring");
@@ -743,8 +748,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kRing);
-    uint64_t* empty = full + kI8Stages;
-    uint64_t* done = empty + kI8Stages;
+    uint64_t* empty = full + S::kStages;
+    uint64_t* done = empty + S::kStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     float* s_scale = reinterpret_cast<float*>(smem + S::kRing + 256);
@@ -760,7 +765,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
     const int nkb = (part + 1) * p.num_kb / p.parts - kb0;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kI8Stages; ++s) {
+        for (int s = 0; s < S::kStages; ++s) {
             tc::mbar_init(&full[s], 1);
             tc::mbar_init(&empty[s], 1);
         }
@@ -785,7 +790,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
             // ---- producer.  The weight tiles do not depend on the previous kernel (the activation
             // quantisation, when launched from sbq_linear_dyn as its programmatic dependent): those of
             // the first stages are requested before griddepcontrol.wait, the activation tiles after it.
-            const int pre = nkb < kI8Stages ? nkb : kI8Stages;
+            const int pre = nkb < S::kStages ? nkb : S::kStages;
             for (int i = 0; i < pre; ++i) {
                 uint8_t* b_s = smem + i * S::kStage + S::kA;
                 const int kb = kb0 + i;
@@ -796,8 +801,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
             asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int i = 0; i < pre; ++i) tc::tma_load_2d(smem + i * S::kStage, &tmap_a, &full[i], (kb0 + i) * kI8BK, m0);
             for (int i = pre; i < nkb; ++i) {
-                const int s = i % kI8Stages, kb = kb0 + i;
-                const uint32_t phase = (i / kI8Stages) & 1;
+                const int s = i % S::kStages, kb = kb0 + i;
+                const uint32_t phase = (i / S::kStages) & 1;
                 if (!tc::mbar_wait(&empty[s], phase ^ 1)) { *abort_flag = 1; break; }
                 if (*(volatile int*)abort_flag) break;
                 uint8_t* a_s = smem + s * S::kStage;
@@ -813,8 +818,8 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
             // ---- MMA issuer
             constexpr uint32_t idesc = tc::idesc_i8(A_SIGNED, kI8BM, BN);
             for (int i = 0; i < nkb; ++i) {
-                const int s = i % kI8Stages;
-                const uint32_t phase = (i / kI8Stages) & 1;
+                const int s = i % S::kStages;
+                const uint32_t phase = (i / S::kStages) & 1;
                 if (!tc::mbar_wait(&full[s], phase)) { *abort_flag = 1; break; }
                 tc::fence_after_sync();
                 const uint8_t* a_s = smem + s * S::kStage;
