@@ -536,6 +536,8 @@ struct GemmI8Params {
     int vec_y;              // y (and acc_out) rows take 16-byte vector stores: both base pointers 16-byte
                             // aligned, ldy and n multiples of 4; otherwise the epilogue stores element-wise
     int parts;              // K parts of the single-CTA kernel (a cluster along z; 1 = no split)
+    int a_rows;             // xq rows the single-CTA kernel loads per tile (up to 128; the MMA reads 128,
+                            // rows past them hold stale bytes whose products land in unused output rows)
 };
 
 constexpr int kI8BM = 128;         // rows of xq per tile (MMA M)
@@ -763,6 +765,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
     const int part = p.parts > 1 ? (int)tc::cluster_ctarank() : 0;  // K part (cluster along z)
     const int kb0 = part * p.num_kb / p.parts;
     const int nkb = (part + 1) * p.num_kb / p.parts - kb0;
+    const uint32_t stage_bytes = (uint32_t)(p.a_rows * kI8BK + S::kB);  // the xq box plus the weight tile
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S::kStages; ++s) {
@@ -794,7 +797,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
             for (int i = 0; i < pre; ++i) {
                 uint8_t* b_s = smem + i * S::kStage + S::kA;
                 const int kb = kb0 + i;
-                tc::mbar_arrive_expect_tx(&full[i], S::kStage);
+                tc::mbar_arrive_expect_tx(&full[i], stage_bytes);
                 tc::tma_load_4d(b_s, &tmap_b, &full[i], 0, 0, 2 * kb, n0 / 16);
                 tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[i], 0, 0, 2 * kb + 1, n0 / 16);
             }
@@ -807,7 +810,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) gemm_w8a8_kernel(const __grid_c
                 if (*(volatile int*)abort_flag) break;
                 uint8_t* a_s = smem + s * S::kStage;
                 uint8_t* b_s = a_s + S::kA;
-                tc::mbar_arrive_expect_tx(&full[s], S::kStage);
+                tc::mbar_arrive_expect_tx(&full[s], stage_bytes);
                 tc::tma_load_2d(a_s, &tmap_a, &full[s], kb * kI8BK, m0);
                 tc::tma_load_4d(b_s, &tmap_b, &full[s], 0, 0, 2 * kb, n0 / 16);
                 tc::tma_load_4d(b_s + BN * 64, &tmap_b, &full[s], 0, 0, 2 * kb + 1, n0 / 16);
@@ -1175,12 +1178,12 @@ static int quant_token(const void* x, int x_dtype, int64_t ldx, int64_t m, int64
 // Tensor maps: xq [m, k] bytes (SW128, 128 x 128 box) and the packed weight viewed as
 // {64 bytes, 16 rows, KT tiles, NT tile-rows} (SW64, one 64-wide tile column of BN rows per box).
 static int make_gemm_maps(CUtensorMap* ma, CUtensorMap* mb, const void* xq, int64_t m, int64_t k, const void* packed,
-                          int64_t n, int bn) {
+                          int64_t n, int bn, int a_rows) {
     const uint64_t kt = (uint64_t)ceil_div(k, kTileCols), nt = (uint64_t)ceil_div(n, kTileRows);
     {
         const uint64_t dims[2] = {(uint64_t)k, (uint64_t)m};
         const uint64_t strides[1] = {(uint64_t)k};
-        const uint32_t box[2] = {kI8BK, kI8BM};
+        const uint32_t box[2] = {kI8BK, (uint32_t)a_rows};
         int st = encode_tmap(ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xq, dims, strides, box,
                              CU_TENSOR_MAP_SWIZZLE_128B);
         if (st) return st;
@@ -1289,7 +1292,9 @@ static int launch_gemm_i8(const void* xq, bool a_signed, const void* packed, con
             q.parts *= 2;
     }
     CUtensorMap ma, mb, my;
-    int rc = make_gemm_maps(&ma, &mb, xq, p.m, p.k, packed, p.n, pair ? bn / 2 : bn);  // a pair CTA loads bn/2 rows
+    // the single-CTA kernel loads only the xq rows that exist (in 16-row steps), the pair kernel 128
+    q.a_rows = pair ? kI8BM : (int)(p.m >= kI8BM ? kI8BM : ceil_div(p.m, 16) * 16);
+    int rc = make_gemm_maps(&ma, &mb, xq, p.m, p.k, packed, p.n, pair ? bn / 2 : bn, q.a_rows);  // a pair CTA loads bn/2 rows
     if (rc) return rc;
     std::memset(&my, 0, sizeof(my));
     q.tma_y = !p.acc_out && reinterpret_cast<uintptr_t>(p.y) % 16 == 0 && p.ldy % 4 == 0;
