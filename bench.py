@@ -118,11 +118,12 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def traffic_per_launch(launches: int):
-    """DRAM bytes per launch of the grouped decode GEMV, from the committed ncu summary (or None).
+def traffic_per_launch(launches: int, layers: int):
+    """DRAM bytes per launch of the grouped decode GEMV, from the committed ncu summary (or None):
+    the step's traffic (per layer x layers) over the step's ``launches``.
 
     profiles/gemv_w8_stack_decode_traffic.md records dram__bytes_read.sum + dram__bytes_write.sum
-    summed over every launch of a captured decode step of the stack, and the launches it covered.
+    summed over every launch of a captured decode step of the stack, per layer.
     """
     p = ROOT / "profiles" / "gemv_w8_stack_decode_traffic.md"
     if not p.exists():
@@ -134,7 +135,7 @@ def traffic_per_launch(launches: int):
             vals[k] = float(v)
     if len(vals) < 2:
         return None
-    return int(vals["traffic_bytes_per_step_layer:"[:-1]] / vals["launches_per_layer:"[:-1]])
+    return int(vals["traffic_bytes_per_step_layer:"[:-1]] * layers / launches)
 
 
 def dist_setup(args):
@@ -751,7 +752,7 @@ def main() -> None:
                          "per": "GPU" if world > 1 else "job",
                          "bytes_per_launch": total_bytes // world // launches,
                          "us_per_launch": round(ms * 1e3 / launches, 3),
-                         "traffic": traffic_per_launch(launches) if world == 1 else None,
+                         "traffic": traffic_per_launch(launches, len(stack.layers)) if world == 1 else None,
                          "standalone_gateup": {"achieved": round(achieved, 1),
                                                "frac": round(achieved / pk["hbm_gbs"], 4),
                                                "bytes_per_launch": gu_bytes, "us_per_launch": round(gu_ms * 1e3, 3)}},

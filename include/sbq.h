@@ -207,6 +207,19 @@ typedef struct sbq_gemv_job {
  * such a group. */
 SBQ_API int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m, void* stream);
 
+/* sbq_gemv_w8_group with the first n_ready jobs (0 <= n_ready <= njobs) marked ready: their x (and
+ * everything they read) was complete before the previous kernel on the stream began its work, i.e.
+ * it was written two or more kernels back.  Their units run first and do not wait for the previous
+ * kernel to end; the other jobs' units wait for it as in sbq_gemv_w8_group.  So a decode step can
+ * stream projections whose inputs are older (side outputs, a layer's later consumers) across the
+ * boundary that the other jobs must wait at.  Conditions: the previous kernel on the stream is a
+ * grouped GEMV launch of this library (sbq_gemv_w8_group[_ready], sbq_gemv_w8, sbq_mlp_gateup_w8,
+ * sbq_linear_w8 at decode sizes) or a kernel launched without programmatic dependent launch - those
+ * let the next kernel begin only after their own wait for the kernel before them; and a ready job's
+ * y is neither read nor written by the previous kernel.  Results are those of sbq_gemv_w8_group. */
+SBQ_API int sbq_gemv_w8_group_ready(const sbq_gemv_job* jobs, int njobs, int n_ready, int x_dtype, int64_t m,
+                                    void* stream);
+
 /* The K split a grouped launch would choose (host only, no device call): shapes[3 i .. 3 i + 2] =
  * {n, k, matrices (1, or 2 for a fused gate/up job)} of job i, `slots` = CTAs the launch may use (3
  * per SM at m <= 8, 2 per SM at 9..16 rows).  parts[i] receives the K parts of each of job i's

@@ -67,6 +67,7 @@ SIGNATURES = {
     "sbq_lora_pair_w8": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _c_int,
                                   _c_i64, _vp]),
     "sbq_gemv_w8_group": (_c_int, [ctypes.POINTER(GemvJob), _c_int, _c_int, _c_i64, _vp]),
+    "sbq_gemv_w8_group_ready": (_c_int, [ctypes.POINTER(GemvJob), _c_int, _c_int, _c_int, _c_i64, _vp]),
     "sbq_gemv_plan_parts": (_c_int, [ctypes.POINTER(_c_i64), _c_int, _c_int, _c_i64, ctypes.POINTER(_c_int)]),
     "sbq_gemv_program_bytes": (_sz, [_c_int]),
     "sbq_gemv_program_sync_bytes": (_sz, [_c_int]),

@@ -71,6 +71,7 @@ constexpr int kMaxJobs = 8;
 struct GemvGroup {
     GemvJob job[kMaxJobs];
     int njobs;
+    int n_ready;                     // jobs [0, n_ready) are ready: their x is not the previous kernel's output
     int total_units;                 // units of all jobs (a unit = one K part of one 16-row tile)
     int unit_begin[kMaxJobs + 1];    // first unit of each job
     int parts[kMaxJobs];             // K parts per tile of each job (1: a tile is one unit)
@@ -383,10 +384,12 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, unsigned* cl
 // job and the warp split are read once per unit from the first chunk's stage.
 // False (warp-uniformly) on a timeout.
 // `ci` / `units`: ring position and units done so far (both continue across calls).
+// `waited`: null when the consumers have waited for the previous kernel already; else the flag of a
+// deferred wait, taken before the first unit of a job that is not ready.
 template <int XK, int MT, bool PEER>
 __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* ring, float* red, uint64_t* full,
                                               uint64_t* empty, const int4* meta, const PeerSync& ps,
-                                              uint32_t& ci, int& units) {
+                                              uint32_t& ci, int& units, bool* waited = nullptr) {
     constexpr int S = kMaxStages;
     constexpr int kStageBytes = kChunkTiles * kTileBytes;
     constexpr int kEntries = MT * 8 * 16;
@@ -406,6 +409,13 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
         }
         const int j = md.x & 0xff, part = md.x >> 8, tile = md.y, i0 = md.z, cpt = md.w;
         const GemvJob& jb = grp.job[j];
+        if (waited && !*waited && j >= grp.n_ready) {
+            // the first unit whose x is the previous kernel's output: wait for that kernel, then let
+            // the next launch begin (see gemv_w8_kernel)
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+            *waited = true;
+        }
         const bool two = jb.w1 != nullptr;
         const int C = jb.chunk_tiles;
         const int mat = two ? warp >> 2 : 0, slot = two ? warp & 3 : warp;
@@ -621,25 +631,38 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? kCtasPerSm : 2)
         tc::fence_mbar_init();
     }
     __syncthreads();
-    // the next launch may start its own weight stream now (it waits for this grid before reading x)
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // Programmatic dependent launch.  The weights never depend on the previous kernel, so the
+    // producer streams at once; the consumers wait for the previous kernel before reading x.  The
+    // next launch may begin once every CTA here has passed that wait (single GPU; a sharded launch
+    // at once): the ready jobs of the next launch read outputs of the kernel before this one, which
+    // has then completed.  Ready jobs' units come first and run before the wait, which the
+    // consumers take at their first unit of another job (or at the end).
+    if (PEER) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (warp == kGemvWarps) {
         uint32_t pci = 0;
         if (lane == 0 && !produce_units(grp, grp.claim, ring, full, empty, meta, pci)) tc::raise_error(SBQ_ERR_TIMEOUT);
         return;
     }
+    bool waited = true;
     if (PEER && ps.wait_count) {
         // x is the previous launch's output on every rank (this one included): its signal, not
         // the end of the previous grid, is what the consumers need, so they start as soon as the
         // last rank's last CTA has published (the release/acquire pair orders every store before)
         if (threadIdx.x == 0) peer_wait(ps.wait_count, ps.wait_state, ps.wait_expected, ps.wait_limit_ns);
         consumers_sync();
-    } else {
+    } else if (PEER || grp.n_ready == 0) {
         asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
+        if (!PEER) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    } else {
+        waited = false;
     }
     uint32_t ci = 0;
     int units = 0;
-    const bool ok = consume_units<XK, MT, PEER>(grp, ring, red, full, empty, meta, ps, ci, units);
+    const bool ok = consume_units<XK, MT, PEER>(grp, ring, red, full, empty, meta, ps, ci, units, &waited);
+    if (!waited) {  // this CTA's units were all ready ones
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    }
     if (!consumers_sync_and(ok) && threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
     if (PEER && warp == 0) peer_publish(ps, lane);  // also after a timeout, so that the other ranks do not wait in vain
 }
@@ -938,11 +961,17 @@ struct PartsKeyHash {
     }
 };
 
-static void unit_order(int nj, const int64_t* tile_bytes, const int* parts, int* perm) {
+// Job order of a launch: the ready jobs (the first n_ready) before the others, each class by
+// decreasing unit bytes (stable).
+static void unit_order(int nj, const int64_t* tile_bytes, const int* parts, int* perm, int n_ready = 0) {
     for (int i = 0; i < nj; ++i) perm[i] = i;
-    for (int i = 1; i < nj; ++i)  // stable insertion sort by decreasing unit bytes
-        for (int k = i; k > 0 && tile_bytes[perm[k]] * parts[perm[k - 1]] > tile_bytes[perm[k - 1]] * parts[perm[k]]; --k)
-            std::swap(perm[k], perm[k - 1]);
+    auto before = [&](int a, int b) {
+        const bool ra = a < n_ready, rb = b < n_ready;
+        if (ra != rb) return ra;
+        return tile_bytes[a] * parts[b] > tile_bytes[b] * parts[a];
+    };
+    for (int i = 1; i < nj; ++i)  // stable insertion sort
+        for (int k = i; k > 0 && before(perm[k], perm[k - 1]); --k) std::swap(perm[k], perm[k - 1]);
 }
 
 static void choose_parts(const PartsKey& key, int* parts_out) {
@@ -1028,7 +1057,7 @@ static int plan_units(GemvGroup& grp, PeerSync& ps, int slots, int m, int lane) 
     choose_parts(key, parts);
     const int stride = 2 * (m > 8 ? 2 : 1) * 128;  // floats per part partial (entries of both matrices)
     int perm[kMaxJobs];
-    unit_order(nj, tile_bytes, parts, perm);
+    unit_order(nj, tile_bytes, parts, perm, grp.n_ready);
     GemvGroup sorted = grp;
     PeerSync pss = ps;
     int units = 0, split_tiles = 0;
@@ -1421,12 +1450,15 @@ extern "C" int sbq_lora_pair_w8(const void* x, int x_dtype, int64_t ldx, const v
     return check_launch("lora_pair_w8");
 }
 
-extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m, void* stream) {
+extern "C" int sbq_gemv_w8_group_ready(const sbq_gemv_job* jobs, int njobs, int n_ready, int x_dtype, int64_t m,
+                                       void* stream) {
     if (!jobs || njobs < 1 || njobs > kMaxJobs)
         return set_error(SBQ_ERR_INVALID_ARGUMENT, "njobs must be 1..%d", kMaxJobs);
+    if (n_ready < 0 || n_ready > njobs) return set_error(SBQ_ERR_INVALID_ARGUMENT, "n_ready must be 0..njobs");
     if (m < 1 || m > 16) return set_error(SBQ_ERR_UNSUPPORTED, "a grouped launch takes 1..16 rows of x (m=%lld)", (long long)m);
     GemvGroup grp{};
     grp.njobs = njobs;
+    grp.n_ready = n_ready;
     for (int i = 0; i < njobs; ++i) {
         const sbq_gemv_job& j = jobs[i];
         int st = check_linear_args(j.x, x_dtype, j.ldx, j.packed, j.scale, m, j.n, j.k, j.y, j.y_dtype, j.ldy);
@@ -1445,6 +1477,10 @@ extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtyp
     const int st = dispatch_group(grp, x_kind(x_dtype), m > 8 ? 2 : 1, s);
     if (st) return st;
     return check_launch("gemv_w8_group");
+}
+
+extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m, void* stream) {
+    return sbq_gemv_w8_group_ready(jobs, njobs, 0, x_dtype, m, stream);
 }
 
 extern "C" int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m,

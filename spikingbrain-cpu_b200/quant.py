@@ -238,11 +238,16 @@ class Int8Linear(_PackedLinear):
         return out.to("cpu") if on_host else out
 
 
-def gemv_group(jobs, x_dtype: torch.dtype, m: int, device: torch.device) -> None:
+def gemv_group(jobs, x_dtype: torch.dtype, m: int, device: torch.device, n_ready: int = 0) -> None:
     """Run several decode projections (``Int8Linear.gemv_job`` / ``FusedGatedMLP.gateup_job``) in one
-    launch: up to 8 jobs, all with ``m`` <= 16 rows of x of dtype ``x_dtype``."""
+    launch: up to 8 jobs, all with ``m`` <= 16 rows of x of dtype ``x_dtype``.  The first ``n_ready``
+    jobs read inputs written two or more launches back and run without waiting for the previous
+    launch (sbq_gemv_w8_group_ready: the previous kernel must be a grouped GEMV launch)."""
     arr = (L.GemvJob * len(jobs))(*jobs)
-    L.call("sbq_gemv_w8_group", arr, len(jobs), _DTYPE_CODE[x_dtype], m, _stream(device))
+    if n_ready:
+        L.call("sbq_gemv_w8_group_ready", arr, len(jobs), n_ready, _DTYPE_CODE[x_dtype], m, _stream(device))
+    else:
+        L.call("sbq_gemv_w8_group", arr, len(jobs), _DTYPE_CODE[x_dtype], m, _stream(device))
 
 
 class DynamicInt8Linear(_PackedLinear):

@@ -257,7 +257,7 @@ class ProjectionStack(nn.Module):
     """The stack; ``forward(x)`` maps fp16 [m, hidden] to fp16 [m, hidden] on the device."""
 
     def __init__(self, layers: int = W.LAYERS, hidden: int = W.HIDDEN, inter: int = W.INTER, seed: int = 4,
-                 device=None, group=None, exchange: str = "peer"):
+                 device=None, group=None, exchange: str = "peer", overlap: bool = True):
         super().__init__()
         import torch.distributed as dist
 
@@ -275,6 +275,8 @@ class ProjectionStack(nn.Module):
                                     for i in range(layers))
         self.exchange = exchange if self.world > 1 else "none"
         self.peer = PeerExchange(self) if self.exchange == "peer" else None
+        # one GPU, decode sizes: the side-output projections run as ready jobs of the next launch
+        self.overlap = overlap and self.world == 1
         self._side = (None, False)  # the last forward's last-layer side outputs, reordered on access?
 
     @property
@@ -305,7 +307,12 @@ class ProjectionStack(nn.Module):
 
         Decode sizes (m <= 16) run each layer as two grouped launches: [gate/up, q|k|v|delta_in]
         (both read x) and [down, o, delta_out] (after their inputs are gathered); o's output is the
-        next layer's input.
+        next layer's input.  On one GPU (``overlap``) the side outputs move to the next layer's first
+        launch, as ready jobs whose inputs are two launches old: layer i runs [down(h), delta_out of
+        layer i - 1 | gate/up, q|k|v|delta_in] and [o], and one last launch computes the last layer's
+        side outputs.  The ready jobs stream while the o launch before them ends, so that launch
+        boundary overlaps work (measured at full size: 1.69-1.71 -> 1.65 ms per step at batch 1,
+        2.06 -> 1.94 ms at batch 8; the side outputs split between both launches gained less).
         """
         if x.shape[0] <= 16:
             if self.peer is not None:
@@ -340,11 +347,38 @@ class ProjectionStack(nn.Module):
         self._side = (torch.cat([side, dout], 1), False)
         return x
 
+    def _forward_overlapped(self, x: torch.Tensor) -> torch.Tensor:
+        from .quant import gemv_group
+
+        hd, m = self.hidden, x.shape[0]
+        keep = []  # every buffer stays allocated until the step is enqueued: no launch reuses
+        prev = None  # memory that the launch before it may still be reading
+        for layer in self.layers:
+            qkvd = x.new_empty(m, 4 * hd)
+            h = x.new_empty(m, self.inter)
+            od = x.new_empty(m, 2 * hd)
+            xn = x.new_empty(m, hd)
+            keep += [qkvd, h, od, xn]
+            ready = [] if prev is None else [prev[0].mlp.down_proj.gemv_job(prev[2], prev[3][:, :hd]),
+                                             prev[0].dout.gemv_job(prev[1][:, 3 * hd:], prev[3][:, hd:])]
+            gemv_group(ready + [layer.mlp.gateup_job(x, h), layer.qkvd.gemv_job(x, qkvd)], x.dtype, m, x.device,
+                       n_ready=len(ready))
+            gemv_group([layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], xn)], x.dtype, m, x.device)
+            prev = (layer, qkvd, h, od)
+            x = xn
+        last, qkvd, h, od = prev
+        gemv_group([last.mlp.down_proj.gemv_job(h, od[:, :hd]), last.dout.gemv_job(qkvd[:, 3 * hd:], od[:, hd:])],
+                   x.dtype, m, x.device, n_ready=2)
+        self._side = (od, False)
+        return x
+
     def _forward_grouped(self, x: torch.Tensor) -> torch.Tensor:
         from .quant import gemv_group
 
         hd, w = self.hidden, self.world
         m = x.shape[0]
+        if self.overlap:
+            return self._forward_overlapped(x)
         for layer in self.layers:
             qkvd = x.new_empty(m, 4 * hd // w)
             h = x.new_empty(m, self.inter // w)
@@ -368,7 +402,7 @@ class ProjectionStack(nn.Module):
         if program:
             return 1
         if m <= 16:
-            return len(self.layers) * 2 + (1 if self.peer is not None else 0)
+            return len(self.layers) * 2 + (1 if self.peer is not None or self.overlap else 0)
         return len(self.layers) * 5
 
 

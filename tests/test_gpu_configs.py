@@ -158,3 +158,34 @@ def test_config4_prefill_8192_sampled_rows(sbq, full_width_stack):
     want, want_side = _oracle_stack(stack, x.float().cpu().numpy()[rows], gate_rounded=True)
     assert R.rel_l2(y[rows], want) < REL_L2
     assert R.rel_l2(side[rows], want_side) < REL_L2
+
+
+# Configuration 4 sharded over 4 and 8 GPUs gives every rank narrow projections: q|k|v|delta_in as
+# one [4 * 4096 / g, 4096] shard, o and delta_out [4096 / g, 4096], gate/up [12288 / g, 4096] (the
+# fused epilogue) and down [4096 / g, 12288].  One GPU runs them at the decode batches and the
+# prefill size, so the kernels' tile, split-K and CTA-pair choices at these widths are checked
+# against the oracle without a multi-GPU box (rows covering every M tile at m = 8192).
+@pytest.mark.parametrize("world", [4, 8])
+@pytest.mark.parametrize("m", [1, 8, 64, 8192])
+def test_config4_rank_shard_shapes(sbq, world, m):
+    hd, it = 4096, 12288
+    rows = np.unique(np.concatenate([np.arange(0, m, 256), np.arange(255, m, 256), [m - 1]])) if m > 64 \
+        else np.arange(m)
+    xs = {k: sbq.workloads.activation(m, k, seed=k + m + world) for k in (hd, it)}
+    for n, k in ((4 * hd // world, hd), (hd // world, hd), (hd // world, it)):
+        w = sbq.workloads.float_weight(n, k, seed=n + k + world)
+        q, s = R.quantize_per_channel(w.numpy())
+        y = sbq.Int8Linear(w, None)(xs[k].cuda())
+        want = R.int8_linear(xs[k].float().numpy()[rows], q, s)
+        assert R.rel_l2(_np(y)[rows], want) < REL_L2, (n, k)
+    n = it // world
+    g = sbq.workloads.float_weight(n, hd, seed=world + 6)
+    u = sbq.workloads.float_weight(n, hd, seed=world + 7)
+    d = sbq.workloads.float_weight(hd, it, seed=world + 8)
+    mlp = sbq.FusedGatedMLP(sbq.Int8Linear(g, None), sbq.Int8Linear(u, None), sbq.Int8Linear(d, None), shards=world)
+    h = mlp.gateup_into(xs[hd].cuda(), torch.empty(m, n, dtype=torch.float16, device="cuda"))
+    x_rows = xs[hd].float().numpy()[rows]
+    want = R.silu(R.int8_linear(x_rows, *R.quantize_per_channel(g.numpy()))) * \
+        R.int8_linear(x_rows, *R.quantize_per_channel(u.numpy()))
+    assert R.rel_l2(_np(h)[rows], want) < REL_L2
+    assert sbq._lib.load().sbq_check_device_error() == 0

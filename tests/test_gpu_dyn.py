@@ -244,3 +244,27 @@ def test_decode_split_k_bit_exact(sbq, m, n, k, mode):
     assert np.array_equal(_bits(y.cpu().numpy()), _bits(ry))
     assert torch.equal(mod(x.cuda()), y)
     assert sbq._lib.load().sbq_check_device_error() == 0
+
+
+# decode-sized calls through the module (one-CTA quantiser, split-K GEMM): k not a multiple of 128
+# leaves a ragged last k-block; x rows with a stride above k; an all-zero token; the largest k.
+@pytest.mark.parametrize("m,n,k", [(1, 256, 144), (2, 136, 4112), (7, 1000, 2560), (8, 4096, 12288),
+                                   (9, 300, 512), (1, 64, 12304)])
+@pytest.mark.parametrize("xdtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("mode", ["per_tensor", "per_token"])
+def test_decode_fused_quantisation_bit_exact(sbq, m, n, k, xdtype, mode):
+    w = sbq.workloads.float_weight(n, k, seed=n + k)
+    bias = torch.randn(n) if m % 2 else None
+    wide = sbq.workloads.activation(m, k + 64, seed=m + k, dtype=torch.float32) * 3.0
+    if m > 1:
+        wide[-1] = 0.0
+    x = wide.to(xdtype).cuda()[:, 32:32 + k]  # 16-byte aligned rows, row stride k + 64
+    assert x.stride(0) == k + 64
+    q, sc = R.quantize_per_channel(w.numpy())
+    mod = sbq.DynamicInt8Linear(w, bias, mode=mode)
+    y = mod(x).cpu().numpy()
+    xf = x.float().cpu().numpy()
+    b = None if bias is None else bias.numpy()
+    ry = R.dyn_linear(xf, q, sc, b)[0] if mode == "per_tensor" else R.tok_linear(xf, q, sc, b)[0]
+    assert np.array_equal(_bits(y), _bits(ry)), "mismatch fraction %.4f" % float((y != ry).mean())
+    assert sbq._lib.load().sbq_check_device_error() == 0

@@ -103,3 +103,27 @@ def test_module_api_path_host_and_device(sbq, m):
     assert torch.equal(y_host, y_dev.cpu())
     want, _ = _oracle_stack(stack, x)
     assert R.rel_l2(y_host.float().numpy(), want.astype(np.float32)) < 1e-3
+
+
+@pytest.mark.parametrize("m", [1, 8])
+def test_overlapped_launches_match_plain_grouping(sbq, m):
+    # one GPU runs each layer's side outputs as ready jobs of the next launch (they stream while
+    # the launch before ends); the results equal the plain two-launches-per-layer grouping bit for
+    # bit, eagerly and over repeated CUDA-graph replays (which would expose a launch that reads an
+    # input before it is written)
+    kw = dict(layers=4, hidden=1024, inter=3072, seed=7)
+    ov = sbq.stack.ProjectionStack(**kw)
+    plain = sbq.stack.ProjectionStack(overlap=False, **kw)
+    assert ov.overlap and not plain.overlap
+    assert ov.launches_per_step(m) == plain.launches_per_step(m) + 1
+    x = sbq.workloads.activation(m, 1024, seed=8, device="cuda")
+    want = plain(x)
+    want_side = plain.side.clone()
+    assert torch.equal(ov(x), want) and torch.equal(ov.side, want_side)
+    runner = sbq.stack.CapturedStack(ov, m=m)
+    runner.x.copy_(x)
+    for _ in range(20):
+        assert torch.equal(runner.run(), want)
+    assert torch.equal(ov.side, want_side)
+    runner.release()
+    assert sbq._lib.load().sbq_check_device_error() == 0
