@@ -286,6 +286,13 @@ typedef struct sbq_peer_group {
 } sbq_peer_group;
 SBQ_API int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m,
                                    const sbq_peer_group* peers, void* stream);
+/* sbq_gemv_w8_group_peer with the first n_ready jobs ready (see sbq_gemv_w8_group_ready): their x
+ * was gathered on every rank two or more launches back, so their units run before the launch's wait
+ * on wait_count, which the other jobs' units take as usual.  Each CTA lets the next launch begin
+ * only after its own wait (in every sharded launch), so the launch before the previous one has then
+ * completed on every rank.  The previous launch must be a grouped GEMV launch of this library. */
+SBQ_API int sbq_gemv_w8_group_peer_ready(const sbq_gemv_job* jobs, int njobs, int n_ready, int x_dtype, int64_t m,
+                                         const sbq_peer_group* peers, void* stream);
 /* The same wait as a one-CTA launch: the end of a sharded step, before anything else reads the
  * last launch's gathered output.  limit_ns: bound of the wait (0 = 10 s). */
 SBQ_API int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned expected, unsigned long long limit_ns,

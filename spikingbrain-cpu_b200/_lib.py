@@ -81,6 +81,8 @@ SIGNATURES = {
     "sbq_peer_close": (_c_int, [_vp]),
     "sbq_gemv_w8_group_peer": (_c_int, [ctypes.POINTER(GemvJob), _c_int, _c_int, _c_i64, ctypes.POINTER(PeerGroup),
                                         _vp]),
+    "sbq_gemv_w8_group_peer_ready": (_c_int, [ctypes.POINTER(GemvJob), _c_int, _c_int, _c_int, _c_i64,
+                                              ctypes.POINTER(PeerGroup), _vp]),
     "sbq_peer_wait": (_c_int, [_vp, _vp, ctypes.c_uint, ctypes.c_ulonglong, _vp]),
     "sbq_gemv_program_build_peer": (_c_int, [ctypes.POINTER(GemvJob), ctypes.POINTER(ctypes.c_int), _c_int, _c_int,
                                              _c_i64, ctypes.POINTER(_vp), _c_int, ctypes.POINTER(_vp), _vp, _sz]),

@@ -384,12 +384,48 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, unsigned* cl
 // job and the warp split are read once per unit from the first chunk's stage.
 // False (warp-uniformly) on a timeout.
 // `ci` / `units`: ring position and units done so far (both continue across calls).
+// The consumers' wait for the producer of x when it is deferred past the ready jobs' units: the
+// previous grid (griddepcontrol.wait, every thread), or in a sharded launch the producing launch's
+// signal on every rank - thread 0 waits (peer_wait: once per CTA, it also records the CTA's arrival)
+// and releases the other consumer warps through a shared flag, which they poll with a bound (a warp
+// that gave up after a timeout elsewhere cannot hold them at a barrier).  Then the CTA lets the next
+// launch begin.
+template <bool PEER>
+__device__ __forceinline__ void deferred_wait(const PeerSync& ps, int* s_flag) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (PEER && ps.wait_count) {
+        if (lane == 0) {
+            if (warp == 0) {
+                peer_wait(ps.wait_count, ps.wait_state, ps.wait_expected, ps.wait_limit_ns);
+                asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(tc::smem_u32(s_flag)), "r"(1u) : "memory");
+            } else {
+                const uint64_t t0 = tc::now_ns();
+                for (uint32_t i = 1;; ++i) {
+                    unsigned v;
+                    asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(tc::smem_u32(s_flag)) : "memory");
+                    if (v) break;
+                    __nanosleep(32);
+                    if ((i & 63) == 0 && tc::now_ns() - t0 > ps.wait_limit_ns + 1000000000ull) {
+                        tc::raise_error(SBQ_ERR_TIMEOUT);
+                        break;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // `waited`: null when the consumers have waited for the previous kernel already; else the flag of a
-// deferred wait, taken before the first unit of a job that is not ready.
+// deferred wait (deferred_wait), taken before the first unit of a job that is not ready.
 template <int XK, int MT, bool PEER>
 __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* ring, float* red, uint64_t* full,
                                               uint64_t* empty, const int4* meta, const PeerSync& ps,
-                                              uint32_t& ci, int& units, bool* waited = nullptr) {
+                                              uint32_t& ci, int& units, bool* waited = nullptr,
+                                              int* s_flag = nullptr) {
     constexpr int S = kMaxStages;
     constexpr int kStageBytes = kChunkTiles * kTileBytes;
     constexpr int kEntries = MT * 8 * 16;
@@ -410,10 +446,8 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
         const int j = md.x & 0xff, part = md.x >> 8, tile = md.y, i0 = md.z, cpt = md.w;
         const GemvJob& jb = grp.job[j];
         if (waited && !*waited && j >= grp.n_ready) {
-            // the first unit whose x is the previous kernel's output: wait for that kernel, then let
-            // the next launch begin (see gemv_w8_kernel)
-            asm volatile("griddepcontrol.wait;" ::: "memory");
-            asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+            // the first unit whose x is the previous launch's output (see gemv_w8_kernel)
+            deferred_wait<PEER>(ps, s_flag);
             *waited = true;
         }
         const bool two = jb.w1 != nullptr;
@@ -632,37 +666,37 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? kCtasPerSm : 2)
     }
     __syncthreads();
     // Programmatic dependent launch.  The weights never depend on the previous kernel, so the
-    // producer streams at once; the consumers wait for the previous kernel before reading x.  The
-    // next launch may begin once every CTA here has passed that wait (single GPU; a sharded launch
-    // at once): the ready jobs of the next launch read outputs of the kernel before this one, which
-    // has then completed.  Ready jobs' units come first and run before the wait, which the
-    // consumers take at their first unit of another job (or at the end).
-    if (PEER) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // producer streams at once; the consumers wait for the previous kernel (or, sharded, for the
+    // producing launch's signal on every rank) before reading x.  The next launch may begin once
+    // every CTA here has passed that wait: the ready jobs of the next launch read outputs of the
+    // launch before this one, which has then completed (on every rank).  Ready jobs' units come
+    // first and run before the wait, which the consumers take at their first unit of another job
+    // (or at the end).
+    __shared__ int s_flag;
+    if (threadIdx.x == 0) s_flag = 0;
+    __syncthreads();
     if (warp == kGemvWarps) {
         uint32_t pci = 0;
         if (lane == 0 && !produce_units(grp, grp.claim, ring, full, empty, meta, pci)) tc::raise_error(SBQ_ERR_TIMEOUT);
         return;
     }
-    bool waited = true;
-    if (PEER && ps.wait_count) {
-        // x is the previous launch's output on every rank (this one included): its signal, not
-        // the end of the previous grid, is what the consumers need, so they start as soon as the
-        // last rank's last CTA has published (the release/acquire pair orders every store before)
-        if (threadIdx.x == 0) peer_wait(ps.wait_count, ps.wait_state, ps.wait_expected, ps.wait_limit_ns);
-        consumers_sync();
-    } else if (PEER || grp.n_ready == 0) {
-        asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
-        if (!PEER) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    } else {
-        waited = false;
+    bool waited = grp.n_ready == 0;
+    if (waited) {
+        if (PEER && ps.wait_count) {
+            // x is the previous launch's output on every rank (this one included): its signal, not
+            // the end of the previous grid, is what the consumers need, so they start as soon as the
+            // last rank's last CTA has published (the release/acquire pair orders every store before)
+            if (threadIdx.x == 0) peer_wait(ps.wait_count, ps.wait_state, ps.wait_expected, ps.wait_limit_ns);
+            consumers_sync();
+        } else {
+            asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
+        }
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     }
     uint32_t ci = 0;
     int units = 0;
-    const bool ok = consume_units<XK, MT, PEER>(grp, ring, red, full, empty, meta, ps, ci, units, &waited);
-    if (!waited) {  // this CTA's units were all ready ones
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    }
+    const bool ok = consume_units<XK, MT, PEER>(grp, ring, red, full, empty, meta, ps, ci, units, &waited, &s_flag);
+    if (!waited) deferred_wait<PEER>(ps, &s_flag);  // this warp ran ready units only
     if (!consumers_sync_and(ok) && threadIdx.x == 0) tc::raise_error(SBQ_ERR_TIMEOUT);
     if (PEER && warp == 0) peer_publish(ps, lane);  // also after a timeout, so that the other ranks do not wait in vain
 }
@@ -1483,11 +1517,12 @@ extern "C" int sbq_gemv_w8_group(const sbq_gemv_job* jobs, int njobs, int x_dtyp
     return sbq_gemv_w8_group_ready(jobs, njobs, 0, x_dtype, m, stream);
 }
 
-extern "C" int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m,
-                                      const sbq_peer_group* peers, void* stream) {
+extern "C" int sbq_gemv_w8_group_peer_ready(const sbq_gemv_job* jobs, int njobs, int n_ready, int x_dtype, int64_t m,
+                                            const sbq_peer_group* peers, void* stream) {
     if (!peers) return set_error(SBQ_ERR_INVALID_ARGUMENT, "null peer description");
     if (!jobs || njobs < 1 || njobs > kMaxJobs)
         return set_error(SBQ_ERR_INVALID_ARGUMENT, "njobs must be 1..%d", kMaxJobs);
+    if (n_ready < 0 || n_ready > njobs) return set_error(SBQ_ERR_INVALID_ARGUMENT, "n_ready must be 0..njobs");
     if (m < 1 || m > 16) return set_error(SBQ_ERR_UNSUPPORTED, "a grouped launch takes 1..16 rows of x (m=%lld)", (long long)m);
     const sbq_peer_group& pg = *peers;
     if (pg.nranks < 1 || pg.nranks > kMaxPeers)
@@ -1512,6 +1547,7 @@ extern "C" int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x
     }
     GemvGroup grp{};
     grp.njobs = njobs;
+    grp.n_ready = n_ready;
     for (int i = 0; i < njobs; ++i) {
         const sbq_gemv_job& j = jobs[i];
         int st = check_linear_args(j.x, x_dtype, j.ldx, j.packed, j.scale, m, j.n, j.k, j.y, j.y_dtype, j.ldy);
@@ -1536,6 +1572,11 @@ extern "C" int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x
     const int st = dispatch_group_t<true>(grp, ps, x_kind(x_dtype), m > 8 ? 2 : 1, static_cast<cudaStream_t>(stream));
     if (st) return st;
     return check_launch("gemv_w8_group_peer");
+}
+
+extern "C" int sbq_gemv_w8_group_peer(const sbq_gemv_job* jobs, int njobs, int x_dtype, int64_t m,
+                                      const sbq_peer_group* peers, void* stream) {
+    return sbq_gemv_w8_group_peer_ready(jobs, njobs, 0, x_dtype, m, peers, stream);
 }
 
 extern "C" int sbq_peer_wait(const unsigned* count, unsigned* state, unsigned expected, unsigned long long limit_ns,

@@ -151,6 +151,7 @@ class PeerExchange:
         self.done = [[take(128), take(128)] for _ in stack.layers]   # CTA count-out of launch 1 / 2
         self.state = [[take(128), take(128)] for _ in stack.layers]  # wait state of launch 1 / 2
         self.final_state = take(128)
+        self.cnt_last, self.done_last, self.state_last = take(sig), take(128), take(128)  # side-output launch
         self.nstages = 2 * len(stack.layers)
         self.prog_sync = take(int(self.lib.sbq_gemv_program_sync_bytes(self.nstages)))  # sharded decode program
         self.nbytes = off
@@ -207,6 +208,8 @@ class PeerExchange:
             raise ValueError("the peer exchange was laid out for %d rows (got %d)" % (self.m_max, m))
         hd, it, w, r = st.hidden, st.inter, st.world, st.rank
         code, stream = _DTYPE_CODE[x.dtype], _stream(x.device)
+        if st.overlap:
+            return self._forward_overlapped(x, code, stream)
         cur = x
         for i, layer in enumerate(st.layers):
             q_off, h_off, od_off, x_off = self.buf[i]
@@ -226,6 +229,49 @@ class PeerExchange:
             st._side = (od, False)  # stored in place at full width
             cur = xn
         L.call("sbq_peer_wait", ctypes.c_void_p(self.base + self.cnt[-1][1]),
+               ctypes.c_void_p(self.base + self.final_state), w, 0, stream)
+        return cur
+
+    def _forward_overlapped(self, x: torch.Tensor, code: int, stream) -> torch.Tensor:
+        """forward with the side outputs of layer i - 1 as ready jobs of layer i's first launch
+        (their inputs are complete on every rank once the o launch in between has seen its signal),
+        [o] alone in the second launch, and one last launch for the last layer's side outputs."""
+        L, st = self.L, self.stack
+        m = x.shape[0]
+        hd, it, w, r = st.hidden, st.inter, st.world, st.rank
+        hs, qs, s = it // w, 4 * hd // w, hd // w
+        cur = x
+        for i, layer in enumerate(st.layers):
+            q_off, h_off, od_off, x_off = self.buf[i]
+            qkvd, h, od, xn = (self.view(i, k, m) for k in range(4))
+            jobs, dests = [], []
+            if i > 0:
+                pq, ph, pod = (self.view(i - 1, k, m) for k in range(3))
+                prev, pod_off = st.layers[i - 1], self.buf[i - 1][2]
+                jobs += [prev.mlp.down_proj.gemv_job(ph, pod[:, r * s:(r + 1) * s]),
+                         prev.dout.gemv_job(pq[:, 3 * hd:], pod[:, hd + r * s:hd + (r + 1) * s])]
+                dests += [(pod_off, r * s), (pod_off, hd + r * s)]
+            n_ready = len(jobs)
+            jobs += [layer.mlp.gateup_job(cur, h[:, r * hs:(r + 1) * hs]),
+                     layer.qkvd.gemv_job(cur, qkvd[:, r * qs:(r + 1) * qs])]
+            dests += [(h_off, r * hs), (q_off, r * qs)]
+            pg = self._group(dests, self.cnt[i][0], self.done[i][0], None if i == 0 else self.cnt[i - 1][1],
+                             self.state[i][0])
+            L.call("sbq_gemv_w8_group_peer_ready", (L.GemvJob * len(jobs))(*jobs), len(jobs), n_ready, code, m,
+                   ctypes.byref(pg), stream)
+            pg = self._group([(x_off, r * s)], self.cnt[i][1], self.done[i][1], self.cnt[i][0], self.state[i][1])
+            L.call("sbq_gemv_w8_group_peer", (L.GemvJob * 1)(layer.o.gemv_job(qkvd[:, 2 * hd:3 * hd], xn[:, r * s:(r + 1) * s])),
+                   1, code, m, ctypes.byref(pg), stream)
+            cur = xn
+        last, (q_off, h_off, od_off, _) = st.layers[-1], self.buf[-1]
+        qkvd, h, od = (self.view(len(st.layers) - 1, k, m) for k in range(3))
+        jobs = [last.mlp.down_proj.gemv_job(h, od[:, r * s:(r + 1) * s]),
+                last.dout.gemv_job(qkvd[:, 3 * hd:], od[:, hd + r * s:hd + (r + 1) * s])]
+        pg = self._group([(od_off, r * s), (od_off, hd + r * s)], self.cnt_last, self.done_last, self.cnt[-1][1],
+                         self.state_last)
+        L.call("sbq_gemv_w8_group_peer_ready", (L.GemvJob * 2)(*jobs), 2, 2, code, m, ctypes.byref(pg), stream)
+        st._side = (od, False)  # stored in place at full width
+        L.call("sbq_peer_wait", ctypes.c_void_p(self.base + self.cnt_last),
                ctypes.c_void_p(self.base + self.final_state), w, 0, stream)
         return cur
 
@@ -274,9 +320,10 @@ class ProjectionStack(nn.Module):
         self.layers = nn.ModuleList(StackLayer(i, hidden, inter, seed, dev, self.rank, self.world)
                                     for i in range(layers))
         self.exchange = exchange if self.world > 1 else "none"
+        # decode sizes, one GPU or the peer exchange: the side-output projections run as ready jobs
+        # of the next layer's first launch
+        self.overlap = overlap and self.exchange != "nccl"
         self.peer = PeerExchange(self) if self.exchange == "peer" else None
-        # one GPU, decode sizes: the side-output projections run as ready jobs of the next launch
-        self.overlap = overlap and self.world == 1
         self._side = (None, False)  # the last forward's last-layer side outputs, reordered on access?
 
     @property
@@ -402,7 +449,7 @@ class ProjectionStack(nn.Module):
         if program:
             return 1
         if m <= 16:
-            return len(self.layers) * 2 + (1 if self.peer is not None or self.overlap else 0)
+            return len(self.layers) * 2 + (1 if self.peer is not None else 0) + (1 if self.overlap else 0)
         return len(self.layers) * 5
 
 

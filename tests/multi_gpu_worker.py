@@ -46,8 +46,13 @@ def main() -> int:
         if not err < rel:
             failures.append("%s: relative L2 %g" % (name, err))
 
-    for exchange in ("peer", "nccl"):
-        st = sbq.stack.ProjectionStack(group=dist.group.WORLD, exchange=exchange, **shape)
+    # "peer" runs each layer's side outputs as ready jobs of the next layer's first launch by default
+    # ("peer-plain": the two-launches-per-layer grouping)
+    for exchange in ("peer", "peer-plain", "nccl"):
+        st = sbq.stack.ProjectionStack(group=dist.group.WORLD, exchange=exchange.split("-")[0],
+                                       overlap=exchange != "peer-plain", **shape)
+        if st.overlap != (exchange == "peer"):
+            failures.append("%s: overlap %s" % (exchange, st.overlap))
         for m in (1, 3, 16):
             x = sbq.workloads.activation(m, shape["hidden"], seed=20 + m, device=dev)
             check("%s eager m=%d" % (exchange, m), st(x).clone(), ref(x))
