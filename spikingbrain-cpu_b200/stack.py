@@ -367,6 +367,8 @@ class ProjectionStack(nn.Module):
             return self._forward_grouped(x)
         hd, w = self.hidden, self.world
         m = x.shape[0]
+        if self.overlap and w == 1:
+            return self._forward_side_stream(x)
         for layer in self.layers:
             qkvd = self._gather(layer.qkvd.forward_into(x, x.new_empty(m, 4 * hd // w)))
             h = self._gather(layer.mlp.gateup_into(x, x.new_empty(m, self.inter // w)))
@@ -375,6 +377,34 @@ class ProjectionStack(nn.Module):
             layer.dout.forward_into(qkvd[:, 3 * hd:], od[:, hd // w:])
             self._side = (self._gather(od), True)
             x = self._gather(layer.o.forward_into(qkvd[:, 2 * hd:3 * hd], x.new_empty(m, hd // w)))
+        return x
+
+    def _forward_side_stream(self, x: torch.Tensor) -> torch.Tensor:
+        """One GPU above 16 rows (one GEMM launch per projection): the layer chain q|k|v|delta_in,
+        gate/up, o runs on the caller's stream and the side outputs down(h) and delta_out(delta_in),
+        which nothing later in the step reads, on a second stream that waits only for their inputs,
+        so they fill the chain's launch boundaries and tails.  The caller's stream joins it at the
+        end (also inside a CUDA-graph capture: the two streams become parallel branches)."""
+        hd, m = self.hidden, x.shape[0]
+        main = torch.cuda.current_stream(x.device)
+        if getattr(self, "_side_stream", None) is None:
+            self._side_stream = torch.cuda.Stream(x.device)
+        side = self._side_stream
+        side.wait_stream(main)
+        keep = []  # inputs read on the side stream stay allocated until the streams join
+        od = None
+        for layer in self.layers:
+            qkvd = layer.qkvd.forward_into(x, x.new_empty(m, 4 * hd))
+            h = layer.mlp.gateup_into(x, x.new_empty(m, self.inter))
+            od = x.new_empty(m, 2 * hd)
+            keep += [qkvd, h, od]
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                layer.mlp.down_proj.forward_into(h, od[:, :hd])
+                layer.dout.forward_into(qkvd[:, 3 * hd:], od[:, hd:])
+            x = layer.o.forward_into(qkvd[:, 2 * hd:3 * hd], x.new_empty(m, hd))
+        main.wait_stream(side)
+        self._side = (od, False)
         return x
 
     def forward_modules(self, x: torch.Tensor) -> torch.Tensor:
