@@ -12,7 +12,7 @@
  * reference's nn.Linear replacements.
  *
  * Streams and host threads: the entry points may be called from several host threads and launch on
- * any streams.  The decode GEMV (sbq_linear_w8 up to 32 rows, sbq_gemv_w8, sbq_mlp_gateup_w8,
+ * any streams.  The decode GEMV (sbq_linear_w8 up to 16 rows, sbq_gemv_w8, sbq_mlp_gateup_w8,
  * sbq_gemv_w8_group[_peer]) takes a work counter and, for launches whose tiles are cut into K parts,
  * a split-K scratch region from device arrays of the library.  These are divided into 8 lanes per
  * device and each stream is given one lane on first use, so launches on up to 8 distinct streams of
@@ -109,18 +109,18 @@ SBQ_API int sbq_unpack_int8(const void* packed, int64_t n, int64_t k, int8_t* q,
 /* Int8Linear.forward (quant.py:41-53): y[m, n] = (x[m, :] . q[n, :]) * scale[n] (+ bias[n]).
  * x dtype SBQ_F16, SBQ_BF16 or SBQ_F32 (fp32 is split into two bf16 terms, ~17 significant bits);
  * y dtype SBQ_F32 (the reference's output type) or SBQ_F16.  bias may be NULL.  Chooses the
- * decode GEMV up to 32 rows and the tensor-memory GEMM above for fp16 / bf16 x; fp32 x always
+ * decode GEMV up to 16 rows and the tensor-memory GEMM above for fp16 / bf16 x; fp32 x always
  * takes the GEMV here (its GEMM path needs a workspace: sbq_linear_w8_ws). */
 SBQ_API int sbq_linear_w8(const void* x, int x_dtype, int64_t ldx, const void* packed, const float* scale,
                   const float* bias, int64_t m, int64_t n, int64_t k, void* y, int y_dtype, int64_t ldy,
                   void* stream);
 
 /* Bytes of workspace sbq_linear_w8_ws / sbq_mlp_gateup_w8_ws need for x [m, k] of x_dtype: nonzero
- * only for fp32 x above 32 rows (the bf16 high / low parts of x, 4 * m * k bytes rounded up). */
+ * only for fp32 x above 16 rows (the bf16 high / low parts of x, 4 * m * k bytes rounded up). */
 SBQ_API size_t sbq_linear_w8_workspace_bytes(int64_t m, int64_t k, int x_dtype);
 
 /* sbq_linear_w8 with a caller workspace (sbq_linear_w8_workspace_bytes bytes, 256-byte aligned; NULL
- * when that is 0), which puts fp32 activations above 32 rows - the reference's own prefill, fp32
+ * when that is 0), which puts fp32 activations above 16 rows - the reference's own prefill, fp32
  * x in chunks of up to 512 tokens (model.py:439-441, quant.py:47) - on the tensor-memory GEMM:
  * sbq_split_f32_bf16x2 into the workspace, then sbq_gemm_w8a16_x2.  Other calls behave exactly as
  * sbq_linear_w8. */
@@ -156,7 +156,7 @@ SBQ_API int sbq_gemm_w8a16_x2(const void* x_hi, const void* x_lo, int64_t ldx, c
                               void* stream);
 
 /* GatedMLP.forward's first half (model.py:239-240): h = silu(x q_gate^T * s_gate) * (x q_up^T * s_up)
- * with h written as h_dtype (SBQ_F16 or SBQ_F32).  Up to 32 rows (or fp32 x): one pass over
+ * with h written as h_dtype (SBQ_F16 or SBQ_F32).  Up to 16 rows (or fp32 x): one pass over
  * both weights ([n, k] each) in the decode GEMV.  More fp16 / bf16 rows: the gate projection goes into h
  * (rounded to h_dtype) and the up projection's GEMM epilogue replaces it by silu(gate) * up.  The
  * down projection is a separate sbq_linear_w8 call on h. */
@@ -165,7 +165,7 @@ SBQ_API int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const voi
                       int64_t n, int64_t k, void* h, int h_dtype, int64_t ldh, void* stream);
 
 /* sbq_mlp_gateup_w8 with a caller workspace (sbq_linear_w8_workspace_bytes(m, k, x_dtype) bytes):
- * fp32 x above 32 rows is split once and both GEMMs read the split (see sbq_linear_w8_ws). */
+ * fp32 x above 16 rows is split once and both GEMMs read the split (see sbq_linear_w8_ws). */
 SBQ_API int sbq_mlp_gateup_w8_ws(const void* x, int x_dtype, int64_t ldx, const void* packed_gate,
                                  const float* scale_gate, const void* packed_up, const float* scale_up, int64_t m,
                                  int64_t n, int64_t k, void* h, int h_dtype, int64_t ldh, void* workspace,

@@ -27,6 +27,13 @@ constexpr int kTileRows = 16;
 constexpr int kTileCols = 64;
 constexpr int kTileBytes = kTileRows * kTileCols;
 
+// Rows of x above which the int8 weight-only format runs the tensor-memory GEMM (sbq_linear_w8,
+// sbq_mlp_gateup_w8) instead of the decode GEMV, which streams the weight once per 16 rows.
+#ifndef SBQ_GEMM_MIN_ROWS
+#define SBQ_GEMM_MIN_ROWS 16
+#endif
+constexpr int64_t kGemmMinRows = SBQ_GEMM_MIN_ROWS;
+
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // Stream lanes (host): each (device, stream) pair is given one of kStreamLanes lanes, round robin on

@@ -1383,9 +1383,9 @@ int split_into_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, void*
                          void** hi, void** lo, void* stream);
 }
 
-// Rows of x above which the gate/up pair runs as two tensor-memory GEMMs (the gate projection into
-// h, then the up projection whose epilogue turns h into silu(gate) * up) instead of the fused GEMV.
-constexpr int64_t kGateUpGemmMinRows = 32;
+// Above kGemmMinRows rows of x the gate/up pair runs as two tensor-memory GEMMs (the gate projection
+// into h, then the up projection whose epilogue turns h into silu(gate) * up) instead of the fused GEMV.
+constexpr int64_t kGateUpGemmMinRows = kGemmMinRows;
 
 extern "C" int sbq_mlp_gateup_w8(const void* x, int x_dtype, int64_t ldx, const void* packed_gate,
                                  const float* scale_gate, const void* packed_up, const float* scale_up, int64_t m,

@@ -14,10 +14,6 @@ int split_into_workspace(const void* x, int64_t ldx, int64_t m, int64_t k, void*
 
 using namespace sbq;
 
-// Rows of x above which the tensor-memory GEMM (64-token tiles up to 128 rows, 256-token tiles
-// beyond) replaces the weight-streaming GEMV, which re-reads the weight once per 16 rows.
-constexpr int64_t kGemmMinRows = 32;
-
 extern "C" size_t sbq_linear_w8_workspace_bytes(int64_t m, int64_t k, int x_dtype) {
     if (m <= kGemmMinRows || k <= 0 || x_dtype != SBQ_F32) return 0;
     return split_workspace_bytes(m, k);

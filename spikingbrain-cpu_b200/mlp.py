@@ -58,7 +58,7 @@ class FusedGatedMLP(nn.Module):
         """Low-level device call: silu(gate(x2)) * up(x2) into ``h`` [m, n] (fp16/fp32, unit column stride).
 
         x2 is [m, k'] with 16-byte aligned rows (k' = in_features rounded up to 16).  The library
-        picks the kernel: the fused gate/up GEMV up to 32 rows; above, the gate GEMM into ``h`` and the
+        picks the kernel: the fused gate/up GEMV up to 16 rows; above, the gate GEMM into ``h`` and the
         up GEMM whose epilogue replaces it by silu(gate) * up (fp32 x split once into bf16 high / low
         parts in a workspace that both GEMMs read).
         """

@@ -380,25 +380,27 @@ class ProjectionStack(nn.Module):
         return x
 
     def _forward_side_stream(self, x: torch.Tensor) -> torch.Tensor:
-        """One GPU above 16 rows (one GEMM launch per projection): the layer chain q|k|v|delta_in,
-        gate/up, o runs on the caller's stream and the side outputs down(h) and delta_out(delta_in),
-        which nothing later in the step reads, on a second stream that waits only for their inputs,
-        so they fill the chain's launch boundaries and tails.  The caller's stream joins it at the
-        end (also inside a CUDA-graph capture: the two streams become parallel branches)."""
+        """One GPU above 16 rows (one GEMM launch per projection): the layer chain q|k|v|delta_in ->
+        o runs on the caller's stream; gate/up and the side outputs down(h) and delta_out(delta_in),
+        which nothing on the chain reads, run on a second stream that waits only for their inputs
+        (the layer input, then q|k|v|delta_in), so the two streams fill each other's launch
+        boundaries and tails.  The caller's stream joins the second one at the end (also inside a
+        CUDA-graph capture: the two streams become parallel branches)."""
         hd, m = self.hidden, x.shape[0]
         main = torch.cuda.current_stream(x.device)
         if getattr(self, "_side_stream", None) is None:
             self._side_stream = torch.cuda.Stream(x.device)
         side = self._side_stream
-        side.wait_stream(main)
-        keep = []  # inputs read on the side stream stay allocated until the streams join
+        keep = []  # tensors read on the second stream stay allocated until the streams join
         od = None
         for layer in self.layers:
-            qkvd = layer.qkvd.forward_into(x, x.new_empty(m, 4 * hd))
-            h = layer.mlp.gateup_into(x, x.new_empty(m, self.inter))
-            od = x.new_empty(m, 2 * hd)
-            keep += [qkvd, h, od]
-            side.wait_stream(main)
+            h, qkvd, od = x.new_empty(m, self.inter), x.new_empty(m, 4 * hd), x.new_empty(m, 2 * hd)
+            keep += [x, h, qkvd, od]
+            side.wait_stream(main)  # the layer input
+            with torch.cuda.stream(side):
+                layer.mlp.gateup_into(x, h)
+            layer.qkvd.forward_into(x, qkvd)
+            side.wait_stream(main)  # q|k|v|delta_in
             with torch.cuda.stream(side):
                 layer.mlp.down_proj.forward_into(h, od[:, :hd])
                 layer.dout.forward_into(qkvd[:, 3 * hd:], od[:, hd:])

@@ -114,10 +114,10 @@ def test_gemm_small_batch_split_k(sbq, m, n, k, out):
     assert sbq._lib.load().sbq_check_device_error() == 0
 
 
-@pytest.mark.parametrize("m", [40, 64, 300])
+@pytest.mark.parametrize("m", [17, 32, 40, 64, 300])
 @pytest.mark.parametrize("h_dtype", [torch.float16, torch.float32])
 def test_gated_gemm_gateup(sbq, m, h_dtype):
-    # above 32 rows the gate/up pair runs as two GEMMs: the gate projection into h, then the up
+    # above 16 rows the gate/up pair runs as two GEMMs: the gate projection into h, then the up
     # projection whose epilogue replaces it by silu(gate) * up (the gate is rounded to h's dtype)
     n, k = 1536, 1024
     wg = sbq.workloads.float_weight(n, k, seed=m + 1)
@@ -135,7 +135,7 @@ def test_gated_gemm_gateup(sbq, m, h_dtype):
 
 # ---- fp32 and bf16 activations on the tensor-memory GEMM ------------------------------------------
 # The reference's model feeds fp32 activations to every projection, in prefill chunks of up to 512
-# tokens (model.py:439-441, quant.py:47).  Above 32 rows the drop-in splits fp32 x into bf16 high and
+# tokens (model.py:439-441, quant.py:47).  Above 16 rows the drop-in splits fp32 x into bf16 high and
 # low parts (sbq_linear_w8_ws) and the GEMM runs one MMA per part; bf16 x runs on the GEMM directly.
 F32_REL_L2 = 2e-5  # the fp32 GEMV's bar: the split keeps ~17 significant bits of x
 
