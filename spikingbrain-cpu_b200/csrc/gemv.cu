@@ -25,8 +25,10 @@
 //     gate/up of one layer, which read the same x);
 //   * programmatic dependent launch: the weights never depend on the previous kernel, so the
 //     producer starts streaming at once; only the consumers wait (griddepcontrol.wait, or the
-//     peer signal of a sharded step) before reading x, and each CTA releases the next launch as
-//     soon as it starts.
+//     peer signal of a sharded step) before reading x, and each CTA releases the next launch once
+//     its consumers have passed that wait;
+//   * ready jobs (inputs written two or more launches back) are ordered first and their units run
+//     before the wait, which the consumers take at their first unit of another job.
 //
 // fp32 activations are split into a bf16 high and low part (two MMAs, ~16 mantissa bits kept);
 // the dot product of int8 weights and fp16/bf16 activations is exact up to fp32 accumulation.
