@@ -442,6 +442,18 @@ def kernel_cases(sbq, dev, stream, steps: int, warmup: int,
         ms_g = _graph_time(g, stream, max(20, steps // 10), warmup, per=8)
         out["cfg3_dyn"]["gemm_only_us"] = round(ms_g * 1e3, 2)
         out["cfg3_dyn"]["quantise_us"] = round((ms - ms_g) * 1e3, 2)
+        # the configuration's own wording: symmetric per-token scales (s8 x s8; the reference's
+        # DynamicInt8Linear quantises per tensor, the line above)
+        wsb_t = int(L.load().sbq_dyn_workspace_bytes(m, k, L.ACT_PER_TOKEN))
+        ws_t = torch.empty(wsb_t, dtype=torch.uint8, device=dev)
+
+        def f_tok():
+            L.call("sbq_linear_dyn", vp(x.data_ptr()), L.F16, k, L.ACT_PER_TOKEN, vp(p_.data_ptr()), None,
+                   vp(s_.data_ptr()), None, m, n, k, vp(y.data_ptr()), n, vp(ws_t.data_ptr()), wsb_t, st)
+
+        ms_t = _graph_time(f_tok, stream, max(20, steps // 10), warmup, per=8)
+        out["cfg3_dyn"]["per_token"] = {"us": round(ms_t * 1e3, 2), "tops": round(ops / ms_t / 1e9, 1),
+                                        "frac_roofline": round(t_roof * 1e3 / ms_t, 4), "calls_per_graph": 8}
     return out
 
 
