@@ -222,7 +222,7 @@ SBQ_API int sbq_gemv_w8_group_ready(const sbq_gemv_job* jobs, int njobs, int n_r
 
 /* The K split a grouped launch would choose (host only, no device call): shapes[3 i .. 3 i + 2] =
  * {n, k, matrices (1, or 2 for a fused gate/up job)} of job i, `slots` = CTAs the launch may use (3
- * per SM at m <= 8, 2 per SM at 9..16 rows).  parts[i] receives the K parts of each of job i's
+ * per SM at every m).  parts[i] receives the K parts of each of job i's
  * 16-row tiles (1 = unsplit).  Deterministic; the launch uses the same plan for the same shapes. */
 SBQ_API int sbq_gemv_plan_parts(const int64_t* shapes, int njobs, int slots, int64_t m, int* parts);
 

@@ -74,6 +74,7 @@ struct GemvGroup {
     GemvJob job[kMaxJobs];
     int njobs;
     int n_ready;                     // jobs [0, n_ready) are ready: their x is not the previous kernel's output
+    int spread;                      // > 1: CTAs per SM of the grid; first units dealt across SMs (see produce_units)
     int total_units;                 // units of all jobs (a unit = one K part of one 16-row tile)
     int unit_begin[kMaxJobs + 1];    // first unit of each job
     int parts[kMaxJobs];             // K parts per tile of each job (1: a tile is one unit)
@@ -269,6 +270,19 @@ struct GemvSmemSize {
 #define SBQ_GEMV_CTAS_PER_SM 3
 #endif
 constexpr int kCtasPerSm = SBQ_GEMV_CTAS_PER_SM;  // CTAs a launch is sized for (three fit per SM)
+// The same for 9..16 rows (twice the accumulators, 72 registers).  Measured on the 36-layer step:
+// three per SM 2.38 / 2.44 / 2.53 ms at 9 / 12 / 16 rows, two per SM 2.30 / 2.52 / 2.71 ms (a grid of
+// two per SM on a kernel that fits three leaves a third of the SMs idle: 3.08 ms at 9 rows).
+#ifndef SBQ_GEMV_CTAS_PER_SM_16
+#define SBQ_GEMV_CTAS_PER_SM_16 3
+#endif
+constexpr int kCtasPerSm16 = SBQ_GEMV_CTAS_PER_SM_16;
+// Launches with at least one unit per SM take the whole grid with their first units dealt across the
+// SMs (GemvGroup::spread).  Measured on the 36-layer step: batch 1 1.643 -> 1.63 ms, batch 8 1.95 ->
+// 1.88 ms; a 4096 x 4096 launch alone 6.17 -> 6.28 us at one row, 6.81 -> 6.57 us at eight.
+#ifndef SBQ_GEMV_SPREAD
+#define SBQ_GEMV_SPREAD 1
+#endif
 
 // Named barrier 1 over the consumer warps.
 __device__ __forceinline__ void consumers_sync() {
@@ -333,7 +347,13 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, unsigned* cl
                                               uint64_t* empty, int4* meta, uint32_t& ci) {
     constexpr int S = kMaxStages;
     constexpr int kStageBytes = kChunkTiles * kTileBytes;
-    int u = blockIdx.x;  // the first unit of every CTA is its own; later ones are claimed
+    // the first unit of every CTA is its own, later ones are claimed.  With `spread` (a grid of
+    // `spread` CTAs per SM) block b takes unit (b % spread) * (grid / spread) + b / spread: a
+    // permutation of the grid that deals the first units across the SMs however the blocks are
+    // placed (consecutive blocks share an SM or not), so a launch with fewer units than CTA slots
+    // does not crowd them onto a third of the SMs
+    int u = blockIdx.x;
+    if (grp.spread > 1) u = (int)(blockIdx.x % grp.spread) * (int)(gridDim.x / grp.spread) + (int)(blockIdx.x / grp.spread);
     for (;;) {
         if (u >= grp.total_units) {
             const int s = ci % S;
@@ -651,7 +671,7 @@ __device__ __forceinline__ bool consume_units(const GemvGroup& grp, uint8_t* rin
 }
 
 template <int XK, int MT, bool PEER>
-__global__ void __launch_bounds__(kGemvThreads, MT == 1 ? kCtasPerSm : 2)
+__global__ void __launch_bounds__(kGemvThreads, MT == 1 ? kCtasPerSm : kCtasPerSm16)
     gemv_w8_kernel(const __grid_constant__ GemvGroup grp, const __grid_constant__ PeerSync ps) {
     extern __shared__ __align__(128) uint8_t ring[];
     float* red = reinterpret_cast<float*>(ring + kRingBytes);
@@ -1127,6 +1147,11 @@ static int plan_units(GemvGroup& grp, PeerSync& ps, int slots, int m, int lane) 
     sorted.split_count = ub->split_count + region * kSplitTiles;
     grp = sorted;
     ps = pss;
+    if (SBQ_GEMV_SPREAD && units >= sm_count()) {
+        // at least one unit per SM: the whole grid, first units dealt across the SMs
+        grp.spread = slots / sm_count();
+        return slots;
+    }
     return units < slots ? units : slots;
 }
 
@@ -1134,7 +1159,8 @@ template <bool PEER>
 static int dispatch_group_t(GemvGroup& grp, PeerSync ps, int xk, int mt, cudaStream_t s) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return check_launch("cudaGetDevice");
-    const int ctas = plan_units(grp, ps, (mt == 2 ? 2 : kCtasPerSm) * sm_count(), grp.job[0].m, stream_lane(s, dev));
+    const int ctas = plan_units(grp, ps, (mt == 2 ? kCtasPerSm16 : kCtasPerSm) * sm_count(), grp.job[0].m,
+                                stream_lane(s, dev));
     if (ctas <= 0) return set_error(SBQ_ERR_CUDA, "grouped GEMV: no work counter on this device");
     switch (xk) {
         case kXF16:
