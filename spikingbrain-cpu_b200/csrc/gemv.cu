@@ -270,11 +270,11 @@ struct GemvSmemSize {
 #define SBQ_GEMV_CTAS_PER_SM 3
 #endif
 constexpr int kCtasPerSm = SBQ_GEMV_CTAS_PER_SM;  // CTAs a launch is sized for (three fit per SM)
-// The same for 9..16 rows (twice the accumulators, 72 registers).  Measured on the 36-layer step:
-// three per SM 2.38 / 2.44 / 2.53 ms at 9 / 12 / 16 rows, two per SM 2.30 / 2.52 / 2.71 ms (a grid of
-// two per SM on a kernel that fits three leaves a third of the SMs idle: 3.08 ms at 9 rows).
+// The same for 9..16 rows (twice the accumulators).  Measured: three per SM (72 registers) runs the
+// 36-layer step at 9 / 12 / 16 rows in 2.38 / 2.44 / 2.53 ms against 2.30 / 2.52 / 2.71 ms with two,
+// but the fused MLP alone at 16 rows (configuration 1) in 60 us against 52-54 us; two are kept.
 #ifndef SBQ_GEMV_CTAS_PER_SM_16
-#define SBQ_GEMV_CTAS_PER_SM_16 3
+#define SBQ_GEMV_CTAS_PER_SM_16 2
 #endif
 constexpr int kCtasPerSm16 = SBQ_GEMV_CTAS_PER_SM_16;
 // Launches with at least one unit per SM take the whole grid with their first units dealt across the
