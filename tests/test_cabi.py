@@ -91,3 +91,21 @@ def test_peer_group_arguments_rejected_on_the_host(sbq):
     assert lib.sbq_gemv_w8_group_peer(jobs, 1, L.F16, 1, ctypes.byref(pg), None) == L.ERR_INVALID_ARGUMENT
     assert lib.sbq_peer_wait(None, None, 1, 0, None) == L.ERR_INVALID_ARGUMENT
     assert lib.sbq_peer_wait(4100, 4096, 1, 0, None) == L.ERR_ALIGNMENT
+
+
+def test_ready_job_counts_rejected_on_the_host(sbq):
+    """sbq_gemv_w8_group_ready / _peer_ready check n_ready (0..njobs) before any CUDA call."""
+    import ctypes
+
+    L = sbq._lib
+    lib = L.load()
+    job = L.GemvJob(16, 64, 256, 256, None, None, None, 16, 64, 512, L.F32, 16)
+    jobs = (L.GemvJob * 2)(job, job)
+    for n_ready in (-1, 3):
+        assert lib.sbq_gemv_w8_group_ready(jobs, 2, n_ready, L.F16, 1, None) == L.ERR_INVALID_ARGUMENT
+        assert b"n_ready" in lib.sbq_last_error()
+        pg = L.PeerGroup()
+        pg.nranks = 1
+        assert lib.sbq_gemv_w8_group_peer_ready(jobs, 2, n_ready, L.F16, 1, ctypes.byref(pg), None) == \
+            L.ERR_INVALID_ARGUMENT
+    assert lib.sbq_gemv_w8_group_peer_ready(jobs, 2, 1, L.F16, 1, None, None) == L.ERR_INVALID_ARGUMENT
