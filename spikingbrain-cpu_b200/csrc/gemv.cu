@@ -398,14 +398,6 @@ __device__ __forceinline__ bool produce_units(const GemvGroup& grp, unsigned* cl
     }
 }
 
-// Consumers (8 warps): per unit, its chunks (each warp takes tiles slot and slot + 8 of each chunk,
-// or slot and slot + 4 of each matrix of a gate/up chunk - the same tiles, in the same order, as one
-// tile per warp of chunks half the size; per tile two conflict-free 16-byte shared loads per lane,
-// int8 -> fp16/bf16 in registers, m16n8k16 MMAs with the activation rows as the n dimension), then
-// the fixed-order reduction and the epilogue.  The
-// job and the warp split are read once per unit from the first chunk's stage.
-// False (warp-uniformly) on a timeout.
-// `ci` / `units`: ring position and units done so far (both continue across calls).
 // The consumers' wait for the producer of x when it is deferred past the ready jobs' units: the
 // previous grid (griddepcontrol.wait, every thread), or in a sharded launch the producing launch's
 // signal on every rank - thread 0 waits (peer_wait: once per CTA, it also records the CTA's arrival)
@@ -441,6 +433,14 @@ __device__ __forceinline__ void deferred_wait(const PeerSync& ps, int* s_flag) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Consumers (8 warps): per unit, its chunks (each warp takes tiles slot and slot + 8 of each chunk,
+// or slot and slot + 4 of each matrix of a gate/up chunk - the same tiles, in the same order, as one
+// tile per warp of chunks half the size; per tile two conflict-free 16-byte shared loads per lane,
+// int8 -> fp16/bf16 in registers, m16n8k16 MMAs with the activation rows as the n dimension), then
+// the fixed-order reduction and the epilogue.  The
+// job and the warp split are read once per unit from the first chunk's stage.
+// False (warp-uniformly) on a timeout.
+// `ci` / `units`: ring position and units done so far (both continue across calls).
 // `waited`: null when the consumers have waited for the previous kernel already; else the flag of a
 // deferred wait (deferred_wait), taken before the first unit of a job that is not ready.
 template <int XK, int MT, bool PEER>
