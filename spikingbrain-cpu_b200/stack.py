@@ -237,6 +237,8 @@ class PeerExchange:
         (their inputs are complete on every rank once the o launch in between has seen its signal),
         [o] alone in the second launch, and one last launch for the last layer's side outputs."""
         L, st = self.L, self.stack
+        if len(st.layers) == 0:
+            return x
         m = x.shape[0]
         hd, it, w, r = st.hidden, st.inter, st.world, st.rank
         hs, qs, s = it // w, 4 * hd // w, hd // w
@@ -430,6 +432,8 @@ class ProjectionStack(nn.Module):
         from .quant import gemv_group
 
         hd, m = self.hidden, x.shape[0]
+        if len(self.layers) == 0:
+            return x
         keep = []  # every buffer stays allocated until the step is enqueued: no launch reuses
         prev = None  # memory that the launch before it may still be reading
         for layer in self.layers:
