@@ -356,12 +356,14 @@ class ProjectionStack(nn.Module):
 
         Decode sizes (m <= 16) run each layer as two grouped launches: [gate/up, q|k|v|delta_in]
         (both read x) and [down, o, delta_out] (after their inputs are gathered); o's output is the
-        next layer's input.  On one GPU (``overlap``) the side outputs move to the next layer's first
-        launch, as ready jobs whose inputs are two launches old: layer i runs [down(h), delta_out of
-        layer i - 1 | gate/up, q|k|v|delta_in] and [o], and one last launch computes the last layer's
-        side outputs.  The ready jobs stream while the o launch before them ends, so that launch
-        boundary overlaps work (measured at full size: 1.69-1.71 -> 1.65 ms per step at batch 1,
-        2.06 -> 1.94 ms at batch 8; the side outputs split between both launches gained less).
+        next layer's input.  With ``overlap`` (one GPU, or the peer exchange) the side outputs move to
+        the next layer's first launch, as ready jobs whose inputs are two launches old: layer i runs
+        [down(h), delta_out of layer i - 1 | gate/up, q|k|v|delta_in] and [o], and one last launch
+        computes the last layer's side outputs.  The ready jobs stream while the o launch before them
+        ends, so that launch boundary overlaps work (measured at full size: 1.69-1.71 -> 1.65 ms per
+        step at batch 1, 2.06 -> 1.94 ms at batch 8 on one GPU; 1.41 -> 1.26 ms at batch 1 on two).
+        Above 16 rows (one GEMM per projection) one GPU runs the q|k|v|delta_in -> o chain and the
+        other projections on two streams (``_forward_side_stream``).
         """
         if x.shape[0] <= 16:
             if self.peer is not None:
