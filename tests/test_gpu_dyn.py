@@ -252,7 +252,7 @@ def test_decode_split_k_bit_exact(sbq, m, n, k, mode):
                                    (9, 300, 512), (1, 64, 12304)])
 @pytest.mark.parametrize("xdtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("mode", ["per_tensor", "per_token"])
-def test_decode_fused_quantisation_bit_exact(sbq, m, n, k, xdtype, mode):
+def test_decode_sizes_ragged_k_strided_rows_bit_exact(sbq, m, n, k, xdtype, mode):
     w = sbq.workloads.float_weight(n, k, seed=n + k)
     bias = torch.randn(n) if m % 2 else None
     wide = sbq.workloads.activation(m, k + 64, seed=m + k, dtype=torch.float32) * 3.0
